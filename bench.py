@@ -1,0 +1,323 @@
+"""Benchmark: Llama-3.2-1B bf16 batch-1 decode.
+
+Workload (config 2): random-init Llama-3.2-1B geometry (seed 1), a 128-id
+prompt, then greedy decode over positions 128..383 with a contiguous KV cache.
+A step is one decoded token. The K timed steps cycle through that 256-token
+window (the position is reset to 128 every 256 tokens; the prompt stays
+cached). The decode step streams 2.47 GB of weights, far more than the 126 MB
+L2, so no L2 flush is needed between steps.
+
+  value  device throughput: tokens/s from CUDA events on the context's stream
+         around graph launches of the step, token feedback on the device.
+  e2e    the same through the C ABI with host buffers: every step copies its
+         token and position from pinned host memory, runs, and reads the next
+         token back, synchronising each step (the reference's decode loop).
+  roofline  the streaming GEMV (dominant kernel): algorithmic bytes per launch
+         / the CUDA-event launch time measured here, against MEASURED_PEAKS.json.
+
+Multi-GPU (torchrun): every rank decodes its own independent sequence on its
+own GPU with its own weight replica -- the reference has no collective on this
+path, so there is none; value = all ranks' tokens / the slowest rank's time.
+
+--impl reference: the reference has no CPU implementation of the decode step,
+so its arm is the fp32 host evaluation (oracle port) of the same workload on
+the host cores, rank 0 only.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "llama-cuda-runtime_b200"))
+
+import numpy as np  # noqa: E402
+
+PROMPT = 128
+WINDOW = 256
+METRIC = "Llama-3.2-1B bf16 decode tok/s (bs1, config 2)"
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the gate/up GEMV from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "gemv_gate_up_1b.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi clock samples during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/lcr_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        try:
+            rows = [l.split(",") for l in open(self.path).read().strip().splitlines()]
+        except OSError:
+            return None
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 7]
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def reduce_max(world, value):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(block, seconds=12.0, max_tokens=64):
+    """The fp32 host evaluation (oracle port) on this host's cores: decode
+    steps at positions 0.. for about `seconds`."""
+    import oracle
+
+    from lcr_b200 import checkpoint as ck
+
+    m = oracle.Model(block, max_tokens + 1)
+    ids = ck.prompt_ids(1, max_tokens)
+    m.decode(int(ids[0]), 0, oracle.MODE_FP32)  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n + 1 < max_tokens and time.perf_counter() - t0 < seconds:
+        m.decode(int(ids[n + 1]), n + 1, oracle.MODE_FP32)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} Llama-3.2-1B decode steps of the fp32 host oracle at positions 1..{n} "
+                      f"(OpenMP over output rows, {os.cpu_count()} threads)"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from lcr_b200 import checkpoint as ck
+
+    block = ck.generate(ck.LLAMA_3_2_1B, 1)
+    budget = max(1, min(args.steps, 48))
+    base = cpu_baseline(block, seconds=60.0, max_tokens=budget + 1)
+    line = {"metric": METRIC, "value": base["value"], "unit": "tok/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2: Llama-3.2-1B geometry seed 1, bs1 decode, contiguous KV",
+                       "note": "the reference has no CPU decode path; this arm is the fp32 host "
+                               "evaluation (oracle port) of the same step"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2560)
+    ap.add_argument("--warmup", type=int, default=64)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    import torch
+
+    from lcr_b200 import checkpoint as ck
+    from lcr_b200 import runtime as rt
+
+    torch.cuda.set_device(local)
+    g = ck.LLAMA_3_2_1B
+    block = ck.generate(g, 1)
+    prompt = ck.prompt_ids(1, PROMPT)
+    m = rt.Model(block, device=local, max_seq=PROMPT + WINDOW + 8)
+    m.prefill(prompt[:-1])
+    first = int(prompt[-1])
+    stream = torch.cuda.ExternalStream(m.stream, device=f"cuda:{local}")
+
+    def run_window(n, start_pos):
+        """n device-resident greedy steps from start_pos (<= WINDOW)."""
+        tok = np.array([first], np.int32)
+        m.set_token(tok.ctypes.data, start_pos)
+        m.sync()
+        return m.time_steps(n)
+
+    # warm-up (graph capture happens on first use)
+    run_window(min(args.warmup, WINDOW), PROMPT - 1)
+
+    barrier(world)
+    torch.cuda.synchronize()
+    total_ms, done = 0.0, 0
+    with Clocks(local) as clk:
+        while done < args.steps:
+            n = min(WINDOW, args.steps - done)
+            total_ms += run_window(n, PROMPT - 1)
+            done += n
+    torch.cuda.synchronize()
+    barrier(world)
+    max_ms = reduce_max(world, total_ms)
+    value = world * args.steps / (max_ms / 1000.0)
+
+    # end to end: host token in, host token out, every step
+    pinned = torch.empty(2, dtype=torch.int32, pin_memory=True)
+    tok_ptr = pinned.data_ptr()
+    e2e_steps = min(args.steps, 1024)
+    pinned[0] = first
+    m.set_token(tok_ptr, PROMPT - 1)
+    m.sync()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    pos = PROMPT - 1
+    for i in range(e2e_steps):
+        if pos >= PROMPT - 1 + WINDOW:
+            pos = PROMPT - 1
+        m.set_token(tok_ptr, pos)        # H2D: token + position
+        m.enqueue_steps(1)
+        m.read_token(tok_ptr)            # D2H: next token
+        m.sync()
+        pos += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = reduce_max(world, e0.elapsed_time(e1))
+    e2e_value = world * e2e_steps / (e2e_ms / 1000.0)
+
+    # roofline of the dominant kernel: the streaming GEMV (gate/up, 67.1 MB)
+    peak, peak_kind = measured_peaks()
+    per_matrix = {}
+    names = ["qkv", "o_proj", "gate_up", "down", "lm_head"]
+    h, f, q, kv, v = g.hidden_size, g.intermediate_size, g.q_dim, g.kv_dim, g.vocab_size
+    bytes_of = {"qkv": (q + 2 * kv) * h * 2, "o_proj": h * q * 2, "gate_up": 2 * f * h * 2,
+                "down": h * f * 2, "lm_head": v * h * 2}
+    for i, name in enumerate(names):
+        ms = m.time_gemv(i, 0, 20)
+        per_matrix[name] = {"us": round(ms * 1000, 2),
+                            "gbs": round(bytes_of[name] / (ms / 1000) / 1e9, 1)}
+    gu = per_matrix["gate_up"]
+    achieved = bytes_of["gate_up"] / (gu["us"] / 1e6) / 1e9
+
+    ms_per_step = max_ms / args.steps
+    ctx_mean = PROMPT + WINDOW / 2
+    step_bytes = g.weight_bytes_per_token() + ctx_mean * g.kv_bytes_per_position()
+    if rank == 0:
+        base = None if args.no_cpu_baseline or world > 1 else cpu_baseline(block)
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, seed 1; uniform prompt ids)",
+            "config": {"workload": "config2: Llama-3.2-1B geometry, bs1 greedy decode, 128-id "
+                                   "prompt, positions 128..383, contiguous KV",
+                       "global_batch": world, "seq_len": PROMPT + WINDOW,
+                       "parallelism": f"replicas x{world} (independent sequences)",
+                       "l2": "no flush: each step streams 2.47 GB > 126 MB L2"},
+            "hbm": {"bytes_per_token": int(step_bytes),
+                    "achieved_gbs": round(step_bytes / (ms_per_step / 1000) / 1e9, 1),
+                    "frac_of_peak": round(step_bytes / (ms_per_step / 1000) / 1e9 / peak, 4),
+                    "peak_gbs": peak},
+            "roofline": {"kernel": "gemv_stream_kernel (gate/up, K=2048, 16384 rows)",
+                         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profile_traffic(), "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": bytes_of["gate_up"],
+                         "per_matrix_layer0": per_matrix},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4, "steps": e2e_steps},
+            "gpu_launches": args.steps * m.step_launches(),
+            "clocks": clocks,
+            "cpu_baseline": base,
+        }
+        print(json.dumps(line))
+    m.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,267 @@
+/*
+ * lcr_b200 -- C ABI of the B200 (sm_100a) Llama decode step.
+ *
+ * Drop-in boundary for the forward path of mohamadmsalman82/llama-cuda-runtime:
+ *   - one entry point per host launcher of src/kernels.cuh (the `launch_*`
+ *     free functions), same argument meaning, raw device pointers, async on
+ *     the given stream, no allocation inside;
+ *   - lcr_gemm_nt replacing the cuBLAS `gemm_nt` of src/model.cu:38-45;
+ *   - a decode context replacing Model::decode / Model::sample / prefill
+ *     (src/model.h:60-127, src/model.cu:308-597), whose whole step is a
+ *     CUDA graph of hand-written sm_100a kernels with the token, position and
+ *     sampling state resident on the device.
+ *
+ * Conventions: bf16 tensors are `void*` to 16-bit bf16 storage; every function
+ * returns an lcr_status (0 = LCR_OK); no C++ exception crosses this boundary;
+ * lcr_last_error_string() describes the last failure on the calling thread.
+ * The caller owns every buffer passed in; buffers a context allocates are
+ * freed by lcr_ctx_destroy. Where the reference threw lcr::Error (LCR_CHECK),
+ * these functions return LCR_ERR_INVALID / LCR_ERR_SHAPE with the same text.
+ */
+#ifndef LCR_B200_H
+#define LCR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LCR_API __attribute__((visibility("default")))
+#else
+#define LCR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* lcr_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+enum lcr_status {
+  LCR_OK = 0,
+  LCR_ERR_INVALID = 1,     /* bad argument: null pointer, non-positive size */
+  LCR_ERR_SHAPE = 2,       /* shape this build has no kernel for */
+  LCR_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  LCR_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
+  LCR_ERR_POOL = 5,        /* paged KV pool exhausted */
+  LCR_ERR_STATE = 6,       /* call out of order (e.g. sequence full) */
+  LCR_ERR_NO_DEVICE = 7    /* no sm_100 device */
+};
+
+LCR_API const char* lcr_last_error_string(void);
+LCR_API const char* lcr_status_string(int status);
+LCR_API int lcr_version(void); /* major * 10000 + minor * 100 + patch */
+
+/* ------------------------------------------------------------------------- */
+/* KV cache view -- KvCacheView, src/kv_cache.cuh:33-57.                      */
+/* Element offset of (head, position): page * page_stride +                  */
+/* head * head_stride + slot * head_dim, page = page_table[pos / page_size], */
+/* slot = pos % page_size (contiguous: page 0, slot = pos).                  */
+/* ------------------------------------------------------------------------- */
+typedef struct lcr_kv_view {
+  void* keys;
+  void* values;
+  const int32_t* page_table; /* NULL for the contiguous layout */
+  int page_size;
+  int page_stride;
+  int head_stride;
+  int num_kv_heads;
+  int head_dim;
+} lcr_kv_view;
+
+/* ------------------------------------------------------------------------- */
+/* Per-kernel entry points (src/kernels.cuh:17-132)                           */
+/* ------------------------------------------------------------------------- */
+
+/* launch_embedding_lookup, src/kernels.cuh:17-20: out[t,:] = table[ids[t],:] */
+LCR_API int lcr_embedding_lookup(void* out, const void* table, const int32_t* ids,
+                         int tokens, int dim, lcr_stream_t stream);
+
+/* launch_rmsnorm, src/kernels.cuh:22-26 */
+LCR_API int lcr_rmsnorm(void* out, const void* x, const void* weight, int tokens,
+                int dim, float eps, lcr_stream_t stream);
+
+/* launch_add_residual, src/kernels.cuh:28-30 */
+LCR_API int lcr_add_residual(void* x, const void* delta, int64_t count,
+                     lcr_stream_t stream);
+
+/* launch_add_residual_rmsnorm, src/kernels.cuh:32-43 */
+LCR_API int lcr_add_residual_rmsnorm(void* out, void* x, const void* delta,
+                             const void* weight, int tokens, int dim,
+                             float eps, lcr_stream_t stream);
+
+/* launch_swiglu, src/kernels.cuh:45-47 */
+LCR_API int lcr_swiglu(void* out, const void* gate, const void* up, int64_t count,
+               lcr_stream_t stream);
+
+/* launch_swiglu_strided, src/kernels.cuh:49-54 */
+LCR_API int lcr_swiglu_strided(void* out, const void* gate, const void* up, int tokens,
+                       int width, int src_row_stride, lcr_stream_t stream);
+
+/* launch_rope_q, src/kernels.cuh:56-67: [tokens][heads*d] -> [heads][tokens][d] */
+LCR_API int lcr_rope_q(void* q_heads, const void* q_proj, const float* inv_freq,
+               int tokens, int start_position, int num_heads, int head_dim,
+               int src_row_stride, lcr_stream_t stream);
+
+/* launch_rope_write_kv, src/kernels.cuh:69-75 */
+LCR_API int lcr_rope_write_kv(const lcr_kv_view* view, const void* k_proj,
+                      const void* v_proj, const float* inv_freq, int tokens,
+                      int start_position, int paged, int src_row_stride,
+                      lcr_stream_t stream);
+
+/* launch_decode_attention, src/kernels.cuh:96-116: single-token GQA attention
+ * over seq_len cached positions, split-K over `splits` blocks per KV head. */
+LCR_API int lcr_decode_attention(void* out, const void* q, const lcr_kv_view* view,
+                         int num_heads, int heads_per_kv, int seq_len,
+                         float scale, int paged, int splits, float* scratch,
+                         lcr_stream_t stream);
+
+/* decode_attention_scratch_floats, src/kernels.cuh:118-120 */
+LCR_API size_t lcr_decode_attention_scratch_floats(int num_heads, int head_dim,
+                                           int splits);
+
+/* choose_attention_splits, src/kernels.cuh:122-124 */
+LCR_API int lcr_choose_attention_splits(int num_kv_heads, int seq_len,
+                                int multiprocessors);
+
+/* launch_sample, src/kernels.cuh:130-136: temperature 0 = argmax (ties to the
+ * lowest id); otherwise top-k/top-p over the full-vocab softmax with the
+ * host's uniform in [0,1). Deterministic: equal inputs give equal ids. */
+LCR_API int lcr_sample(int32_t* out_id, const float* logits, int vocab,
+               float temperature, int top_k, float top_p, float uniform,
+               float* scratch, lcr_stream_t stream);
+
+/* sample_scratch_floats, src/kernels.cuh:138 */
+LCR_API size_t lcr_sample_scratch_floats(int vocab, int top_k);
+
+/* gemm_nt, src/model.cu:38-45: y[rows][out] = x[rows][in] * w[out][in]^T,
+ * bf16 inputs, fp32 accumulation, bf16 output (y_fp32 = 0) or fp32 output
+ * (y_fp32 = 1, the lm_head case of src/model.cu:481). */
+LCR_API int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, int rows,
+                int in_features, int out_features, lcr_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Decode context -- Model (src/model.h:60-127)                               */
+/* ------------------------------------------------------------------------- */
+
+typedef struct lcr_model_desc { /* ModelConfig, src/config.h:22-60 */
+  int hidden_size;
+  int intermediate_size;
+  int num_layers;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int vocab_size;
+  float rms_norm_eps;
+  float rope_theta;
+  int rope_scaling; /* 1 = llama3 */
+  float rope_factor;
+  float rope_low_freq_factor;
+  float rope_high_freq_factor;
+  int rope_original_max_position_embeddings;
+} lcr_model_desc;
+
+typedef struct lcr_layer_weights { /* LayerWeights, src/model.h:29-43 */
+  const void* input_norm;          /* [hidden] */
+  const void* qkv_proj;            /* [q_dim + 2 kv_dim][hidden], rows q;k;v */
+  const void* o_proj;              /* [hidden][q_dim] */
+  const void* post_attention_norm; /* [hidden] */
+  const void* gate_up_proj;        /* [2 ffn][hidden], rows gate;up */
+  const void* down_proj;           /* [hidden][ffn] */
+} lcr_layer_weights;
+
+typedef struct lcr_weights { /* device pointers, caller-owned */
+  const void* embedding;  /* [vocab][hidden] */
+  const void* final_norm; /* [hidden] */
+  const void* lm_head;    /* [vocab][hidden]; the embedding when tied */
+  const lcr_layer_weights* layers; /* host array of num_layers entries */
+} lcr_weights;
+
+typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
+  int device;
+  int max_seq;          /* KV positions per sequence */
+  int paged;            /* 0 = contiguous, 1 = paged */
+  int page_size;        /* positions per page (paged); 16 in the reference */
+  int attention_splits; /* split-K blocks per KV head; 0 = choose */
+  uint64_t page_order_seed; /* 0 = pages handed out in counter order;
+                               otherwise a seeded permutation of the pool */
+  int gemv_ctas;        /* CTAs per streaming GEMV; 0 = one per SM */
+  int flags;            /* bit 0: disable programmatic dependent launch */
+} lcr_options;
+
+typedef struct lcr_ctx lcr_ctx;
+
+LCR_API int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* weights,
+                   const lcr_options* options, lcr_ctx** out);
+LCR_API void lcr_ctx_destroy(lcr_ctx* ctx);
+
+/* Model::reset, src/model.h:91: position back to 0 (the cache is reused). */
+LCR_API int lcr_reset(lcr_ctx* ctx);
+/* Model::position */
+LCR_API int lcr_position(const lcr_ctx* ctx);
+
+/* Model::decode, src/model.cu:347-368: one token at the current position;
+ * *logits receives the device fp32 logits [vocab], valid until the next
+ * call. Synchronous, like the reference. */
+LCR_API int lcr_decode(lcr_ctx* ctx, int token, const float** logits);
+
+/* Model::prefill, src/model.cu:308-345: the prompt, one decode step per token
+ * (the same maths as a decode step); *logits for the last token. */
+LCR_API int lcr_prefill(lcr_ctx* ctx, const int32_t* tokens, int count,
+                const float** logits);
+
+/* Model::logits_to_host, src/model.cu:599-604: copies the [vocab] fp32 logits
+ * of the last step to host memory (synchronous). */
+LCR_API int lcr_logits_to_host(lcr_ctx* ctx, float* host);
+
+/* Model::sample, src/model.cu:584-597: a token id from device logits. */
+LCR_API int lcr_sample_logits(lcr_ctx* ctx, const float* logits, float temperature,
+                      int top_k, float top_p, float uniform, int* token);
+
+/* Device-resident greedy generation: the step graph replayed `steps` times,
+ * each step's argmax feeding the next with no host round trip. Starts from
+ * `first_token` at the current position; tokens_out (host, nullable) receives
+ * the `steps` generated ids. Synchronous. */
+LCR_API int lcr_generate_greedy(lcr_ctx* ctx, int first_token, int steps,
+                        int32_t* tokens_out);
+
+/* Asynchronous pieces of the same loop, for timing and for host pipelines:
+ * lcr_set_token stages (token, position) into device state on the context's
+ * stream from host memory; lcr_enqueue_steps launches `steps` step graphs;
+ * lcr_read_token copies the latest device token to host memory (pinned for
+ * true async) and lcr_sync waits for the stream. */
+LCR_API int lcr_set_token(lcr_ctx* ctx, const int32_t* host_token, int position);
+LCR_API int lcr_enqueue_steps(lcr_ctx* ctx, int steps);
+LCR_API int lcr_read_token(lcr_ctx* ctx, int32_t* host_token);
+LCR_API int lcr_sync(lcr_ctx* ctx);
+LCR_API lcr_stream_t lcr_ctx_stream(lcr_ctx* ctx);
+
+/* The device KV view of one layer (KvCache::view, src/kv_cache.cu:121-144). */
+LCR_API int lcr_kv_view_of(const lcr_ctx* ctx, int layer, lcr_kv_view* view);
+/* Copies the host mirror of the page tables ([layers][max_pages] int32) to
+ * `tables`; returns the number of pages handed out in *pages_mapped. */
+LCR_API int lcr_page_tables(const lcr_ctx* ctx, int32_t* tables, int* pages_mapped);
+/* KvCache::reserve_length, src/kv_cache.cu:73-102 */
+LCR_API int lcr_reserve_length(lcr_ctx* ctx, int length);
+
+/* Bytes one decode step streams from HBM (src/model.cu:91-102) and the KV
+ * bytes per cached position (src/config.h:47-49). */
+LCR_API size_t lcr_weight_bytes_per_token(const lcr_ctx* ctx);
+LCR_API size_t lcr_kv_bytes_per_position(const lcr_ctx* ctx);
+/* Kernel launches in one decode step. */
+LCR_API int lcr_step_launches(const lcr_ctx* ctx);
+/* Reads and clears the device status word the context's kernels report
+ * bounded-wait failures and out-of-range tokens / positions / pages through:
+ * LCR_OK, LCR_ERR_TIMEOUT, LCR_ERR_INVALID, LCR_ERR_POOL or LCR_ERR_STATE. */
+LCR_API int lcr_device_status(lcr_ctx* ctx);
+
+/* Measurement: `steps` step graphs timed with CUDA events on the context's
+ * stream (device state advances as in lcr_enqueue_steps), and `reps`
+ * back-to-back launches of one streaming GEMV of the step (matrix 0 qkv,
+ * 1 o_proj, 2 gate_up, 3 down, 4 lm_head; reps <= 128), in ms per launch. */
+LCR_API int lcr_time_steps(lcr_ctx* ctx, int steps, float* ms);
+LCR_API int lcr_time_gemv(lcr_ctx* ctx, int matrix, int layer, int reps, float* ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,837 @@
+// The decode context: Model (src/model.h:60-127) for the B200.
+//
+// A step is one token of one sequence through every layer. It is launched as
+// a chain of 5 kernels per layer plus the output head, with programmatic
+// dependent launch so each kernel's weight stream starts while the previous
+// kernel drains, and captured once as a CUDA graph. Everything a step needs
+// from the host -- the token and its position -- lives in device memory, and
+// the output head's last CTA writes the argmax back there, so a greedy
+// generation is a sequence of graph launches with no host round trip.
+//
+//   per layer  qkv GEMV   (RMSNorm prologue; embedding row for layer 0)
+//              attention  (RoPE of q and the new k, KV write, split-K, merge)
+//              o GEMV     (residual epilogue)
+//              gate/up GEMV (RMSNorm prologue, SwiGLU epilogue)
+//              down GEMV  (residual epilogue)
+//   then       lm_head GEMV (final-norm prologue, fp32 logits + argmax)
+//
+// The KV cache is the reference's (src/kv_cache.cu): contiguous
+// [layer][kv_head][max_seq][d], or a paged pool of [kv_head][page][d] pages
+// with one table per layer, pages handed out layer by layer from a counter --
+// optionally through a seeded permutation of the pool (shuffled physical
+// order).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "dispatch.h"
+#include "gemv_dispatch.h"
+#include "lcr_b200.h"
+
+using namespace lcrb;
+
+namespace {
+
+enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2 };
+constexpr int kPinnedRing = 256;
+constexpr int kTimingSlots = 128;
+
+uint64_t splitmix64(uint64_t* s) {
+  uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// The RoPE table of src/config.cpp:223-259 (double math, float table).
+std::vector<float> rope_inv_freq(const lcr_model_desc& d) {
+  const int pairs = d.head_dim / 2;
+  std::vector<float> f(static_cast<size_t>(pairs));
+  for (int i = 0; i < pairs; ++i) {
+    f[static_cast<size_t>(i)] = static_cast<float>(
+        1.0 / std::pow(static_cast<double>(d.rope_theta), static_cast<double>(2 * i) / d.head_dim));
+  }
+  if (!d.rope_scaling) return f;
+  const double old_context = d.rope_original_max_position_embeddings;
+  const double low_wavelen = old_context / d.rope_low_freq_factor;
+  const double high_wavelen = old_context / d.rope_high_freq_factor;
+  for (int i = 0; i < pairs; ++i) {
+    const double freq = f[static_cast<size_t>(i)];
+    const double wavelen = 2.0 * M_PI / freq;
+    double scaled;
+    if (wavelen < high_wavelen) {
+      scaled = freq;
+    } else if (wavelen > low_wavelen) {
+      scaled = freq / d.rope_factor;
+    } else {
+      const double smooth = (old_context / wavelen - d.rope_low_freq_factor) /
+                            (d.rope_high_freq_factor - d.rope_low_freq_factor);
+      scaled = (1.0 - smooth) * (freq / d.rope_factor) + smooth * freq;
+    }
+    f[static_cast<size_t>(i)] = static_cast<float>(scaled);
+  }
+  return f;
+}
+
+}  // namespace
+
+struct lcr_ctx {
+  int device = 0;
+  lcr_model_desc d{};
+  lcr_options o{};
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  bool pdl = true;
+  bool use_graph = true;
+
+  const bf16* embed = nullptr;
+  const bf16* final_norm = nullptr;
+  const bf16* lm_head = nullptr;
+  std::vector<lcr_layer_weights> layers;
+
+  char* buf = nullptr;
+  bf16* x = nullptr;
+  float* xsum = nullptr;
+  bf16* qkv = nullptr;
+  bf16* attn = nullptr;
+  bf16* act = nullptr;
+  float* logits = nullptr;
+  float* partials = nullptr;
+  unsigned* attn_ctr = nullptr;
+  unsigned* sched = nullptr;
+  int sched_slots = 0;
+  unsigned long long* argmax_acc = nullptr;
+  int32_t* state = nullptr;  // [0] token, [1] position
+  int32_t* history = nullptr;
+  uint32_t* status = nullptr;
+  float* inv_freq = nullptr;
+  float* sample_params = nullptr;
+  int32_t* sampled = nullptr;
+
+  bf16* kpool = nullptr;
+  bf16* vpool = nullptr;
+  int32_t* tables_dev = nullptr;
+  std::vector<int32_t> tables_host;
+  std::vector<int32_t> order;
+  int max_pages = 0, pool_pages = 0, pages_mapped = 0, length = 0;
+  int splits = 1;
+
+  cudaGraphExec_t exec = nullptr;
+  int launches = 0;
+  int position = 0;
+
+  int32_t* pinned = nullptr;  // ring of [token, position] pairs
+  int ring_next = 0;
+  int32_t* pinned_prompt = nullptr;
+  size_t pinned_prompt_cap = 0;
+  float* pinned_params = nullptr;
+};
+
+namespace {
+
+int q_dim(const lcr_ctx* c) { return c->d.num_heads * c->d.head_dim; }
+int kv_dim(const lcr_ctx* c) { return c->d.num_kv_heads * c->d.head_dim; }
+
+int gemv_node(lcr_ctx* c, GemvArgs a, int K, int pro, int epi, int n_out, int* slot) {
+  const int per = gemv_outputs_per_chunk(K, epi);
+  a.n_out = n_out;
+  a.n_chunks = (n_out + per - 1) / per;
+  LCRB_REQUIRE(*slot < c->sched_slots, LCR_ERR_STATE, "GEMV scheduler slots exhausted");
+  a.sched = c->sched + 2 * (*slot)++;
+  a.status = c->status;
+  a.eps = c->d.rms_norm_eps;
+  const int want = c->o.gemv_ctas > 0 ? c->o.gemv_ctas : c->sms;
+  const int ctas = std::max(1, std::min(a.n_chunks, want));
+  ++c->launches;
+  return gemv_launch(a, K, pro, epi, true, ctas, c->stream, c->pdl);
+}
+
+int attention_node(lcr_ctx* c, int layer) {
+  const lcr_model_desc& d = c->d;
+  AttnArgs a = {};
+  a.qkv = c->qkv;
+  a.qkv_stride = q_dim(c) + 2 * kv_dim(c);
+  a.q_dim = q_dim(c);
+  a.kv_dim = kv_dim(c);
+  a.inv_freq = c->inv_freq;
+  a.max_seq = c->o.max_seq;
+  if (c->o.paged) {
+    a.kpool = c->kpool;
+    a.vpool = c->vpool;
+    a.tables = c->tables_dev + static_cast<size_t>(layer) * c->max_pages;
+    a.table_seq_stride = 0;
+    a.max_pages = c->max_pages;
+    a.pool_pages = c->pool_pages;
+    a.page_size = c->o.page_size;
+    a.page_stride = static_cast<long long>(d.num_kv_heads) * c->o.page_size * d.head_dim;
+    a.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
+  } else {
+    const size_t layer_elems = static_cast<size_t>(d.num_kv_heads) * c->o.max_seq * d.head_dim;
+    a.kpool = c->kpool + layer * layer_elems;
+    a.vpool = c->vpool + layer * layer_elems;
+    a.page_size = 1;
+    a.head_stride = static_cast<long long>(c->o.max_seq) * d.head_dim;
+    a.seq_stride = static_cast<long long>(layer_elems);
+  }
+  a.positions = c->state + 1;
+  a.splits = c->splits;
+  a.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
+  a.out = c->attn;
+  a.partials = c->partials;
+  a.counters = c->attn_ctr + static_cast<size_t>(layer) * d.num_kv_heads;
+  a.status = c->status;
+  ++c->launches;
+  return attn_launch(a, true, d.head_dim, d.num_heads / d.num_kv_heads, c->o.paged != 0,
+                     d.num_kv_heads, 1, c->stream, c->pdl);
+}
+
+// Launches one decode step on the context's stream.
+int enqueue_step(lcr_ctx* c) {
+  const lcr_model_desc& d = c->d;
+  const int H = d.hidden_size, F = d.intermediate_size;
+  int slot = 0;
+  c->launches = 0;
+  for (int l = 0; l < d.num_layers; ++l) {
+    const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+    {
+      GemvArgs a = {};
+      a.w = static_cast<const bf16*>(w.qkv_proj);
+      a.norm_w = static_cast<const bf16*>(w.input_norm);
+      a.y = c->qkv;
+      int pro = PRO_NORM;
+      if (l == 0) {
+        pro = PRO_EMBED_NORM;
+        a.embed = c->embed;
+        a.token = c->state;
+        a.vocab = d.vocab_size;
+        a.x_out = c->x;
+        a.xsum_out = c->xsum;
+      } else {
+        a.x_in = c->x;
+        a.xsum = c->xsum;
+      }
+      LCRB_TRY(gemv_node(c, a, H, pro, EPI_STORE, q_dim(c) + 2 * kv_dim(c), &slot));
+    }
+    LCRB_TRY(attention_node(c, l));
+    {
+      GemvArgs a = {};
+      a.w = static_cast<const bf16*>(w.o_proj);
+      a.x_in = c->attn;
+      a.resid = c->x;
+      a.resid_sum = c->xsum;
+      LCRB_TRY(gemv_node(c, a, q_dim(c), PRO_PLAIN, EPI_RESID, H, &slot));
+    }
+    {
+      GemvArgs a = {};
+      a.w = static_cast<const bf16*>(w.gate_up_proj);
+      a.x_in = c->x;
+      a.xsum = c->xsum;
+      a.norm_w = static_cast<const bf16*>(w.post_attention_norm);
+      a.y = c->act;
+      LCRB_TRY(gemv_node(c, a, H, PRO_NORM, EPI_SWIGLU, F, &slot));
+    }
+    {
+      GemvArgs a = {};
+      a.w = static_cast<const bf16*>(w.down_proj);
+      a.x_in = c->act;
+      a.resid = c->x;
+      a.resid_sum = c->xsum;
+      LCRB_TRY(gemv_node(c, a, F, PRO_PLAIN, EPI_RESID, H, &slot));
+    }
+  }
+  GemvArgs a = {};
+  a.w = c->lm_head;
+  a.x_in = c->x;
+  a.xsum = c->xsum;
+  a.norm_w = c->final_norm;
+  a.yf = c->logits;
+  a.argmax_acc = c->argmax_acc;
+  a.state_token = c->state;
+  a.state_pos = c->state + 1;
+  a.history = c->history;
+  a.history_len = c->o.max_seq;
+  a.advance = 1;
+  return gemv_node(c, a, H, PRO_NORM, EPI_LOGITS_ARGMAX, d.vocab_size, &slot);
+}
+
+int build_graph(lcr_ctx* c) {
+  if (!c->use_graph || c->exec != nullptr) return LCR_OK;
+  cudaGraph_t graph = nullptr;
+  LCRB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  const int st = enqueue_step(c);
+  const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+  if (st != LCR_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return st;
+  }
+  if (e != cudaSuccess) return fail(LCR_ERR_CUDA, "step capture failed: %s", cudaGetErrorString(e));
+  const cudaError_t ie = cudaGraphInstantiate(&c->exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) {
+    c->exec = nullptr;
+    return fail(LCR_ERR_CUDA, "step graph instantiation failed: %s", cudaGetErrorString(ie));
+  }
+  return LCR_OK;
+}
+
+int launch_steps(lcr_ctx* c, int steps) {
+  LCRB_CUDA(cudaSetDevice(c->device));
+  if (c->use_graph) {
+    LCRB_TRY(build_graph(c));
+    for (int i = 0; i < steps; ++i) LCRB_CUDA(cudaGraphLaunch(c->exec, c->stream));
+    return LCR_OK;
+  }
+  for (int i = 0; i < steps; ++i) LCRB_TRY(enqueue_step(c));
+  return LCR_OK;
+}
+
+int check_status(lcr_ctx* c) {
+  uint32_t st = 0;
+  LCRB_CUDA(cudaMemcpyAsync(&st, c->status, sizeof st, cudaMemcpyDeviceToHost, c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  if (st == 0) return LCR_OK;
+  LCRB_CUDA(cudaMemsetAsync(c->status, 0, sizeof st, c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  if (st & (kStatusTimeoutFull | kStatusTimeoutEmpty)) {
+    return fail(LCR_ERR_TIMEOUT, "a device-side wait gave up (status 0x%x)", st);
+  }
+  if (st & kStatusBadToken) return fail(LCR_ERR_INVALID, "token id outside the vocabulary (status 0x%x)", st);
+  if (st & kStatusBadPage) return fail(LCR_ERR_POOL, "page table entry outside the pool (status 0x%x)", st);
+  return fail(LCR_ERR_STATE, "position outside the KV cache (status 0x%x)", st);
+}
+
+int stage_state(lcr_ctx* c, const int32_t* token_src, int position) {
+  int32_t* slot = c->pinned + 2 * c->ring_next;
+  c->ring_next = (c->ring_next + 1) % kPinnedRing;
+  if (token_src == nullptr) {
+    slot[1] = position;
+    LCRB_CUDA(cudaMemcpyAsync(c->state + 1, slot + 1, sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+    return LCR_OK;
+  }
+  slot[1] = position;
+  LCRB_CUDA(cudaMemcpyAsync(c->state, token_src, sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+  LCRB_CUDA(cudaMemcpyAsync(c->state + 1, slot + 1, sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+  return LCR_OK;
+}
+
+void release(lcr_ctx* c) {
+  if (c == nullptr) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->exec) cudaGraphExecDestroy(c->exec);
+  cudaFree(c->buf);
+  cudaFree(c->kpool);
+  cudaFree(c->vpool);
+  cudaFree(c->tables_dev);
+  cudaFreeHost(c->pinned);
+  cudaFreeHost(c->pinned_prompt);
+  cudaFreeHost(c->pinned_params);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+}  // namespace
+
+// ===========================================================================
+
+extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* weights,
+                              const lcr_options* options, lcr_ctx** out) {
+  LCRB_REQUIRE(desc && weights && options && out, LCR_ERR_INVALID, "lcr_ctx_create: null argument");
+  *out = nullptr;
+  const lcr_model_desc& d = *desc;
+  LCRB_REQUIRE(d.hidden_size > 0 && d.intermediate_size > 0 && d.num_layers > 0, LCR_ERR_INVALID,
+               "model has a non-positive hidden_size, intermediate_size, or num_hidden_layers");
+  LCRB_REQUIRE(d.num_heads > 0 && d.num_kv_heads > 0 && d.num_heads % d.num_kv_heads == 0,
+               LCR_ERR_INVALID, "num_attention_heads (%d) must be a multiple of num_key_value_heads (%d)",
+               d.num_heads, d.num_kv_heads);
+  LCRB_REQUIRE(d.head_dim == 64 || d.head_dim == 128, LCR_ERR_SHAPE,
+               "decode attention is compiled for head_dim 64 or 128, this model has %d", d.head_dim);
+  LCRB_REQUIRE(d.vocab_size > 0 && d.rms_norm_eps > 0.f && d.rope_theta > 1.f, LCR_ERR_INVALID,
+               "bad vocab_size / rms_norm_eps / rope_theta");
+  const int qd = d.num_heads * d.head_dim, kvd = d.num_kv_heads * d.head_dim;
+  LCRB_REQUIRE(gemv_supported(d.hidden_size, PRO_NORM, EPI_SWIGLU) &&
+                   gemv_supported(qd, PRO_PLAIN, EPI_RESID) &&
+                   gemv_supported(d.intermediate_size, PRO_PLAIN, EPI_RESID),
+               LCR_ERR_SHAPE, "no streaming GEMV for hidden %d / q_dim %d / ffn %d", d.hidden_size, qd,
+               d.intermediate_size);
+  LCRB_REQUIRE(weights->embedding && weights->final_norm && weights->layers, LCR_ERR_INVALID,
+               "lcr_weights: null embedding, final_norm or layers");
+  const lcr_options& o = *options;
+  LCRB_REQUIRE(o.max_seq > 0, LCR_ERR_INVALID, "max_seq must be positive");
+  LCRB_REQUIRE(!o.paged || (o.page_size > 0 && o.page_size % 16 == 0), LCR_ERR_SHAPE,
+               "paged KV cache needs a page size that is a positive multiple of 16, got %d",
+               o.page_size);
+
+  int devices = 0;
+  if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) {
+    cudaGetLastError();
+    return fail(LCR_ERR_NO_DEVICE, "no CUDA device");
+  }
+  LCRB_REQUIRE(o.device >= 0 && o.device < devices, LCR_ERR_INVALID, "device %d of %d", o.device, devices);
+  LCRB_CUDA(cudaSetDevice(o.device));
+  int major = 0;
+  LCRB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, o.device));
+  LCRB_REQUIRE(major == 10, LCR_ERR_NO_DEVICE, "this library is built for sm_100a; device %d is sm_%d",
+               o.device, major * 10);
+
+  lcr_ctx* c = new (std::nothrow) lcr_ctx();
+  LCRB_REQUIRE(c != nullptr, LCR_ERR_INVALID, "out of host memory");
+  c->device = o.device;
+  c->d = d;
+  c->o = o;
+  c->pdl = (o.flags & kFlagNoPdl) == 0;
+  c->use_graph = (o.flags & kFlagNoGraph) == 0;
+  cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, o.device);
+  c->embed = static_cast<const bf16*>(weights->embedding);
+  c->final_norm = static_cast<const bf16*>(weights->final_norm);
+  c->lm_head = static_cast<const bf16*>(weights->lm_head ? weights->lm_head : weights->embedding);
+  c->layers.assign(weights->layers, weights->layers + d.num_layers);
+  for (const lcr_layer_weights& w : c->layers) {
+    if (!(w.input_norm && w.qkv_proj && w.o_proj && w.post_attention_norm && w.gate_up_proj &&
+          w.down_proj)) {
+      release(c);
+      return fail(LCR_ERR_INVALID, "lcr_layer_weights: null tensor pointer");
+    }
+    for (const void* p : {w.input_norm, w.qkv_proj, w.o_proj, w.post_attention_norm, w.gate_up_proj,
+                          w.down_proj}) {
+      if (reinterpret_cast<uintptr_t>(p) & 15u) {
+        release(c);
+        return fail(LCR_ERR_INVALID, "weights must be 16-byte aligned");
+      }
+    }
+  }
+
+  int st = LCR_OK;
+  auto cuda = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && st == LCR_OK) st = fail(LCR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  };
+  cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+
+  // Split-K width: enough (kv_head, split) CTAs to cover every SM once.
+  c->splits = o.attention_splits > 0 ? o.attention_splits : std::max(1, c->sms / d.num_kv_heads);
+  // One scheduler slot per GEMV node of the step, plus kTimingSlots for
+  // lcr_time_gemv (back-to-back launches may overlap, so none share a slot).
+  c->sched_slots = 5 * d.num_layers + 8 + kTimingSlots;
+
+  // One allocation for the activations and device state, 256-byte aligned.
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t at = off;
+    off = (off + bytes + 255) / 256 * 256;
+    return at;
+  };
+  const size_t o_x = carve(sizeof(bf16) * d.hidden_size);
+  const size_t o_xsum = carve(sizeof(float) * d.hidden_size);
+  const size_t o_qkv = carve(sizeof(bf16) * (qd + 2 * kvd));
+  const size_t o_attn = carve(sizeof(bf16) * qd);
+  const size_t o_act = carve(sizeof(bf16) * d.intermediate_size);
+  const size_t o_logits = carve(sizeof(float) * d.vocab_size);
+  const size_t o_part = carve(sizeof(float) * d.num_heads * c->splits * (2 + d.head_dim));
+  const size_t o_actr = carve(sizeof(unsigned) * d.num_layers * d.num_kv_heads);
+  const size_t o_sched = carve(sizeof(unsigned) * 2 * c->sched_slots);
+  const size_t o_amax = carve(sizeof(unsigned long long));
+  const size_t o_state = carve(sizeof(int32_t) * 4);
+  const size_t o_hist = carve(sizeof(int32_t) * o.max_seq);
+  const size_t o_status = carve(sizeof(uint32_t));
+  const size_t o_freq = carve(sizeof(float) * d.head_dim / 2);
+  const size_t o_sparams = carve(sizeof(float) * 8);
+  const size_t o_sampled = carve(sizeof(int32_t) * 4);
+  if (st == LCR_OK) cuda(cudaMalloc(&c->buf, off), "cudaMalloc(activations)");
+  if (st == LCR_OK) cuda(cudaMemset(c->buf, 0, off), "cudaMemset(activations)");
+  if (st == LCR_OK) {
+    char* b = c->buf;
+    c->x = reinterpret_cast<bf16*>(b + o_x);
+    c->xsum = reinterpret_cast<float*>(b + o_xsum);
+    c->qkv = reinterpret_cast<bf16*>(b + o_qkv);
+    c->attn = reinterpret_cast<bf16*>(b + o_attn);
+    c->act = reinterpret_cast<bf16*>(b + o_act);
+    c->logits = reinterpret_cast<float*>(b + o_logits);
+    c->partials = reinterpret_cast<float*>(b + o_part);
+    c->attn_ctr = reinterpret_cast<unsigned*>(b + o_actr);
+    c->sched = reinterpret_cast<unsigned*>(b + o_sched);
+    c->argmax_acc = reinterpret_cast<unsigned long long*>(b + o_amax);
+    c->state = reinterpret_cast<int32_t*>(b + o_state);
+    c->history = reinterpret_cast<int32_t*>(b + o_hist);
+    c->status = reinterpret_cast<uint32_t*>(b + o_status);
+    c->inv_freq = reinterpret_cast<float*>(b + o_freq);
+    c->sample_params = reinterpret_cast<float*>(b + o_sparams);
+    c->sampled = reinterpret_cast<int32_t*>(b + o_sampled);
+    const std::vector<float> freq = rope_inv_freq(d);
+    cuda(cudaMemcpy(c->inv_freq, freq.data(), freq.size() * sizeof(float), cudaMemcpyHostToDevice),
+         "upload inv_freq");
+  }
+
+  // KV cache (src/kv_cache.cu:24-63).
+  if (st == LCR_OK) {
+    size_t elems;
+    if (o.paged) {
+      c->max_pages = (o.max_seq + o.page_size - 1) / o.page_size;
+      c->pool_pages = c->max_pages * d.num_layers;
+      elems = static_cast<size_t>(c->pool_pages) * d.num_kv_heads * o.page_size * d.head_dim;
+      c->tables_host.assign(static_cast<size_t>(d.num_layers) * c->max_pages, -1);
+      c->order.resize(static_cast<size_t>(c->pool_pages));
+      for (int i = 0; i < c->pool_pages; ++i) c->order[static_cast<size_t>(i)] = i;
+      if (o.page_order_seed != 0) {
+        uint64_t s = o.page_order_seed;
+        for (int i = c->pool_pages - 1; i > 0; --i) {
+          const int j = static_cast<int>(splitmix64(&s) % static_cast<uint64_t>(i + 1));
+          std::swap(c->order[static_cast<size_t>(i)], c->order[static_cast<size_t>(j)]);
+        }
+      }
+      cuda(cudaMalloc(&c->tables_dev, c->tables_host.size() * sizeof(int32_t)), "cudaMalloc(page tables)");
+      if (st == LCR_OK) {
+        cuda(cudaMemcpy(c->tables_dev, c->tables_host.data(), c->tables_host.size() * sizeof(int32_t),
+                        cudaMemcpyHostToDevice),
+             "upload page tables");
+      }
+    } else {
+      elems = static_cast<size_t>(d.num_layers) * d.num_kv_heads * o.max_seq * d.head_dim;
+    }
+    if (st == LCR_OK) cuda(cudaMalloc(&c->kpool, elems * sizeof(bf16)), "cudaMalloc(K pool)");
+    if (st == LCR_OK) cuda(cudaMalloc(&c->vpool, elems * sizeof(bf16)), "cudaMalloc(V pool)");
+    if (st == LCR_OK) cuda(cudaMemset(c->kpool, 0, elems * sizeof(bf16)), "cudaMemset(K pool)");
+    if (st == LCR_OK) cuda(cudaMemset(c->vpool, 0, elems * sizeof(bf16)), "cudaMemset(V pool)");
+  }
+  if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * kPinnedRing), "cudaMallocHost");
+  if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned_params, sizeof(float) * 8), "cudaMallocHost");
+  if (st != LCR_OK) {
+    release(c);
+    return st;
+  }
+  *out = c;
+  return LCR_OK;
+}
+
+extern "C" void lcr_ctx_destroy(lcr_ctx* ctx) { release(ctx); }
+
+extern "C" int lcr_reset(lcr_ctx* ctx) {
+  LCRB_REQUIRE(ctx, LCR_ERR_INVALID, "null context");
+  ctx->position = 0;
+  return LCR_OK;
+}
+
+extern "C" int lcr_position(const lcr_ctx* ctx) { return ctx ? ctx->position : -1; }
+
+extern "C" int lcr_reserve_length(lcr_ctx* c, int length) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null context");
+  LCRB_REQUIRE(length <= c->o.max_seq, LCR_ERR_STATE,
+               "sequence reached %d positions but the KV cache was built for %d", length, c->o.max_seq);
+  if (length <= c->length) return LCR_OK;
+  if (c->o.paged) {
+    const int P = c->o.page_size;
+    const int have = (c->length + P - 1) / P;
+    const int need = (length + P - 1) / P;
+    if (need > have) {
+      LCRB_CUDA(cudaSetDevice(c->device));
+      LCRB_CUDA(cudaStreamSynchronize(c->stream));
+      for (int l = 0; l < c->d.num_layers; ++l) {
+        int32_t* table = c->tables_host.data() + static_cast<size_t>(l) * c->max_pages;
+        for (int p = have; p < need; ++p) {
+          LCRB_REQUIRE(c->pages_mapped < c->pool_pages, LCR_ERR_POOL,
+                       "paged KV cache pool is exhausted after %d pages", c->pages_mapped);
+          table[p] = c->order[static_cast<size_t>(c->pages_mapped++)];
+        }
+        LCRB_CUDA(cudaMemcpy(c->tables_dev + static_cast<size_t>(l) * c->max_pages + have, table + have,
+                             static_cast<size_t>(need - have) * sizeof(int32_t), cudaMemcpyHostToDevice));
+      }
+    }
+  }
+  c->length = length;
+  return LCR_OK;
+}
+
+extern "C" int lcr_decode(lcr_ctx* c, int token, const float** logits) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null context");
+  LCRB_REQUIRE(c->position < c->o.max_seq, LCR_ERR_STATE,
+               "sequence reached %d positions, the cache limit", c->position);
+  LCRB_REQUIRE(token >= 0 && token < c->d.vocab_size, LCR_ERR_INVALID, "token %d outside the vocabulary",
+               token);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(lcr_reserve_length(c, c->position + 1));
+  int32_t* slot = c->pinned + 2 * c->ring_next;
+  c->ring_next = (c->ring_next + 1) % kPinnedRing;
+  slot[0] = token;
+  slot[1] = c->position;
+  LCRB_CUDA(cudaMemcpyAsync(c->state, slot, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+  LCRB_TRY(launch_steps(c, 1));
+  LCRB_TRY(check_status(c));
+  c->position += 1;
+  if (logits) *logits = c->logits;
+  return LCR_OK;
+}
+
+extern "C" int lcr_prefill(lcr_ctx* c, const int32_t* tokens, int count, const float** logits) {
+  LCRB_REQUIRE(c && tokens, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(count > 0, LCR_ERR_INVALID, "prefill needs at least one token");
+  LCRB_REQUIRE(c->position + count <= c->o.max_seq, LCR_ERR_STATE,
+               "prompt of %d tokens at position %d exceeds the cache built for %d", count, c->position,
+               c->o.max_seq);
+  for (int i = 0; i < count; ++i) {
+    LCRB_REQUIRE(tokens[i] >= 0 && tokens[i] < c->d.vocab_size, LCR_ERR_INVALID,
+                 "token %d outside the vocabulary", tokens[i]);
+  }
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(lcr_reserve_length(c, c->position + count));
+  const size_t need = static_cast<size_t>(count) * 2;
+  if (c->pinned_prompt_cap < need) {
+    LCRB_CUDA(cudaStreamSynchronize(c->stream));
+    cudaFreeHost(c->pinned_prompt);
+    c->pinned_prompt = nullptr;
+    c->pinned_prompt_cap = 0;
+    LCRB_CUDA(cudaMallocHost(&c->pinned_prompt, need * sizeof(int32_t)));
+    c->pinned_prompt_cap = need;
+  } else {
+    LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  }
+  for (int i = 0; i < count; ++i) {
+    c->pinned_prompt[2 * i] = tokens[i];
+    c->pinned_prompt[2 * i + 1] = c->position + i;
+  }
+  for (int i = 0; i < count; ++i) {
+    LCRB_CUDA(cudaMemcpyAsync(c->state, c->pinned_prompt + 2 * i, 2 * sizeof(int32_t),
+                              cudaMemcpyHostToDevice, c->stream));
+    LCRB_TRY(launch_steps(c, 1));
+  }
+  LCRB_TRY(check_status(c));
+  c->position += count;
+  if (logits) *logits = c->logits;
+  return LCR_OK;
+}
+
+extern "C" int lcr_logits_to_host(lcr_ctx* c, float* host) {
+  LCRB_REQUIRE(c && host, LCR_ERR_INVALID, "null argument");
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_CUDA(cudaMemcpyAsync(host, c->logits, sizeof(float) * c->d.vocab_size, cudaMemcpyDeviceToHost,
+                            c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  return LCR_OK;
+}
+
+extern "C" int lcr_sample_logits(lcr_ctx* c, const float* logits, float temperature, int top_k,
+                                 float top_p, float uniform, int* token) {
+  LCRB_REQUIRE(c && logits && token, LCR_ERR_INVALID, "null argument");
+  if (temperature > 0.0f) {
+    LCRB_REQUIRE(top_p > 0.0f && top_p <= 1.0f, LCR_ERR_INVALID, "top_p must be in (0, 1], got %g",
+                 static_cast<double>(top_p));
+  }
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  float* p = c->pinned_params;
+  p[0] = temperature > 0.0f ? 1.0f / temperature : 0.0f;
+  std::memcpy(&p[1], &top_k, sizeof(int));
+  p[2] = top_p;
+  p[3] = uniform;
+  LCRB_CUDA(cudaMemcpyAsync(c->sample_params, p, 4 * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+  SampleArgs a = {};
+  a.logits = logits;
+  a.row_stride = c->d.vocab_size;
+  a.vocab = c->d.vocab_size;
+  a.inv_temperature = c->sample_params;
+  a.top_k = reinterpret_cast<const int*>(c->sample_params + 1);
+  a.top_p = c->sample_params + 2;
+  a.uniform = c->sample_params + 3;
+  a.out = c->sampled;
+  LCRB_TRY(sample_launch(a, 1, c->stream, false));
+  int32_t id = -1;
+  LCRB_CUDA(cudaMemcpyAsync(&id, c->sampled, sizeof id, cudaMemcpyDeviceToHost, c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  LCRB_REQUIRE(id >= 0 && id < c->d.vocab_size, LCR_ERR_STATE,
+               "sampling produced token id %d, outside the vocabulary", id);
+  *token = id;
+  return LCR_OK;
+}
+
+extern "C" int lcr_generate_greedy(lcr_ctx* c, int first_token, int steps, int32_t* tokens_out) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null context");
+  LCRB_REQUIRE(steps >= 0, LCR_ERR_INVALID, "negative step count");
+  if (steps == 0) return LCR_OK;
+  LCRB_REQUIRE(c->position + steps <= c->o.max_seq, LCR_ERR_STATE,
+               "%d steps at position %d exceed the cache built for %d", steps, c->position, c->o.max_seq);
+  LCRB_REQUIRE(first_token >= 0 && first_token < c->d.vocab_size, LCR_ERR_INVALID,
+               "token %d outside the vocabulary", first_token);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(lcr_reserve_length(c, c->position + steps));
+  int32_t* slot = c->pinned + 2 * c->ring_next;
+  c->ring_next = (c->ring_next + 1) % kPinnedRing;
+  slot[0] = first_token;
+  slot[1] = c->position;
+  LCRB_CUDA(cudaMemcpyAsync(c->state, slot, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+  LCRB_TRY(launch_steps(c, steps));
+  if (tokens_out) {
+    LCRB_CUDA(cudaMemcpyAsync(tokens_out, c->history + c->position, sizeof(int32_t) * steps,
+                              cudaMemcpyDeviceToHost, c->stream));
+  }
+  LCRB_TRY(check_status(c));
+  c->position += steps;
+  return LCR_OK;
+}
+
+extern "C" int lcr_set_token(lcr_ctx* c, const int32_t* host_token, int position) {
+  LCRB_REQUIRE(c && host_token, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(position >= 0 && position < c->o.max_seq, LCR_ERR_STATE,
+               "position %d outside the cache built for %d", position, c->o.max_seq);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(stage_state(c, host_token, position));
+  c->position = position;
+  return LCR_OK;
+}
+
+extern "C" int lcr_enqueue_steps(lcr_ctx* c, int steps) {
+  LCRB_REQUIRE(c && steps >= 0, LCR_ERR_INVALID, "bad arguments");
+  LCRB_TRY(launch_steps(c, steps));
+  c->position += steps;
+  return LCR_OK;
+}
+
+extern "C" int lcr_read_token(lcr_ctx* c, int32_t* host_token) {
+  LCRB_REQUIRE(c && host_token, LCR_ERR_INVALID, "null argument");
+  LCRB_CUDA(cudaMemcpyAsync(host_token, c->state, sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream));
+  return LCR_OK;
+}
+
+extern "C" int lcr_sync(lcr_ctx* c) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null context");
+  LCRB_CUDA(cudaSetDevice(c->device));
+  return check_status(c);
+}
+
+extern "C" lcr_stream_t lcr_ctx_stream(lcr_ctx* c) {
+  return c ? reinterpret_cast<lcr_stream_t>(c->stream) : nullptr;
+}
+
+extern "C" int lcr_kv_view_of(const lcr_ctx* c, int layer, lcr_kv_view* v) {
+  LCRB_REQUIRE(c && v, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(layer >= 0 && layer < c->d.num_layers, LCR_ERR_INVALID, "layer %d is out of range", layer);
+  const lcr_model_desc& d = c->d;
+  v->num_kv_heads = d.num_kv_heads;
+  v->head_dim = d.head_dim;
+  if (c->o.paged) {
+    v->keys = c->kpool;
+    v->values = c->vpool;
+    v->page_table = c->tables_dev + static_cast<size_t>(layer) * c->max_pages;
+    v->page_size = c->o.page_size;
+    v->page_stride = d.num_kv_heads * c->o.page_size * d.head_dim;
+    v->head_stride = c->o.page_size * d.head_dim;
+  } else {
+    const size_t base = static_cast<size_t>(layer) * d.num_kv_heads * c->o.max_seq * d.head_dim;
+    v->keys = c->kpool + base;
+    v->values = c->vpool + base;
+    v->page_table = nullptr;
+    v->page_size = c->o.max_seq;
+    v->page_stride = 0;
+    v->head_stride = c->o.max_seq * d.head_dim;
+  }
+  return LCR_OK;
+}
+
+extern "C" int lcr_page_tables(const lcr_ctx* c, int32_t* tables, int* pages_mapped) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null context");
+  if (tables && !c->tables_host.empty()) {
+    std::memcpy(tables, c->tables_host.data(), c->tables_host.size() * sizeof(int32_t));
+  }
+  if (pages_mapped) *pages_mapped = c->pages_mapped;
+  return LCR_OK;
+}
+
+extern "C" size_t lcr_weight_bytes_per_token(const lcr_ctx* c) {
+  if (!c) return 0;
+  const lcr_model_desc& d = c->d;
+  const size_t h = d.hidden_size, q = static_cast<size_t>(d.num_heads) * d.head_dim;
+  const size_t kv = static_cast<size_t>(d.num_kv_heads) * d.head_dim, f = d.intermediate_size;
+  size_t per = static_cast<size_t>(d.num_layers) * (h * 2 + q * h + kv * h * 2 + h * q + f * h * 3);
+  per += h + static_cast<size_t>(d.vocab_size) * h;
+  return per * 2;
+}
+
+extern "C" size_t lcr_kv_bytes_per_position(const lcr_ctx* c) {
+  if (!c) return 0;
+  return static_cast<size_t>(c->d.num_layers) * 2 * c->d.num_kv_heads * c->d.head_dim * 2;
+}
+
+extern "C" int lcr_step_launches(const lcr_ctx* c) {
+  return c ? 5 * c->d.num_layers + 1 : 0;
+}
+
+extern "C" int lcr_device_status(lcr_ctx* c) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null context");
+  LCRB_CUDA(cudaSetDevice(c->device));
+  return check_status(c);
+}
+
+extern "C" int lcr_time_steps(lcr_ctx* c, int steps, float* ms) {
+  LCRB_REQUIRE(c && ms && steps > 0, LCR_ERR_INVALID, "bad arguments");
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(build_graph(c));
+  cudaEvent_t e0, e1;
+  LCRB_CUDA(cudaEventCreate(&e0));
+  LCRB_CUDA(cudaEventCreate(&e1));
+  cudaEventRecord(e0, c->stream);
+  int st = launch_steps(c, steps);
+  cudaEventRecord(e1, c->stream);
+  cudaEventSynchronize(e1);
+  float t = 0.f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (st != LCR_OK) return st;
+  c->position += steps;
+  *ms = t;
+  return check_status(c);
+}
+
+extern "C" int lcr_time_gemv(lcr_ctx* c, int matrix, int layer, int reps, float* ms) {
+  LCRB_REQUIRE(c && ms && reps > 0, LCR_ERR_INVALID, "bad arguments");
+  LCRB_REQUIRE(layer >= 0 && layer < c->d.num_layers, LCR_ERR_INVALID, "layer %d out of range", layer);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  const lcr_model_desc& d = c->d;
+  const lcr_layer_weights& w = c->layers[static_cast<size_t>(layer)];
+  GemvArgs a = {};
+  int K = d.hidden_size, pro = PRO_NORM, epi = EPI_STORE, n = 0;
+  switch (matrix) {
+    case 0:
+      a.w = static_cast<const bf16*>(w.qkv_proj); a.x_in = c->x; a.xsum = c->xsum;
+      a.norm_w = static_cast<const bf16*>(w.input_norm); a.y = c->qkv; n = q_dim(c) + 2 * kv_dim(c);
+      break;
+    case 1:
+      a.w = static_cast<const bf16*>(w.o_proj); a.x_in = c->attn; a.y = c->qkv;
+      K = q_dim(c); pro = PRO_PLAIN; n = d.hidden_size;
+      break;
+    case 2:
+      a.w = static_cast<const bf16*>(w.gate_up_proj); a.x_in = c->x; a.xsum = c->xsum;
+      a.norm_w = static_cast<const bf16*>(w.post_attention_norm); a.y = c->act; epi = EPI_SWIGLU;
+      n = d.intermediate_size;
+      break;
+    case 3:
+      a.w = static_cast<const bf16*>(w.down_proj); a.x_in = c->act; a.y = c->qkv;
+      K = d.intermediate_size; pro = PRO_PLAIN; n = d.hidden_size;
+      break;
+    default:
+      a.w = c->lm_head; a.x_in = c->x; a.xsum = c->xsum; a.norm_w = c->final_norm; a.yf = c->logits;
+      epi = EPI_STORE_F32; n = d.vocab_size;
+      break;
+  }
+  LCRB_REQUIRE(reps <= kTimingSlots, LCR_ERR_INVALID, "at most %d repetitions", kTimingSlots);
+  cudaEvent_t e0, e1;
+  LCRB_CUDA(cudaEventCreate(&e0));
+  LCRB_CUDA(cudaEventCreate(&e1));
+  cudaEventRecord(e0, c->stream);
+  int st = LCR_OK;
+  for (int i = 0; i < reps && st == LCR_OK; ++i) {
+    int slot = c->sched_slots - kTimingSlots + i;
+    st = gemv_node(c, a, K, pro, epi, n, &slot);
+  }
+  cudaEventRecord(e1, c->stream);
+  cudaEventSynchronize(e1);
+  float t = 0.f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (st != LCR_OK) return st;
+  *ms = t / reps;
+  return check_status(c);
+}

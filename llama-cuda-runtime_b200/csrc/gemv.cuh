@@ -1,0 +1,397 @@
+// Weight-streaming matrix-vector kernel for batch-1 decode: y = W x with W a
+// row-major bf16 [N][K] matrix read exactly once from HBM.
+//
+// Replaces the reference's cublasGemmEx at m = 1 (gemm_nt, src/model.cu:38-45)
+// and folds the small kernels around each projection into it:
+//   prologue  PLAIN        x = a bf16 vector written by the previous kernel
+//             NORM         x = bf16(rmsnorm(resid) * gain)  (rmsnorm.cu:21-119)
+//             EMBED_NORM   the same on the embedding row of the device token
+//                          (elementwise.cu:25-41), CTA 0 storing the row
+//   epilogue  STORE / STORE_F32   y as bf16 / fp32
+//             RESID        resid = bf16(resid + bf16(y)), unrounded sum kept
+//                          for the next norm (the fused join, rmsnorm.cu:68-119)
+//             SWIGLU       act = bf16(silu(bf16(gate)) * bf16(up)) with the
+//                          gate and up rows of one output in the same CTA
+//                          (elementwise.cu:96-121)
+//             LOGITS_ARGMAX  fp32 logits plus the packed (value, ~index)
+//                          argmax of sampling.cu:42-67; the last CTA to finish
+//                          writes the next token into device state
+//
+// Structure (one CTA per SM by default, 288 threads):
+//   warp 8, lane 0  producer: takes the next chunk of rows from a global
+//                   counter (dynamic scheduling, so CTAs that start late or
+//                   share an SM still balance; the allocation-free standalone
+//                   entry uses a fixed strided schedule instead), and streams
+//                   it into a ring of
+//                   shared-memory stages with cp.async.bulk (TMA, 1-D, L2
+//                   evict-first), completing on the stage's mbarrier.
+//   warps 0-7       consumers: each thread owns CPT 16-byte column chunks of
+//                   the input vector in registers for the whole kernel; per
+//                   stage it forms RPT row partials, the warp reduces them with
+//                   a transposing butterfly, warps combine through shared memory.
+// Weights do not depend on the previous kernel, so the producer starts before
+// griddepcontrol.wait: with programmatic dependent launch the next matrix is
+// already in flight while the previous kernel drains.
+#pragma once
+
+#include "common.cuh"
+
+namespace lcrb {
+
+enum GemvPro { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
+enum GemvEpi { EPI_STORE = 0, EPI_STORE_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS_ARGMAX = 4 };
+
+struct GemvArgs {
+  const bf16* w;      // [N][K]; SWIGLU: rows [0, F) gate, [F, 2F) up
+  int n_out;          // outputs (rows; SWIGLU: F)
+  int n_chunks;       // ceil(n_out / rows-per-chunk)
+  unsigned* sched;    // [2] next chunk, CTAs done -- zero before the first
+                      //     launch; the last CTA resets them
+  uint32_t* status;   // device status word (bounded-wait failures)
+  // prologue
+  const bf16* x_in;       // PLAIN: input; NORM: residual stream (bf16)
+  const float* xsum;      // NORM: unrounded residual sums (nullptr: use x_in)
+  const bf16* norm_w;     // NORM / EMBED_NORM gain
+  float eps;
+  const bf16* embed;      // EMBED_NORM: table [vocab][K]
+  const int32_t* token;   // EMBED_NORM: device token id
+  int vocab;
+  bf16* x_out;            // EMBED_NORM: residual stream written by CTA 0
+  float* xsum_out;
+  // epilogue
+  bf16* y;                // STORE / SWIGLU output
+  float* yf;              // STORE_F32 / LOGITS output
+  bf16* resid;            // RESID: residual stream, updated in place
+  float* resid_sum;       // RESID: unrounded sums
+  unsigned long long* argmax_acc;  // LOGITS_ARGMAX accumulator (0 between uses)
+  int32_t* state_token;   // LOGITS_ARGMAX: next token
+  int32_t* state_pos;     //   position, advanced by one when `advance`
+  int32_t* history;       //   history[pos] = next token (nullable)
+  int history_len;
+  int advance;
+};
+
+template <int K, int STAGE_BYTES>
+struct GemvGeom {
+  static constexpr int KC = K / 8;               // 16-byte chunks per row
+  static constexpr int TPR = KC < 256 ? KC : 256;  // threads per row
+  static constexpr int CPT = KC / TPR;           // chunks per thread
+  static constexpr int SLOTS = 256 / TPR;        // rows in flight per pass
+  static constexpr int WPR = TPR / 32;           // warps per row
+  static constexpr int ROW_BYTES = K * 2;
+  static constexpr int RPS = STAGE_BYTES / ROW_BYTES;  // rows per stage
+  static constexpr int RPT = RPS / SLOTS;        // rows per thread per stage
+  static_assert(K % 256 == 0 && KC % 32 == 0, "K must be a multiple of 256");
+  static_assert(TPR * CPT == KC, "K/8 must split evenly over the row's threads");
+  static_assert(RPS >= SLOTS && RPS % SLOTS == 0, "stage too small for this K");
+  static_assert(RPT == 1 || RPT == 2 || RPT == 4 || RPT == 8 || RPT == 16, "RPT");
+};
+
+constexpr int kGemvConsumers = 256;
+constexpr int kGemvThreads = kGemvConsumers + 32;
+
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Transposing butterfly: each lane enters with RPT row partials, and leaves
+// holding the warp total of row warp_row_of_lane() (lanes whose low bits are
+// zero are the unique holders).
+template <int RPT>
+__device__ __forceinline__ float warp_reduce_rows(float (&v)[RPT], int lane) {
+  int n = RPT;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (n > 1) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < RPT / 2; ++i) {
+        if (i < n / 2) {
+          const float send = upper ? v[i] : v[i + n / 2];
+          const float keep = upper ? v[i + n / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      n >>= 1;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+  return v[0];
+}
+
+template <int RPT>
+__device__ __forceinline__ int warp_row_of_lane(int lane) {
+  // Halving step k (offset 16 >> k) sends the lane with that bit set to the
+  // upper half of the remaining rows.
+  int r = 0;
+#pragma unroll
+  for (int k = 0, n = RPT; n > 1; ++k, n >>= 1) r += ((lane >> (4 - k)) & 1) * (n >> 1);
+  return r;
+}
+
+template <int RPT>
+__device__ __forceinline__ bool warp_row_owner(int lane) {
+  constexpr int m = (RPT >= 16) ? 4 : (RPT >= 8) ? 3 : (RPT >= 4) ? 2 : (RPT >= 2) ? 1 : 0;
+  return (lane & ((1 << (5 - m)) - 1)) == 0;
+}
+
+template <int K, int STAGE_BYTES, int STAGES, int PRO, int EPI, bool DYNAMIC>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const GemvArgs a) {
+  using G = GemvGeom<K, STAGE_BYTES>;
+  constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR;
+  constexpr int PAIRS = RPS / 2;  // SWIGLU outputs per chunk
+  constexpr int OUT_PER_CHUNK = (EPI == EPI_SWIGLU) ? PAIRS : RPS;
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
+  int* info = reinterpret_cast<int*>(cta_best + 1);      // [STAGES]
+  float* red8 = reinterpret_cast<float*>(info + STAGES);  // [8]
+  float* red = red8 + 8;                                  // [2][RPS][WPR]
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvConsumers / 32);
+    }
+    *cta_best = 0ull;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_launch_next();
+
+  if (warp == kGemvConsumers / 32) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      const char* wbase = reinterpret_cast<const char*>(a.w);
+      int it = 0;
+      for (;; ++it) {
+        const int slot = it % STAGES;
+        if (it >= STAGES) {
+          if (!mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
+            info[slot] = -1;
+            mbar_arrive(&full[slot]);
+            break;
+          }
+        }
+        const int chunk = DYNAMIC ? static_cast<int>(atomicAdd(&a.sched[0], 1u))
+                                  : static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x);
+        if (chunk >= a.n_chunks) {
+          info[slot] = -1;
+          mbar_arrive(&full[slot]);
+          break;
+        }
+        info[slot] = chunk;
+        uint8_t* dst = ring + slot * STAGE_BYTES;
+        const int first = chunk * OUT_PER_CHUNK;
+        const int rows = min(OUT_PER_CHUNK, a.n_out - first);
+        if constexpr (EPI == EPI_SWIGLU) {
+          const uint32_t bytes = static_cast<uint32_t>(rows) * G::ROW_BYTES;
+          mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+          bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
+          bulk_g2s(dst + PAIRS * G::ROW_BYTES,
+                   wbase + static_cast<size_t>(a.n_out + first) * G::ROW_BYTES, bytes, &full[slot],
+                   policy);
+        } else {
+          const uint32_t bytes = static_cast<uint32_t>(rows) * G::ROW_BYTES;
+          mbar_arrive_expect_tx(&full[slot], bytes);
+          bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
+        }
+      }
+      // Stage `it` carried the end marker (and stage it - STAGES, in the same
+      // slot, was consumed before it); never leave the CTA with a copy still
+      // writing its shared memory.
+      for (int k = it >= STAGES ? it - STAGES + 1 : 0; k < it; ++k) {
+        mbar_wait(&full[k % STAGES], (k / STAGES) & 1, a.status, kStatusTimeoutFull);
+      }
+    }
+  } else {
+    // ---------------- consumers ----------------
+    const int slotrow = tid / TPR;  // which row of each pass this thread serves
+    const int ci = tid % TPR;       // chunk index within the row
+    float xr[CPT][8];
+
+    if constexpr (PRO == PRO_PLAIN) {
+      pdl_wait();
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        unpack8(ldg16(a.x_in + (ci + j * TPR) * 8), xr[j]);
+      }
+    } else {
+      uint4 gain[CPT];
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) gain[j] = ldg16(a.norm_w + (ci + j * TPR) * 8);
+      pdl_wait();
+      const bf16* src = a.x_in;
+      if constexpr (PRO == PRO_EMBED_NORM) {
+        int tok = *a.token;
+        if (tok < 0 || tok >= a.vocab) {
+          if (tid == 0 && a.status) atomicOr(a.status, kStatusBadToken);
+          tok = 0;
+        }
+        src = a.embed + static_cast<size_t>(tok) * K;
+      }
+      float xv[CPT][8], sq[CPT][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int col = (ci + j * TPR) * 8;
+        const uint4 raw = ldg16(src + col);
+        unpack8(raw, xv[j]);
+        if (PRO == PRO_NORM && a.xsum != nullptr) {
+          const float4 s0 = *reinterpret_cast<const float4*>(a.xsum + col);
+          const float4 s1 = *reinterpret_cast<const float4*>(a.xsum + col + 4);
+          sq[j][0] = s0.x; sq[j][1] = s0.y; sq[j][2] = s0.z; sq[j][3] = s0.w;
+          sq[j][4] = s1.x; sq[j][5] = s1.y; sq[j][6] = s1.z; sq[j][7] = s1.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sq[j][e] = xv[j][e];
+        }
+        if (slotrow == 0) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss = fmaf(sq[j][e], sq[j][e], ss);
+        }
+        if (PRO == PRO_EMBED_NORM && blockIdx.x == 0 && slotrow == 0) {
+          *reinterpret_cast<uint4*>(a.x_out + col) = raw;
+          *reinterpret_cast<float4*>(a.xsum_out + col) =
+              make_float4(xv[j][0], xv[j][1], xv[j][2], xv[j][3]);
+          *reinterpret_cast<float4*>(a.xsum_out + col + 4) =
+              make_float4(xv[j][4], xv[j][5], xv[j][6], xv[j][7]);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) red8[warp] = ss;
+      named_sync(1, kGemvConsumers);
+      float total = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) total += red8[w];
+      const float scale = rsqrtf(total / static_cast<float>(K) + a.eps);
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        float gf[8];
+        unpack8(gain[j], gf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xr[j][e] = rbf(__fmul_rn(__fmul_rn(xv[j][e], scale), gf[e]));
+      }
+    }
+
+    unsigned long long best = 0ull;
+    for (int it = 0;; ++it) {
+      const int slot = it % STAGES;
+      const bool ok = mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
+      const int chunk = ok ? info[slot] : -1;
+      const uint8_t* stage = ring + slot * STAGE_BYTES;
+
+      float part[RPT];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) part[r] = 0.f;
+      if (chunk >= 0) {
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        const int row = slotrow * RPT + r;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES +
+                                                           (ci + j * TPR) * 16);
+          acc = fmaf(bf_lo(wv.x), xr[j][0], acc);
+          acc = fmaf(bf_hi(wv.x), xr[j][1], acc);
+          acc = fmaf(bf_lo(wv.y), xr[j][2], acc);
+          acc = fmaf(bf_hi(wv.y), xr[j][3], acc);
+          acc = fmaf(bf_lo(wv.z), xr[j][4], acc);
+          acc = fmaf(bf_hi(wv.z), xr[j][5], acc);
+          acc = fmaf(bf_lo(wv.w), xr[j][6], acc);
+          acc = fmaf(bf_hi(wv.w), xr[j][7], acc);
+        }
+        part[r] = acc;
+      }
+      }
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&empty[slot]);
+
+      const float wsum = warp_reduce_rows<RPT>(part, lane);
+      float* rb = red + (it & 1) * RPS * G::WPR;
+      if (warp_row_owner<RPT>(lane)) {
+        const int row = slotrow * RPT + warp_row_of_lane<RPT>(lane);
+        rb[row * G::WPR + (warp % G::WPR)] = wsum;
+      }
+      // One barrier both publishes the partials and votes on leaving: every
+      // consumer sees the same `stop`, so no warp is left at a later barrier.
+      if (named_sync_or(1, kGemvConsumers, chunk < 0)) break;
+
+      const int first = chunk * OUT_PER_CHUNK;
+      const int rows = min(OUT_PER_CHUNK, a.n_out - first);
+      if (tid < rows) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < G::WPR; ++w) v += rb[tid * G::WPR + w];
+        const int out = first + tid;
+        if constexpr (EPI == EPI_STORE) {
+          a.y[out] = __ushort_as_bfloat16(f2bf(v));
+        } else if constexpr (EPI == EPI_STORE_F32) {
+          a.yf[out] = v;
+        } else if constexpr (EPI == EPI_RESID) {
+          const float s = __fadd_rn(bf2f(__bfloat16_as_ushort(a.resid[out])), rbf(v));
+          a.resid[out] = __ushort_as_bfloat16(f2bf(s));
+          a.resid_sum[out] = s;
+        } else if constexpr (EPI == EPI_SWIGLU) {
+          float u = 0.f;
+#pragma unroll
+          for (int w = 0; w < G::WPR; ++w) u += rb[(tid + PAIRS) * G::WPR + w];
+          const float g = rbf(v);
+          const float silu = g / (1.0f + __expf(-g));
+          a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(u)));
+        } else if constexpr (EPI == EPI_LOGITS_ARGMAX) {
+          a.yf[out] = v;
+          const unsigned long long packed =
+              (static_cast<unsigned long long>(order_key(v)) << 32) |
+              static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(out));
+          best = best > packed ? best : packed;
+        }
+      }
+    }
+    if constexpr (EPI == EPI_LOGITS_ARGMAX) {
+      if (best != 0ull) atomicMax(cta_best, best);
+    }
+  }
+
+  __syncthreads();
+  if (DYNAMIC && tid == 0) {
+    if constexpr (EPI == EPI_LOGITS_ARGMAX) atomicMax(a.argmax_acc, *cta_best);
+    __threadfence();
+    const unsigned prev = atomicAdd(&a.sched[1], 1u);
+    if (prev == gridDim.x - 1) {
+      // Last CTA: every chunk has been taken and every CTA's results are
+      // visible. Reset the scheduler for the next launch of this node.
+      __threadfence();
+      atomicExch(&a.sched[0], 0u);
+      atomicExch(&a.sched[1], 0u);
+      if constexpr (EPI == EPI_LOGITS_ARGMAX) {
+        const unsigned long long packed = atomicExch(a.argmax_acc, 0ull);
+        const int next = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed & 0xFFFFFFFFull));
+        const int pos = *a.state_pos;
+        *a.state_token = next;
+        if (a.history != nullptr && pos >= 0 && pos < a.history_len) a.history[pos] = next;
+        if (a.advance) *a.state_pos = pos + 1;
+      }
+    }
+  }
+}
+
+template <int K, int STAGE_BYTES, int STAGES>
+constexpr size_t gemv_smem_bytes() {
+  using G = GemvGeom<K, STAGE_BYTES>;
+  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) +
+         STAGES * sizeof(int) + (2 * G::RPS * G::WPR + 8) * sizeof(float) + 16 + 64;
+}
+
+}  // namespace lcrb

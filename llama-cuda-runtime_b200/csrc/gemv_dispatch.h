@@ -1,0 +1,24 @@
+// Host-side launcher of the streaming GEMV instantiations (gemv_dispatch.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "gemv.cuh"
+
+namespace lcrb {
+
+// Stage geometry shared by every instantiation.
+constexpr int kGemvStageBytes = 16384;
+constexpr int kGemvStages = 6;
+
+bool gemv_supported(int K, int pro, int epi);
+// Outputs (rows, or SWIGLU pairs) per chunk of one stage.
+int gemv_outputs_per_chunk(int K, int epi);
+size_t gemv_smem(int K);
+// Launches y = W x with the given prologue / epilogue on `ctas` CTAs
+// (dynamic = chunk counter in a.sched; otherwise a strided static schedule).
+// `pdl` sets programmatic stream serialization on the launch.
+int gemv_launch(const GemvArgs& a, int K, int pro, int epi, bool dynamic, int ctas,
+                cudaStream_t stream, bool pdl);
+
+}  // namespace lcrb

@@ -3,10 +3,12 @@
 The reference loads a real checkpoint (src/model.cu:112-213); this build runs on
 random-init weights of the same architecture, generated from a seed:
 
-* tensors are drawn in ``required_weights`` order (src/config.cpp:197-221):
-  the embedding, then per layer q, k, v, o, gate, up, down; each is
-  ``Generator.standard_normal(n, dtype=float32) * float32(0.02)`` from
-  ``numpy.random.default_rng(seed)``, rounded to bf16 (nearest, ties to even);
+* tensors are numbered in ``required_weights`` order (src/config.cpp:197-221):
+  the embedding 0, then per layer q, k, v, o, gate, up, down; tensor t is cut
+  into chunks of 2**24 elements and chunk c is
+  ``default_rng([seed, t, c]).standard_normal(n, dtype=float32) * float32(0.02)``
+  (numpy), rounded to bf16 (nearest, ties to even) -- independent streams, so
+  the chunks are generated in parallel threads;
 * every RMSNorm gain is exactly 1.0 (not drawn);
 * there is no lm_head tensor: the output head is the embedding (tied,
   src/model.cu:212).
@@ -189,41 +191,48 @@ def block_layout(geom: Geometry) -> Tuple[Dict[str, Tuple[int, int]], int]:
     return offsets, _align(off)
 
 
-def _fill_normal(rng: np.random.Generator, out: np.ndarray, chunk: int = 1 << 26) -> None:
-    scale = np.float32(0.02)
-    n = out.size
-    for start in range(0, n, chunk):
-        m = min(chunk, n - start)
-        v = rng.standard_normal(m, dtype=np.float32)
-        v *= scale
-        out[start:start + m] = float_to_bf16_bits(v)
+CHUNK = 1 << 24
 
 
-def generate(geom: Geometry, seed: int) -> WeightBlock:
+def _normal_bf16(seed: int, tensor: int, chunk: int, n: int) -> np.ndarray:
+    v = np.random.default_rng([seed, tensor, chunk]).standard_normal(n, dtype=np.float32)
+    v *= np.float32(0.02)
+    return float_to_bf16_bits(v)
+
+
+def generate(geom: Geometry, seed: int, threads: Optional[int] = None) -> WeightBlock:
     """The seeded random-init checkpoint (procedure in the module docstring)."""
+    from concurrent.futures import ThreadPoolExecutor
+
     offsets, total = block_layout(geom)
     data = np.zeros(total, dtype=np.uint16)
-    rng = np.random.default_rng(seed)
     g = geom
-    one = np.uint16(0x3F80)  # bf16 1.0
-
-    def sl(name, row0, rows, cols):
-        off, _ = offsets[name]
-        return data[off + row0 * cols: off + (row0 + rows) * cols]
-
-    _fill_normal(rng, sl("embed", 0, g.vocab_size, g.hidden_size))
+    h = g.hidden_size
+    # (element offset, element count) of every drawn tensor, in draw order.
+    tensors: List[Tuple[int, int]] = [(offsets["embed"][0], g.vocab_size * h)]
     for l in range(g.num_layers):
         p = f"layers.{l}."
-        h = g.hidden_size
-        _fill_normal(rng, sl(p + "qkv", 0, g.q_dim, h))
-        _fill_normal(rng, sl(p + "qkv", g.q_dim, g.kv_dim, h))
-        _fill_normal(rng, sl(p + "qkv", g.q_dim + g.kv_dim, g.kv_dim, h))
-        _fill_normal(rng, sl(p + "o", 0, h, g.q_dim))
-        _fill_normal(rng, sl(p + "gate_up", 0, g.intermediate_size, h))
-        _fill_normal(rng, sl(p + "gate_up", g.intermediate_size, g.intermediate_size, h))
-        _fill_normal(rng, sl(p + "down", 0, h, g.intermediate_size))
+        qkv, o = offsets[p + "qkv"][0], offsets[p + "o"][0]
+        gu, dn = offsets[p + "gate_up"][0], offsets[p + "down"][0]
+        f_ = g.intermediate_size
+        tensors += [(qkv, g.q_dim * h), (qkv + g.q_dim * h, g.kv_dim * h),
+                    (qkv + (g.q_dim + g.kv_dim) * h, g.kv_dim * h), (o, h * g.q_dim),
+                    (gu, f_ * h), (gu + f_ * h, f_ * h), (dn, h * f_)]
+    jobs = []
+    for t, (off, n) in enumerate(tensors):
+        for c, start in enumerate(range(0, n, CHUNK)):
+            jobs.append((t, c, off + start, min(CHUNK, n - start)))
+
+    def run(job):
+        t, c, at, m = job
+        data[at:at + m] = _normal_bf16(seed, t, c, m)
+
+    with ThreadPoolExecutor(threads or min(32, os.cpu_count() or 1)) as ex:
+        list(ex.map(run, jobs))
+    one = np.uint16(0x3F80)  # bf16 1.0
+    for l in range(g.num_layers):
         for nm in ("input_norm", "post_norm"):
-            off, n = offsets[p + nm]
+            off, n = offsets[f"layers.{l}.{nm}"]
             data[off:off + n] = one
     off, n = offsets["final_norm"]
     data[off:off + n] = one

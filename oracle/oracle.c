@@ -100,21 +100,33 @@ size_t orc_weight_bytes_per_token(const orc_config* c) {
 /* Kernel maths                                                              */
 /* ------------------------------------------------------------------------ */
 
-/* y[r] = sum_k W[r][k] x[k], accumulated in double (cuBLAS gemm_nt with fp32
- * compute, src/model.cu:38-45, is the operation being restated). */
+/* y[r] = sum_k W[r][k] x[k] in fp32 (cuBLAS gemm_nt with fp32 compute,
+ * src/model.cu:38-45, is the operation being restated): sixteen interleaved
+ * fp32 partial sums, added in double at the end. */
 static void gemv_f(float* y, const uint16_t* w, const float* x, int rows,
                    int cols) {
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint16_t* row = w + (size_t)r * cols;
-    double acc = 0.0;
-#pragma omp simd reduction(+ : acc)
-    for (int k = 0; k < cols; ++k) {
+    /* 16 fp32 partial sums (columns k mod 16), combined in double. */
+    float part[16] = {0};
+    int k = 0;
+    for (; k + 16 <= cols; k += 16) {
+      for (int j = 0; j < 16; ++j) {
+        uint32_t u = (uint32_t)row[k + j] << 16;
+        float wf;
+        memcpy(&wf, &u, 4);
+        part[j] = fmaf(wf, x[k + j], part[j]);
+      }
+    }
+    for (; k < cols; ++k) {
       uint32_t u = (uint32_t)row[k] << 16;
       float wf;
       memcpy(&wf, &u, 4);
-      acc += (double)wf * (double)x[k];
+      part[k & 15] = fmaf(wf, x[k], part[k & 15]);
     }
+    double acc = 0.0;
+    for (int j = 0; j < 16; ++j) acc += part[j];
     y[r] = (float)acc;
   }
 }

@@ -1,0 +1,171 @@
+"""The whole decode step through the C ABI against the fp32 host oracle on the
+same random-init checkpoints (greedy ids identical,
+per-step logits max-abs <= 3e-2 and cosine >= 0.999), plus the step's
+variants that must agree with each other bit for bit."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from lcr_b200 import checkpoint as ck
+from lcr_b200 import runtime as rt
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+MAX_ABS = 3e-2
+MIN_COS = 0.999
+
+
+def cos(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    block = ck.cached(ck.TINY, 0)
+    return block, rt.upload_block(block)
+
+
+def test_tiny_prefill_and_greedy_vs_oracle(tiny):
+    block, wdev = tiny
+    prompt = ck.prompt_ids(0, 32)
+    m = rt.Model(block, wdev, max_seq=64)
+    ref32 = oracle.Model(block, 64)
+    ref16 = oracle.Model(block, 64)
+    m.prefill(prompt)
+    for pos, tok in enumerate(prompt):
+        l32 = ref32.decode(int(tok), pos, oracle.MODE_FP32)
+        l16 = ref16.decode(int(tok), pos, oracle.MODE_BF16)
+    got = m.logits_to_host()
+    assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS
+    assert np.abs(got - l16).max() <= 1e-2
+    pos = len(prompt)
+    for step in range(16):
+        tok = int(np.argmax(got))
+        assert tok == oracle.argmax(l16), f"step {step}: greedy id differs from the bf16 oracle"
+        m.decode(tok)
+        got = m.logits_to_host()
+        l32 = ref32.decode(tok, pos, oracle.MODE_FP32)
+        l16 = ref16.decode(tok, pos, oracle.MODE_BF16)
+        assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS, step
+        pos += 1
+
+
+def test_device_greedy_loop_matches_host_loop(tiny):
+    block, wdev = tiny
+    prompt = ck.prompt_ids(0, 20)
+    a = rt.Model(block, wdev, max_seq=128)
+    a.prefill(prompt[:-1])
+    dev_tokens = a.generate_greedy(int(prompt[-1]), 40)
+    b = rt.Model(block, wdev, max_seq=128)
+    b.prefill(prompt)
+    host_tokens = []
+    for _ in range(40):
+        t = int(np.argmax(b.logits_to_host()))
+        host_tokens.append(t)
+        b.decode(t)
+    assert dev_tokens.tolist() == host_tokens
+    assert a.position == b.position == 19 + 40
+
+
+@pytest.mark.parametrize("variant", [dict(paged=True, page_order_seed=7),
+                                     dict(paged=True, page_size=32),
+                                     dict(flags=rt.FLAG_NO_GRAPH), dict(flags=rt.FLAG_NO_PDL),
+                                     dict(attention_splits=3), dict(gemv_ctas=37)])
+def test_step_variants_are_bit_identical(tiny, variant):
+    block, wdev = tiny
+    prompt = ck.prompt_ids(3, 40)
+    base = rt.Model(block, wdev, max_seq=96)
+    other = rt.Model(block, wdev, max_seq=96, **variant)
+    base.prefill(prompt)
+    other.prefill(prompt)
+    a, b = base.logits_to_host(), other.logits_to_host()
+    if "attention_splits" in variant or "gemv_ctas" in variant:
+        # a different split / CTA count changes fp32 summation order only
+        assert np.abs(a - b).max() < 1e-3
+    else:
+        assert np.array_equal(a, b)
+    ta = base.generate_greedy(int(np.argmax(a)), 8)
+    tb = other.generate_greedy(int(np.argmax(b)), 8)
+    assert ta.tolist() == tb.tolist()
+
+
+def test_paged_block_tables_match_oracle_allocator(tiny):
+    block, wdev = tiny
+    g = block.geom
+    seed = 12345
+    m = rt.Model(block, wdev, max_seq=200, paged=True, page_size=16, page_order_seed=seed)
+    m.prefill(ck.prompt_ids(5, 10))
+    m.generate_greedy(1, 23)  # length 34 -> 3 pages per layer
+    tables, mapped = m.page_tables()
+    max_pages = (200 + 15) // 16
+    pool = max_pages * g.num_layers
+    want = np.full((g.num_layers, max_pages), -1, np.int32)
+    order = oracle.page_permutation(pool, seed)
+    n = oracle.paged_reserve(want, 16, 0, 10, 0, pool, order)
+    n = oracle.paged_reserve(want, 16, 10, 33, n, pool, order)
+    n = oracle.paged_reserve(want, 16, 33, 34, n, pool, order)
+    assert mapped == n
+    assert np.array_equal(tables, want)
+
+
+def test_bad_inputs_are_rejected(tiny):
+    block, wdev = tiny
+    m = rt.Model(block, wdev, max_seq=8)
+    with pytest.raises(rt.LcrError) as e:
+        m.decode(-1)
+    assert e.value.status == 1
+    m.prefill([1, 2, 3, 4, 5, 6, 7, 8])
+    with pytest.raises(rt.LcrError) as e:
+        m.decode(3)
+    assert e.value.status == 6  # the cache is full
+    with pytest.raises(rt.LcrError):
+        rt.Model(block, wdev, max_seq=8, paged=True, page_size=8)
+
+
+def test_1b_config2_teacher_forced_vs_oracle():
+    """Config 2: Llama-3.2-1B geometry, seed 1, 128-id prompt, 256 greedy
+    tokens on the device; every step re-evaluated by the fp32 oracle on the
+    GPU's tokens."""
+    g = ck.LLAMA_3_2_1B
+    block = ck.cached(g, 1)
+    prompt = ck.prompt_ids(1, 128)
+    steps = int(os.environ.get("LCR_TEST_1B_STEPS", "256"))
+    m = rt.Model(block, max_seq=512)
+    m.prefill(prompt[:-1])
+    gen = m.generate_greedy(int(prompt[-1]), steps)
+    ref = oracle.Model(block, 512)
+    for pos, tok in enumerate(prompt[:-1]):
+        ref.decode(int(tok), pos, oracle.MODE_FP32)
+    # replay on the GPU with per-step logits for the comparison
+    m2 = rt.Model(block, m.weights_dev, max_seq=512)
+    m2.prefill(prompt[:-1])
+    tok, pos = int(prompt[-1]), len(prompt) - 1
+    worst_abs, worst_cos, near_ties, mismatches = 0.0, 1.0, 0, []
+    for s in range(steps):
+        m2.decode(tok)
+        got = m2.logits_to_host()
+        want = ref.decode(tok, pos, oracle.MODE_FP32)
+        worst_abs = max(worst_abs, float(np.abs(got - want).max()))
+        worst_cos = min(worst_cos, cos(got, want))
+        top2 = np.sort(want)[-2:]
+        if int(np.argmax(got)) != int(gen[s]):
+            mismatches.append(("graph-vs-step", s))
+        if int(gen[s]) != oracle.argmax(want):
+            gap = float(top2[1] - top2[0])
+            if gap < 2 * MAX_ABS:
+                near_ties += 1
+            else:
+                mismatches.append(("oracle", s, gap))
+        tok, pos = int(gen[s]), pos + 1
+    print(f"1B: worst max-abs {worst_abs:.4f}, worst cos {worst_cos:.6f}, near ties {near_ties}")
+    assert not mismatches, mismatches
+    assert worst_abs <= MAX_ABS and worst_cos >= MIN_COS
+    assert near_ties <= steps // 50
