@@ -140,13 +140,12 @@ int kv_dim(const lcr_ctx* c) { return c->d.num_kv_heads * c->d.head_dim; }
 int gemv_node(lcr_ctx* c, GemvArgs a, int K, int pro, int epi, int n_out, int* slot) {
   const int per = gemv_outputs_per_chunk(K, epi);
   a.n_out = n_out;
-  a.n_chunks = (n_out + per - 1) / per;
   LCRB_REQUIRE(*slot < c->sched_slots, LCR_ERR_STATE, "GEMV scheduler slots exhausted");
   a.sched = c->sched + 2 * (*slot)++;
   a.status = c->status;
   a.eps = c->d.rms_norm_eps;
   const int want = c->o.gemv_ctas > 0 ? c->o.gemv_ctas : c->sms;
-  const int ctas = std::max(1, std::min(a.n_chunks, want));
+  const int ctas = std::max(1, std::min((n_out + per - 1) / per, want));
   ++c->launches;
   return gemv_launch(a, K, pro, epi, true, ctas, c->stream, c->pdl);
 }

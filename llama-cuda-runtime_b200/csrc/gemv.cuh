@@ -44,9 +44,8 @@ enum GemvEpi { EPI_STORE = 0, EPI_STORE_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, 
 struct GemvArgs {
   const bf16* w;      // [N][K]; SWIGLU: rows [0, F) gate, [F, 2F) up
   int n_out;          // outputs (rows; SWIGLU: F)
-  int n_chunks;       // ceil(n_out / rows-per-chunk)
-  unsigned* sched;    // [2] next chunk, CTAs done -- zero before the first
-                      //     launch; the last CTA resets them
+  unsigned* sched;    // LOGITS_ARGMAX: [2], [1] counts finished CTAs -- zero
+                      //     before the first launch; the last CTA resets it
   uint32_t* status;   // device status word (bounded-wait failures)
   // prologue
   const bf16* x_in;       // PLAIN: input; NORM: residual stream (bf16)
@@ -88,6 +87,9 @@ struct GemvGeom {
 };
 
 constexpr int kGemvConsumers = 256;
+// Stages whose row partials are gathered in shared memory before one
+// cross-warp reduction and epilogue pass (<= 8 KB of partials for any K).
+constexpr int kGemvSegment = 64;
 constexpr int kGemvThreads = kGemvConsumers + 32;
 
 __device__ __forceinline__ uint32_t order_key(float v) {
@@ -137,24 +139,29 @@ __device__ __forceinline__ bool warp_row_owner(int lane) {
   return (lane & ((1 << (5 - m)) - 1)) == 0;
 }
 
-template <int K, int STAGE_BYTES, int STAGES, int PRO, int EPI, bool DYNAMIC>
+template <int K, int STAGE_BYTES, int STAGES, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const GemvArgs a) {
   using G = GemvGeom<K, STAGE_BYTES>;
-  constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR;
-  constexpr int PAIRS = RPS / 2;  // SWIGLU outputs per chunk
-  constexpr int OUT_PER_CHUNK = (EPI == EPI_SWIGLU) ? PAIRS : RPS;
+  constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR, WPR = G::WPR;
+  constexpr int PAIRS = RPS / 2;                              // SWIGLU outputs per stage
+  constexpr int UNIT = (EPI == EPI_SWIGLU) ? PAIRS : RPS;     // outputs per stage
+  constexpr int SEG = kGemvSegment;                           // stages per reduction pass
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
-  int* info = reinterpret_cast<int*>(cta_best + 1);      // [STAGES]
-  float* red8 = reinterpret_cast<float*>(info + STAGES);  // [8]
-  float* red = red8 + 8;                                  // [2][RPS][WPR]
+  float* red8 = reinterpret_cast<float*>(cta_best + 1);   // [8]
+  float* red = red8 + 8;                                    // [SEG * RPS][WPR]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+
+  // This CTA's contiguous share of the outputs (rows, or SWIGLU pairs).
+  const int o0 = static_cast<int>(static_cast<long long>(blockIdx.x) * a.n_out / gridDim.x);
+  const int o1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * a.n_out / gridDim.x);
+  const int n_stages = (o1 - o0 + UNIT - 1) / UNIT;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -172,50 +179,36 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
       const char* wbase = reinterpret_cast<const char*>(a.w);
-      int it = 0;
-      for (;; ++it) {
-        const int slot = it % STAGES;
-        if (it >= STAGES) {
-          if (!mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
-            info[slot] = -1;
-            mbar_arrive(&full[slot]);
-            break;
-          }
-        }
-        const int chunk = DYNAMIC ? static_cast<int>(atomicAdd(&a.sched[0], 1u))
-                                  : static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x);
-        if (chunk >= a.n_chunks) {
-          info[slot] = -1;
-          mbar_arrive(&full[slot]);
+      int issued = 0;
+      for (int st = 0; st < n_stages; ++st) {
+        const int slot = st % STAGES;
+        if (st >= STAGES &&
+            !mbar_wait(&empty[slot], ((st / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
           break;
         }
-        info[slot] = chunk;
         uint8_t* dst = ring + slot * STAGE_BYTES;
-        const int first = chunk * OUT_PER_CHUNK;
-        const int rows = min(OUT_PER_CHUNK, a.n_out - first);
+        const int first = o0 + st * UNIT;
+        const uint32_t bytes = static_cast<uint32_t>(min(UNIT, o1 - first)) * G::ROW_BYTES;
         if constexpr (EPI == EPI_SWIGLU) {
-          const uint32_t bytes = static_cast<uint32_t>(rows) * G::ROW_BYTES;
           mbar_arrive_expect_tx(&full[slot], 2 * bytes);
           bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
           bulk_g2s(dst + PAIRS * G::ROW_BYTES,
                    wbase + static_cast<size_t>(a.n_out + first) * G::ROW_BYTES, bytes, &full[slot],
                    policy);
         } else {
-          const uint32_t bytes = static_cast<uint32_t>(rows) * G::ROW_BYTES;
           mbar_arrive_expect_tx(&full[slot], bytes);
           bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
         }
+        issued = st + 1;
       }
-      // Stage `it` carried the end marker (and stage it - STAGES, in the same
-      // slot, was consumed before it); never leave the CTA with a copy still
-      // writing its shared memory.
-      for (int k = it >= STAGES ? it - STAGES + 1 : 0; k < it; ++k) {
+      // Never leave the CTA with a copy still writing its shared memory.
+      for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k) {
         mbar_wait(&full[k % STAGES], (k / STAGES) & 1, a.status, kStatusTimeoutFull);
       }
     }
   } else {
     // ---------------- consumers ----------------
-    const int slotrow = tid / TPR;  // which row of each pass this thread serves
+    const int slotrow = tid / TPR;  // which rows of each stage this thread serves
     const int ci = tid % TPR;       // chunk index within the row
     float xr[CPT][8];
 
@@ -285,56 +278,51 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
     }
 
     unsigned long long best = 0ull;
-    for (int it = 0;; ++it) {
-      const int slot = it % STAGES;
-      const bool ok = mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
-      const int chunk = ok ? info[slot] : -1;
-      const uint8_t* stage = ring + slot * STAGE_BYTES;
-
-      float part[RPT];
+    bool failed = false;
+    for (int seg0 = 0; seg0 < n_stages; seg0 += SEG) {
+      const int seg1 = min(n_stages, seg0 + SEG);
+      for (int st = seg0; st < seg1; ++st) {
+        const int slot = st % STAGES;
+        if (!failed) failed = !mbar_wait(&full[slot], (st / STAGES) & 1, a.status, kStatusTimeoutFull);
+        const uint8_t* stage = ring + slot * STAGE_BYTES;
+        float part[RPT];
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) part[r] = 0.f;
-      if (chunk >= 0) {
+        for (int r = 0; r < RPT; ++r) {
+          const int row = slotrow * RPT + r;
+          float acc = 0.f;
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int row = slotrow * RPT + r;
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES +
-                                                           (ci + j * TPR) * 16);
-          acc = fmaf(bf_lo(wv.x), xr[j][0], acc);
-          acc = fmaf(bf_hi(wv.x), xr[j][1], acc);
-          acc = fmaf(bf_lo(wv.y), xr[j][2], acc);
-          acc = fmaf(bf_hi(wv.y), xr[j][3], acc);
-          acc = fmaf(bf_lo(wv.z), xr[j][4], acc);
-          acc = fmaf(bf_hi(wv.z), xr[j][5], acc);
-          acc = fmaf(bf_lo(wv.w), xr[j][6], acc);
-          acc = fmaf(bf_hi(wv.w), xr[j][7], acc);
+          for (int j = 0; j < CPT; ++j) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES +
+                                                             (ci + j * TPR) * 16);
+            acc = fmaf(bf_lo(wv.x), xr[j][0], acc);
+            acc = fmaf(bf_hi(wv.x), xr[j][1], acc);
+            acc = fmaf(bf_lo(wv.y), xr[j][2], acc);
+            acc = fmaf(bf_hi(wv.y), xr[j][3], acc);
+            acc = fmaf(bf_lo(wv.z), xr[j][4], acc);
+            acc = fmaf(bf_hi(wv.z), xr[j][5], acc);
+            acc = fmaf(bf_lo(wv.w), xr[j][6], acc);
+            acc = fmaf(bf_hi(wv.w), xr[j][7], acc);
+          }
+          part[r] = acc;
         }
-        part[r] = acc;
+        __syncwarp();
+        if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
+        const float wsum = warp_reduce_rows<RPT>(part, lane);
+        if (warp_row_owner<RPT>(lane)) {
+          const int row = slotrow * RPT + warp_row_of_lane<RPT>(lane);
+          red[((st - seg0) * RPS + row) * WPR + (warp % WPR)] = wsum;
+        }
       }
-      }
-      __syncwarp();
-      if (lane == 0 && ok) mbar_arrive(&empty[slot]);
-
-      const float wsum = warp_reduce_rows<RPT>(part, lane);
-      float* rb = red + (it & 1) * RPS * G::WPR;
-      if (warp_row_owner<RPT>(lane)) {
-        const int row = slotrow * RPT + warp_row_of_lane<RPT>(lane);
-        rb[row * G::WPR + (warp % G::WPR)] = wsum;
-      }
-      // One barrier both publishes the partials and votes on leaving: every
-      // consumer sees the same `stop`, so no warp is left at a later barrier.
-      if (named_sync_or(1, kGemvConsumers, chunk < 0)) break;
-
-      const int first = chunk * OUT_PER_CHUNK;
-      const int rows = min(OUT_PER_CHUNK, a.n_out - first);
-      if (tid < rows) {
+      named_sync(1, kGemvConsumers);  // the segment's partials are in shared memory
+      const int first = o0 + seg0 * UNIT;
+      const int outs = min(o1, o0 + seg1 * UNIT) - first;
+      for (int u = tid; u < outs && !failed; u += kGemvConsumers) {
+        const int st = u / UNIT, r = u % UNIT;
+        const float* rr = red + (st * RPS + r) * WPR;
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < G::WPR; ++w) v += rb[tid * G::WPR + w];
-        const int out = first + tid;
+        for (int w = 0; w < WPR; ++w) v += rr[w];
+        const int out = first + u;
         if constexpr (EPI == EPI_STORE) {
           a.y[out] = __ushort_as_bfloat16(f2bf(v));
         } else if constexpr (EPI == EPI_STORE_F32) {
@@ -344,12 +332,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
           a.resid[out] = __ushort_as_bfloat16(f2bf(s));
           a.resid_sum[out] = s;
         } else if constexpr (EPI == EPI_SWIGLU) {
-          float u = 0.f;
+          const float* ru = red + (st * RPS + r + PAIRS) * WPR;
+          float up = 0.f;
 #pragma unroll
-          for (int w = 0; w < G::WPR; ++w) u += rb[(tid + PAIRS) * G::WPR + w];
+          for (int w = 0; w < WPR; ++w) up += ru[w];
           const float g = rbf(v);
           const float silu = g / (1.0f + __expf(-g));
-          a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(u)));
+          a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
         } else if constexpr (EPI == EPI_LOGITS_ARGMAX) {
           a.yf[out] = v;
           const unsigned long long packed =
@@ -358,6 +347,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
           best = best > packed ? best : packed;
         }
       }
+      named_sync(1, kGemvConsumers);  // the next segment may overwrite `red`
     }
     if constexpr (EPI == EPI_LOGITS_ARGMAX) {
       if (best != 0ull) atomicMax(cta_best, best);
@@ -365,17 +355,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   }
 
   __syncthreads();
-  if (DYNAMIC && tid == 0) {
-    if constexpr (EPI == EPI_LOGITS_ARGMAX) atomicMax(a.argmax_acc, *cta_best);
-    __threadfence();
-    const unsigned prev = atomicAdd(&a.sched[1], 1u);
-    if (prev == gridDim.x - 1) {
-      // Last CTA: every chunk has been taken and every CTA's results are
-      // visible. Reset the scheduler for the next launch of this node.
+  if constexpr (EPI == EPI_LOGITS_ARGMAX) {
+    if (tid == 0) {
+      atomicMax(a.argmax_acc, *cta_best);
       __threadfence();
-      atomicExch(&a.sched[0], 0u);
-      atomicExch(&a.sched[1], 0u);
-      if constexpr (EPI == EPI_LOGITS_ARGMAX) {
+      const unsigned prev = atomicAdd(&a.sched[1], 1u);
+      if (prev == gridDim.x - 1) {
+        // Last CTA: every CTA's maximum is in the accumulator. Publish the
+        // token, advance the position, and reset for the next launch.
+        __threadfence();
+        atomicExch(&a.sched[1], 0u);
         const unsigned long long packed = atomicExch(a.argmax_acc, 0ull);
         const int next = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed & 0xFFFFFFFFull));
         const int pos = *a.state_pos;
@@ -390,8 +379,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
 template <int K, int STAGE_BYTES, int STAGES>
 constexpr size_t gemv_smem_bytes() {
   using G = GemvGeom<K, STAGE_BYTES>;
-  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) +
-         STAGES * sizeof(int) + (2 * G::RPS * G::WPR + 8) * sizeof(float) + 16 + 64;
+  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) + 8 +
+         (8 + static_cast<size_t>(kGemvSegment) * G::RPS * G::WPR) * sizeof(float) + 64;
 }
 
 }  // namespace lcrb

@@ -4,9 +4,9 @@
 namespace lcrb {
 namespace {
 
-template <int K, int PRO, int EPI, bool DYN>
+template <int K, int PRO, int EPI>
 int launch_one(const GemvArgs& a, int ctas, cudaStream_t stream, bool pdl) {
-  auto kernel = gemv_stream_kernel<K, kGemvStageBytes, kGemvStages, PRO, EPI, DYN>;
+  auto kernel = gemv_stream_kernel<K, kGemvStageBytes, kGemvStages, PRO, EPI>;
   constexpr size_t smem = gemv_smem_bytes<K, kGemvStageBytes, kGemvStages>();
   // Per device and cheap; set on every launch so multi-GPU processes work.
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -26,9 +26,8 @@ int launch_one(const GemvArgs& a, int ctas, cudaStream_t stream, bool pdl) {
 }
 
 template <int K, int PRO, int EPI>
-int launch_k(const GemvArgs& a, bool dyn, int ctas, cudaStream_t s, bool pdl) {
-  return dyn ? launch_one<K, PRO, EPI, true>(a, ctas, s, pdl)
-             : launch_one<K, PRO, EPI, false>(a, ctas, s, pdl);
+int launch_k(const GemvArgs& a, bool, int ctas, cudaStream_t s, bool pdl) {
+  return launch_one<K, PRO, EPI>(a, ctas, s, pdl);
 }
 
 template <int K>

@@ -15,9 +15,9 @@ bool gemv_supported(int K, int pro, int epi);
 // Outputs (rows, or SWIGLU pairs) per chunk of one stage.
 int gemv_outputs_per_chunk(int K, int epi);
 size_t gemv_smem(int K);
-// Launches y = W x with the given prologue / epilogue on `ctas` CTAs
-// (dynamic = chunk counter in a.sched; otherwise a strided static schedule).
-// `pdl` sets programmatic stream serialization on the launch.
+// Launches y = W x with the given prologue / epilogue on `ctas` CTAs, each
+// streaming a contiguous share of the outputs (`dynamic` is ignored and kept
+// for call-site compatibility). `pdl` sets programmatic stream serialization.
 int gemv_launch(const GemvArgs& a, int K, int pro, int epi, bool dynamic, int ctas,
                 cudaStream_t stream, bool pdl);
 

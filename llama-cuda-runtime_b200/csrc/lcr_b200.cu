@@ -287,7 +287,6 @@ extern "C" int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, in
       GemvArgs a = {};
       a.w = cb(w);
       a.n_out = out_features;
-      a.n_chunks = chunks;
       a.x_in = cb(x) + static_cast<size_t>(r) * in_features;
       if (y_fp32) a.yf = reinterpret_cast<float*>(y) + static_cast<size_t>(r) * out_features;
       else a.y = mb(y) + static_cast<size_t>(r) * out_features;

@@ -18,6 +18,7 @@ REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_host.so")
 
 MODE_FP32 = 0
 MODE_BF16 = 1
+MODE_BF16_REORDERED = 2
 
 
 def build(ref: bool = False) -> None:

@@ -131,6 +131,26 @@ static void gemv_f(float* y, const uint16_t* w, const float* x, int rows,
   }
 }
 
+/* The same product summed in the opposite order, one fp32 accumulator
+ * (ORC_MODE_BF16_REORDERED): a second, equally valid evaluation order, to
+ * measure how far two implementations of the bf16-storage algorithm drift
+ * apart from summation order alone. */
+static void gemv_f_reordered(float* y, const uint16_t* w, const float* x,
+                             int rows, int cols) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t* row = w + (size_t)r * cols;
+    float acc = 0.f;
+    for (int k = cols - 1; k >= 0; --k) {
+      uint32_t u = (uint32_t)row[k] << 16;
+      float wf;
+      memcpy(&wf, &u, 4);
+      acc = fmaf(wf, x[k], acc);
+    }
+    y[r] = acc;
+  }
+}
+
 void orc_gemv(float* y, const uint16_t* w, const uint16_t* x, int rows,
               int cols) {
   float* xf = (float*)malloc(sizeof(float) * (size_t)cols);
@@ -304,7 +324,9 @@ void orc_state_reset(orc_state* s) {
 int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
                int token, int position, int mode, float* logits, float* taps) {
   if (token < 0 || token >= c->vocab || position < 0 || position >= s->max_seq) return 1;
-  const int bf = (mode == ORC_MODE_BF16);
+  const int bf = (mode == ORC_MODE_BF16 || mode == ORC_MODE_BF16_REORDERED);
+  void (*gemv)(float*, const uint16_t*, const float*, int, int) =
+      mode == ORC_MODE_BF16_REORDERED ? gemv_f_reordered : gemv_f;
   const int H = c->hidden, F = c->ffn, d = c->head_dim;
   const int qd = c->heads * d, kvd = c->kv_heads * d, group = c->heads / c->kv_heads;
   const int seq = position + 1;
@@ -331,7 +353,7 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
        layer's MLP residual join (src/model.cu:384-388, 449-458) */
     rmsnorm_f(normed, x, xsum, w->input_norm[l], H, c->eps, bf);
 
-    gemv_f(qkv, w->qkv[l], normed, qd + 2 * kvd, H);
+    gemv(qkv, w->qkv[l], normed, qd + 2 * kvd, H);
     if (bf) orc_round_bf16_inplace(qkv, (size_t)(qd + 2 * kvd));
 
     /* RoPE on Q (head-major out, bf16) and K, plus the cache write
@@ -380,7 +402,7 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
 
     /* o_proj, then the attention residual join fused with the post-attention
        norm (src/model.cu:418-428). */
-    gemv_f(proj, w->o[l], attn, H, qd);
+    gemv(proj, w->o[l], attn, H, qd);
     if (bf) orc_round_bf16_inplace(proj, (size_t)H);
     for (int i = 0; i < H; ++i) {
       xsum[i] = x[i] + proj[i];
@@ -390,7 +412,7 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
 
     /* gate/up as one [2F][H] GEMM, then SwiGLU on the two halves
        (src/model.cu:429-438). */
-    gemv_f(gu, w->gate_up[l], normed, 2 * F, H);
+    gemv(gu, w->gate_up[l], normed, 2 * F, H);
     if (bf) orc_round_bf16_inplace(gu, (size_t)2 * F);
     for (int i = 0; i < F; ++i) {
       const float a = silu_f(gu[i]) * gu[F + i];
@@ -398,7 +420,7 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
     }
 
     /* down_proj and the MLP residual join (src/model.cu:439-458). */
-    gemv_f(proj, w->down[l], act, H, F);
+    gemv(proj, w->down[l], act, H, F);
     if (bf) orc_round_bf16_inplace(proj, (size_t)H);
     for (int i = 0; i < H; ++i) {
       xsum[i] = x[i] + proj[i];
@@ -411,7 +433,7 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
      the last row with fp32 logits (src/model.cu:449-483). */
   rmsnorm_f(normed, x, xsum, w->final_norm, H, c->eps, bf);
   if (taps) memcpy(taps + (size_t)(c->layers + 1) * H, normed, sizeof(float) * H);
-  gemv_f(logits, w->lm_head, normed, c->vocab, H);
+  gemv(logits, w->lm_head, normed, c->vocab, H);
 
   free(x); free(xsum); free(normed); free(qkv); free(qr); free(attn);
   free(proj); free(gu); free(act); free(sc);

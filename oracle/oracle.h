@@ -30,6 +30,9 @@
  *                     tensor (normed, qkv, roped q/k, attention output,
  *                     projections, residual stream, SwiGLU output); math in
  *                     between is fp32/fp64. This is the reference algorithm.
+ *   ORC_MODE_BF16_REORDERED  the same with every dot product summed in the
+ *                     opposite order: the spread between the two bf16 modes
+ *                     is the reproducibility floor of the algorithm itself.
  *
  * Parity pins: the RoPE table against tests/test_config.cpp:120-182, sampling
  * against tests/test_kernels.cu:468-508, page accounting against
@@ -48,7 +51,7 @@
 extern "C" {
 #endif
 
-enum { ORC_MODE_FP32 = 0, ORC_MODE_BF16 = 1 };
+enum { ORC_MODE_FP32 = 0, ORC_MODE_BF16 = 1, ORC_MODE_BF16_REORDERED = 2 };
 
 typedef struct {
   int hidden, ffn, layers, heads, kv_heads, head_dim, vocab;
