@@ -63,6 +63,13 @@ constexpr int kAttnConsumerWarps = 4;
 constexpr int kAttnThreads = (kAttnConsumerWarps + 1) * 32;
 constexpr int kAttnBlock = 16;  // positions per stage
 
+// Largest split count whose partials for one (sequence, KV head) group fit the
+// stage ring, so the last CTA can merge them from shared memory.
+template <int D, int STAGES>
+constexpr int attn_max_staged_splits(int group) {
+  return (STAGES * 2 * kAttnBlock * D * 2) / (group * (2 + D) * 4);
+}
+
 template <int D, int STAGES>
 constexpr size_t attn_smem_bytes() {
   return static_cast<size_t>(STAGES) * 2 * kAttnBlock * D * 2 + 2 * STAGES * 8 +
@@ -381,18 +388,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       }
       named_sync(1, kAttnConsumerWarps * 32);
       if (s_last) {
+        // Stage the group's split partials -- one contiguous span of
+        // G * splits * (2 + D) floats -- into the (now idle) ring with
+        // coalesced L2 loads, then merge from shared memory.
+        const int span = G * a.splits * (2 + D);
+        const float* src = a.partials + (static_cast<size_t>(b) * heads + kvh * G) * a.splits * (2 + D);
+        float* stg = reinterpret_cast<float*>(ring);
+        if (span * static_cast<int>(sizeof(float)) <= STAGES * 2 * KB) {
+#pragma unroll 8
+          for (int i = tid; i < span; i += kAttnConsumerWarps * 32) stg[i] = __ldcg(src + i);
+          named_sync(1, kAttnConsumerWarps * 32);
+        } else {
+          stg = nullptr;  // too many splits to stage: merge straight from L2
+        }
         for (int idx = tid; idx < G * D; idx += kAttnConsumerWarps * 32) {
           const int g = idx / D, d = idx % D;
           const int h = kvh * G + g;
-          const volatile float* base =
-              a.partials + (static_cast<size_t>(b) * heads + h) * a.splits * (2 + D);
+          const float* base = stg ? stg + g * a.splits * (2 + D)
+                                  : src + g * a.splits * (2 + D);
           float M = kNegBig;
-          for (int s = 0; s < a.splits; ++s) M = fmaxf(M, base[s * (2 + D)]);
+          for (int s = 0; s < a.splits; ++s) M = fmaxf(M, stg ? base[s * (2 + D)] : __ldcg(base + s * (2 + D)));
           float L = 0.f, A = 0.f;
           for (int s = 0; s < a.splits; ++s) {
-            const float sc = ex2_approx(base[s * (2 + D)] - M);
-            L += base[s * (2 + D) + 1] * sc;
-            A += base[s * (2 + D) + 2 + d] * sc;
+            const float m_s = stg ? base[s * (2 + D)] : __ldcg(base + s * (2 + D));
+            const float l_s = stg ? base[s * (2 + D) + 1] : __ldcg(base + s * (2 + D) + 1);
+            const float a_s = stg ? base[s * (2 + D) + 2 + d] : __ldcg(base + s * (2 + D) + 2 + d);
+            const float sc = ex2_approx(m_s - M);
+            L += l_s * sc;
+            A += a_s * sc;
           }
           a.out[static_cast<size_t>(b) * heads * D + h * D + d] =
               __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));

@@ -413,6 +413,13 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
 
   // Split-K width: enough (kv_head, split) CTAs to cover every SM once.
   c->splits = o.attention_splits > 0 ? o.attention_splits : std::max(1, c->sms / d.num_kv_heads);
+  {
+    // Keep the last CTA's merge in shared memory (attn_max_staged_splits).
+    const int group = d.num_heads / d.num_kv_heads;
+    const int cap = d.head_dim == 64 ? attn_max_staged_splits<64, kAttnStages>(group)
+                                     : attn_max_staged_splits<128, kAttnStages>(group);
+    if (o.attention_splits <= 0) c->splits = std::max(1, std::min(c->splits, cap));
+  }
   // One scheduler slot per GEMV node of the step, plus kTimingSlots for
   // lcr_time_gemv (back-to-back launches may overlap, so none share a slot).
   c->sched_slots = 5 * d.num_layers + 8 + kTimingSlots;

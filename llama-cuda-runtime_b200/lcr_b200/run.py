@@ -1,0 +1,112 @@
+"""llama-run for the B200 build (the reference's src/main.cu CLI surface, on the
+seeded random-init checkpoints: there is no tokenizer on this path, so the
+prompt is token ids).
+
+  python -m lcr_b200.run --model 1b --prompt-len 128 --max-tokens 256 --bench
+  python -m lcr_b200.run --model tiny --prompt 1,2,3 --max-tokens 16 --json
+
+--bench / --json report the numbers of main.cu:195-334: decode tokens/s,
+ms/token, bytes per token (weights + mean-length KV read) and the achieved
+bandwidth against --peak-bandwidth (GB/s).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import time
+
+import numpy as np
+
+from . import checkpoint as ck
+from . import runtime as rt
+
+MODELS = {"1b": ck.LLAMA_3_2_1B, "tiny": ck.TINY}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="lcr_b200.run")
+    ap.add_argument("--model", default="1b", choices=sorted(MODELS))
+    ap.add_argument("--seed", type=int, default=None, help="checkpoint seed (1b: 1, tiny: 0)")
+    ap.add_argument("--prompt", default=None, help="comma-separated token ids")
+    ap.add_argument("--prompt-len", type=int, default=128, help="uniform random prompt length")
+    ap.add_argument("--max-tokens", type=int, default=128)
+    ap.add_argument("--max-seq", type=int, default=0)
+    ap.add_argument("--paged", action="store_true")
+    ap.add_argument("--page-size", type=int, default=16)
+    ap.add_argument("--page-order-seed", type=int, default=0)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--temperature", type=float, default=0.0)
+    ap.add_argument("--top-k", type=int, default=0)
+    ap.add_argument("--top-p", type=float, default=0.95)
+    ap.add_argument("--peak-bandwidth", type=float, default=8000.0, help="GB/s")
+    ap.add_argument("--bench", action="store_true")
+    ap.add_argument("--json", action="store_true")
+    args = ap.parse_args(argv)
+
+    geom = MODELS[args.model]
+    seed = args.seed if args.seed is not None else (1 if args.model == "1b" else 0)
+    block = ck.generate(geom, seed)
+    if args.prompt:
+        prompt = np.array([int(t) for t in args.prompt.split(",")], np.int32)
+    else:
+        prompt = ck.prompt_ids(seed, args.prompt_len)
+    max_seq = args.max_seq or (len(prompt) + args.max_tokens + 8)
+    t0 = time.perf_counter()
+    m = rt.Model(block, device=args.device, max_seq=max_seq, paged=args.paged,
+                 page_size=args.page_size, attention_splits=args.splits,
+                 page_order_seed=args.page_order_seed)
+    load_ms = (time.perf_counter() - t0) * 1000
+
+    t0 = time.perf_counter()
+    logits_ptr = m.prefill(prompt)
+    prefill_ms = (time.perf_counter() - t0) * 1000
+    tokens = []
+    t0 = time.perf_counter()
+    if args.temperature <= 0.0:
+        first = int(np.argmax(m.logits_to_host()))
+        tokens = [first] + m.generate_greedy(first, max(0, args.max_tokens - 1)).tolist()
+    else:
+        # The host draws the uniform, as main.cu:442-443 does with mt19937_64.
+        rng = np.random.default_rng(seed)
+        for _ in range(args.max_tokens):
+            tok = m.sample(logits_ptr, args.temperature, args.top_k, args.top_p,
+                           float(np.float32(rng.random())))
+            tokens.append(tok)
+            logits_ptr = m.decode(tok)
+    decode_ms = (time.perf_counter() - t0) * 1000
+    steps = max(1, args.max_tokens - 1)
+    mean_len = len(prompt) + (steps + 1) / 2.0
+    bytes_per_token = geom.weight_bytes_per_token() + mean_len * geom.kv_bytes_per_position()
+    report = {
+        "runtime": "llama-cuda-runtime_b200", "model": geom.name, "seed": seed,
+        "load_ms": load_ms, "prompt_tokens": int(len(prompt)), "prefill_ms": prefill_ms,
+        "decode_steps": steps, "decode_ms": decode_ms,
+        "decode_ms_per_token": decode_ms / steps,
+        "decode_tokens_per_second": steps / (decode_ms / 1000),
+        "weight_bytes_per_token": geom.weight_bytes_per_token(),
+        "kv_bytes_per_position": geom.kv_bytes_per_position(),
+        "bytes_per_token": bytes_per_token,
+        "achieved_bandwidth_bytes_per_second": bytes_per_token / (decode_ms / 1000 / steps),
+        "peak_bandwidth_bytes_per_second": args.peak_bandwidth * 1e9,
+        "kv_layout": "paged" if args.paged else "contiguous", "kv_page_size": args.page_size,
+        "sequence_length": int(len(prompt) + args.max_tokens), "tokens": tokens[:32],
+    }
+    report["bandwidth_utilization"] = (report["achieved_bandwidth_bytes_per_second"]
+                                       / report["peak_bandwidth_bytes_per_second"])
+    if args.json:
+        print(json.dumps(report))
+    elif args.bench:
+        print(f"decode  {steps} steps in {decode_ms:.2f} ms ({decode_ms / steps:.3f} ms/token, "
+              f"{report['decode_tokens_per_second']:.1f} tokens/s)")
+        print(f"achieved {report['achieved_bandwidth_bytes_per_second'] / 1e9:.0f} GB/s, "
+              f"{100 * report['bandwidth_utilization']:.1f}% of {args.peak_bandwidth:.0f} GB/s")
+    else:
+        print(" ".join(str(t) for t in tokens))
+    m.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

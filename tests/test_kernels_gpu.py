@@ -38,6 +38,18 @@ def dev(a):
     return torch.from_numpy(a).cuda()
 
 
+_KEEP = []
+
+
+def dptr(a):
+    """Device copy of `a` kept alive for the test session (kernels run
+    asynchronously, so an inline temporary could be freed and its memory
+    handed to the next upload before the kernel reads it)."""
+    t = dev(a)
+    _KEEP.append(t)
+    return t.data_ptr()
+
+
 def host_bf(t):
     return t.cpu().numpy().view(np.uint16)
 
@@ -50,7 +62,9 @@ def expect_close(got, want, tol=TOL, what=""):
     got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
     scale = max(np.abs(want).max(), 1e-6)
     err = np.abs(got - want).max() / scale
-    assert err <= tol, f"{what}: worst relative error {err:.3g} > {tol}"
+    i = int(np.argmax(np.abs(got - want)))
+    assert err <= tol, (f"{what}: worst relative error {err:.3g} > {tol} at {i} "
+                        f"(got {got.flat[i]:.6g}, want {want.flat[i]:.6g}, scale {scale:.4g})")
 
 
 def run(status):
@@ -62,7 +76,7 @@ def test_rmsnorm():
     x = bf(RNG.normal(size=(5, 2048)))
     w = bf(RNG.normal(0, 0.5, 2048))
     out = torch.empty(5 * 2048, dtype=torch.int16, device="cuda")
-    run(L.lcr_rmsnorm(out.data_ptr(), dev(x).data_ptr(), dev(w).data_ptr(), 5, 2048, 1e-5, S()))
+    run(L.lcr_rmsnorm(out.data_ptr(), dptr(x), dptr(w), 5, 2048, 1e-5, S()))
     want = oracle.rmsnorm(x, w, 1e-5, round_out=True)
     expect_close(fl(host_bf(out)).reshape(5, 2048), want, 1e-2, "rmsnorm")
 
@@ -72,15 +86,15 @@ def test_add_residual_rmsnorm_and_residual():
     d = bf(RNG.normal(size=(3, 2048)))
     w = bf(RNG.normal(0, 0.5, 2048))
     xd, out = dev(x), torch.empty(3 * 2048, dtype=torch.int16, device="cuda")
-    run(L.lcr_add_residual_rmsnorm(out.data_ptr(), xd.data_ptr(), dev(d).data_ptr(),
-                                   dev(w).data_ptr(), 3, 2048, 1e-5, S()))
+    run(L.lcr_add_residual_rmsnorm(out.data_ptr(), xd.data_ptr(), dptr(d),
+                                   dptr(w), 3, 2048, 1e-5, S()))
     want_out, want_x = oracle.add_residual_rmsnorm(x, d, w, 1e-5)
     assert np.array_equal(host_bf(xd).reshape(3, 2048), want_x)  # stored sum is exact
     expect_close(fl(host_bf(out)).reshape(3, 2048), want_out, 1e-2, "add_residual_rmsnorm")
     count = 8192 * 3 + 5  # not a multiple of eight (tests/test_kernels.cu:156)
     a, b = bf(RNG.normal(size=count)), bf(RNG.normal(size=count))
     ad = dev(a)
-    run(L.lcr_add_residual(ad.data_ptr(), dev(b).data_ptr(), count, S()))
+    run(L.lcr_add_residual(ad.data_ptr(), dptr(b), count, S()))
     assert np.array_equal(host_bf(ad), bf(fl(a) + fl(b)))
 
 
@@ -88,7 +102,7 @@ def test_swiglu_plain_and_strided():
     count = 8192 * 3 + 5
     g, u = bf(RNG.normal(size=count)), bf(RNG.normal(size=count))
     out = torch.empty(count, dtype=torch.int16, device="cuda")
-    run(L.lcr_swiglu(out.data_ptr(), dev(g).data_ptr(), dev(u).data_ptr(), count, S()))
+    run(L.lcr_swiglu(out.data_ptr(), dptr(g), dptr(u), count, S()))
     expect_close(fl(host_bf(out)), oracle.swiglu(g, u), TOL, "swiglu")
     tokens, width = 3, 1000
     gu = bf(RNG.normal(size=(tokens, 2 * width)))
@@ -104,7 +118,7 @@ def test_embedding_lookup_exact():
     table = bf(RNG.normal(size=(128, 2048)))
     ids = np.array([7, 0, 127, 63], np.int32)
     out = torch.empty(4 * 2048, dtype=torch.int16, device="cuda")
-    run(L.lcr_embedding_lookup(out.data_ptr(), dev(table).data_ptr(), dev(ids).data_ptr(), 4, 2048,
+    run(L.lcr_embedding_lookup(out.data_ptr(), dptr(table), dptr(ids), 4, 2048,
                                S()))
     assert np.array_equal(host_bf(out).reshape(4, 2048), table[ids])
 
@@ -114,7 +128,7 @@ def test_rope_q():
     q = bf(RNG.normal(size=(tokens, heads * d)))
     inv = (500000.0 ** (-2.0 * np.arange(32) / 64)).astype(np.float32)
     out = torch.empty(tokens * heads * d, dtype=torch.int16, device="cuda")
-    run(L.lcr_rope_q(out.data_ptr(), dev(q).data_ptr(), dev(inv).data_ptr(), tokens, start, heads, d,
+    run(L.lcr_rope_q(out.data_ptr(), dptr(q), dptr(inv), tokens, start, heads, d,
                      heads * d, S()))
     want = oracle.rope_rows(q, inv, start, heads, d, heads * d, head_major=True)
     expect_close(fl(host_bf(out)), want, TOL, "rope_q")
@@ -127,7 +141,7 @@ def test_gemm_nt(rows, k, n, fp32):
     x = bf(RNG.normal(size=(rows, k)))
     w = bf(RNG.normal(0, 0.02, size=(n, k)))
     y = torch.empty(rows * n, dtype=torch.float32 if fp32 else torch.int16, device="cuda")
-    run(L.lcr_gemm_nt(y.data_ptr(), fp32, dev(x).data_ptr(), dev(w).data_ptr(), rows, k, n, S()))
+    run(L.lcr_gemm_nt(y.data_ptr(), fp32, dptr(x), dptr(w), rows, k, n, S()))
     got = y.cpu().numpy() if fp32 else fl(host_bf(y))
     want = np.concatenate([oracle.gemv(w, x[r]) for r in range(rows)])
     expect_close(got, want, 1e-5 if fp32 else 1e-2, "gemm_nt")
@@ -168,7 +182,7 @@ def _attention_case(heads, kv_heads, d, positions, splits, paged, shuffled=False
     nscr = max(2, L.lcr_decode_attention_scratch_floats(heads, d, splits))
     scr = torch.empty(nscr, dtype=torch.float32, device="cuda")
     scale = float(np.float32(1.0) / np.sqrt(np.float32(d)))
-    run(L.lcr_decode_attention(out.data_ptr(), dev(q).data_ptr(), ctypes.byref(view), heads,
+    run(L.lcr_decode_attention(out.data_ptr(), dptr(q), ctypes.byref(view), heads,
                                heads // kv_heads, positions, scale, int(paged), splits,
                                scr.data_ptr(), S()))
     want = oracle.attention(q, keys, values, heads, kv_heads, d, positions)
