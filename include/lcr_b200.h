@@ -185,7 +185,9 @@ typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
   uint64_t page_order_seed; /* 0 = pages handed out in counter order;
                                otherwise a seeded permutation of the pool */
   int gemv_ctas;        /* CTAs per streaming GEMV; 0 = one per SM */
-  int flags;            /* bit 0: disable programmatic dependent launch */
+  int flags;            /* bit 0: no programmatic dependent launch,
+                           bit 1: no CUDA graph, bit 2: multi-kernel step
+                           instead of the persistent single-kernel step */
 } lcr_options;
 
 typedef struct lcr_ctx lcr_ctx;

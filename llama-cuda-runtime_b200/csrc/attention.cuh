@@ -82,23 +82,36 @@ __device__ __forceinline__ int attn_chunk(int seq_len, int splits) {
 }
 
 // Loads 8 dims of one head from a bf16 row and applies the rotate-half RoPE
-// for this lane's dims, returning bf16-rounded values.
+// for this lane's dims with the step's precomputed cos/sin table (cs[i] =
+// cos, cs[HALF + i] = sin of float(pos) * inv_freq[i]), returning the
+// bf16-rounded values the reference stores.
 template <int D>
-__device__ __forceinline__ void rope8(const bf16* head, int lig, int pos, const float* inv_freq,
-                                      float* outv) {
+__device__ __forceinline__ void rope8(const bf16* head, int lig, const float* cs, float* outv) {
   constexpr int HALF = D / 2;
   const int d0 = lig * 8;
   float self[8], other[8];
-  unpack8(ldg16(head + d0), self);
+  unpack8(ldg_cg16(head + d0), self);
   const bool lo = d0 < HALF;
-  unpack8(ldg16(head + (lo ? d0 + HALF : d0 - HALF)), other);
+  unpack8(ldg_cg16(head + (lo ? d0 + HALF : d0 - HALF)), other);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int i = (d0 + e) % HALF;
-    float s, c;
-    sincosf(static_cast<float>(pos) * inv_freq[i], &s, &c);
+    const float c = cs[i], s = cs[HALF + i];
     const float v = lo ? (self[e] * c - other[e] * s) : (self[e] * c + other[e] * s);
     outv[e] = rbf(v);
+  }
+}
+
+// cos/sin of float(pos) * inv_freq[i] for the D/2 rotation pairs (sincosf,
+// as src/kernels/rope.cu:50, 77 evaluates them), one pair per thread.
+template <int D>
+__device__ __forceinline__ void rope_table(float* cs, int pos, const float* inv_freq) {
+  constexpr int HALF = D / 2;
+  for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+    float s, c;
+    sincosf(static_cast<float>(pos) * inv_freq[i], &s, &c);
+    cs[i] = c;
+    cs[HALF + i] = s;
   }
 }
 
@@ -129,6 +142,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   uint64_t* empty = full + STAGES;
   float* comb = reinterpret_cast<float*>(empty + STAGES);  // [warps][G][D + 2]
   __shared__ int s_last;
+  __shared__ float rope_cs[D];  // cos / sin of this step's angles
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -150,6 +164,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   const int cache_end = min(end, pos);  // positions read from the cache
   const int nblocks = cache_end > begin ? (cache_end - begin + kAttnBlock - 1) / kAttnBlock : 0;
 
+  if constexpr (FUSED) {
+    // The angles depend only on the position: one sincosf per pair per CTA,
+    // before the wait on the QKV projection.
+    rope_table<D>(rope_cs, valid ? pos : 0, a.inv_freq);
+  }
   if (tid == 0) {
     if (!valid && split == 0 && kvh == 0 && a.status) atomicOr(a.status, kStatusBadPosition);
     for (int s = 0; s < STAGES; ++s) {
@@ -185,10 +204,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
           off = static_cast<long long>(b) * a.seq_stride + kvh * a.head_stride +
                 static_cast<long long>(p0) * D;
         }
+        // Copy only positions below cache_end: the caller's cache may end
+        // inside this 16-position block.
+        const uint32_t bytes = static_cast<uint32_t>(min(kAttnBlock, cache_end - p0)) * ROWB;
         uint8_t* dst = ring + slot * 2 * KB;
-        mbar_arrive_expect_tx(&full[slot], 2 * KB);
-        bulk_g2s(dst, a.kpool + off, KB, &full[slot]);
-        bulk_g2s(dst + KB, a.vpool + off, KB, &full[slot]);
+        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+        bulk_g2s(dst, a.kpool + off, bytes, &full[slot]);
+        bulk_g2s(dst + KB, a.vpool + off, bytes, &full[slot]);
         issued = blk + 1;
       }
       // Never leave the CTA with a copy still writing its shared memory.
@@ -207,7 +229,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     for (int g = 0; g < G; ++g) {
       const int h = kvh * G + g;
       if constexpr (FUSED) {
-        rope8<D>(a.qkv + static_cast<size_t>(b) * a.qkv_stride + h * D, lig, pos, a.inv_freq, q[g]);
+        rope8<D>(a.qkv + static_cast<size_t>(b) * a.qkv_stride + h * D, lig, rope_cs, q[g]);
       } else {
         unpack8(ldg16(a.q + h * D + lig * 8), q[g]);
       }
@@ -273,8 +295,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       if (valid && pos >= begin && pos < end && grp == 0) {
         const bf16* row = a.qkv + static_cast<size_t>(b) * a.qkv_stride;
         float kf[8], vf[8];
-        rope8<D>(row + a.q_dim + kvh * D, lig, pos, a.inv_freq, kf);
-        unpack8(ldg16(row + a.q_dim + a.kv_dim + kvh * D + lig * 8), vf);
+        rope8<D>(row + a.q_dim + kvh * D, lig, rope_cs, kf);
+        unpack8(ldg_cg16(row + a.q_dim + a.kv_dim + kvh * D + lig * 8), vf);
         long long off;
         if constexpr (PAGED) {
           const int32_t* table = a.tables + static_cast<size_t>(b) * a.table_seq_stride;
@@ -291,7 +313,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         kw.z = pack_bf2(kf[4], kf[5]); kw.w = pack_bf2(kf[6], kf[7]);
         *reinterpret_cast<uint4*>(a.kpool + off + lig * 8) = kw;
         *reinterpret_cast<uint4*>(a.vpool + off + lig * 8) =
-            ldg16(row + a.q_dim + a.kv_dim + kvh * D + lig * 8);
+            ldg_cg16(row + a.q_dim + a.kv_dim + kvh * D + lig * 8);
         float sc[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {

@@ -83,9 +83,14 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                : "l"(p));
   return v;
 }
-// Plain coherent 16-byte load (data another kernel of this step wrote).
+// Plain 16-byte load.
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return *reinterpret_cast<const uint4*>(p);
+}
+// 16-byte load cached in L2 only: for activations other CTAs of the same
+// kernel may have rewritten since this SM last read them (L1 is not coherent).
+__device__ __forceinline__ uint4 ldg_cg16(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
 }
 
 // ---------------------------------------------------------------------------

@@ -32,12 +32,13 @@
 #include "dispatch.h"
 #include "gemv_dispatch.h"
 #include "lcr_b200.h"
+#include "mega_dispatch.h"
 
 using namespace lcrb;
 
 namespace {
 
-enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2 };
+enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4 };
 constexpr int kPinnedRing = 256;
 constexpr int kTimingSlots = 128;
 
@@ -88,6 +89,7 @@ struct lcr_ctx {
   cudaStream_t stream = nullptr;
   bool pdl = true;
   bool use_graph = true;
+  bool persistent = false;  // the whole step as one cooperative kernel
 
   const bf16* embed = nullptr;
   const bf16* final_norm = nullptr;
@@ -120,6 +122,9 @@ struct lcr_ctx {
   std::vector<int32_t> order;
   int max_pages = 0, pool_pages = 0, pages_mapped = 0, length = 0;
   int splits = 1;
+
+  MegaLayer* mega_layers = nullptr;  // device copy of the per-layer pointers
+  unsigned* mega_bar = nullptr;
 
   cudaGraphExec_t exec = nullptr;
   int launches = 0;
@@ -189,11 +194,60 @@ int attention_node(lcr_ctx* c, int layer) {
                      d.num_kv_heads, 1, c->stream, c->pdl);
 }
 
+int enqueue_persistent_step(lcr_ctx* c) {
+  const lcr_model_desc& d = c->d;
+  MegaArgs a = {};
+  a.layers = d.num_layers;
+  a.vocab = d.vocab_size;
+  a.num_kv = d.num_kv_heads;
+  a.max_seq = c->o.max_seq;
+  a.splits = c->splits;
+  a.eps = d.rms_norm_eps;
+  a.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
+  a.embed = c->embed;
+  a.final_norm = c->final_norm;
+  a.lm_head = c->lm_head;
+  a.L = c->mega_layers;
+  a.inv_freq = c->inv_freq;
+  a.state = c->state;
+  a.x = c->x;
+  a.xsum = c->xsum;
+  a.qkv = c->qkv;
+  a.attn = c->attn;
+  a.act = c->act;
+  a.logits = c->logits;
+  a.partials = c->partials;
+  a.attn_ctr = c->attn_ctr;
+  a.bar = c->mega_bar;
+  a.argmax_acc = c->argmax_acc;
+  a.argmax_done = c->sched;  // slot 0 of the scheduler words
+  a.history = c->history;
+  a.history_len = c->o.max_seq;
+  a.status = c->status;
+  a.kpool = c->kpool;
+  a.vpool = c->vpool;
+  if (c->o.paged) {
+    a.tables = c->tables_dev;
+    a.max_pages = c->max_pages;
+    a.pool_pages = c->pool_pages;
+    a.page_size = c->o.page_size;
+    a.page_stride = static_cast<long long>(d.num_kv_heads) * c->o.page_size * d.head_dim;
+    a.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
+  } else {
+    a.head_stride = static_cast<long long>(c->o.max_seq) * d.head_dim;
+    a.layer_stride = static_cast<long long>(d.num_kv_heads) * c->o.max_seq * d.head_dim;
+  }
+  c->launches = 1;
+  return mega_launch(a, d.hidden_size, d.num_heads * d.head_dim, d.intermediate_size, d.head_dim,
+                     d.num_heads / d.num_kv_heads, c->o.paged != 0, c->sms, c->stream);
+}
+
 // Launches one decode step on the context's stream.
 int enqueue_step(lcr_ctx* c) {
+  if (c->persistent) return enqueue_persistent_step(c);
   const lcr_model_desc& d = c->d;
   const int H = d.hidden_size, F = d.intermediate_size;
-  int slot = 0;
+  int slot = 1;  // slot 0 belongs to the persistent kernel's argmax hand-off
   c->launches = 0;
   for (int l = 0; l < d.num_layers; ++l) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
@@ -296,7 +350,7 @@ int check_status(lcr_ctx* c) {
   if (st == 0) return LCR_OK;
   LCRB_CUDA(cudaMemsetAsync(c->status, 0, sizeof st, c->stream));
   LCRB_CUDA(cudaStreamSynchronize(c->stream));
-  if (st & (kStatusTimeoutFull | kStatusTimeoutEmpty)) {
+  if (st & (kStatusTimeoutFull | kStatusTimeoutEmpty | kStatusTimeoutBarrier | kStatusAbort)) {
     return fail(LCR_ERR_TIMEOUT, "a device-side wait gave up (status 0x%x)", st);
   }
   if (st & kStatusBadToken) return fail(LCR_ERR_INVALID, "token id outside the vocabulary (status 0x%x)", st);
@@ -327,6 +381,8 @@ void release(lcr_ctx* c) {
   cudaFree(c->kpool);
   cudaFree(c->vpool);
   cudaFree(c->tables_dev);
+  cudaFree(c->mega_layers);
+  cudaFree(c->mega_bar);
   cudaFreeHost(c->pinned);
   cudaFreeHost(c->pinned_prompt);
   cudaFreeHost(c->pinned_params);
@@ -411,6 +467,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   };
   cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
 
+  const int group = d.num_heads / d.num_kv_heads;
+  c->persistent = (o.flags & kFlagNoPersistent) == 0 &&
+                  mega_supported(d.hidden_size, qd, d.intermediate_size, d.head_dim, group);
   // Split-K width: enough (kv_head, split) CTAs to cover every SM once.
   c->splits = o.attention_splits > 0 ? o.attention_splits : std::max(1, c->sms / d.num_kv_heads);
   {
@@ -419,6 +478,7 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     const int cap = d.head_dim == 64 ? attn_max_staged_splits<64, kAttnStages>(group)
                                      : attn_max_staged_splits<128, kAttnStages>(group);
     if (o.attention_splits <= 0) c->splits = std::max(1, std::min(c->splits, cap));
+    if (c->persistent) c->splits = std::max(1, std::min(c->splits, mega_max_splits(c->sms, d.num_kv_heads)));
   }
   // One scheduler slot per GEMV node of the step, plus kTimingSlots for
   // lcr_time_gemv (back-to-back launches may overlap, so none share a slot).
@@ -502,6 +562,22 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     if (st == LCR_OK) cuda(cudaMalloc(&c->vpool, elems * sizeof(bf16)), "cudaMalloc(V pool)");
     if (st == LCR_OK) cuda(cudaMemset(c->kpool, 0, elems * sizeof(bf16)), "cudaMemset(K pool)");
     if (st == LCR_OK) cuda(cudaMemset(c->vpool, 0, elems * sizeof(bf16)), "cudaMemset(V pool)");
+  }
+  if (st == LCR_OK && c->persistent) {
+    std::vector<MegaLayer> ml(static_cast<size_t>(d.num_layers));
+    for (int l = 0; l < d.num_layers; ++l) {
+      const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+      ml[static_cast<size_t>(l)] = {static_cast<const bf16*>(w.input_norm), static_cast<const bf16*>(w.qkv_proj),
+                                    static_cast<const bf16*>(w.o_proj), static_cast<const bf16*>(w.post_attention_norm),
+                                    static_cast<const bf16*>(w.gate_up_proj), static_cast<const bf16*>(w.down_proj)};
+    }
+    cuda(cudaMalloc(&c->mega_layers, ml.size() * sizeof(MegaLayer)), "cudaMalloc(layer table)");
+    if (st == LCR_OK) {
+      cuda(cudaMemcpy(c->mega_layers, ml.data(), ml.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice),
+           "upload layer table");
+    }
+    if (st == LCR_OK) cuda(cudaMalloc(&c->mega_bar, sizeof(unsigned)), "cudaMalloc(barrier)");
+    if (st == LCR_OK) cuda(cudaMemset(c->mega_bar, 0, sizeof(unsigned)), "cudaMemset(barrier)");
   }
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * kPinnedRing), "cudaMallocHost");
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned_params, sizeof(float) * 8), "cudaMallocHost");
@@ -760,7 +836,8 @@ extern "C" size_t lcr_kv_bytes_per_position(const lcr_ctx* c) {
 }
 
 extern "C" int lcr_step_launches(const lcr_ctx* c) {
-  return c ? 5 * c->d.num_layers + 1 : 0;
+  if (!c) return 0;
+  return c->persistent ? 1 : 5 * c->d.num_layers + 1;
 }
 
 extern "C" int lcr_device_status(lcr_ctx* c) {

@@ -139,14 +139,242 @@ __device__ __forceinline__ bool warp_row_owner(int lane) {
   return (lane & ((1 << (5 - m)) - 1)) == 0;
 }
 
+// Outputs [o0, o1) of the contiguous share CTA `cta` of `ctas` owns.
+__device__ __forceinline__ int gemv_share(int n_out, int cta, int ctas) {
+  return static_cast<int>(static_cast<long long>(cta) * n_out / ctas);
+}
+
+// ---------------------------------------------------------------------------
+// Building blocks, shared by the standalone kernel below and the persistent
+// decode kernel. A "ring" is STAGES shared-memory stages with a full and an
+// empty mbarrier each; `it` is the running stage sequence number, advanced
+// identically by the producer and the consumers.
+// ---------------------------------------------------------------------------
+
+// Producer: streams weight rows [o0, o1) (SWIGLU: pairs, gate and up rows) of
+// a [rows][K] matrix into the ring. Returns false if a bounded wait expired.
+template <int K, int STAGE_BYTES, int STAGES, bool SWIGLU>
+__device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                             int& it, const bf16* w, int n_out, int o0, int o1,
+                                             uint64_t policy, uint32_t* status) {
+  using G = GemvGeom<K, STAGE_BYTES>;
+  constexpr int PAIRS = G::RPS / 2;
+  constexpr int UNIT = SWIGLU ? PAIRS : G::RPS;
+  const char* wbase = reinterpret_cast<const char*>(w);
+  for (int first = o0; first < o1; first += UNIT, ++it) {
+    const int slot = it % STAGES;
+    if (it >= STAGES &&
+        !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, status, kStatusTimeoutEmpty)) {
+      return false;
+    }
+    uint8_t* dst = ring + slot * STAGE_BYTES;
+    const uint32_t bytes = static_cast<uint32_t>(min(UNIT, o1 - first)) * G::ROW_BYTES;
+    if constexpr (SWIGLU) {
+      mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+      bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
+      bulk_g2s(dst + PAIRS * G::ROW_BYTES, wbase + static_cast<size_t>(n_out + first) * G::ROW_BYTES,
+               bytes, &full[slot], policy);
+    } else {
+      mbar_arrive_expect_tx(&full[slot], bytes);
+      bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
+    }
+  }
+  return true;
+}
+
+// Waits (bounded) until every copy issued into the ring has landed, so a CTA
+// never exits with a copy still writing its shared memory. `issued` is the
+// producer's stage count; the last STAGES stages are the only ones that can
+// still be in flight.
+template <int STAGES>
+__device__ __forceinline__ void ring_drain(uint64_t* full, int issued, uint32_t* status) {
+  for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k) {
+    mbar_wait(&full[k % STAGES], (k / STAGES) & 1, status, kStatusTimeoutFull);
+  }
+}
+
+// Consumers (256 threads): the input vector into registers. NORM / EMBED_NORM
+// apply RMSNorm (sum of squares over the unrounded residual sums when given)
+// and round to bf16 as the reference stores `normed`. Uses named barrier 1.
+template <int K, int STAGE_BYTES, int PRO>
+__device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
+                                            float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8],
+                                            float* red8) {
+  using G = GemvGeom<K, STAGE_BYTES>;
+  constexpr int CPT = G::CPT, TPR = G::TPR;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int slotrow = tid / TPR, ci = tid % TPR;
+  if constexpr (PRO == PRO_PLAIN) {
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) unpack8(ldg_cg16(a.x_in + (ci + j * TPR) * 8), xr[j]);
+  } else {
+    uint4 gain[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) gain[j] = ldg16(a.norm_w + (ci + j * TPR) * 8);
+    const bf16* src = a.x_in;
+    if constexpr (PRO == PRO_EMBED_NORM) {
+      int tok = __ldcg(a.token);
+      if (tok < 0 || tok >= a.vocab) {
+        if (tid == 0 && a.status) atomicOr(a.status, kStatusBadToken);
+        tok = 0;
+      }
+      src = a.embed + static_cast<size_t>(tok) * K;
+    }
+    float xv[CPT][8], sq[CPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int col = (ci + j * TPR) * 8;
+      const uint4 raw = ldg_cg16(src + col);
+      unpack8(raw, xv[j]);
+      if (PRO == PRO_NORM && a.xsum != nullptr) {
+        const float4 s0 = __ldcg(reinterpret_cast<const float4*>(a.xsum + col));
+        const float4 s1 = __ldcg(reinterpret_cast<const float4*>(a.xsum + col + 4));
+        sq[j][0] = s0.x; sq[j][1] = s0.y; sq[j][2] = s0.z; sq[j][3] = s0.w;
+        sq[j][4] = s1.x; sq[j][5] = s1.y; sq[j][6] = s1.z; sq[j][7] = s1.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sq[j][e] = xv[j][e];
+      }
+      if (slotrow == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(sq[j][e], sq[j][e], ss);
+      }
+      if (PRO == PRO_EMBED_NORM && blockIdx.x == 0 && slotrow == 0) {
+        *reinterpret_cast<uint4*>(a.x_out + col) = raw;
+        *reinterpret_cast<float4*>(a.xsum_out + col) = make_float4(xv[j][0], xv[j][1], xv[j][2], xv[j][3]);
+        *reinterpret_cast<float4*>(a.xsum_out + col + 4) = make_float4(xv[j][4], xv[j][5], xv[j][6], xv[j][7]);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) red8[warp] = ss;
+    named_sync(1, kGemvConsumers);
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) total += red8[w];
+    named_sync(1, kGemvConsumers);  // red8 may be reused right after
+    const float scale = rsqrtf(total / static_cast<float>(K) + a.eps);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      float gf[8];
+      unpack8(gain[j], gf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xr[j][e] = rbf(__fmul_rn(__fmul_rn(xv[j][e], scale), gf[e]));
+    }
+  }
+}
+
+// Consumers (256 threads): dot products of the streamed rows [o0, o1) with
+// the register-resident x, segmented cross-warp reduction in `red`
+// (kGemvSegment * RPS * WPR floats) and the epilogue. LOGITS_ARGMAX folds the
+// packed (order key, ~index) maximum into `best`. Uses named barrier 1.
+template <int K, int STAGE_BYTES, int STAGES, int EPI>
+__device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                             int& it, const GemvArgs& a, int o0, int o1,
+                                             const float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8],
+                                             float* red, unsigned long long& best, bool& failed) {
+  using G = GemvGeom<K, STAGE_BYTES>;
+  constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR, WPR = G::WPR;
+  constexpr int PAIRS = RPS / 2;
+  constexpr int UNIT = (EPI == EPI_SWIGLU) ? PAIRS : RPS;
+  constexpr int SEG = kGemvSegment;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int slotrow = tid / TPR, ci = tid % TPR;
+  const int n_stages = (o1 - o0 + UNIT - 1) / UNIT;
+  for (int seg0 = 0; seg0 < n_stages; seg0 += SEG) {
+    const int seg1 = min(n_stages, seg0 + SEG);
+    for (int st = seg0; st < seg1; ++st, ++it) {
+      const int slot = it % STAGES;
+      if (!failed) failed = !mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
+      const uint8_t* stage = ring + slot * STAGE_BYTES;
+      float part[RPT];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        const int row = slotrow * RPT + r;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES + (ci + j * TPR) * 16);
+          acc = fmaf(bf_lo(wv.x), xr[j][0], acc);
+          acc = fmaf(bf_hi(wv.x), xr[j][1], acc);
+          acc = fmaf(bf_lo(wv.y), xr[j][2], acc);
+          acc = fmaf(bf_hi(wv.y), xr[j][3], acc);
+          acc = fmaf(bf_lo(wv.z), xr[j][4], acc);
+          acc = fmaf(bf_hi(wv.z), xr[j][5], acc);
+          acc = fmaf(bf_lo(wv.w), xr[j][6], acc);
+          acc = fmaf(bf_hi(wv.w), xr[j][7], acc);
+        }
+        part[r] = acc;
+      }
+      __syncwarp();
+      if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
+      const float wsum = warp_reduce_rows<RPT>(part, lane);
+      if (warp_row_owner<RPT>(lane)) {
+        const int row = slotrow * RPT + warp_row_of_lane<RPT>(lane);
+        red[((st - seg0) * RPS + row) * WPR + (warp % WPR)] = wsum;
+      }
+    }
+    named_sync(1, kGemvConsumers);  // the segment's partials are in shared memory
+    const int first = o0 + seg0 * UNIT;
+    const int outs = min(o1, o0 + seg1 * UNIT) - first;
+    for (int u = tid; u < outs && !failed; u += kGemvConsumers) {
+      const int st = u / UNIT, r = u % UNIT;
+      const float* rr = red + (st * RPS + r) * WPR;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) v += rr[w];
+      const int out = first + u;
+      if constexpr (EPI == EPI_STORE) {
+        a.y[out] = __ushort_as_bfloat16(f2bf(v));
+      } else if constexpr (EPI == EPI_STORE_F32) {
+        a.yf[out] = v;
+      } else if constexpr (EPI == EPI_RESID) {
+        const float s = __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)), rbf(v));
+        a.resid[out] = __ushort_as_bfloat16(f2bf(s));
+        a.resid_sum[out] = s;
+      } else if constexpr (EPI == EPI_SWIGLU) {
+        const float* ru = red + (st * RPS + r + PAIRS) * WPR;
+        float up = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPR; ++w) up += ru[w];
+        const float g = rbf(v);
+        const float silu = g / (1.0f + __expf(-g));
+        a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
+      } else if constexpr (EPI == EPI_LOGITS_ARGMAX) {
+        a.yf[out] = v;
+        const unsigned long long packed =
+            (static_cast<unsigned long long>(order_key(v)) << 32) |
+            static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(out));
+        best = best > packed ? best : packed;
+      }
+    }
+    named_sync(1, kGemvConsumers);  // the next segment may overwrite `red`
+  }
+}
+
+// Argmax hand-off after the lm_head: the CTA maximum into the global
+// accumulator, and the last CTA to finish writes the next token, the history
+// entry and the advanced position, then resets for the next step.
+__device__ __forceinline__ void argmax_finish(const GemvArgs& a, unsigned long long cta_best) {
+  atomicMax(a.argmax_acc, cta_best);
+  __threadfence();
+  const unsigned prev = atomicAdd(&a.sched[1], 1u);
+  if (prev == gridDim.x - 1) {
+    __threadfence();
+    atomicExch(&a.sched[1], 0u);
+    const unsigned long long packed = atomicExch(a.argmax_acc, 0ull);
+    const int next = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed & 0xFFFFFFFFull));
+    const int pos = __ldcg(a.state_pos);
+    *a.state_token = next;
+    if (a.history != nullptr && pos >= 0 && pos < a.history_len) a.history[pos] = next;
+    if (a.advance) *a.state_pos = pos + 1;
+  }
+}
+
 template <int K, int STAGE_BYTES, int STAGES, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const GemvArgs a) {
   using G = GemvGeom<K, STAGE_BYTES>;
-  constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR, WPR = G::WPR;
-  constexpr int PAIRS = RPS / 2;                              // SWIGLU outputs per stage
-  constexpr int UNIT = (EPI == EPI_SWIGLU) ? PAIRS : RPS;     // outputs per stage
-  constexpr int SEG = kGemvSegment;                           // stages per reduction pass
-
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -155,13 +383,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   float* red8 = reinterpret_cast<float*>(cta_best + 1);   // [8]
   float* red = red8 + 8;                                    // [SEG * RPS][WPR]
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-
-  // This CTA's contiguous share of the outputs (rows, or SWIGLU pairs).
-  const int o0 = static_cast<int>(static_cast<long long>(blockIdx.x) * a.n_out / gridDim.x);
-  const int o1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * a.n_out / gridDim.x);
-  const int n_stages = (o1 - o0 + UNIT - 1) / UNIT;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int o0 = gemv_share(a.n_out, blockIdx.x, gridDim.x);
+  const int o1 = gemv_share(a.n_out, blockIdx.x + 1, gridDim.x);
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -175,204 +399,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   pdl_launch_next();
 
   if (warp == kGemvConsumers / 32) {
-    // ---------------- producer ----------------
+    // Weights do not depend on the previous kernel: stream before the wait.
     if (lane == 0) {
-      const uint64_t policy = l2_policy_evict_first();
-      const char* wbase = reinterpret_cast<const char*>(a.w);
-      int issued = 0;
-      for (int st = 0; st < n_stages; ++st) {
-        const int slot = st % STAGES;
-        if (st >= STAGES &&
-            !mbar_wait(&empty[slot], ((st / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
-          break;
-        }
-        uint8_t* dst = ring + slot * STAGE_BYTES;
-        const int first = o0 + st * UNIT;
-        const uint32_t bytes = static_cast<uint32_t>(min(UNIT, o1 - first)) * G::ROW_BYTES;
-        if constexpr (EPI == EPI_SWIGLU) {
-          mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-          bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
-          bulk_g2s(dst + PAIRS * G::ROW_BYTES,
-                   wbase + static_cast<size_t>(a.n_out + first) * G::ROW_BYTES, bytes, &full[slot],
-                   policy);
-        } else {
-          mbar_arrive_expect_tx(&full[slot], bytes);
-          bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
-        }
-        issued = st + 1;
-      }
-      // Never leave the CTA with a copy still writing its shared memory.
-      for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k) {
-        mbar_wait(&full[k % STAGES], (k / STAGES) & 1, a.status, kStatusTimeoutFull);
-      }
+      int it = 0;
+      gemv_produce<K, STAGE_BYTES, STAGES, EPI == EPI_SWIGLU>(ring, full, empty, it, a.w, a.n_out, o0, o1,
+                                                          l2_policy_evict_first(), a.status);
+      ring_drain<STAGES>(full, it, a.status);
     }
   } else {
-    // ---------------- consumers ----------------
-    const int slotrow = tid / TPR;  // which rows of each stage this thread serves
-    const int ci = tid % TPR;       // chunk index within the row
-    float xr[CPT][8];
-
-    if constexpr (PRO == PRO_PLAIN) {
-      pdl_wait();
-#pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        unpack8(ldg16(a.x_in + (ci + j * TPR) * 8), xr[j]);
-      }
-    } else {
-      uint4 gain[CPT];
-#pragma unroll
-      for (int j = 0; j < CPT; ++j) gain[j] = ldg16(a.norm_w + (ci + j * TPR) * 8);
-      pdl_wait();
-      const bf16* src = a.x_in;
-      if constexpr (PRO == PRO_EMBED_NORM) {
-        int tok = *a.token;
-        if (tok < 0 || tok >= a.vocab) {
-          if (tid == 0 && a.status) atomicOr(a.status, kStatusBadToken);
-          tok = 0;
-        }
-        src = a.embed + static_cast<size_t>(tok) * K;
-      }
-      float xv[CPT][8], sq[CPT][8];
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        const int col = (ci + j * TPR) * 8;
-        const uint4 raw = ldg16(src + col);
-        unpack8(raw, xv[j]);
-        if (PRO == PRO_NORM && a.xsum != nullptr) {
-          const float4 s0 = *reinterpret_cast<const float4*>(a.xsum + col);
-          const float4 s1 = *reinterpret_cast<const float4*>(a.xsum + col + 4);
-          sq[j][0] = s0.x; sq[j][1] = s0.y; sq[j][2] = s0.z; sq[j][3] = s0.w;
-          sq[j][4] = s1.x; sq[j][5] = s1.y; sq[j][6] = s1.z; sq[j][7] = s1.w;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) sq[j][e] = xv[j][e];
-        }
-        if (slotrow == 0) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ss = fmaf(sq[j][e], sq[j][e], ss);
-        }
-        if (PRO == PRO_EMBED_NORM && blockIdx.x == 0 && slotrow == 0) {
-          *reinterpret_cast<uint4*>(a.x_out + col) = raw;
-          *reinterpret_cast<float4*>(a.xsum_out + col) =
-              make_float4(xv[j][0], xv[j][1], xv[j][2], xv[j][3]);
-          *reinterpret_cast<float4*>(a.xsum_out + col + 4) =
-              make_float4(xv[j][4], xv[j][5], xv[j][6], xv[j][7]);
-        }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (lane == 0) red8[warp] = ss;
-      named_sync(1, kGemvConsumers);
-      float total = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) total += red8[w];
-      const float scale = rsqrtf(total / static_cast<float>(K) + a.eps);
-#pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        float gf[8];
-        unpack8(gain[j], gf);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) xr[j][e] = rbf(__fmul_rn(__fmul_rn(xv[j][e], scale), gf[e]));
-      }
-    }
-
+    float xr[G::CPT][8];
+    pdl_wait();
+    gemv_load_x<K, STAGE_BYTES, PRO>(a, xr, red8);
+    int it = 0;
     unsigned long long best = 0ull;
     bool failed = false;
-    for (int seg0 = 0; seg0 < n_stages; seg0 += SEG) {
-      const int seg1 = min(n_stages, seg0 + SEG);
-      for (int st = seg0; st < seg1; ++st) {
-        const int slot = st % STAGES;
-        if (!failed) failed = !mbar_wait(&full[slot], (st / STAGES) & 1, a.status, kStatusTimeoutFull);
-        const uint8_t* stage = ring + slot * STAGE_BYTES;
-        float part[RPT];
-#pragma unroll
-        for (int r = 0; r < RPT; ++r) {
-          const int row = slotrow * RPT + r;
-          float acc = 0.f;
-#pragma unroll
-          for (int j = 0; j < CPT; ++j) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES +
-                                                             (ci + j * TPR) * 16);
-            acc = fmaf(bf_lo(wv.x), xr[j][0], acc);
-            acc = fmaf(bf_hi(wv.x), xr[j][1], acc);
-            acc = fmaf(bf_lo(wv.y), xr[j][2], acc);
-            acc = fmaf(bf_hi(wv.y), xr[j][3], acc);
-            acc = fmaf(bf_lo(wv.z), xr[j][4], acc);
-            acc = fmaf(bf_hi(wv.z), xr[j][5], acc);
-            acc = fmaf(bf_lo(wv.w), xr[j][6], acc);
-            acc = fmaf(bf_hi(wv.w), xr[j][7], acc);
-          }
-          part[r] = acc;
-        }
-        __syncwarp();
-        if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
-        const float wsum = warp_reduce_rows<RPT>(part, lane);
-        if (warp_row_owner<RPT>(lane)) {
-          const int row = slotrow * RPT + warp_row_of_lane<RPT>(lane);
-          red[((st - seg0) * RPS + row) * WPR + (warp % WPR)] = wsum;
-        }
-      }
-      named_sync(1, kGemvConsumers);  // the segment's partials are in shared memory
-      const int first = o0 + seg0 * UNIT;
-      const int outs = min(o1, o0 + seg1 * UNIT) - first;
-      for (int u = tid; u < outs && !failed; u += kGemvConsumers) {
-        const int st = u / UNIT, r = u % UNIT;
-        const float* rr = red + (st * RPS + r) * WPR;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < WPR; ++w) v += rr[w];
-        const int out = first + u;
-        if constexpr (EPI == EPI_STORE) {
-          a.y[out] = __ushort_as_bfloat16(f2bf(v));
-        } else if constexpr (EPI == EPI_STORE_F32) {
-          a.yf[out] = v;
-        } else if constexpr (EPI == EPI_RESID) {
-          const float s = __fadd_rn(bf2f(__bfloat16_as_ushort(a.resid[out])), rbf(v));
-          a.resid[out] = __ushort_as_bfloat16(f2bf(s));
-          a.resid_sum[out] = s;
-        } else if constexpr (EPI == EPI_SWIGLU) {
-          const float* ru = red + (st * RPS + r + PAIRS) * WPR;
-          float up = 0.f;
-#pragma unroll
-          for (int w = 0; w < WPR; ++w) up += ru[w];
-          const float g = rbf(v);
-          const float silu = g / (1.0f + __expf(-g));
-          a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
-        } else if constexpr (EPI == EPI_LOGITS_ARGMAX) {
-          a.yf[out] = v;
-          const unsigned long long packed =
-              (static_cast<unsigned long long>(order_key(v)) << 32) |
-              static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(out));
-          best = best > packed ? best : packed;
-        }
-      }
-      named_sync(1, kGemvConsumers);  // the next segment may overwrite `red`
-    }
+    gemv_consume<K, STAGE_BYTES, STAGES, EPI>(ring, full, empty, it, a, o0, o1, xr, red, best, failed);
     if constexpr (EPI == EPI_LOGITS_ARGMAX) {
       if (best != 0ull) atomicMax(cta_best, best);
     }
   }
-
   __syncthreads();
   if constexpr (EPI == EPI_LOGITS_ARGMAX) {
-    if (tid == 0) {
-      atomicMax(a.argmax_acc, *cta_best);
-      __threadfence();
-      const unsigned prev = atomicAdd(&a.sched[1], 1u);
-      if (prev == gridDim.x - 1) {
-        // Last CTA: every CTA's maximum is in the accumulator. Publish the
-        // token, advance the position, and reset for the next launch.
-        __threadfence();
-        atomicExch(&a.sched[1], 0u);
-        const unsigned long long packed = atomicExch(a.argmax_acc, 0ull);
-        const int next = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(packed & 0xFFFFFFFFull));
-        const int pos = *a.state_pos;
-        *a.state_token = next;
-        if (a.history != nullptr && pos >= 0 && pos < a.history_len) a.history[pos] = next;
-        if (a.advance) *a.state_pos = pos + 1;
-      }
-    }
+    if (tid == 0) argmax_finish(a, *cta_best);
   }
 }
 

@@ -1,0 +1,585 @@
+// The whole decode step as ONE persistent cooperative kernel.
+//
+// One CTA per SM (cooperative launch guarantees they are co-resident), 8
+// consumer warps + 1 producer warp, a 12-stage x 16 KB shared-memory ring.
+// Per layer the step has five phases, each needing every output of the one
+// before (a batch-1 step is a chain of full reductions):
+//
+//   QKV   rows of [q;k;v]: RMSNorm prologue (embedding row for layer 0)
+//   ATTN  one (KV head, split) item per CTA: RoPE, KV write, split-K
+//         online softmax over the KV pages, last-CTA merge of the splits
+//   O     rows of o_proj, residual epilogue
+//   GU    gate/up row pairs: RMSNorm prologue, SwiGLU epilogue
+//   DOWN  rows of down_proj, residual epilogue
+//
+// then the lm_head rows with the final norm and the argmax hand-off. Between
+// phases the consumers meet at a grid barrier (an arrival counter with a
+// bounded acquire spin). The producer never waits at barriers: it walks the
+// same schedule -- this CTA's rows of every matrix, and the KV blocks of its
+// attention item -- and keeps the ring full, so HBM keeps streaming the next
+// matrices while the consumers synchronise. The arithmetic per output is that
+// of the multi-kernel step (the same device functions), so the two paths
+// agree bit for bit.
+#pragma once
+
+#include "attention.cuh"
+#include "gemv.cuh"
+
+namespace lcrb {
+
+constexpr int kMegaStageBytes = 16384;
+constexpr int kMegaStages = 12;
+constexpr int kMegaThreads = kGemvConsumers + 32;
+constexpr int kMegaWarps = kGemvConsumers / 32;
+
+struct MegaLayer {
+  const bf16* input_norm;
+  const bf16* qkv;
+  const bf16* o;
+  const bf16* post_norm;
+  const bf16* gate_up;
+  const bf16* down;
+};
+
+struct MegaArgs {
+  int layers, vocab, num_kv, max_seq, splits;
+  float eps, scale_log2;
+  const bf16* embed;
+  const bf16* final_norm;
+  const bf16* lm_head;
+  const MegaLayer* L;  // device array [layers]
+  const float* inv_freq;
+  int32_t* state;      // [0] token, [1] position
+  bf16* x;
+  float* xsum;
+  bf16* qkv;
+  bf16* attn;
+  bf16* act;
+  float* logits;
+  float* partials;     // [heads][splits][2 + D]
+  unsigned* attn_ctr;  // [layers][num_kv]
+  unsigned* bar;       // grid barrier arrivals, zero at launch
+  unsigned long long* argmax_acc;
+  unsigned* argmax_done;  // [2], [1] counts finished CTAs
+  int32_t* history;
+  int history_len;
+  uint32_t* status;
+  // KV cache
+  bf16* kpool;
+  bf16* vpool;
+  const int32_t* tables;  // paged: [layers][max_pages]
+  int max_pages, pool_pages, page_size;
+  long long page_stride, head_stride, layer_stride;  // layer_stride: contiguous
+};
+
+enum : uint32_t { kStatusAbort = 1u << 8, kStatusTimeoutBarrier = 1u << 5 };
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier over the consumer threads of every CTA. Returns false (and
+// raises the abort bit so every other CTA stops waiting too) if the bounded
+// wait expired or another CTA already aborted.
+__device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, uint32_t* status,
+                                               int* s_abort) {
+  named_sync(1, kGemvConsumers);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    uint64_t start = 0;
+    for (uint32_t spin = 0;; ++spin) {
+      if (ld_acquire_u32(bar) >= target) break;
+      if ((spin & 63u) == 63u) {
+        if (__ldcg(status) & kStatusAbort) {
+          *s_abort = 1;
+          break;
+        }
+        const uint64_t now = globaltimer_ns();
+        if (start == 0) {
+          start = now;
+        } else if (now - start > kWaitLimitNs) {
+          atomicOr(status, kStatusTimeoutBarrier | kStatusAbort);
+          *s_abort = 1;
+          break;
+        }
+      }
+    }
+  }
+  named_sync(1, kGemvConsumers);
+  return *s_abort == 0;
+}
+
+// ---------------------------------------------------------------------------
+// Attention phase
+// ---------------------------------------------------------------------------
+
+template <int D>
+struct MegaAttnGeom {
+  static constexpr int LPP = D / 8;            // lanes per position
+  static constexpr int GPW = 32 / LPP;         // positions per warp per pass
+  static constexpr int P = kMegaWarps * GPW;   // positions per stage
+  static constexpr int SUB = 16;               // positions per bulk copy
+  static constexpr int ROWB = D * 2;
+  static_assert(2 * P * D * 2 <= kMegaStageBytes, "KV stage must fit a ring stage");
+  static_assert(P % SUB == 0, "stage must be whole 16-position blocks");
+};
+
+__device__ __forceinline__ int mega_attn_chunk(int seq_len, int splits, int p) {
+  const int per = (seq_len + splits - 1) / splits;
+  return (per + p - 1) / p * p;
+}
+
+// Physical element offset of (kv head, position) in layer `l` of the cache.
+template <bool PAGED>
+__device__ __forceinline__ long long kv_offset(const MegaArgs& a, int l, int kvh, int pos, int D) {
+  if constexpr (PAGED) {
+    int page = a.tables[static_cast<size_t>(l) * a.max_pages + pos / a.page_size];
+    if (page < 0 || page >= a.pool_pages) page = 0;  // an unmapped page reads page 0
+    return static_cast<long long>(page) * a.page_stride + kvh * a.head_stride +
+           static_cast<long long>(pos % a.page_size) * D;
+  } else {
+    return static_cast<long long>(l) * a.layer_stride + kvh * a.head_stride +
+           static_cast<long long>(pos) * D;
+  }
+}
+
+struct AttnItem {
+  int kvh, split, begin, end, cache_end, nblocks;
+};
+
+template <int D>
+__device__ __forceinline__ AttnItem mega_attn_item(const MegaArgs& a, int pos) {
+  using AG = MegaAttnGeom<D>;
+  AttnItem it{};
+  const int items = a.num_kv * a.splits;
+  if (static_cast<int>(blockIdx.x) >= items || pos < 0 || pos >= a.max_seq) {
+    it.nblocks = 0;
+    it.kvh = -1;
+    return it;
+  }
+  it.kvh = blockIdx.x / a.splits;
+  it.split = blockIdx.x % a.splits;
+  const int seq_len = pos + 1;
+  const int chunk = mega_attn_chunk(seq_len, a.splits, AG::P);
+  it.begin = it.split * chunk;
+  it.end = min(seq_len, it.begin + chunk);
+  it.cache_end = min(it.end, pos);
+  it.nblocks = it.cache_end > it.begin ? (it.cache_end - it.begin + AG::P - 1) / AG::P : 0;
+  return it;
+}
+
+template <int D, int STAGES, bool PAGED>
+__device__ __forceinline__ bool mega_attn_produce(uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                                  int& it, const MegaArgs& a, int l, int pos) {
+  using AG = MegaAttnGeom<D>;
+  const AttnItem item = mega_attn_item<D>(a, pos);
+  for (int blk = 0; blk < item.nblocks; ++blk, ++it) {
+    const int slot = it % STAGES;
+    if (it >= STAGES &&
+        !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
+      return false;
+    }
+    const int p0 = item.begin + blk * AG::P;
+    // Only positions below cache_end are copied, in runs that never cross a
+    // 16-position (page-aligned) block.
+    const int nvalid = min(AG::P, item.cache_end - p0);
+    uint8_t* dst = ring + slot * kMegaStageBytes;
+    mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nvalid) * 2 * AG::ROWB);
+    for (int sb = 0; sb * AG::SUB < nvalid; ++sb) {
+      const uint32_t bytes = static_cast<uint32_t>(min(AG::SUB, nvalid - sb * AG::SUB)) * AG::ROWB;
+      const long long off = kv_offset<PAGED>(a, l, item.kvh, p0 + sb * AG::SUB, D);
+      bulk_g2s(dst + sb * AG::SUB * AG::ROWB, a.kpool + off, bytes, &full[slot]);
+      bulk_g2s(dst + AG::P * AG::ROWB + sb * AG::SUB * AG::ROWB, a.vpool + off, bytes, &full[slot]);
+    }
+  }
+  return true;
+}
+
+// Consumers: one (KV head, split) item -> partials (or the output when there
+// is a single split); the last CTA of a KV head merges its splits.
+// `cs` is the step's RoPE table, `scratch` >= kMegaWarps * G * (D + 2) floats.
+template <int D, int G, int STAGES, bool PAGED>
+__device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t* full,
+                                                  uint64_t* empty, int& it, const MegaArgs& a,
+                                                  int l, int pos, const float* cs, float* scratch,
+                                                  int* s_last, bool& failed) {
+  using AG = MegaAttnGeom<D>;
+  constexpr int LPP = AG::LPP, GPW = AG::GPW, P = AG::P;
+  const AttnItem item = mega_attn_item<D>(a, pos);
+  if (item.kvh < 0) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lig = lane % LPP, grp = warp * GPW + lane / LPP;
+  const int heads = a.num_kv * G;
+  const int qd = heads * D, kvd = a.num_kv * D;
+
+  float q[G][8], acc[G][8], m[G], l_[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, q[g]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      q[g][e] *= a.scale_log2;
+      acc[g][e] = 0.f;
+    }
+    m[g] = kNegBig;
+    l_[g] = 0.f;
+  }
+
+  for (int blk = 0; blk < item.nblocks; ++blk, ++it) {
+    const int slot = it % STAGES;
+    if (!failed) failed = !mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
+    const uint8_t* kst = ring + slot * kMegaStageBytes;
+    const uint8_t* vst = kst + P * AG::ROWB;
+    const bool live = !failed && item.begin + blk * P + grp < item.cache_end;
+    float kf[8], vf[8];
+    unpack8(*reinterpret_cast<const uint4*>(kst + grp * AG::ROWB + lig * 16), kf);
+    unpack8(*reinterpret_cast<const uint4*>(vst + grp * AG::ROWB + lig * 16), vf);
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[e], s);
+      sc[g] = s;
+    }
+#pragma unroll
+    for (int off = LPP / 2; off >= 1; off >>= 1) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], off, LPP);
+    }
+    if (live) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float mn = fmaxf(m[g], sc[g]);
+        const float alpha = ex2_approx(m[g] - mn);
+        const float p = ex2_approx(sc[g] - mn);
+        l_[g] = l_[g] * alpha + p;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * alpha);
+        m[g] = mn;
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
+  }
+
+  // The new position (this step's token): rotate K, store K and V, attend.
+  if (pos >= item.begin && pos < item.end && grp == 0) {
+    float kf[8], vf[8];
+    rope8<D>(a.qkv + qd + item.kvh * D, lig, cs, kf);
+    const uint4 vraw = ldg_cg16(a.qkv + qd + kvd + item.kvh * D + lig * 8);
+    unpack8(vraw, vf);
+    const long long off = kv_offset<PAGED>(a, l, item.kvh, pos, D);
+    uint4 kw;
+    kw.x = pack_bf2(kf[0], kf[1]); kw.y = pack_bf2(kf[2], kf[3]);
+    kw.z = pack_bf2(kf[4], kf[5]); kw.w = pack_bf2(kf[6], kf[7]);
+    *reinterpret_cast<uint4*>(a.kpool + off + lig * 8) = kw;
+    *reinterpret_cast<uint4*>(a.vpool + off + lig * 8) = vraw;
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[e], s);
+      sc[g] = s;
+    }
+#pragma unroll
+    for (int off2 = LPP / 2; off2 >= 1; off2 >>= 1) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu >> (32 - LPP), sc[g], off2, LPP);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mn = fmaxf(m[g], sc[g]);
+      const float alpha = ex2_approx(m[g] - mn);
+      const float p = ex2_approx(sc[g] - mn);
+      l_[g] = l_[g] * alpha + p;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * alpha);
+      m[g] = mn;
+    }
+  }
+
+  // Groups of a warp hold the same dims for other positions: combine them.
+#pragma unroll
+  for (int off = LPP; off < 32; off <<= 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float om = __shfl_xor_sync(0xffffffffu, m[g], off);
+      const float ol = __shfl_xor_sync(0xffffffffu, l_[g], off);
+      float oacc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) oacc[e] = __shfl_xor_sync(0xffffffffu, acc[g][e], off);
+      softmax_merge<G>(m[g], l_[g], acc, g, om, ol, oacc);
+    }
+  }
+  if (lane < LPP) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float* c = scratch + (warp * G + g) * (D + 2);
+      if (lane == 0) {
+        c[0] = m[g];
+        c[1] = l_[g];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) c[2 + lane * 8 + e] = acc[g][e];
+    }
+  }
+  named_sync(1, kGemvConsumers);
+  float* part_base = a.partials + (static_cast<size_t>(item.kvh) * G) * a.splits * (2 + D);
+  for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
+    const int g = idx / D, d = idx % D;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < kMegaWarps; ++w) M = fmaxf(M, scratch[(w * G + g) * (D + 2)]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMegaWarps; ++w) {
+      const float* c = scratch + (w * G + g) * (D + 2);
+      const float s = ex2_approx(c[0] - M);
+      L += c[1] * s;
+      A += c[2 + d] * s;
+    }
+    if (a.splits == 1) {
+      a.attn[(item.kvh * G + g) * D + d] = __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
+    } else {
+      float* slotp = part_base + (g * a.splits + item.split) * (2 + D);
+      if (d == 0) {
+        slotp[0] = M;
+        slotp[1] = L;
+      }
+      slotp[2 + d] = A;
+      __threadfence();
+    }
+  }
+  if (a.splits == 1) return;
+  named_sync(1, kGemvConsumers);
+  if (tid == 0) {
+    unsigned* ctr = a.attn_ctr + l * a.num_kv + item.kvh;
+    const unsigned prev = atomicAdd(ctr, 1u);
+    *s_last = prev == static_cast<unsigned>(a.splits) - 1;
+    if (*s_last) {
+      __threadfence();
+      *ctr = 0u;
+    }
+  }
+  named_sync(1, kGemvConsumers);
+  if (!*s_last) return;
+  // Merge: per-split (m, l) and weights in shared memory, acc straight from L2.
+  const int S = a.splits;
+  float* wts = scratch;  // [G][S] weights, then [G] totals
+  for (int i = tid; i < G * S; i += kGemvConsumers) wts[i] = __ldcg(part_base + i * (2 + D));
+  named_sync(1, kGemvConsumers);
+  if (tid < G) {
+    float M = kNegBig;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, wts[tid * S + s]);
+    float L = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float w = ex2_approx(wts[tid * S + s] - M);
+      L += __ldcg(part_base + (tid * S + s) * (2 + D) + 1) * w;
+      wts[tid * S + s] = w;
+    }
+    wts[G * S + tid] = L;
+  }
+  named_sync(1, kGemvConsumers);
+  for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
+    const int g = idx / D, d = idx % D;
+    float A = 0.f;
+#pragma unroll 6
+    for (int s = 0; s < S; ++s) A += wts[g * S + s] * __ldcg(part_base + (g * S + s) * (2 + D) + 2 + d);
+    const float L = wts[G * S + g];
+    a.attn[(item.kvh * G + g) * D + d] = __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+
+template <int H, int QD, int F, int D, int G, bool PAGED>
+struct MegaShape {
+  static constexpr int RED_FLOATS = 2048 + 512;  // >= GEMV segments, attention scratch
+  static_assert(kGemvSegment * GemvGeom<H, kMegaStageBytes>::RPS * GemvGeom<H, kMegaStageBytes>::WPR <= RED_FLOATS, "red");
+  static_assert(kGemvSegment * GemvGeom<F, kMegaStageBytes>::RPS * GemvGeom<F, kMegaStageBytes>::WPR <= RED_FLOATS, "red");
+  static_assert(kMegaWarps * G * (D + 2) <= RED_FLOATS, "attention scratch");
+  static constexpr size_t SMEM = static_cast<size_t>(kMegaStages) * kMegaStageBytes +
+                                 2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 + 64;
+};
+
+template <int H, int QD, int F, int D, int G, bool PAGED>
+__global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const MegaArgs a) {
+  using Shape = MegaShape<H, QD, F, D, G, PAGED>;
+  constexpr int STAGES = kMegaStages;
+  constexpr int SB = kMegaStageBytes;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * SB);
+  uint64_t* empty = full + STAGES;
+  unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
+  int* s_flags = reinterpret_cast<int*>(cta_best + 1);  // [0] abort, [1] last-CTA
+  float* red8 = reinterpret_cast<float*>(s_flags + 4);
+  float* red = red8 + 8;
+  float* cs = red + Shape::RED_FLOATS;  // RoPE cos/sin [D]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pos = __ldcg(a.state + 1);
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kMegaWarps);
+    }
+    *cta_best = 0ull;
+    s_flags[0] = 0;
+    s_flags[1] = 0;
+    mbar_fence_init();
+    if (blockIdx.x == 0 && (pos < 0 || pos >= a.max_seq)) atomicOr(a.status, kStatusBadPosition);
+  }
+  rope_table<D>(cs, (pos >= 0 && pos < a.max_seq) ? pos : 0, a.inv_freq);
+  __syncthreads();
+
+  const int ctas = gridDim.x;
+  if (warp == kMegaWarps) {
+    // ---------------- producer: this CTA's share of every matrix, in order.
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      int it = 0;
+      bool ok = true;
+      for (int l = 0; l < a.layers && ok; ++l) {
+        const MegaLayer& w = a.L[l];
+        const int nqkv = QD + 2 * (D * a.num_kv);
+        ok = ok && gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, w.qkv, nqkv,
+                                                     gemv_share(nqkv, blockIdx.x, ctas),
+                                                     gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status);
+        ok = ok && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
+        ok = ok && gemv_produce<QD, SB, STAGES, false>(ring, full, empty, it, w.o, H,
+                                                      gemv_share(H, blockIdx.x, ctas),
+                                                      gemv_share(H, blockIdx.x + 1, ctas), policy, a.status);
+        ok = ok && gemv_produce<H, SB, STAGES, true>(ring, full, empty, it, w.gate_up, F,
+                                                    gemv_share(F, blockIdx.x, ctas),
+                                                    gemv_share(F, blockIdx.x + 1, ctas), policy, a.status);
+        ok = ok && gemv_produce<F, SB, STAGES, false>(ring, full, empty, it, w.down, H,
+                                                     gemv_share(H, blockIdx.x, ctas),
+                                                     gemv_share(H, blockIdx.x + 1, ctas), policy, a.status);
+      }
+      if (ok) {
+        gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, a.lm_head, a.vocab,
+                                          gemv_share(a.vocab, blockIdx.x, ctas),
+                                          gemv_share(a.vocab, blockIdx.x + 1, ctas), policy, a.status);
+      }
+      ring_drain<STAGES>(full, it, a.status);
+    }
+  } else {
+    // ---------------- consumers
+    int it = 0;
+    bool failed = false;
+    unsigned nbar = 0;
+    unsigned long long best = 0ull;
+    auto sync = [&]() -> bool {
+      ++nbar;
+      if (failed) atomicOr(a.status, kStatusAbort);
+      return mega_grid_sync(a.bar, nbar * static_cast<unsigned>(ctas), a.status, &s_flags[0]) && !failed;
+    };
+    bool run = true;
+    for (int l = 0; l < a.layers && run; ++l) {
+      const MegaLayer& w = a.L[l];
+      const int nqkv = QD + 2 * (D * a.num_kv);
+      {  // QKV
+        GemvArgs g = {};
+        g.status = a.status;
+        g.eps = a.eps;
+        g.norm_w = w.input_norm;
+        g.y = a.qkv;
+        float xr[GemvGeom<H, SB>::CPT][8];
+        if (l == 0) {
+          g.embed = a.embed;
+          g.token = a.state;
+          g.vocab = a.vocab;
+          g.x_out = a.x;
+          g.xsum_out = a.xsum;
+          gemv_load_x<H, SB, PRO_EMBED_NORM>(g, xr, red8);
+        } else {
+          g.x_in = a.x;
+          g.xsum = a.xsum;
+          gemv_load_x<H, SB, PRO_NORM>(g, xr, red8);
+        }
+        gemv_consume<H, SB, STAGES, EPI_STORE>(ring, full, empty, it, g, gemv_share(nqkv, blockIdx.x, ctas),
+                                               gemv_share(nqkv, blockIdx.x + 1, ctas), xr, red, best, failed);
+      }
+      if (!(run = sync())) break;
+      mega_attn_consume<D, G, STAGES, PAGED>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed);
+      if (!(run = sync())) break;
+      {  // O
+        GemvArgs g = {};
+        g.status = a.status;
+        g.x_in = a.attn;
+        g.resid = a.x;
+        g.resid_sum = a.xsum;
+        float xr[GemvGeom<QD, SB>::CPT][8];
+        gemv_load_x<QD, SB, PRO_PLAIN>(g, xr, red8);
+        gemv_consume<QD, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
+                                                gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
+      }
+      if (!(run = sync())) break;
+      {  // GU
+        GemvArgs g = {};
+        g.status = a.status;
+        g.eps = a.eps;
+        g.x_in = a.x;
+        g.xsum = a.xsum;
+        g.norm_w = w.post_norm;
+        g.y = a.act;
+        float xr[GemvGeom<H, SB>::CPT][8];
+        gemv_load_x<H, SB, PRO_NORM>(g, xr, red8);
+        gemv_consume<H, SB, STAGES, EPI_SWIGLU>(ring, full, empty, it, g, gemv_share(F, blockIdx.x, ctas),
+                                                gemv_share(F, blockIdx.x + 1, ctas), xr, red, best, failed);
+      }
+      if (!(run = sync())) break;
+      {  // DOWN
+        GemvArgs g = {};
+        g.status = a.status;
+        g.x_in = a.act;
+        g.resid = a.x;
+        g.resid_sum = a.xsum;
+        float xr[GemvGeom<F, SB>::CPT][8];
+        gemv_load_x<F, SB, PRO_PLAIN>(g, xr, red8);
+        gemv_consume<F, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
+                                               gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
+      }
+      if (!(run = sync())) break;
+    }
+    if (run) {  // lm_head
+      GemvArgs g = {};
+      g.status = a.status;
+      g.eps = a.eps;
+      g.x_in = a.x;
+      g.xsum = a.xsum;
+      g.norm_w = a.final_norm;
+      g.yf = a.logits;
+      float xr[GemvGeom<H, SB>::CPT][8];
+      gemv_load_x<H, SB, PRO_NORM>(g, xr, red8);
+      gemv_consume<H, SB, STAGES, EPI_LOGITS_ARGMAX>(ring, full, empty, it, g,
+                                                     gemv_share(a.vocab, blockIdx.x, ctas),
+                                                     gemv_share(a.vocab, blockIdx.x + 1, ctas), xr, red,
+                                                     best, failed);
+      if (best != 0ull) atomicMax(cta_best, best);
+    }
+    if (failed) atomicOr(a.status, kStatusAbort);
+  }
+  __syncthreads();
+  if (tid == 0 && !(__ldcg(a.status) & kStatusAbort)) {
+    GemvArgs g = {};
+    g.argmax_acc = a.argmax_acc;
+    g.sched = a.argmax_done;
+    g.state_token = a.state;
+    g.state_pos = a.state + 1;
+    g.history = a.history;
+    g.history_len = a.history_len;
+    g.advance = 1;
+    argmax_finish(g, *cta_best);
+  }
+}
+
+}  // namespace lcrb

@@ -26,6 +26,7 @@ STATUS_NAMES = {0: "LCR_OK", 1: "LCR_ERR_INVALID", 2: "LCR_ERR_SHAPE", 3: "LCR_E
                 4: "LCR_ERR_TIMEOUT", 5: "LCR_ERR_POOL", 6: "LCR_ERR_STATE", 7: "LCR_ERR_NO_DEVICE"}
 FLAG_NO_PDL = 1
 FLAG_NO_GRAPH = 2
+FLAG_NO_PERSISTENT = 4
 
 
 class LcrError(RuntimeError):
