@@ -187,7 +187,8 @@ typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
   int gemv_ctas;        /* CTAs per streaming GEMV; 0 = one per SM */
   int flags;            /* bit 0: no programmatic dependent launch,
                            bit 1: no CUDA graph, bit 2: multi-kernel step
-                           instead of the persistent single-kernel step */
+                           instead of the persistent single-kernel step,
+                           bit 3: record per-phase timestamps (trace) */
 } lcr_options;
 
 typedef struct lcr_ctx lcr_ctx;
@@ -261,6 +262,12 @@ LCR_API int lcr_device_status(lcr_ctx* ctx);
  * back-to-back launches of one streaming GEMV of the step (matrix 0 qkv,
  * 1 o_proj, 2 gate_up, 3 down, 4 lm_head; reps <= 128), in ms per launch. */
 LCR_API int lcr_time_steps(lcr_ctx* ctx, int steps, float* ms);
+/* With flags bit 3 (trace) on a persistent-step context: copies the last
+ * step's per-CTA phase timestamps (globaltimer ns; per CTA 512 slots: [0]
+ * consumers start, [2k+1]/[2k+2] arrival at / departure from grid barrier k,
+ * [255] consumers end, [256 + p] producer starting phase p); *count gets
+ * the number of values copied. */
+LCR_API int lcr_copy_trace(lcr_ctx* ctx, unsigned long long* host, int capacity, int* count);
 LCR_API int lcr_time_gemv(lcr_ctx* ctx, int matrix, int layer, int reps, float* ms);
 
 #ifdef __cplusplus

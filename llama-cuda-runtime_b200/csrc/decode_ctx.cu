@@ -38,7 +38,7 @@ using namespace lcrb;
 
 namespace {
 
-enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4 };
+enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8 };
 constexpr int kPinnedRing = 256;
 constexpr int kTimingSlots = 128;
 
@@ -125,6 +125,7 @@ struct lcr_ctx {
 
   MegaLayer* mega_layers = nullptr;  // device copy of the per-layer pointers
   unsigned* mega_bar = nullptr;
+  unsigned long long* trace = nullptr;  // kFlagTrace: per-CTA phase timestamps
 
   cudaGraphExec_t exec = nullptr;
   int launches = 0;
@@ -226,6 +227,7 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.status = c->status;
   a.kpool = c->kpool;
   a.vpool = c->vpool;
+  a.trace = c->trace;
   if (c->o.paged) {
     a.tables = c->tables_dev;
     a.max_pages = c->max_pages;
@@ -383,6 +385,7 @@ void release(lcr_ctx* c) {
   cudaFree(c->tables_dev);
   cudaFree(c->mega_layers);
   cudaFree(c->mega_bar);
+  cudaFree(c->trace);
   cudaFreeHost(c->pinned);
   cudaFreeHost(c->pinned_prompt);
   cudaFreeHost(c->pinned_params);
@@ -578,6 +581,11 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     }
     if (st == LCR_OK) cuda(cudaMalloc(&c->mega_bar, sizeof(unsigned)), "cudaMalloc(barrier)");
     if (st == LCR_OK) cuda(cudaMemset(c->mega_bar, 0, sizeof(unsigned)), "cudaMemset(barrier)");
+    if (st == LCR_OK && (o.flags & kFlagTrace)) {
+      const size_t n = static_cast<size_t>(c->sms) * kMegaTraceEvents;
+      cuda(cudaMalloc(&c->trace, n * sizeof(unsigned long long)), "cudaMalloc(trace)");
+      if (st == LCR_OK) cuda(cudaMemset(c->trace, 0, n * sizeof(unsigned long long)), "cudaMemset(trace)");
+    }
   }
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * kPinnedRing), "cudaMallocHost");
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned_params, sizeof(float) * 8), "cudaMallocHost");
@@ -917,4 +925,16 @@ extern "C" int lcr_time_gemv(lcr_ctx* c, int matrix, int layer, int reps, float*
   if (st != LCR_OK) return st;
   *ms = t / reps;
   return check_status(c);
+}
+
+extern "C" int lcr_copy_trace(lcr_ctx* c, unsigned long long* host, int capacity, int* count) {
+  LCRB_REQUIRE(c && host && count, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(c->trace != nullptr, LCR_ERR_STATE,
+               "tracing is off (create the context with flags bit 3 on the persistent step)");
+  const int n = std::min(capacity, c->sms * kMegaTraceEvents);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  LCRB_CUDA(cudaMemcpy(host, c->trace, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost));
+  *count = n;
+  return LCR_OK;
 }

@@ -70,7 +70,14 @@ struct MegaArgs {
   const int32_t* tables;  // paged: [layers][max_pages]
   int max_pages, pool_pages, page_size;
   long long page_stride, head_stride, layer_stride;  // layer_stride: contiguous
+  // Optional phase trace (globaltimer ns), per CTA kMegaTraceEvents slots:
+  // [0] consumers start, [1 + 2k] arrival at barrier k, [2 + 2k] departure,
+  // [kMegaTraceProducer + p] producer starting phase p.
+  unsigned long long* trace;
 };
+
+constexpr int kMegaTraceEvents = 512;
+constexpr int kMegaTraceProducer = 256;
 
 enum : uint32_t { kStatusAbort = 1u << 8, kStatusTimeoutBarrier = 1u << 5 };
 
@@ -84,9 +91,10 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 // raises the abort bit so every other CTA stops waiting too) if the bounded
 // wait expired or another CTA already aborted.
 __device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, uint32_t* status,
-                                               int* s_abort) {
+                                               int* s_abort, unsigned long long* trace = nullptr) {
   named_sync(1, kGemvConsumers);
   if (threadIdx.x == 0) {
+    if (trace) trace[0] = globaltimer_ns();
     __threadfence();
     atomicAdd(bar, 1u);
     uint64_t start = 0;
@@ -107,6 +115,7 @@ __device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, u
         }
       }
     }
+    if (trace) trace[1] = globaltimer_ns();
   }
   named_sync(1, kGemvConsumers);
   return *s_abort == 0;
@@ -447,24 +456,32 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       const uint64_t policy = l2_policy_evict_first();
       int it = 0;
       bool ok = true;
+      unsigned long long* ptrace = a.trace ? a.trace + blockIdx.x * kMegaTraceEvents + kMegaTraceProducer : nullptr;
+      int phase = 0;
+      auto mark = [&]() {
+        if (ptrace && phase < kMegaTraceEvents - kMegaTraceProducer) ptrace[phase] = globaltimer_ns();
+        ++phase;
+        return true;
+      };
       for (int l = 0; l < a.layers && ok; ++l) {
         const MegaLayer& w = a.L[l];
         const int nqkv = QD + 2 * (D * a.num_kv);
-        ok = ok && gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, w.qkv, nqkv,
+        ok = ok && mark() && gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, w.qkv, nqkv,
                                                      gemv_share(nqkv, blockIdx.x, ctas),
                                                      gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status);
-        ok = ok && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
-        ok = ok && gemv_produce<QD, SB, STAGES, false>(ring, full, empty, it, w.o, H,
+        ok = ok && mark() && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
+        ok = ok && mark() && gemv_produce<QD, SB, STAGES, false>(ring, full, empty, it, w.o, H,
                                                       gemv_share(H, blockIdx.x, ctas),
                                                       gemv_share(H, blockIdx.x + 1, ctas), policy, a.status);
-        ok = ok && gemv_produce<H, SB, STAGES, true>(ring, full, empty, it, w.gate_up, F,
+        ok = ok && mark() && gemv_produce<H, SB, STAGES, true>(ring, full, empty, it, w.gate_up, F,
                                                     gemv_share(F, blockIdx.x, ctas),
                                                     gemv_share(F, blockIdx.x + 1, ctas), policy, a.status);
-        ok = ok && gemv_produce<F, SB, STAGES, false>(ring, full, empty, it, w.down, H,
+        ok = ok && mark() && gemv_produce<F, SB, STAGES, false>(ring, full, empty, it, w.down, H,
                                                      gemv_share(H, blockIdx.x, ctas),
                                                      gemv_share(H, blockIdx.x + 1, ctas), policy, a.status);
       }
       if (ok) {
+        mark();
         gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, a.lm_head, a.vocab,
                                           gemv_share(a.vocab, blockIdx.x, ctas),
                                           gemv_share(a.vocab, blockIdx.x + 1, ctas), policy, a.status);
@@ -477,10 +494,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     bool failed = false;
     unsigned nbar = 0;
     unsigned long long best = 0ull;
+    unsigned long long* ctrace = a.trace ? a.trace + blockIdx.x * kMegaTraceEvents : nullptr;
+    if (ctrace && tid == 0) ctrace[0] = globaltimer_ns();
     auto sync = [&]() -> bool {
       ++nbar;
       if (failed) atomicOr(a.status, kStatusAbort);
-      return mega_grid_sync(a.bar, nbar * static_cast<unsigned>(ctas), a.status, &s_flags[0]) && !failed;
+      unsigned long long* t = (ctrace && 2 * nbar < kMegaTraceProducer) ? ctrace + 2 * nbar - 1 : nullptr;
+      return mega_grid_sync(a.bar, nbar * static_cast<unsigned>(ctas), a.status, &s_flags[0], t) && !failed;
     };
     bool run = true;
     for (int l = 0; l < a.layers && run; ++l) {
@@ -565,6 +585,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
                                                      gemv_share(a.vocab, blockIdx.x + 1, ctas), xr, red,
                                                      best, failed);
       if (best != 0ull) atomicMax(cta_best, best);
+      if (ctrace && tid == 0) ctrace[kMegaTraceProducer - 1] = globaltimer_ns();
     }
     if (failed) atomicOr(a.status, kStatusAbort);
   }

@@ -24,6 +24,34 @@ from . import runtime as rt
 MODELS = {"1b": ck.LLAMA_3_2_1B, "tiny": ck.TINY}
 
 
+PHASES = ("qkv", "attn", "o", "gate_up", "down")
+
+
+def print_trace(t: np.ndarray, layers: int) -> None:
+    """Phase timeline of one persistent decode step: per phase, the consumers'
+    working time (previous barrier departure -> next barrier arrival) and the
+    barrier wait, averaged over layers (mean / max over CTAs, microseconds)."""
+    t = t.astype(np.int64)
+    t0 = t[:, 0].min()
+    nbar = 5 * layers
+    arrive = t[:, 1:2 * nbar:2]
+    depart = t[:, 2:2 * nbar + 1:2]
+    start = np.concatenate([t[:, :1], depart[:, :-1]], axis=1)
+    work = (arrive - start) / 1e3
+    wait = (depart - arrive) / 1e3
+    prod = t[:, 256:256 + nbar + 1]
+    print(f"{'phase':8s} {'work mean':>10s} {'work max':>9s} {'wait mean':>10s} {'producer lead':>14s}  (us)")
+    for k, name in enumerate(PHASES):
+        cols = list(range(k, nbar, 5))
+        lead = (start[:, cols] - prod[:, cols]) / 1e3  # >0: producer started this phase earlier
+        print(f"{name:8s} {work[:, cols].mean():10.2f} {work[:, cols].max(axis=0).mean():9.2f} "
+              f"{wait[:, cols].mean():10.2f} {lead.mean():14.2f}")
+    lm = (t[:, 255] - depart[:, -1]) / 1e3
+    total = (t[:, 255].max() - t0) / 1e3
+    print(f"lm_head  {lm.mean():10.2f} {lm.max():9.2f}")
+    print(f"step (consumers start -> last CTA done): {total:.1f} us")
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="lcr_b200.run")
     ap.add_argument("--model", default="1b", choices=sorted(MODELS))
@@ -43,6 +71,8 @@ def main(argv=None) -> int:
     ap.add_argument("--peak-bandwidth", type=float, default=8000.0, help="GB/s")
     ap.add_argument("--bench", action="store_true")
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--trace", action="store_true",
+                    help="per-phase timeline of the last decode step (persistent kernel)")
     args = ap.parse_args(argv)
 
     geom = MODELS[args.model]
@@ -56,7 +86,8 @@ def main(argv=None) -> int:
     t0 = time.perf_counter()
     m = rt.Model(block, device=args.device, max_seq=max_seq, paged=args.paged,
                  page_size=args.page_size, attention_splits=args.splits,
-                 page_order_seed=args.page_order_seed)
+                 page_order_seed=args.page_order_seed,
+                 flags=rt.FLAG_TRACE if args.trace else 0)
     load_ms = (time.perf_counter() - t0) * 1000
 
     t0 = time.perf_counter()
@@ -95,6 +126,8 @@ def main(argv=None) -> int:
     }
     report["bandwidth_utilization"] = (report["achieved_bandwidth_bytes_per_second"]
                                        / report["peak_bandwidth_bytes_per_second"])
+    if args.trace:
+        print_trace(m.trace(), geom.num_layers)
     if args.json:
         print(json.dumps(report))
     elif args.bench:

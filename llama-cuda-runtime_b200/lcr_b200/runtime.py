@@ -27,6 +27,7 @@ STATUS_NAMES = {0: "LCR_OK", 1: "LCR_ERR_INVALID", 2: "LCR_ERR_SHAPE", 3: "LCR_E
 FLAG_NO_PDL = 1
 FLAG_NO_GRAPH = 2
 FLAG_NO_PERSISTENT = 4
+FLAG_TRACE = 8
 
 
 class LcrError(RuntimeError):
@@ -118,6 +119,7 @@ _SIGS = {
     "lcr_device_status": (_I, [_V]),
     "lcr_time_steps": (_I, [_V, _I, ctypes.POINTER(_F)]),
     "lcr_time_gemv": (_I, [_V, _I, _I, _I, ctypes.POINTER(_F)]),
+    "lcr_copy_trace": (_I, [_V, _V, _I, ctypes.POINTER(_I)]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -307,6 +309,14 @@ class Model:
         ms = ctypes.c_float()
         check(lib().lcr_time_steps(self.ctx, int(steps), ctypes.byref(ms)))
         return ms.value
+
+    def trace(self) -> np.ndarray:
+        """Per-CTA phase timestamps of the last step ([ctas][512] ns)."""
+        n = 1024 * 512
+        buf = np.zeros(n, dtype=np.uint64)
+        got = ctypes.c_int()
+        check(lib().lcr_copy_trace(self.ctx, buf.ctypes.data, n, ctypes.byref(got)))
+        return buf[:got.value].reshape(-1, 512)
 
     def time_gemv(self, matrix: int, layer: int = 0, reps: int = 20) -> float:
         ms = ctypes.c_float()
