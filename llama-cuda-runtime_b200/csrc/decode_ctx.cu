@@ -24,6 +24,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -126,6 +127,7 @@ struct lcr_ctx {
   MegaLayer* mega_layers = nullptr;  // device copy of the per-layer pointers
   unsigned* mega_bar = nullptr;
   unsigned long long* trace = nullptr;  // kFlagTrace: per-CTA phase timestamps
+  unsigned long long prefetch_bytes = 0;  // persistent step: L2 prefetch lead per CTA
 
   cudaGraphExec_t exec = nullptr;
   int launches = 0;
@@ -228,6 +230,7 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.kpool = c->kpool;
   a.vpool = c->vpool;
   a.trace = c->trace;
+  a.prefetch_bytes = c->prefetch_bytes;
   if (c->o.paged) {
     a.tables = c->tables_dev;
     a.max_pages = c->max_pages;
@@ -471,6 +474,13 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
 
   const int group = d.num_heads / d.num_kv_heads;
+  // LCR_PREFETCH_KIB: the persistent step's L2 prefetch lead per CTA, a tuning
+  // knob for measurements (default below).
+  if (const char* env = std::getenv("LCR_PREFETCH_KIB")) {
+    c->prefetch_bytes = static_cast<unsigned long long>(std::max(0, std::atoi(env))) << 10;
+  } else {
+    c->prefetch_bytes = 0;
+  }
   c->persistent = (o.flags & kFlagNoPersistent) == 0 &&
                   mega_supported(d.hidden_size, qd, d.intermediate_size, d.head_dim, group);
   // Split-K width: enough (kv_head, split) CTAs to cover every SM once.
@@ -481,7 +491,10 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     const int cap = d.head_dim == 64 ? attn_max_staged_splits<64, kAttnStages>(group)
                                      : attn_max_staged_splits<128, kAttnStages>(group);
     if (o.attention_splits <= 0) c->splits = std::max(1, std::min(c->splits, cap));
-    if (c->persistent) c->splits = std::max(1, std::min(c->splits, mega_max_splits(c->sms, d.num_kv_heads)));
+    if (c->persistent) {
+      c->splits = std::max(1, std::min({c->splits, mega_max_splits(c->sms, d.num_kv_heads),
+                                        kMegaMaxMergeSplits}));
+    }
   }
   // One scheduler slot per GEMV node of the step, plus kTimingSlots for
   // lcr_time_gemv (back-to-back launches may overlap, so none share a slot).
@@ -500,7 +513,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   const size_t o_attn = carve(sizeof(bf16) * qd);
   const size_t o_act = carve(sizeof(bf16) * d.intermediate_size);
   const size_t o_logits = carve(sizeof(float) * d.vocab_size);
-  const size_t o_part = carve(sizeof(float) * d.num_heads * c->splits * (2 + d.head_dim));
+  // Split partial records: (2 + D) floats in the multi-kernel step, (D + 4) in
+  // the persistent one.
+  const size_t o_part = carve(sizeof(float) * d.num_heads * c->splits * (4 + d.head_dim));
   const size_t o_actr = carve(sizeof(unsigned) * d.num_layers * d.num_kv_heads);
   const size_t o_sched = carve(sizeof(unsigned) * 2 * c->sched_slots);
   const size_t o_amax = carve(sizeof(unsigned long long));

@@ -151,17 +151,26 @@ __device__ __forceinline__ int gemv_share(int n_out, int cta, int ctas) {
 // identically by the producer and the consumers.
 // ---------------------------------------------------------------------------
 
+// Something the producer can do while it would otherwise block on a full
+// ring (the persistent kernel's L2 prefetch window); `bytes` is the weight
+// volume issued into the ring so far.
+struct NoPrefetch {
+  __device__ __forceinline__ void top_up(unsigned long long) {}
+};
+
 // Producer: streams weight rows [o0, o1) (SWIGLU: pairs, gate and up rows) of
 // a [rows][K] matrix into the ring. Returns false if a bounded wait expired.
-template <int K, int STAGE_BYTES, int STAGES, bool SWIGLU>
+template <int K, int STAGE_BYTES, int STAGES, bool SWIGLU, class PF = NoPrefetch>
 __device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint64_t* empty,
                                              int& it, const bf16* w, int n_out, int o0, int o1,
-                                             uint64_t policy, uint32_t* status) {
+                                             uint64_t policy, uint32_t* status,
+                                             PF* pf = nullptr, unsigned long long* issued = nullptr) {
   using G = GemvGeom<K, STAGE_BYTES>;
   constexpr int PAIRS = G::RPS / 2;
   constexpr int UNIT = SWIGLU ? PAIRS : G::RPS;
   const char* wbase = reinterpret_cast<const char*>(w);
   for (int first = o0; first < o1; first += UNIT, ++it) {
+    if (pf) pf->top_up(*issued);
     const int slot = it % STAGES;
     if (it >= STAGES &&
         !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, status, kStatusTimeoutEmpty)) {
@@ -178,6 +187,7 @@ __device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint
       mbar_arrive_expect_tx(&full[slot], bytes);
       bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
     }
+    if (issued) *issued += (SWIGLU ? 2ull : 1ull) * bytes;
   }
   return true;
 }

@@ -70,6 +70,7 @@ struct MegaArgs {
   const int32_t* tables;  // paged: [layers][max_pages]
   int max_pages, pool_pages, page_size;
   long long page_stride, head_stride, layer_stride;  // layer_stride: contiguous
+  unsigned long long prefetch_bytes;  // L2 prefetch lead of the producer (0: off)
   // Optional phase trace (globaltimer ns), per CTA kMegaTraceEvents slots:
   // [0] consumers start, [1 + 2k] arrival at barrier k, [2 + 2k] departure,
   // [kMegaTraceProducer + p] producer starting phase p.
@@ -95,8 +96,9 @@ __device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, u
   named_sync(1, kGemvConsumers);
   if (threadIdx.x == 0) {
     if (trace) trace[0] = globaltimer_ns();
-    __threadfence();
-    atomicAdd(bar, 1u);
+    // Release at GPU scope: every write this CTA's consumers made before the
+    // named barrier is visible to whoever acquires the count.
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
     uint64_t start = 0;
     for (uint32_t spin = 0;; ++spin) {
       if (ld_acquire_u32(bar) >= target) break;
@@ -156,8 +158,18 @@ __device__ __forceinline__ long long kv_offset(const MegaArgs& a, int l, int kvh
 }
 
 struct AttnItem {
-  int kvh, split, begin, end, cache_end, nblocks;
+  int kvh, split, splits, begin, end, cache_end, nblocks;
 };
+
+__device__ __forceinline__ int mega_attn_splits(int seq_len, int max_splits, int p) {
+  return max(1, min(max_splits, (seq_len + 2 * p - 1) / (2 * p)));
+}
+
+// Split partial record: acc[D], m, l, two floats of padding (16-byte rows).
+template <int D>
+constexpr int kMegaPartStride = D + 4;
+// The O-phase merge holds this many splits in registers.
+constexpr int kMegaMaxMergeSplits = 32;
 
 template <int D>
 __device__ __forceinline__ AttnItem mega_attn_item(const MegaArgs& a, int pos) {
@@ -169,10 +181,19 @@ __device__ __forceinline__ AttnItem mega_attn_item(const MegaArgs& a, int pos) {
     it.kvh = -1;
     return it;
   }
-  it.kvh = blockIdx.x / a.splits;
-  it.split = blockIdx.x % a.splits;
   const int seq_len = pos + 1;
-  const int chunk = mega_attn_chunk(seq_len, a.splits, AG::P);
+  // Splits this step: enough for about two stages of positions each, at most
+  // the configured count -- a short context merges a handful, not all.
+  const int splits = mega_attn_splits(seq_len, a.splits, AG::P);
+  if (static_cast<int>(blockIdx.x) >= a.num_kv * splits) {
+    it.nblocks = 0;
+    it.kvh = -1;
+    return it;
+  }
+  it.splits = splits;
+  it.kvh = blockIdx.x / splits;
+  it.split = blockIdx.x % splits;
+  const int chunk = mega_attn_chunk(seq_len, splits, AG::P);
   it.begin = it.split * chunk;
   it.end = min(seq_len, it.begin + chunk);
   it.cache_end = min(it.end, pos);
@@ -338,7 +359,9 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
     }
   }
   named_sync(1, kGemvConsumers);
-  float* part_base = a.partials + (static_cast<size_t>(item.kvh) * G) * a.splits * (2 + D);
+  // Publish this split's (acc[D], m, l) record; the O phase merges the splits
+  // of every head in its prologue (mega_load_attention_merged).
+  float* part_base = a.partials + static_cast<size_t>(item.kvh) * G * a.splits * kMegaPartStride<D>;
   for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
     const int g = idx / D, d = idx % D;
     float M = kNegBig;
@@ -352,57 +375,129 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
       L += c[1] * s;
       A += c[2 + d] * s;
     }
-    if (a.splits == 1) {
-      a.attn[(item.kvh * G + g) * D + d] = __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
-    } else {
-      float* slotp = part_base + (g * a.splits + item.split) * (2 + D);
-      if (d == 0) {
-        slotp[0] = M;
-        slotp[1] = L;
-      }
-      slotp[2 + d] = A;
-      __threadfence();
+    float* rec = part_base + (g * a.splits + item.split) * kMegaPartStride<D>;
+    rec[d] = A;
+    if (d == 0) {
+      rec[D] = M;
+      rec[D + 1] = L;
     }
-  }
-  if (a.splits == 1) return;
-  named_sync(1, kGemvConsumers);
-  if (tid == 0) {
-    unsigned* ctr = a.attn_ctr + l * a.num_kv + item.kvh;
-    const unsigned prev = atomicAdd(ctr, 1u);
-    *s_last = prev == static_cast<unsigned>(a.splits) - 1;
-    if (*s_last) {
-      __threadfence();
-      *ctr = 0u;
-    }
-  }
-  named_sync(1, kGemvConsumers);
-  if (!*s_last) return;
-  // Merge: per-split (m, l) and weights in shared memory, acc straight from L2.
-  const int S = a.splits;
-  float* wts = scratch;  // [G][S] weights, then [G] totals
-  for (int i = tid; i < G * S; i += kGemvConsumers) wts[i] = __ldcg(part_base + i * (2 + D));
-  named_sync(1, kGemvConsumers);
-  if (tid < G) {
-    float M = kNegBig;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, wts[tid * S + s]);
-    float L = 0.f;
-    for (int s = 0; s < S; ++s) {
-      const float w = ex2_approx(wts[tid * S + s] - M);
-      L += __ldcg(part_base + (tid * S + s) * (2 + D) + 1) * w;
-      wts[tid * S + s] = w;
-    }
-    wts[G * S + tid] = L;
-  }
-  named_sync(1, kGemvConsumers);
-  for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
-    const int g = idx / D, d = idx % D;
-    float A = 0.f;
-#pragma unroll 6
-    for (int s = 0; s < S; ++s) A += wts[g * S + s] * __ldcg(part_base + (g * S + s) * (2 + D) + 2 + d);
-    const float L = wts[G * S + g];
-    a.attn[(item.kvh * G + g) * D + d] = __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
   }
 }
+
+// O-phase prologue: the attention output this CTA's threads need (8 dims each,
+// the GEMV's column chunks), merged from the split partials of the step with
+// the logsumexp rule -- one parallel round of L2 loads -- and rounded to bf16
+// as the reference stores attn_out.
+template <int QD, int D>
+__device__ __forceinline__ void mega_load_attention_merged(
+    const MegaArgs& a, int pos, float (&xr)[GemvGeom<QD, kMegaStageBytes>::CPT][8]) {
+  using GG = GemvGeom<QD, kMegaStageBytes>;
+  constexpr int CPT = GG::CPT, TPR = GG::TPR;
+  const int splits = mega_attn_splits(pos + 1, a.splits, MegaAttnGeom<D>::P);
+  const int ci = threadIdx.x % TPR;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int col = (ci + j * TPR) * 8;
+    const int h = col / D, d0 = col % D;
+    const float* rec0 = a.partials + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>;
+    float M = kNegBig;
+    float ms[kMegaMaxMergeSplits], ls[kMegaMaxMergeSplits];
+    float4 lo[kMegaMaxMergeSplits], hi[kMegaMaxMergeSplits];
+#pragma unroll
+    for (int s = 0; s < kMegaMaxMergeSplits; ++s) {
+      if (s < splits) {
+        const float* rec = rec0 + s * kMegaPartStride<D>;
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + D));
+        ms[s] = ml.x;
+        ls[s] = ml.y;
+        lo[s] = __ldcg(reinterpret_cast<const float4*>(rec + d0));
+        hi[s] = __ldcg(reinterpret_cast<const float4*>(rec + d0 + 4));
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < kMegaMaxMergeSplits; ++s) {
+      if (s < splits) M = fmaxf(M, ms[s]);
+    }
+    float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < kMegaMaxMergeSplits; ++s) {
+      if (s < splits) {
+        const float w = ex2_approx(ms[s] - M);
+        L += ls[s] * w;
+        acc[0] += lo[s].x * w; acc[1] += lo[s].y * w; acc[2] += lo[s].z * w; acc[3] += lo[s].w * w;
+        acc[4] += hi[s].x * w; acc[5] += hi[s].y * w; acc[6] += hi[s].z * w; acc[7] += hi[s].w * w;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xr[j][e] = rbf(L > 0.f ? acc[e] / L : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// L2 prefetch window
+// ---------------------------------------------------------------------------
+
+// Walks this CTA's weight slices in schedule order -- per layer qkv, o, gate,
+// up, down, then the lm_head -- and keeps cp.async.bulk.prefetch.L2 up to
+// MegaArgs::prefetch_bytes ahead of what the producer has issued into the ring.
+// HBM then keeps streaming the next matrices while the consumers work through
+// barriers, attention and the small projections, and the ring refills from L2.
+constexpr unsigned kMegaPrefetchChunk = 32u << 10;
+
+template <int H, int QD, int F, int D>
+struct MegaPrefetch {
+  const MegaArgs* a;
+  int slice;           // index into the schedule: 5 per layer, then lm_head
+  const char* ptr;     // next byte to prefetch in the current slice
+  unsigned long long left;  // bytes left in the current slice
+  unsigned long long done;  // bytes prefetched so far
+
+  __device__ __forceinline__ void open(int s) {
+    slice = s;
+    left = 0;
+    const int c = blockIdx.x, n = gridDim.x;
+    if (s < 5 * a->layers) {
+      const MegaLayer& w = a->L[s / 5];
+      const int nqkv = QD + 2 * D * a->num_kv;
+      int o0, o1, K;
+      const bf16* base;
+      switch (s % 5) {
+        case 0: o0 = gemv_share(nqkv, c, n); o1 = gemv_share(nqkv, c + 1, n); K = H; base = w.qkv; break;
+        case 1: o0 = gemv_share(H, c, n); o1 = gemv_share(H, c + 1, n); K = QD; base = w.o; break;
+        case 2: o0 = gemv_share(F, c, n); o1 = gemv_share(F, c + 1, n); K = H; base = w.gate_up; break;
+        case 3: o0 = F + gemv_share(F, c, n); o1 = F + gemv_share(F, c + 1, n); K = H; base = w.gate_up; break;
+        default: o0 = gemv_share(H, c, n); o1 = gemv_share(H, c + 1, n); K = F; base = w.down; break;
+      }
+      ptr = reinterpret_cast<const char*>(base + static_cast<size_t>(o0) * K);
+      left = static_cast<unsigned long long>(o1 - o0) * K * 2;
+    } else if (s == 5 * a->layers) {
+      const int o0 = gemv_share(a->vocab, c, n), o1 = gemv_share(a->vocab, c + 1, n);
+      ptr = reinterpret_cast<const char*>(a->lm_head + static_cast<size_t>(o0) * H);
+      left = static_cast<unsigned long long>(o1 - o0) * H * 2;
+    }
+  }
+
+  __device__ __forceinline__ void init(const MegaArgs* args) {
+    a = args;
+    done = 0;
+    open(0);
+  }
+
+  __device__ __forceinline__ void top_up(unsigned long long issued) {
+    while (done < issued + a->prefetch_bytes) {
+      if (left == 0) {
+        if (slice >= 5 * a->layers) return;
+        open(slice + 1);
+        continue;
+      }
+      const unsigned bytes = static_cast<unsigned>(left < kMegaPrefetchChunk ? left : kMegaPrefetchChunk);
+      prefetch_l2(ptr, bytes);
+      ptr += bytes;
+      left -= bytes;
+      done += bytes;
+    }
+  }
+};
 
 // ---------------------------------------------------------------------------
 // The kernel
@@ -463,28 +558,36 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         ++phase;
         return true;
       };
+      MegaPrefetch<H, QD, F, D> pf;
+      pf.init(&a);
+      unsigned long long issued = 0;
       for (int l = 0; l < a.layers && ok; ++l) {
         const MegaLayer& w = a.L[l];
         const int nqkv = QD + 2 * (D * a.num_kv);
         ok = ok && mark() && gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, w.qkv, nqkv,
                                                      gemv_share(nqkv, blockIdx.x, ctas),
-                                                     gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status);
+                                                     gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status,
+                                                     &pf, &issued);
         ok = ok && mark() && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
         ok = ok && mark() && gemv_produce<QD, SB, STAGES, false>(ring, full, empty, it, w.o, H,
                                                       gemv_share(H, blockIdx.x, ctas),
-                                                      gemv_share(H, blockIdx.x + 1, ctas), policy, a.status);
+                                                      gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
+                                                      &pf, &issued);
         ok = ok && mark() && gemv_produce<H, SB, STAGES, true>(ring, full, empty, it, w.gate_up, F,
                                                     gemv_share(F, blockIdx.x, ctas),
-                                                    gemv_share(F, blockIdx.x + 1, ctas), policy, a.status);
+                                                    gemv_share(F, blockIdx.x + 1, ctas), policy, a.status,
+                                                    &pf, &issued);
         ok = ok && mark() && gemv_produce<F, SB, STAGES, false>(ring, full, empty, it, w.down, H,
                                                      gemv_share(H, blockIdx.x, ctas),
-                                                     gemv_share(H, blockIdx.x + 1, ctas), policy, a.status);
+                                                     gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
+                                                     &pf, &issued);
       }
       if (ok) {
         mark();
         gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, a.lm_head, a.vocab,
                                           gemv_share(a.vocab, blockIdx.x, ctas),
-                                          gemv_share(a.vocab, blockIdx.x + 1, ctas), policy, a.status);
+                                          gemv_share(a.vocab, blockIdx.x + 1, ctas), policy, a.status,
+                                          &pf, &issued);
       }
       ring_drain<STAGES>(full, it, a.status);
     }
@@ -534,11 +637,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       {  // O
         GemvArgs g = {};
         g.status = a.status;
-        g.x_in = a.attn;
         g.resid = a.x;
         g.resid_sum = a.xsum;
         float xr[GemvGeom<QD, SB>::CPT][8];
-        gemv_load_x<QD, SB, PRO_PLAIN>(g, xr, red8);
+        mega_load_attention_merged<QD, D>(a, pos, xr);
         gemv_consume<QD, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
                                                 gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
       }
