@@ -168,7 +168,7 @@ __device__ __forceinline__ int mega_attn_splits(int seq_len, int max_splits, int
 // Split partial record: acc[D], m, l, two floats of padding (16-byte rows).
 template <int D>
 constexpr int kMegaPartStride = D + 4;
-// The O-phase merge holds this many splits in registers.
+// Largest split count the persistent step uses.
 constexpr int kMegaMaxMergeSplits = 32;
 
 template <int D>
@@ -400,33 +400,38 @@ __device__ __forceinline__ void mega_load_attention_merged(
     const int col = (ci + j * TPR) * 8;
     const int h = col / D, d0 = col % D;
     const float* rec0 = a.partials + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>;
-    float M = kNegBig;
-    float ms[kMegaMaxMergeSplits], ls[kMegaMaxMergeSplits];
-    float4 lo[kMegaMaxMergeSplits], hi[kMegaMaxMergeSplits];
+    // Online logsumexp merge, kMergeBatch splits per round of loads.
+    constexpr int B = 4;
+    float M = kNegBig, L = 0.f;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < splits; s0 += B) {
+      float ms[B], ls[B];
+      float4 lo[B], hi[B];
 #pragma unroll
-    for (int s = 0; s < kMegaMaxMergeSplits; ++s) {
-      if (s < splits) {
+      for (int b = 0; b < B; ++b) {
+        const int s = min(s0 + b, splits - 1);  // clamp: a repeat is masked below
         const float* rec = rec0 + s * kMegaPartStride<D>;
         const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + D));
-        ms[s] = ml.x;
-        ls[s] = ml.y;
-        lo[s] = __ldcg(reinterpret_cast<const float4*>(rec + d0));
-        hi[s] = __ldcg(reinterpret_cast<const float4*>(rec + d0 + 4));
+        ms[b] = s0 + b < splits ? ml.x : kNegBig;
+        ls[b] = s0 + b < splits ? ml.y : 0.f;
+        lo[b] = __ldcg(reinterpret_cast<const float4*>(rec + d0));
+        hi[b] = __ldcg(reinterpret_cast<const float4*>(rec + d0 + 4));
       }
-    }
+      float Mn = M;
 #pragma unroll
-    for (int s = 0; s < kMegaMaxMergeSplits; ++s) {
-      if (s < splits) M = fmaxf(M, ms[s]);
-    }
-    float L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int b = 0; b < B; ++b) Mn = fmaxf(Mn, ms[b]);
+      const float keep = ex2_approx(M - Mn);
+      L *= keep;
 #pragma unroll
-    for (int s = 0; s < kMegaMaxMergeSplits; ++s) {
-      if (s < splits) {
-        const float w = ex2_approx(ms[s] - M);
-        L += ls[s] * w;
-        acc[0] += lo[s].x * w; acc[1] += lo[s].y * w; acc[2] += lo[s].z * w; acc[3] += lo[s].w * w;
-        acc[4] += hi[s].x * w; acc[5] += hi[s].y * w; acc[6] += hi[s].z * w; acc[7] += hi[s].w * w;
+      for (int e = 0; e < 8; ++e) acc[e] *= keep;
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float w = s0 + b < splits ? ex2_approx(ms[b] - Mn) : 0.f;
+        L += ls[b] * w;
+        acc[0] += lo[b].x * w; acc[1] += lo[b].y * w; acc[2] += lo[b].z * w; acc[3] += lo[b].w * w;
+        acc[4] += hi[b].x * w; acc[5] += hi[b].y * w; acc[6] += hi[b].z * w; acc[7] += hi[b].w * w;
       }
+      M = Mn;
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) xr[j][e] = rbf(L > 0.f ? acc[e] / L : 0.f);
@@ -558,8 +563,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         ++phase;
         return true;
       };
-      MegaPrefetch<H, QD, F, D> pf;
-      pf.init(&a);
+      MegaPrefetch<H, QD, F, D> pf_state;
+      pf_state.init(&a);
+      // A zero lead means no prefetching at all (a trailing prefetch would
+      // re-read lines the ring already consumed).
+      MegaPrefetch<H, QD, F, D>* pf = a.prefetch_bytes ? &pf_state : nullptr;
       unsigned long long issued = 0;
       for (int l = 0; l < a.layers && ok; ++l) {
         const MegaLayer& w = a.L[l];
@@ -567,27 +575,27 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         ok = ok && mark() && gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, w.qkv, nqkv,
                                                      gemv_share(nqkv, blockIdx.x, ctas),
                                                      gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status,
-                                                     &pf, &issued);
+                                                     pf, &issued);
         ok = ok && mark() && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
         ok = ok && mark() && gemv_produce<QD, SB, STAGES, false>(ring, full, empty, it, w.o, H,
                                                       gemv_share(H, blockIdx.x, ctas),
                                                       gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
-                                                      &pf, &issued);
+                                                      pf, &issued);
         ok = ok && mark() && gemv_produce<H, SB, STAGES, true>(ring, full, empty, it, w.gate_up, F,
                                                     gemv_share(F, blockIdx.x, ctas),
                                                     gemv_share(F, blockIdx.x + 1, ctas), policy, a.status,
-                                                    &pf, &issued);
+                                                    pf, &issued);
         ok = ok && mark() && gemv_produce<F, SB, STAGES, false>(ring, full, empty, it, w.down, H,
                                                      gemv_share(H, blockIdx.x, ctas),
                                                      gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
-                                                     &pf, &issued);
+                                                     pf, &issued);
       }
       if (ok) {
         mark();
         gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, a.lm_head, a.vocab,
                                           gemv_share(a.vocab, blockIdx.x, ctas),
                                           gemv_share(a.vocab, blockIdx.x + 1, ctas), policy, a.status,
-                                          &pf, &issued);
+                                          pf, &issued);
       }
       ring_drain<STAGES>(full, it, a.status);
     }
