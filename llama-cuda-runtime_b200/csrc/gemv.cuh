@@ -72,24 +72,29 @@ struct GemvArgs {
 
 template <int K, int STAGE_BYTES>
 struct GemvGeom {
-  static constexpr int KC = K / 8;               // 16-byte chunks per row
-  static constexpr int TPR = KC < 256 ? KC : 256;  // threads per row
-  static constexpr int CPT = KC / TPR;           // chunks per thread
-  static constexpr int SLOTS = 256 / TPR;        // rows in flight per pass
-  static constexpr int WPR = TPR / 32;           // warps per row
+  static constexpr int KC = K / 8;                       // 16-byte chunks per row
+  // A warp per row up to K = 2048 (64 elements a lane), more warps beyond, so
+  // the reduction is amortised over many multiply-adds.
+  static constexpr int TPR = (K / 64) > 32 ? (K / 64) : 32;  // threads per row
+  static constexpr int CPT = KC / TPR;                   // chunks per thread (<= 8)
+  static constexpr int SLOTS = 256 / TPR;                // rows in flight per pass
+  static constexpr int WPR = TPR / 32;                   // warps per row
   static constexpr int ROW_BYTES = K * 2;
-  static constexpr int RPS = STAGE_BYTES / ROW_BYTES;  // rows per stage
-  static constexpr int RPT = RPS / SLOTS;        // rows per thread per stage
+  static constexpr int RPS = STAGE_BYTES / ROW_BYTES;    // rows per stage
+  static constexpr int RPT = RPS / SLOTS;                // rows per thread per stage
+  // Stages per reduction segment: 2048 floats (8 KB) of row partials.
+  static constexpr int SEG = 2048 / (RPS * WPR) > 0 ? 2048 / (RPS * WPR) : 1;
   static_assert(K % 256 == 0 && KC % 32 == 0, "K must be a multiple of 256");
-  static_assert(TPR * CPT == KC, "K/8 must split evenly over the row's threads");
+  static_assert(TPR * CPT == KC && CPT <= 8, "K/8 must split evenly over the row's threads");
+  static_assert(TPR <= 256 && 256 % TPR == 0, "rows must split the 8 consumer warps");
   static_assert(RPS >= SLOTS && RPS % SLOTS == 0, "stage too small for this K");
   static_assert(RPT == 1 || RPT == 2 || RPT == 4 || RPT == 8 || RPT == 16, "RPT");
 };
 
 constexpr int kGemvConsumers = 256;
-// Stages whose row partials are gathered in shared memory before one
-// cross-warp reduction and epilogue pass (<= 8 KB of partials for any K).
-constexpr int kGemvSegment = 64;
+// Shared-memory row partials gathered before one cross-warp reduction and
+// epilogue pass (GemvGeom::SEG stages' worth).
+constexpr int kGemvRedFloats = 2048;
 constexpr int kGemvThreads = kGemvConsumers + 32;
 
 __device__ __forceinline__ uint32_t order_key(float v) {
@@ -277,7 +282,7 @@ __device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
 
 // Consumers (256 threads): dot products of the streamed rows [o0, o1) with
 // the register-resident x, segmented cross-warp reduction in `red`
-// (kGemvSegment * RPS * WPR floats) and the epilogue. LOGITS_ARGMAX folds the
+// (kGemvRedFloats floats) and the epilogue. LOGITS_ARGMAX folds the
 // packed (order key, ~index) maximum into `best`. Uses named barrier 1.
 template <int K, int STAGE_BYTES, int STAGES, int EPI>
 __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full, uint64_t* empty,
@@ -288,7 +293,7 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
   constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR, WPR = G::WPR;
   constexpr int PAIRS = RPS / 2;
   constexpr int UNIT = (EPI == EPI_SWIGLU) ? PAIRS : RPS;
-  constexpr int SEG = kGemvSegment;
+  constexpr int SEG = G::SEG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int slotrow = tid / TPR, ci = tid % TPR;
   const int n_stages = (o1 - o0 + UNIT - 1) / UNIT;
@@ -302,20 +307,17 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
 #pragma unroll
       for (int r = 0; r < RPT; ++r) {
         const int row = slotrow * RPT + r;
-        float acc = 0.f;
+        // Packed fp32x2 multiply-adds (sm_100 FFMA2), two accumulator pairs.
+        float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < CPT; ++j) {
           const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES + (ci + j * TPR) * 16);
-          acc = fmaf(bf_lo(wv.x), xr[j][0], acc);
-          acc = fmaf(bf_hi(wv.x), xr[j][1], acc);
-          acc = fmaf(bf_lo(wv.y), xr[j][2], acc);
-          acc = fmaf(bf_hi(wv.y), xr[j][3], acc);
-          acc = fmaf(bf_lo(wv.z), xr[j][4], acc);
-          acc = fmaf(bf_hi(wv.z), xr[j][5], acc);
-          acc = fmaf(bf_lo(wv.w), xr[j][6], acc);
-          acc = fmaf(bf_hi(wv.w), xr[j][7], acc);
+          a0 = __ffma2_rn(make_float2(bf_lo(wv.x), bf_hi(wv.x)), make_float2(xr[j][0], xr[j][1]), a0);
+          a1 = __ffma2_rn(make_float2(bf_lo(wv.y), bf_hi(wv.y)), make_float2(xr[j][2], xr[j][3]), a1);
+          a0 = __ffma2_rn(make_float2(bf_lo(wv.z), bf_hi(wv.z)), make_float2(xr[j][4], xr[j][5]), a0);
+          a1 = __ffma2_rn(make_float2(bf_lo(wv.w), bf_hi(wv.w)), make_float2(xr[j][6], xr[j][7]), a1);
         }
-        part[r] = acc;
+        part[r] = (a0.x + a1.x) + (a0.y + a1.y);
       }
       __syncwarp();
       if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   uint64_t* empty = full + STAGES;
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
   float* red8 = reinterpret_cast<float*>(cta_best + 1);   // [8]
-  float* red = red8 + 8;                                    // [SEG * RPS][WPR]
+  float* red = red8 + 8;                                    // [kGemvRedFloats]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int o0 = gemv_share(a.n_out, blockIdx.x, gridDim.x);
@@ -436,9 +438,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
 
 template <int K, int STAGE_BYTES, int STAGES>
 constexpr size_t gemv_smem_bytes() {
-  using G = GemvGeom<K, STAGE_BYTES>;
   return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) + 8 +
-         (8 + static_cast<size_t>(kGemvSegment) * G::RPS * G::WPR) * sizeof(float) + 64;
+         (8 + kGemvRedFloats) * sizeof(float) + 64;
 }
 
 }  // namespace lcrb

@@ -8,8 +8,10 @@
 namespace lcrb {
 
 // Stage geometry shared by every instantiation.
-constexpr int kGemvStageBytes = 16384;
-constexpr int kGemvStages = 6;
+constexpr int kGemvStageBytes = 32768;
+// Three 32 KB stages: small enough that the next kernel's CTA fits beside
+// this one on an SM, so programmatic dependent launch overlaps them.
+constexpr int kGemvStages = 3;
 
 bool gemv_supported(int K, int pro, int epi);
 // Outputs (rows, or SWIGLU pairs) per chunk of one stage.

@@ -27,8 +27,8 @@
 
 namespace lcrb {
 
-constexpr int kMegaStageBytes = 16384;
-constexpr int kMegaStages = 12;
+constexpr int kMegaStageBytes = 32768;
+constexpr int kMegaStages = 6;
 constexpr int kMegaThreads = kGemvConsumers + 32;
 constexpr int kMegaWarps = kGemvConsumers / 32;
 
@@ -510,9 +510,7 @@ struct MegaPrefetch {
 
 template <int H, int QD, int F, int D, int G, bool PAGED>
 struct MegaShape {
-  static constexpr int RED_FLOATS = 2048 + 512;  // >= GEMV segments, attention scratch
-  static_assert(kGemvSegment * GemvGeom<H, kMegaStageBytes>::RPS * GemvGeom<H, kMegaStageBytes>::WPR <= RED_FLOATS, "red");
-  static_assert(kGemvSegment * GemvGeom<F, kMegaStageBytes>::RPS * GemvGeom<F, kMegaStageBytes>::WPR <= RED_FLOATS, "red");
+  static constexpr int RED_FLOATS = kGemvRedFloats + 512;  // GEMV segments, attention scratch
   static_assert(kMegaWarps * G * (D + 2) <= RED_FLOATS, "attention scratch");
   static constexpr size_t SMEM = static_cast<size_t>(kMegaStages) * kMegaStageBytes +
                                  2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 + 64;
