@@ -208,24 +208,24 @@ __device__ __forceinline__ void ring_drain(uint64_t* full, int issued, uint32_t*
   }
 }
 
-// Consumers (256 threads): the input vector into registers. NORM / EMBED_NORM
-// apply RMSNorm (sum of squares over the unrounded residual sums when given)
-// and round to bf16 as the reference stores `normed`. Uses named barrier 1.
-template <int K, int STAGE_BYTES, int PRO>
-__device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
-                                            float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8],
-                                            float* red8) {
-  using G = GemvGeom<K, STAGE_BYTES>;
-  constexpr int CPT = G::CPT, TPR = G::TPR;
+// Consumers (256 threads): the input vector, staged ONCE per CTA in shared
+// memory as bf16 (`xs`, K elements; every value the GEMV multiplies is
+// bf16-exact), each thread preparing 8-element chunks: a plain copy, or
+// RMSNorm (sum of squares over the unrounded residual sums when given, scale
+// applied to the bf16 residual, rounded to bf16 as the reference stores
+// `normed`). Uses named barrier 1; `xs` is complete on return.
+template <int K, int PRO>
+__device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, bf16* xs, float* red8) {
+  constexpr int KC = K / 8;
+  constexpr int PER = (KC + kGemvConsumers - 1) / kGemvConsumers;  // chunks per thread
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int slotrow = tid / TPR, ci = tid % TPR;
   if constexpr (PRO == PRO_PLAIN) {
 #pragma unroll
-    for (int j = 0; j < CPT; ++j) unpack8(ldg_cg16(a.x_in + (ci + j * TPR) * 8), xr[j]);
+    for (int p = 0; p < PER; ++p) {
+      const int c = tid + p * kGemvConsumers;
+      if (c < KC) reinterpret_cast<uint4*>(xs)[c] = ldg_cg16(a.x_in + c * 8);
+    }
   } else {
-    uint4 gain[CPT];
-#pragma unroll
-    for (int j = 0; j < CPT; ++j) gain[j] = ldg16(a.norm_w + (ci + j * TPR) * 8);
     const bf16* src = a.x_in;
     if constexpr (PRO == PRO_EMBED_NORM) {
       int tok = __ldcg(a.token);
@@ -235,30 +235,32 @@ __device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
       }
       src = a.embed + static_cast<size_t>(tok) * K;
     }
-    float xv[CPT][8], sq[CPT][8];
+    uint4 raw[PER], gain[PER];
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < CPT; ++j) {
-      const int col = (ci + j * TPR) * 8;
-      const uint4 raw = ldg_cg16(src + col);
-      unpack8(raw, xv[j]);
-      if (PRO == PRO_NORM && a.xsum != nullptr) {
-        const float4 s0 = __ldcg(reinterpret_cast<const float4*>(a.xsum + col));
-        const float4 s1 = __ldcg(reinterpret_cast<const float4*>(a.xsum + col + 4));
-        sq[j][0] = s0.x; sq[j][1] = s0.y; sq[j][2] = s0.z; sq[j][3] = s0.w;
-        sq[j][4] = s1.x; sq[j][5] = s1.y; sq[j][6] = s1.z; sq[j][7] = s1.w;
-      } else {
+    for (int p = 0; p < PER; ++p) {
+      const int c = tid + p * kGemvConsumers;
+      if (c < KC) {
+        gain[p] = ldg16(a.norm_w + c * 8);
+        raw[p] = ldg_cg16(src + c * 8);
+        float v[8];
+        if (PRO == PRO_NORM && a.xsum != nullptr) {
+          const float4 s0 = __ldcg(reinterpret_cast<const float4*>(a.xsum + c * 8));
+          const float4 s1 = __ldcg(reinterpret_cast<const float4*>(a.xsum + c * 8 + 4));
+          v[0] = s0.x; v[1] = s0.y; v[2] = s0.z; v[3] = s0.w;
+          v[4] = s1.x; v[5] = s1.y; v[6] = s1.z; v[7] = s1.w;
+        } else {
+          unpack8(raw[p], v);
+        }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sq[j][e] = xv[j][e];
-      }
-      if (slotrow == 0) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss = fmaf(sq[j][e], sq[j][e], ss);
-      }
-      if (PRO == PRO_EMBED_NORM && blockIdx.x == 0 && slotrow == 0) {
-        *reinterpret_cast<uint4*>(a.x_out + col) = raw;
-        *reinterpret_cast<float4*>(a.xsum_out + col) = make_float4(xv[j][0], xv[j][1], xv[j][2], xv[j][3]);
-        *reinterpret_cast<float4*>(a.xsum_out + col + 4) = make_float4(xv[j][4], xv[j][5], xv[j][6], xv[j][7]);
+        for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+        if (PRO == PRO_EMBED_NORM && blockIdx.x == 0) {
+          float xv[8];
+          unpack8(raw[p], xv);
+          *reinterpret_cast<uint4*>(a.x_out + c * 8) = raw[p];
+          *reinterpret_cast<float4*>(a.xsum_out + c * 8) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+          *reinterpret_cast<float4*>(a.xsum_out + c * 8 + 4) = make_float4(xv[4], xv[5], xv[6], xv[7]);
+        }
       }
     }
 #pragma unroll
@@ -268,16 +270,42 @@ __device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
     float total = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) total += red8[w];
-    named_sync(1, kGemvConsumers);  // red8 may be reused right after
     const float scale = rsqrtf(total / static_cast<float>(K) + a.eps);
 #pragma unroll
-    for (int j = 0; j < CPT; ++j) {
-      float gf[8];
-      unpack8(gain[j], gf);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) xr[j][e] = rbf(__fmul_rn(__fmul_rn(xv[j][e], scale), gf[e]));
+    for (int p = 0; p < PER; ++p) {
+      const int c = tid + p * kGemvConsumers;
+      if (c < KC) {
+        float xv[8], gf[8];
+        unpack8(raw[p], xv);
+        unpack8(gain[p], gf);
+        uint4 o;
+        o.x = pack_bf2(__fmul_rn(__fmul_rn(xv[0], scale), gf[0]), __fmul_rn(__fmul_rn(xv[1], scale), gf[1]));
+        o.y = pack_bf2(__fmul_rn(__fmul_rn(xv[2], scale), gf[2]), __fmul_rn(__fmul_rn(xv[3], scale), gf[3]));
+        o.z = pack_bf2(__fmul_rn(__fmul_rn(xv[4], scale), gf[4]), __fmul_rn(__fmul_rn(xv[5], scale), gf[5]));
+        o.w = pack_bf2(__fmul_rn(__fmul_rn(xv[6], scale), gf[6]), __fmul_rn(__fmul_rn(xv[7], scale), gf[7]));
+        reinterpret_cast<uint4*>(xs)[c] = o;
+      }
     }
   }
+  named_sync(1, kGemvConsumers);  // xs complete (and red8 free again)
+}
+
+// Each thread's column chunks of the staged input vector, widened to fp32.
+template <int K, int STAGE_BYTES>
+__device__ __forceinline__ void gemv_x_regs(const bf16* xs,
+                                            float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8]) {
+  using G = GemvGeom<K, STAGE_BYTES>;
+  const int ci = threadIdx.x % G::TPR;
+#pragma unroll
+  for (int j = 0; j < G::CPT; ++j) unpack8(reinterpret_cast<const uint4*>(xs)[ci + j * G::TPR], xr[j]);
+}
+
+template <int K, int STAGE_BYTES, int PRO>
+__device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
+                                            float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8],
+                                            bf16* xs, float* red8) {
+  gemv_stage_x<K, PRO>(a, xs, red8);
+  gemv_x_regs<K, STAGE_BYTES>(xs, xr);
 }
 
 // Consumers (256 threads): dot products of the streamed rows [o0, o1) with
@@ -394,6 +422,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
   float* red8 = reinterpret_cast<float*>(cta_best + 1);   // [8]
   float* red = red8 + 8;                                    // [kGemvRedFloats]
+  bf16* xs = reinterpret_cast<bf16*>(red + kGemvRedFloats);  // [K]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int o0 = gemv_share(a.n_out, blockIdx.x, gridDim.x);
@@ -421,7 +450,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   } else {
     float xr[G::CPT][8];
     pdl_wait();
-    gemv_load_x<K, STAGE_BYTES, PRO>(a, xr, red8);
+    gemv_load_x<K, STAGE_BYTES, PRO>(a, xr, xs, red8);
     int it = 0;
     unsigned long long best = 0ull;
     bool failed = false;
@@ -439,7 +468,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
 template <int K, int STAGE_BYTES, int STAGES>
 constexpr size_t gemv_smem_bytes() {
   return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) + 8 +
-         (8 + kGemvRedFloats) * sizeof(float) + 64;
+         (8 + kGemvRedFloats) * sizeof(float) + static_cast<size_t>(K) * 2 + 64;
 }
 
 }  // namespace lcrb

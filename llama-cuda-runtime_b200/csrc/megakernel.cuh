@@ -384,23 +384,18 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
   }
 }
 
-// O-phase prologue: the attention output this CTA's threads need (8 dims each,
-// the GEMV's column chunks), merged from the split partials of the step with
-// the logsumexp rule -- one parallel round of L2 loads -- and rounded to bf16
-// as the reference stores attn_out.
+// O-phase prologue: the attention output, merged from the step's split
+// partials with the logsumexp rule (an online merge over batches of four
+// splits, one round of L2 loads per batch), rounded to bf16 as the reference
+// stores attn_out, and staged in shared memory: each thread one 8-element
+// chunk. Uses named barrier 1; `xs` is complete on return.
 template <int QD, int D>
-__device__ __forceinline__ void mega_load_attention_merged(
-    const MegaArgs& a, int pos, float (&xr)[GemvGeom<QD, kMegaStageBytes>::CPT][8]) {
-  using GG = GemvGeom<QD, kMegaStageBytes>;
-  constexpr int CPT = GG::CPT, TPR = GG::TPR;
+__device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos, bf16* xs) {
   const int splits = mega_attn_splits(pos + 1, a.splits, MegaAttnGeom<D>::P);
-  const int ci = threadIdx.x % TPR;
-#pragma unroll
-  for (int j = 0; j < CPT; ++j) {
-    const int col = (ci + j * TPR) * 8;
+  for (int c = threadIdx.x; c < QD / 8; c += kGemvConsumers) {
+    const int col = c * 8;
     const int h = col / D, d0 = col % D;
     const float* rec0 = a.partials + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>;
-    // Online logsumexp merge, kMergeBatch splits per round of loads.
     constexpr int B = 4;
     float M = kNegBig, L = 0.f;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -433,9 +428,15 @@ __device__ __forceinline__ void mega_load_attention_merged(
       }
       M = Mn;
     }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) xr[j][e] = rbf(L > 0.f ? acc[e] / L : 0.f);
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint4 o;
+    o.x = pack_bf2(acc[0] * inv, acc[1] * inv);
+    o.y = pack_bf2(acc[2] * inv, acc[3] * inv);
+    o.z = pack_bf2(acc[4] * inv, acc[5] * inv);
+    o.w = pack_bf2(acc[6] * inv, acc[7] * inv);
+    reinterpret_cast<uint4*>(xs)[c] = o;
   }
+  named_sync(1, kGemvConsumers);
 }
 
 // ---------------------------------------------------------------------------
@@ -512,8 +513,10 @@ template <int H, int QD, int F, int D, int G, bool PAGED>
 struct MegaShape {
   static constexpr int RED_FLOATS = kGemvRedFloats + 512;  // GEMV segments, attention scratch
   static_assert(kMegaWarps * G * (D + 2) <= RED_FLOATS, "attention scratch");
+  static constexpr int XS = (H > F ? H : F) > QD ? (H > F ? H : F) : QD;
   static constexpr size_t SMEM = static_cast<size_t>(kMegaStages) * kMegaStageBytes +
-                                 2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 + 64;
+                                 2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 +
+                                 static_cast<size_t>(XS) * 2 + 64;
 };
 
 template <int H, int QD, int F, int D, int G, bool PAGED>
@@ -530,6 +533,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
   float* red8 = reinterpret_cast<float*>(s_flags + 4);
   float* red = red8 + 8;
   float* cs = red + Shape::RED_FLOATS;  // RoPE cos/sin [D]
+  bf16* xs = reinterpret_cast<bf16*>(cs + D);  // staged input vector [max(H, QD, F)]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pos = __ldcg(a.state + 1);
@@ -605,6 +609,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     unsigned long long best = 0ull;
     unsigned long long* ctrace = a.trace ? a.trace + blockIdx.x * kMegaTraceEvents : nullptr;
     if (ctrace && tid == 0) ctrace[0] = globaltimer_ns();
+    int phase_no = 0;
+    auto pro_done = [&]() {
+      if (ctrace && tid == 0 && 163 + phase_no < kMegaTraceProducer - 1) ctrace[163 + phase_no] = globaltimer_ns();
+      ++phase_no;
+    };
     auto sync = [&]() -> bool {
       ++nbar;
       if (failed) atomicOr(a.status, kStatusAbort);
@@ -628,16 +637,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
           g.vocab = a.vocab;
           g.x_out = a.x;
           g.xsum_out = a.xsum;
-          gemv_load_x<H, SB, PRO_EMBED_NORM>(g, xr, red8);
+          gemv_load_x<H, SB, PRO_EMBED_NORM>(g, xr, xs, red8);
+        pro_done();
         } else {
           g.x_in = a.x;
           g.xsum = a.xsum;
-          gemv_load_x<H, SB, PRO_NORM>(g, xr, red8);
+          gemv_load_x<H, SB, PRO_NORM>(g, xr, xs, red8);
+        pro_done();
         }
         gemv_consume<H, SB, STAGES, EPI_STORE>(ring, full, empty, it, g, gemv_share(nqkv, blockIdx.x, ctas),
                                                gemv_share(nqkv, blockIdx.x + 1, ctas), xr, red, best, failed);
       }
       if (!(run = sync())) break;
+      pro_done();  // attention: no separate prologue
       mega_attn_consume<D, G, STAGES, PAGED>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed);
       if (!(run = sync())) break;
       {  // O
@@ -646,7 +658,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.resid = a.x;
         g.resid_sum = a.xsum;
         float xr[GemvGeom<QD, SB>::CPT][8];
-        mega_load_attention_merged<QD, D>(a, pos, xr);
+        mega_stage_attention<QD, D>(a, pos, xs);
+        gemv_x_regs<QD, SB>(xs, xr);
+        pro_done();
         gemv_consume<QD, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
                                                 gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
       }
@@ -660,7 +674,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.norm_w = w.post_norm;
         g.y = a.act;
         float xr[GemvGeom<H, SB>::CPT][8];
-        gemv_load_x<H, SB, PRO_NORM>(g, xr, red8);
+        gemv_load_x<H, SB, PRO_NORM>(g, xr, xs, red8);
+        pro_done();
         gemv_consume<H, SB, STAGES, EPI_SWIGLU>(ring, full, empty, it, g, gemv_share(F, blockIdx.x, ctas),
                                                 gemv_share(F, blockIdx.x + 1, ctas), xr, red, best, failed);
       }
@@ -672,7 +687,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.resid = a.x;
         g.resid_sum = a.xsum;
         float xr[GemvGeom<F, SB>::CPT][8];
-        gemv_load_x<F, SB, PRO_PLAIN>(g, xr, red8);
+        gemv_load_x<F, SB, PRO_PLAIN>(g, xr, xs, red8);
+        pro_done();
         gemv_consume<F, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
                                                gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
       }
@@ -687,7 +703,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       g.norm_w = a.final_norm;
       g.yf = a.logits;
       float xr[GemvGeom<H, SB>::CPT][8];
-      gemv_load_x<H, SB, PRO_NORM>(g, xr, red8);
+      gemv_load_x<H, SB, PRO_NORM>(g, xr, xs, red8);
+        pro_done();
       gemv_consume<H, SB, STAGES, EPI_LOGITS_ARGMAX>(ring, full, empty, it, g,
                                                      gemv_share(a.vocab, blockIdx.x, ctas),
                                                      gemv_share(a.vocab, blockIdx.x + 1, ctas), xr, red,

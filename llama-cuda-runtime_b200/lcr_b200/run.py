@@ -40,12 +40,15 @@ def print_trace(t: np.ndarray, layers: int) -> None:
     work = (arrive - start) / 1e3
     wait = (depart - arrive) / 1e3
     prod = t[:, 256:256 + nbar + 1]
-    print(f"{'phase':8s} {'work mean':>10s} {'work max':>9s} {'wait mean':>10s} {'producer lead':>14s}  (us)")
+    pro = t[:, 163:163 + nbar]
+    prologue = (pro - start) / 1e3
+    print(f"{'phase':8s} {'work mean':>10s} {'work max':>9s} {'prologue':>9s} {'wait mean':>10s} "
+          f"{'producer lead':>14s}  (us)")
     for k, name in enumerate(PHASES):
         cols = list(range(k, nbar, 5))
         lead = (start[:, cols] - prod[:, cols]) / 1e3  # >0: producer started this phase earlier
         print(f"{name:8s} {work[:, cols].mean():10.2f} {work[:, cols].max(axis=0).mean():9.2f} "
-              f"{wait[:, cols].mean():10.2f} {lead.mean():14.2f}")
+              f"{prologue[:, cols].mean():9.2f} {wait[:, cols].mean():10.2f} {lead.mean():14.2f}")
     lm = (t[:, 255] - depart[:, -1]) / 1e3
     total = (t[:, 255].max() - t0) / 1e3
     print(f"lm_head  {lm.mean():10.2f} {lm.max():9.2f}")
