@@ -97,6 +97,13 @@ __device__ __forceinline__ uint4 ldg_cg16(const void* p) {
 // Shared memory, mbarriers, bulk copies
 // ---------------------------------------------------------------------------
 
+// Rounds a shared-memory pointer up to `align` bytes (a power of two): every
+// region read with 16-byte vector accesses starts on such a boundary.
+template <typename T>
+__device__ __forceinline__ T* align_smem(void* p, uintptr_t align) {
+  return reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(p) + align - 1) & ~(align - 1));
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
   float* red8 = reinterpret_cast<float*>(cta_best + 1);   // [8]
   float* red = red8 + 8;                                    // [kGemvRedFloats]
-  bf16* xs = reinterpret_cast<bf16*>(red + kGemvRedFloats);  // [K]
+  bf16* xs = align_smem<bf16>(red + kGemvRedFloats, 128);  // [K], 16-byte vector access
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int o0 = gemv_share(a.n_out, blockIdx.x, gridDim.x);
@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
 template <int K, int STAGE_BYTES, int STAGES>
 constexpr size_t gemv_smem_bytes() {
   return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) + 8 +
-         (8 + kGemvRedFloats) * sizeof(float) + static_cast<size_t>(K) * 2 + 64;
+         (8 + kGemvRedFloats) * sizeof(float) + 128 + static_cast<size_t>(K) * 2 + 64;
 }
 
 }  // namespace lcrb

@@ -515,7 +515,7 @@ struct MegaShape {
   static_assert(kMegaWarps * G * (D + 2) <= RED_FLOATS, "attention scratch");
   static constexpr int XS = (H > F ? H : F) > QD ? (H > F ? H : F) : QD;
   static constexpr size_t SMEM = static_cast<size_t>(kMegaStages) * kMegaStageBytes +
-                                 2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 +
+                                 2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 + 128 +
                                  static_cast<size_t>(XS) * 2 + 64;
 };
 
@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
   float* red8 = reinterpret_cast<float*>(s_flags + 4);
   float* red = red8 + 8;
   float* cs = red + Shape::RED_FLOATS;  // RoPE cos/sin [D]
-  bf16* xs = reinterpret_cast<bf16*>(cs + D);  // staged input vector [max(H, QD, F)]
+  bf16* xs = align_smem<bf16>(cs + D, 128);  // staged input vector [max(H, QD, F)], 16-byte access
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pos = __ldcg(a.state + 1);
