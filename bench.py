@@ -12,8 +12,12 @@ L2, so no L2 flush is needed between steps.
   e2e    the same through the C ABI with host buffers: every step copies its
          token and position from pinned host memory, runs, and reads the next
          token back, synchronising each step (the reference's decode loop).
-  roofline  the streaming GEMV (dominant kernel): algorithmic bytes per launch
-         / the CUDA-event launch time measured here, against MEASURED_PEAKS.json.
+  roofline  decode_step_kernel, the dominant kernel (one persistent launch per
+         token): algorithmic bytes per launch (weights + the KV read at the
+         window's mean context) / the CUDA-event time per launch measured
+         here, against MEASURED_PEAKS.json; traffic is the DRAM bytes of one
+         launch from the committed ncu summary. The standalone streaming
+         GEMV of each matrix is timed beside it (per_matrix_layer0).
 
 Multi-GPU (torchrun): every rank decodes its own independent sequence on its
 own GPU with its own weight replica -- the reference has no collective on this
@@ -51,8 +55,8 @@ def measured_peaks():
 
 
 def profile_traffic():
-    """Per-launch DRAM bytes of the gate/up GEMV from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", "gemv_gate_up_1b.md")
+    """DRAM bytes of one decode_step_kernel launch from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "decode_step_1b.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -108,7 +112,9 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def dist_setup(n_gpus):
+def dist_setup(n_gpus, backend=None):
+    """One process per GPU from the torchrun environment. NCCL on GPUs; gloo
+    (host tensors) when asked for or when there is no GPU."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -118,9 +124,12 @@ def dist_setup(n_gpus):
         import torch
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device(f"cuda:{local}"))
+        backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
+        kw = {}
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device(f"cuda:{local}")
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300), **kw)
     return world, rank, local
 
 
@@ -132,14 +141,23 @@ def barrier(world):
 
 
 def reduce_max(world, value):
+    """The largest `value` over all ranks (every rank takes part)."""
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def aggregate(world, rank_ms, steps):
+    """Whole-job throughput of `world` replicas that each decoded `steps`
+    tokens: (slowest rank's ms, all ranks' tokens / that time)."""
+    max_ms = reduce_max(world, rank_ms)
+    return max_ms, world * steps / (max_ms / 1000.0)
 
 
 def cpu_baseline(block, seconds=12.0, max_tokens=64):
@@ -216,32 +234,39 @@ def main():
     first = int(prompt[-1])
     stream = torch.cuda.ExternalStream(m.stream, device=f"cuda:{local}")
 
-    def run_window(n, start_pos):
-        """n device-resident greedy steps from start_pos (<= WINDOW)."""
-        tok = np.array([first], np.int32)
-        m.set_token(tok.ctypes.data, start_pos)
-        m.sync()
-        return m.time_steps(n)
-
-    # warm-up (graph capture happens on first use)
-    run_window(min(args.warmup, WINDOW), PROMPT - 1)
-
-    barrier(world)
-    torch.cuda.synchronize()
-    total_ms, done = 0.0, 0
-    with Clocks(local) as clk:
-        while done < args.steps:
-            n = min(WINDOW, args.steps - done)
-            total_ms += run_window(n, PROMPT - 1)
-            done += n
-    torch.cuda.synchronize()
-    barrier(world)
-    max_ms = reduce_max(world, total_ms)
-    value = world * args.steps / (max_ms / 1000.0)
-
-    # end to end: host token in, host token out, every step
     pinned = torch.empty(2, dtype=torch.int32, pin_memory=True)
     tok_ptr = pinned.data_ptr()
+    pinned[0] = first
+
+    def enqueue(steps):
+        """`steps` device-resident greedy steps in windows of WINDOW tokens:
+        each window restarts at position PROMPT - 1 from the same token (an
+        8-byte async copy from pinned memory), so the context stays in
+        128..383 however many steps run."""
+        done = 0
+        while done < steps:
+            n = min(WINDOW, steps - done)
+            m.set_token(tok_ptr, PROMPT - 1)
+            m.enqueue_steps(n)
+            done += n
+
+    # warm-up (graph capture happens on first use)
+    enqueue(args.warmup)
+    m.sync()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        enqueue(args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    m.sync()
+    barrier(world)
+    max_ms, value = aggregate(world, e0.elapsed_time(e1), args.steps)
+
+    # end to end: host token in, host token out, every step
     e2e_steps = min(args.steps, 1024)
     pinned[0] = first
     m.set_token(tok_ptr, PROMPT - 1)
@@ -264,7 +289,8 @@ def main():
     e2e_ms = reduce_max(world, e0.elapsed_time(e1))
     e2e_value = world * e2e_steps / (e2e_ms / 1000.0)
 
-    # roofline of the dominant kernel: the streaming GEMV (gate/up, 67.1 MB)
+    # roofline of the dominant kernel (decode_step_kernel, one launch per
+    # token); the standalone GEMV of each layer-0 matrix beside it
     peak, peak_kind = measured_peaks()
     per_matrix = {}
     names = ["qkv", "o_proj", "gate_up", "down", "lm_head"]
@@ -272,15 +298,15 @@ def main():
     bytes_of = {"qkv": (q + 2 * kv) * h * 2, "o_proj": h * q * 2, "gate_up": 2 * f * h * 2,
                 "down": h * f * 2, "lm_head": v * h * 2}
     for i, name in enumerate(names):
+        m.time_gemv(i, 0, 3)  # first launch of a kernel loads its module
         ms = m.time_gemv(i, 0, 20)
         per_matrix[name] = {"us": round(ms * 1000, 2),
                             "gbs": round(bytes_of[name] / (ms / 1000) / 1e9, 1)}
-    gu = per_matrix["gate_up"]
-    achieved = bytes_of["gate_up"] / (gu["us"] / 1e6) / 1e9
-
     ms_per_step = max_ms / args.steps
-    ctx_mean = PROMPT + WINDOW / 2
+    # positions 127..382 read 128..383 cached positions: mean 255.5
+    ctx_mean = PROMPT + (WINDOW - 1) / 2
     step_bytes = g.weight_bytes_per_token() + ctx_mean * g.kv_bytes_per_position()
+    achieved = step_bytes / (ms_per_step / 1000) / 1e9
     if rank == 0:
         base = None if args.no_cpu_baseline or world > 1 else cpu_baseline(block)
         clocks = clk.summary()
@@ -298,11 +324,13 @@ def main():
                     "achieved_gbs": round(step_bytes / (ms_per_step / 1000) / 1e9, 1),
                     "frac_of_peak": round(step_bytes / (ms_per_step / 1000) / 1e9 / peak, 4),
                     "peak_gbs": peak},
-            "roofline": {"kernel": "gemv_stream_kernel (gate/up, K=2048, 16384 rows)",
+            "roofline": {"kernel": "decode_step_kernel<2048, 2048, 8192, 64, 4, 0> "
+                                   "(persistent step, one launch per token)",
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profile_traffic(), "peak_source": peak_kind,
-                         "algorithmic_bytes_per_launch": bytes_of["gate_up"],
+                         "algorithmic_bytes_per_launch": int(step_bytes),
+                         "launch_us": round(ms_per_step * 1000, 2),
                          "per_matrix_layer0": per_matrix},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4, "steps": e2e_steps},
