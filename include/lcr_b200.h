@@ -115,6 +115,22 @@ LCR_API int lcr_decode_attention(void* out, const void* q, const lcr_kv_view* vi
                          float scale, int paged, int splits, float* scratch,
                          lcr_stream_t stream);
 
+/* No counterpart in the reference. lcr_decode_attention without caller
+ * scratch, for callers that must not allocate device memory (an allocator
+ * that forbids it, or a fixed memory budget set up before serving): the
+ * split partials live in one static device array of
+ * LCR_NOALLOC_ATTENTION_SCRATCH_FLOATS floats (2 MiB). A call that needs more
+ * (num_heads x splits x (head_dim + 2), splits after the 16-position clamp)
+ * returns LCR_ERR_SHAPE. The first call on each device looks the array up
+ * (cudaGetSymbolAddress, with that device current): make it before any stream
+ * capture. Every call on a device shares the array, so calls whose kernels
+ * may overlap race; order them on one stream. */
+#define LCR_NOALLOC_ATTENTION_SCRATCH_FLOATS (1 << 19)
+LCR_API int lcr_decode_attention_noalloc(void* out, const void* q,
+                                 const lcr_kv_view* view, int num_heads,
+                                 int heads_per_kv, int seq_len, float scale,
+                                 int paged, int splits, lcr_stream_t stream);
+
 /* decode_attention_scratch_floats, src/kernels.cuh:118-120 */
 LCR_API size_t lcr_decode_attention_scratch_floats(int num_heads, int head_dim,
                                            int splits);
