@@ -279,10 +279,13 @@ LCR_API int lcr_device_status(lcr_ctx* ctx);
  * 1 o_proj, 2 gate_up, 3 down, 4 lm_head; reps <= 128), in ms per launch. */
 LCR_API int lcr_time_steps(lcr_ctx* ctx, int steps, float* ms);
 /* With flags bit 3 (trace) on a persistent-step context: copies the last
- * step's per-CTA phase timestamps (globaltimer ns; per CTA 512 slots: [0]
- * consumers start, [2k+1]/[2k+2] arrival at / departure from grid barrier k,
- * [255] consumers end, [256 + p] producer starting phase p); *count gets
- * the number of values copied. */
+ * step's per-CTA phase timestamps (globaltimer ns unless noted; per CTA 1024
+ * slots: [0] consumers start, [2k+1]/[2k+2] arrival at / departure from grid
+ * barrier k, [163 + p] prologue of phase p done, [255] consumers end,
+ * [256 + p] producer starting phase p, [340 + p] / [424 + p] SM cycles the
+ * consumers / the producer waited on the ring in matrix phase p, and for
+ * layer 8's gate/up phase per stage s: [512 + s] issued, [576 + s] ready,
+ * [640 + s] released); *count gets the number of values copied. */
 LCR_API int lcr_copy_trace(lcr_ctx* ctx, unsigned long long* host, int capacity, int* count);
 LCR_API int lcr_time_gemv(lcr_ctx* ctx, int matrix, int layer, int reps, float* ms);
 

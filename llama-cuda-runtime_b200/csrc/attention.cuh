@@ -85,14 +85,17 @@ __device__ __forceinline__ int attn_chunk(int seq_len, int splits) {
 // for this lane's dims with the step's precomputed cos/sin table (cs[i] =
 // cos, cs[HALF + i] = sin of float(pos) * inv_freq[i]), returning the
 // bf16-rounded values the reference stores.
+// Rotate-half RoPE (src/kernels/rope.cu:9-11) of lane `lig`'s 8 dims from
+// the raw 16-byte vectors of its own dims (`self`) and their partners.
 template <int D>
-__device__ __forceinline__ void rope8(const bf16* head, int lig, const float* cs, float* outv) {
+__device__ __forceinline__ void rope8_from(uint4 self_raw, uint4 other_raw, int lig, const float* cs,
+                                           float* outv) {
   constexpr int HALF = D / 2;
   const int d0 = lig * 8;
   float self[8], other[8];
-  unpack8(ldg_cg16(head + d0), self);
+  unpack8(self_raw, self);
+  unpack8(other_raw, other);
   const bool lo = d0 < HALF;
-  unpack8(ldg_cg16(head + (lo ? d0 + HALF : d0 - HALF)), other);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int i = (d0 + e) % HALF;
@@ -100,6 +103,15 @@ __device__ __forceinline__ void rope8(const bf16* head, int lig, const float* cs
     const float v = lo ? (self[e] * c - other[e] * s) : (self[e] * c + other[e] * s);
     outv[e] = rbf(v);
   }
+}
+
+template <int D>
+__device__ __forceinline__ void rope8(const bf16* head, int lig, const float* cs, float* outv) {
+  constexpr int HALF = D / 2;
+  const int d0 = lig * 8;
+  const uint4 self = ldg_cg16(head + d0);
+  const uint4 other = ldg_cg16(head + (d0 < HALF ? d0 + HALF : d0 - HALF));
+  rope8_from<D>(self, other, lig, cs, outv);
 }
 
 // cos/sin of float(pos) * inv_freq[i] for the D/2 rotation pairs (sincosf,

@@ -3,6 +3,7 @@
 // wrappers, bounded waits, and host-side status plumbing for the C ABI.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (type only; the encoder is reached through cudart)
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -47,6 +48,7 @@ enum : uint32_t {
   kStatusBadToken = 1u << 2,      // token id outside the vocabulary
   kStatusBadPosition = 1u << 3,   // position outside the cache
   kStatusBadPage = 1u << 4,       // page table entry outside the pool
+  kStatusBadSmem = 1u << 6,       // ring not 1024-byte aligned for swizzled tensor copies
 };
 
 // ---------------------------------------------------------------------------
@@ -185,6 +187,35 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       " [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+
+// Tiled tensor copies global -> shared (TMA with a tensor map in global or
+// param memory), completing on an mbarrier's transaction count, L2 hint as
+// for bulk_g2s. No cluster multicast. The innermost coordinate is always 0
+// here (whole 64-element chunks), so every copy starts 16-byte aligned.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// One 128-byte L2 line through the load/store path (not the TMA queue).
+__device__ __forceinline__ void prefetch_line_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {

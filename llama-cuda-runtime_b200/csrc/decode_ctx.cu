@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "dispatch.h"
 #include "gemv_dispatch.h"
+#include "tmap.h"
 #include "lcr_b200.h"
 #include "mega_dispatch.h"
 
@@ -125,6 +126,11 @@ struct lcr_ctx {
   int splits = 1;
 
   MegaLayer* mega_layers = nullptr;  // device copy of the per-layer pointers
+  // Tensor maps of every streamed matrix (make_weight_map): [layer * 4 + m],
+  // m = 0 qkv, 1 o, 2 gate/up, 3 down; then the lm_head. Host copy for the
+  // multi-kernel launches, device copy for the persistent kernel.
+  std::vector<CUtensorMap> wmaps;
+  CUtensorMap* wmaps_dev = nullptr;
   unsigned* mega_bar = nullptr;
   unsigned long long* trace = nullptr;  // kFlagTrace: per-CTA phase timestamps
   unsigned long long prefetch_bytes = 0;  // persistent step: L2 prefetch lead per CTA
@@ -145,7 +151,7 @@ namespace {
 int q_dim(const lcr_ctx* c) { return c->d.num_heads * c->d.head_dim; }
 int kv_dim(const lcr_ctx* c) { return c->d.num_kv_heads * c->d.head_dim; }
 
-int gemv_node(lcr_ctx* c, GemvArgs a, int K, int pro, int epi, int n_out, int* slot) {
+int gemv_node(lcr_ctx* c, GemvArgs a, int K, int pro, int epi, int n_out, int* slot, int map) {
   const int per = gemv_outputs_per_chunk(K, epi);
   a.n_out = n_out;
   LCRB_REQUIRE(*slot < c->sched_slots, LCR_ERR_STATE, "GEMV scheduler slots exhausted");
@@ -155,7 +161,7 @@ int gemv_node(lcr_ctx* c, GemvArgs a, int K, int pro, int epi, int n_out, int* s
   const int want = c->o.gemv_ctas > 0 ? c->o.gemv_ctas : c->sms;
   const int ctas = std::max(1, std::min((n_out + per - 1) / per, want));
   ++c->launches;
-  return gemv_launch(a, K, pro, epi, true, ctas, c->stream, c->pdl);
+  return gemv_launch(a, c->wmaps[static_cast<size_t>(map)], K, pro, epi, ctas, c->stream, c->pdl);
 }
 
 int attention_node(lcr_ctx* c, int layer) {
@@ -211,6 +217,7 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.final_norm = c->final_norm;
   a.lm_head = c->lm_head;
   a.L = c->mega_layers;
+  a.wmaps = c->wmaps_dev;
   a.inv_freq = c->inv_freq;
   a.state = c->state;
   a.x = c->x;
@@ -273,7 +280,7 @@ int enqueue_step(lcr_ctx* c) {
         a.x_in = c->x;
         a.xsum = c->xsum;
       }
-      LCRB_TRY(gemv_node(c, a, H, pro, EPI_STORE, q_dim(c) + 2 * kv_dim(c), &slot));
+      LCRB_TRY(gemv_node(c, a, H, pro, EPI_STORE, q_dim(c) + 2 * kv_dim(c), &slot, 4 * l));
     }
     LCRB_TRY(attention_node(c, l));
     {
@@ -282,7 +289,7 @@ int enqueue_step(lcr_ctx* c) {
       a.x_in = c->attn;
       a.resid = c->x;
       a.resid_sum = c->xsum;
-      LCRB_TRY(gemv_node(c, a, q_dim(c), PRO_PLAIN, EPI_RESID, H, &slot));
+      LCRB_TRY(gemv_node(c, a, q_dim(c), PRO_PLAIN, EPI_RESID, H, &slot, 4 * l + 1));
     }
     {
       GemvArgs a = {};
@@ -291,7 +298,7 @@ int enqueue_step(lcr_ctx* c) {
       a.xsum = c->xsum;
       a.norm_w = static_cast<const bf16*>(w.post_attention_norm);
       a.y = c->act;
-      LCRB_TRY(gemv_node(c, a, H, PRO_NORM, EPI_SWIGLU, F, &slot));
+      LCRB_TRY(gemv_node(c, a, H, PRO_NORM, EPI_SWIGLU, F, &slot, 4 * l + 2));
     }
     {
       GemvArgs a = {};
@@ -299,7 +306,7 @@ int enqueue_step(lcr_ctx* c) {
       a.x_in = c->act;
       a.resid = c->x;
       a.resid_sum = c->xsum;
-      LCRB_TRY(gemv_node(c, a, F, PRO_PLAIN, EPI_RESID, H, &slot));
+      LCRB_TRY(gemv_node(c, a, F, PRO_PLAIN, EPI_RESID, H, &slot, 4 * l + 3));
     }
   }
   GemvArgs a = {};
@@ -314,7 +321,7 @@ int enqueue_step(lcr_ctx* c) {
   a.history = c->history;
   a.history_len = c->o.max_seq;
   a.advance = 1;
-  return gemv_node(c, a, H, PRO_NORM, EPI_LOGITS_ARGMAX, d.vocab_size, &slot);
+  return gemv_node(c, a, H, PRO_NORM, EPI_LOGITS_ARGMAX, d.vocab_size, &slot, 4 * d.num_layers);
 }
 
 int build_graph(lcr_ctx* c) {
@@ -387,6 +394,7 @@ void release(lcr_ctx* c) {
   cudaFree(c->vpool);
   cudaFree(c->tables_dev);
   cudaFree(c->mega_layers);
+  cudaFree(c->wmaps_dev);
   cudaFree(c->mega_bar);
   cudaFree(c->trace);
   cudaFreeHost(c->pinned);
@@ -475,11 +483,13 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
 
   const int group = d.num_heads / d.num_kv_heads;
   // LCR_PREFETCH_KIB: the persistent step's L2 prefetch lead per CTA, a tuning
-  // knob for measurements (default below).
+  // knob for measurements. 384 KiB per CTA (57 MB over 148 CTAs) measured
+  // best on the 1B model; from 768 KiB on, prefetched lines are evicted from
+  // L2 before the ring reads them.
   if (const char* env = std::getenv("LCR_PREFETCH_KIB")) {
     c->prefetch_bytes = static_cast<unsigned long long>(std::max(0, std::atoi(env))) << 10;
   } else {
-    c->prefetch_bytes = 0;
+    c->prefetch_bytes = 384ull << 10;
   }
   c->persistent = (o.flags & kFlagNoPersistent) == 0 &&
                   mega_supported(d.hidden_size, qd, d.intermediate_size, d.head_dim, group);
@@ -580,6 +590,24 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     if (st == LCR_OK) cuda(cudaMalloc(&c->vpool, elems * sizeof(bf16)), "cudaMalloc(V pool)");
     if (st == LCR_OK) cuda(cudaMemset(c->kpool, 0, elems * sizeof(bf16)), "cudaMemset(K pool)");
     if (st == LCR_OK) cuda(cudaMemset(c->vpool, 0, elems * sizeof(bf16)), "cudaMemset(V pool)");
+  }
+  // Tensor maps of the streamed matrices (one TMA copy per GEMV stage).
+  if (st == LCR_OK) {
+    c->wmaps.resize(static_cast<size_t>(4 * d.num_layers + 1));
+    for (int l = 0; l < d.num_layers && st == LCR_OK; ++l) {
+      const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+      CUtensorMap* m = &c->wmaps[static_cast<size_t>(4 * l)];
+      st = make_weight_map(m, w.qkv_proj, qd + 2 * kvd, d.hidden_size, false);
+      if (st == LCR_OK) st = make_weight_map(m + 1, w.o_proj, d.hidden_size, qd, false);
+      if (st == LCR_OK) st = make_weight_map(m + 2, w.gate_up_proj, d.intermediate_size, d.hidden_size, true);
+      if (st == LCR_OK) st = make_weight_map(m + 3, w.down_proj, d.hidden_size, d.intermediate_size, false);
+    }
+    if (st == LCR_OK) st = make_weight_map(&c->wmaps.back(), c->lm_head, d.vocab_size, d.hidden_size, false);
+    if (st == LCR_OK) cuda(cudaMalloc(&c->wmaps_dev, c->wmaps.size() * sizeof(CUtensorMap)), "cudaMalloc(tensor maps)");
+    if (st == LCR_OK) {
+      cuda(cudaMemcpy(c->wmaps_dev, c->wmaps.data(), c->wmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice),
+           "upload tensor maps");
+    }
   }
   if (st == LCR_OK && c->persistent) {
     std::vector<MegaLayer> ml(static_cast<size_t>(d.num_layers));
@@ -929,7 +957,7 @@ extern "C" int lcr_time_gemv(lcr_ctx* c, int matrix, int layer, int reps, float*
   int st = LCR_OK;
   for (int i = 0; i < reps && st == LCR_OK; ++i) {
     int slot = c->sched_slots - kTimingSlots + i;
-    st = gemv_node(c, a, K, pro, epi, n, &slot);
+    st = gemv_node(c, a, K, pro, epi, n, &slot, matrix < 4 ? 4 * layer + matrix : 4 * d.num_layers);
   }
   cudaEventRecord(e1, c->stream);
   cudaEventSynchronize(e1);

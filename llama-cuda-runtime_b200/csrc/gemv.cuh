@@ -17,18 +17,20 @@
 //                          argmax of sampling.cu:42-67; the last CTA to finish
 //                          writes the next token into device state
 //
-// Structure (one CTA per SM by default, 288 threads):
-//   warp 8, lane 0  producer: takes the next chunk of rows from a global
-//                   counter (dynamic scheduling, so CTAs that start late or
-//                   share an SM still balance; the allocation-free standalone
-//                   entry uses a fixed strided schedule instead), and streams
-//                   it into a ring of
-//                   shared-memory stages with cp.async.bulk (TMA, 1-D, L2
-//                   evict-first), completing on the stage's mbarrier.
-//   warps 0-7       consumers: each thread owns CPT 16-byte column chunks of
-//                   the input vector in registers for the whole kernel; per
-//                   stage it forms RPT row partials, the warp reduces them with
-//                   a transposing butterfly, warps combine through shared memory.
+// Structure (288 threads per CTA):
+//   warp 8, lane 0  producer: streams the CTA's contiguous share of rows into a
+//                   ring of shared-memory stages, one cp.async.bulk (1-D TMA,
+//                   L2 evict-first) per row segment, completing on the
+//                   stage's mbarrier. Rows land at a pitch of 16 bytes more
+//                   than their length, so the eight rows an ldmatrix reads
+//                   sit in distinct banks.
+//   warps 0-7       consumers: the dot products run on the tensor pipe as
+//                   mma.sync m16n8k16 (bf16 in, fp32 accumulate): per 32
+//                   columns one ldmatrix.x4 loads 8 weight rows (the B
+//                   operand, B[k][n] = W[n][k]) and one loads the matching
+//                   32 staged x values (A rows 0-7 all x, rows 8-15 zero);
+//                   lane t then holds rows 2t and 2t+1 of the 8. Warps split
+//                   a stage's columns; their partials meet in shared memory.
 // Weights do not depend on the previous kernel, so the producer starts before
 // griddepcontrol.wait: with programmatic dependent launch the next matrix is
 // already in flight while the previous kernel drains.
@@ -68,27 +70,36 @@ struct GemvArgs {
   int32_t* history;       //   history[pos] = next token (nullable)
   int history_len;
   int advance;
+  unsigned long long* wait_cycles;  // trace: SM cycles thread 0 waited on full stages (nullable)
+  unsigned long long* stage_ns;     // trace: [s] stage s ready, [64 + s] released (nullable)
 };
 
-template <int K, int STAGE_BYTES>
+// Stage geometry for a K-column matrix. A stage holds RPS rows of KC columns
+// (the whole row for K <= 2048, a 2048-column segment beyond), 32 KB of
+// weights; CHUNKS stages make one group of rows. A whole group arrives as one
+// tensor copy per stage in the swizzled chunk-major layout of make_weight_map
+// (byte (c / 64 * RPS + r) * 128 + ((c % 64 / 8) ^ (r % 8)) * 16 + c % 8 * 2
+// holds row r, column c); the last, partial group of a CTA's share arrives
+// as one bulk copy per row at PITCH = 2 KC + 16 bytes. In both layouts the
+// eight rows of an 8x8 ldmatrix tile fall in distinct banks.
+template <int K>
 struct GemvGeom {
-  static constexpr int KC = K / 8;                       // 16-byte chunks per row
-  // A warp per row up to K = 2048 (64 elements a lane), more warps beyond, so
-  // the reduction is amortised over many multiply-adds.
-  static constexpr int TPR = (K / 64) > 32 ? (K / 64) : 32;  // threads per row
-  static constexpr int CPT = KC / TPR;                   // chunks per thread (<= 8)
-  static constexpr int SLOTS = 256 / TPR;                // rows in flight per pass
-  static constexpr int WPR = TPR / 32;                   // warps per row
+  static constexpr int KC = K < 2048 ? K : 2048;  // columns per stage
+  static constexpr int CHUNKS = K / KC;           // stages per row group
+  static constexpr int G8 = 2048 / KC;            // 8-row MMA tiles per stage
+  static constexpr int RPS = 8 * G8;              // rows per stage
+  static constexpr int WPG = 8 / G8;              // consumer warps per tile
+  static constexpr int KW = KC / WPG;             // columns per warp per stage
+  static constexpr int STEPS = KW / 32;           // ldmatrix.x4 pairs per warp per stage
   static constexpr int ROW_BYTES = K * 2;
-  static constexpr int RPS = STAGE_BYTES / ROW_BYTES;    // rows per stage
-  static constexpr int RPT = RPS / SLOTS;                // rows per thread per stage
-  // Stages per reduction segment: 2048 floats (8 KB) of row partials.
-  static constexpr int SEG = 2048 / (RPS * WPR) > 0 ? 2048 / (RPS * WPR) : 1;
-  static_assert(K % 256 == 0 && KC % 32 == 0, "K must be a multiple of 256");
-  static_assert(TPR * CPT == KC && CPT <= 8, "K/8 must split evenly over the row's threads");
-  static_assert(TPR <= 256 && 256 % TPR == 0, "rows must split the 8 consumer warps");
-  static_assert(RPS >= SLOTS && RPS % SLOTS == 0, "stage too small for this K");
-  static_assert(RPT == 1 || RPT == 2 || RPT == 4 || RPT == 8 || RPT == 16, "RPT");
+  static constexpr int SEG_BYTES = KC * 2;        // bytes of one row copy
+  static constexpr int PITCH = SEG_BYTES + 16;
+  static constexpr int BYTES = RPS * PITCH;       // padded layout (a group's tail)
+  static constexpr int TILE_BYTES = RPS * KC * 2;  // swizzled layout (whole groups)
+  // Row groups per reduction segment: 2048 floats (8 KB) of warp partials.
+  static constexpr int SEG = 2048 / (RPS * WPG);
+  static_assert(K % 256 == 0 && (K <= 2048 || K % 2048 == 0), "K must be 256..2048 or a multiple of 2048");
+  static_assert(KW == 256 && STEPS == 8, "every consumer warp covers 256 columns of a stage");
 };
 
 constexpr int kGemvConsumers = 256;
@@ -96,52 +107,13 @@ constexpr int kGemvConsumers = 256;
 // epilogue pass (GemvGeom::SEG stages' worth).
 constexpr int kGemvRedFloats = 2048;
 constexpr int kGemvThreads = kGemvConsumers + 32;
+// Ring slot stride: every GemvGeom<K>::BYTES (at most 64 rows x (512 + 16)
+// bytes) fits.
+constexpr int kGemvSlotBytes = 33792;
 
 __device__ __forceinline__ uint32_t order_key(float v) {
   const uint32_t b = __float_as_uint(v);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
-// Transposing butterfly: each lane enters with RPT row partials, and leaves
-// holding the warp total of row warp_row_of_lane() (lanes whose low bits are
-// zero are the unique holders).
-template <int RPT>
-__device__ __forceinline__ float warp_reduce_rows(float (&v)[RPT], int lane) {
-  int n = RPT;
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    if (n > 1) {
-      const bool upper = (lane & off) != 0;
-#pragma unroll
-      for (int i = 0; i < RPT / 2; ++i) {
-        if (i < n / 2) {
-          const float send = upper ? v[i] : v[i + n / 2];
-          const float keep = upper ? v[i + n / 2] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-      }
-      n >>= 1;
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-    }
-  }
-  return v[0];
-}
-
-template <int RPT>
-__device__ __forceinline__ int warp_row_of_lane(int lane) {
-  // Halving step k (offset 16 >> k) sends the lane with that bit set to the
-  // upper half of the remaining rows.
-  int r = 0;
-#pragma unroll
-  for (int k = 0, n = RPT; n > 1; ++k, n >>= 1) r += ((lane >> (4 - k)) & 1) * (n >> 1);
-  return r;
-}
-
-template <int RPT>
-__device__ __forceinline__ bool warp_row_owner(int lane) {
-  constexpr int m = (RPT >= 16) ? 4 : (RPT >= 8) ? 3 : (RPT >= 4) ? 2 : (RPT >= 2) ? 1 : 0;
-  return (lane & ((1 << (5 - m)) - 1)) == 0;
 }
 
 // Outputs [o0, o1) of the contiguous share CTA `cta` of `ctas` owns.
@@ -164,35 +136,69 @@ struct NoPrefetch {
 };
 
 // Producer: streams weight rows [o0, o1) (SWIGLU: pairs, gate and up rows) of
-// a [rows][K] matrix into the ring. Returns false if a bounded wait expired.
-template <int K, int STAGE_BYTES, int STAGES, bool SWIGLU, class PF = NoPrefetch>
+// a [rows][K] matrix into the ring: whole groups with one tensor copy per
+// stage through `map` (make_weight_map of the same matrix), the last partial
+// group one bulk copy per row from `w`. The consumers' results for rows past
+// o1 are never stored. Returns false if a bounded wait expired or the ring is
+// not 1024-byte aligned. `wait_cycles` (nullable) accumulates SM cycles spent
+// waiting for free slots; `issue_ns` (nullable) records when each of the
+// first 64 stages was issued.
+template <int K, int STAGES, bool SWIGLU, class PF = NoPrefetch>
 __device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                             int& it, const bf16* w, int n_out, int o0, int o1,
-                                             uint64_t policy, uint32_t* status,
-                                             PF* pf = nullptr, unsigned long long* issued = nullptr) {
-  using G = GemvGeom<K, STAGE_BYTES>;
-  constexpr int PAIRS = G::RPS / 2;
-  constexpr int UNIT = SWIGLU ? PAIRS : G::RPS;
+                                             int& it, const CUtensorMap* map, const bf16* w, int n_out,
+                                             int o0, int o1, uint64_t policy, uint32_t* status,
+                                             PF* pf = nullptr, unsigned long long* issued = nullptr,
+                                             unsigned long long* wait_cycles = nullptr,
+                                             unsigned long long* issue_ns = nullptr) {
+  using G = GemvGeom<K>;
+  constexpr int UNIT = SWIGLU ? G::RPS / 2 : G::RPS;
+  constexpr int CHUNK_STEP = G::KC / 64;  // tensor-map chunk coordinate per stage
+  if ((smem_addr(ring) & 1023u) != 0) {
+    if (status) atomicOr(status, kStatusBadSmem);
+    return false;
+  }
   const char* wbase = reinterpret_cast<const char*>(w);
-  for (int first = o0; first < o1; first += UNIT, ++it) {
-    if (pf) pf->top_up(*issued);
-    const int slot = it % STAGES;
-    if (it >= STAGES &&
-        !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, status, kStatusTimeoutEmpty)) {
-      return false;
+  for (int first = o0; first < o1; first += UNIT) {
+    const int rows = min(UNIT, o1 - first);
+    for (int c = 0; c < G::CHUNKS; ++c, ++it) {
+      if (pf) pf->top_up(*issued);
+      const int slot = it % STAGES;
+      const long long w0 = wait_cycles ? clock64() : 0;
+      if (it >= STAGES &&
+          !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, status, kStatusTimeoutEmpty)) {
+        return false;
+      }
+      if (wait_cycles) *wait_cycles += static_cast<unsigned long long>(clock64() - w0);
+      if (issue_ns) {
+        const int k = (first - o0) / UNIT * G::CHUNKS + c;
+        if (k < 64) issue_ns[k] = globaltimer_ns();
+      }
+      uint8_t* dst = ring + slot * kGemvSlotBytes;
+      unsigned long long bytes;
+      if (rows == UNIT) {
+        bytes = G::TILE_BYTES;
+        mbar_arrive_expect_tx(&full[slot], G::TILE_BYTES);
+        if constexpr (SWIGLU) {
+          tma_load_4d(dst, map, 0, first, 0, c * CHUNK_STEP, &full[slot], policy);
+        } else {
+          tma_load_3d(dst, map, 0, first, c * CHUNK_STEP, &full[slot], policy);
+        }
+      } else {
+        bytes = static_cast<unsigned long long>(SWIGLU ? 2 : 1) * rows * G::SEG_BYTES;
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(bytes));
+        const char* src = wbase + (static_cast<size_t>(first) * K + c * G::KC) * 2;
+        for (int r = 0; r < rows; ++r) {
+          bulk_g2s(dst + r * G::PITCH, src + static_cast<size_t>(r) * G::ROW_BYTES, G::SEG_BYTES,
+                   &full[slot], policy);
+          if constexpr (SWIGLU) {
+            bulk_g2s(dst + (UNIT + r) * G::PITCH,
+                     src + (static_cast<size_t>(n_out) + r) * G::ROW_BYTES, G::SEG_BYTES, &full[slot],
+                     policy);
+          }
+        }
+      }
+      if (issued) *issued += bytes;
     }
-    uint8_t* dst = ring + slot * STAGE_BYTES;
-    const uint32_t bytes = static_cast<uint32_t>(min(UNIT, o1 - first)) * G::ROW_BYTES;
-    if constexpr (SWIGLU) {
-      mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-      bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
-      bulk_g2s(dst + PAIRS * G::ROW_BYTES, wbase + static_cast<size_t>(n_out + first) * G::ROW_BYTES,
-               bytes, &full[slot], policy);
-    } else {
-      mbar_arrive_expect_tx(&full[slot], bytes);
-      bulk_g2s(dst, wbase + static_cast<size_t>(first) * G::ROW_BYTES, bytes, &full[slot], policy);
-    }
-    if (issued) *issued += (SWIGLU ? 2ull : 1ull) * bytes;
   }
   return true;
 }
@@ -290,107 +296,141 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, bf16* xs, float*
   named_sync(1, kGemvConsumers);  // xs complete (and red8 free again)
 }
 
-// Each thread's column chunks of the staged input vector, widened to fp32.
-template <int K, int STAGE_BYTES>
-__device__ __forceinline__ void gemv_x_regs(const bf16* xs,
-                                            float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8]) {
-  using G = GemvGeom<K, STAGE_BYTES>;
-  const int ci = threadIdx.x % G::TPR;
-#pragma unroll
-  for (int j = 0; j < G::CPT; ++j) unpack8(reinterpret_cast<const uint4*>(xs)[ci + j * G::TPR], xr[j]);
+// ldmatrix.x4: lane l supplies the shared address of row l % 8 of 8x8 tile
+// l / 8; r[i] receives tile i's elements (lane / 4, 2 (lane % 4) .. + 1).
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
 }
 
-template <int K, int STAGE_BYTES, int PRO>
-__device__ __forceinline__ void gemv_load_x(const GemvArgs& a,
-                                            float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8],
-                                            bf16* xs, float* red8) {
-  gemv_stage_x<K, PRO>(a, xs, red8);
-  gemv_x_regs<K, STAGE_BYTES>(xs, xr);
+// d += A B for one m16n8k16 tile, bf16 operands, fp32 accumulation; A rows
+// 8-15 are zero (a1 = a3 = 0), so d[2], d[3] stay as they were.
+__device__ __forceinline__ void mma_x_rows(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                           uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
 // Consumers (256 threads): dot products of the streamed rows [o0, o1) with
-// the register-resident x, segmented cross-warp reduction in `red`
-// (kGemvRedFloats floats) and the epilogue. LOGITS_ARGMAX folds the
-// packed (order key, ~index) maximum into `best`. Uses named barrier 1.
-template <int K, int STAGE_BYTES, int STAGES, int EPI>
+// the staged input `xs` (bf16 [K] in shared memory, 16-byte aligned) on the
+// tensor pipe, partials of the WPG warps sharing a row tile combined through
+// `red` (kGemvRedFloats floats) once per segment, then the epilogue.
+// LOGITS_ARGMAX folds the packed (order key, ~index) maximum into `best`.
+// Uses named barrier 1.
+template <int K, int STAGES, int EPI>
 __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full, uint64_t* empty,
                                              int& it, const GemvArgs& a, int o0, int o1,
-                                             const float (&xr)[GemvGeom<K, STAGE_BYTES>::CPT][8],
-                                             float* red, unsigned long long& best, bool& failed) {
-  using G = GemvGeom<K, STAGE_BYTES>;
-  constexpr int RPS = G::RPS, RPT = G::RPT, CPT = G::CPT, TPR = G::TPR, WPR = G::WPR;
+                                             const bf16* xs, float* red, unsigned long long& best,
+                                             bool& failed) {
+  using G = GemvGeom<K>;
+  constexpr int RPS = G::RPS, WPG = G::WPG, STEPS = G::STEPS, CHUNKS = G::CHUNKS;
   constexpr int PAIRS = RPS / 2;
   constexpr int UNIT = (EPI == EPI_SWIGLU) ? PAIRS : RPS;
   constexpr int SEG = G::SEG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int slotrow = tid / TPR, ci = tid % TPR;
-  const int n_stages = (o1 - o0 + UNIT - 1) / UNIT;
-  for (int seg0 = 0; seg0 < n_stages; seg0 += SEG) {
-    const int seg1 = min(n_stages, seg0 + SEG);
-    for (int st = seg0; st < seg1; ++st, ++it) {
-      const int slot = it % STAGES;
-      if (!failed) failed = !mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
-      const uint8_t* stage = ring + slot * STAGE_BYTES;
-      float part[RPT];
+  const int tile = warp / WPG, ks = warp % WPG;
+  // This lane's ldmatrix row addresses: weight row (tile * 8 + lane % 8) and
+  // the x chunk of tile lane / 8, at the warp's first column of a stage --
+  // padded layout: w_lane + 64 j for the j-th 32 columns; swizzled layout:
+  // 64-column chunk ks * 4 + j / 2, 16-byte piece (j % 2) * 4 + lane / 8
+  // rotated by the row.
+  const int r8 = lane & 7, piece = lane >> 3;
+  const uint32_t w_lane = static_cast<uint32_t>((tile * 8 + r8) * G::PITCH + (ks * G::KW + piece * 8) * 2);
+  const uint32_t s_lane = static_cast<uint32_t>(((ks * 4) * G::RPS + tile * 8 + r8) * 128);
+  const uint32_t s_even = static_cast<uint32_t>((piece ^ r8) << 4);
+  const uint32_t s_odd = static_cast<uint32_t>(((4 + piece) ^ r8) << 4);
+  const uint32_t x_lane = smem_addr(xs) + static_cast<uint32_t>((ks * G::KW + (lane >> 3) * 8) * 2);
+  const uint32_t ring_base = smem_addr(ring);
+  // With one stage per group the warp's x fragments never change.
+  uint32_t xf[CHUNKS == 1 ? STEPS : 1][4];
+  if constexpr (CHUNKS == 1) {
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int row = slotrow * RPT + r;
-        // Packed fp32x2 multiply-adds (sm_100 FFMA2), two accumulator pairs.
-        float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+    for (int j = 0; j < STEPS; ++j) ldmatrix_x4(xf[j], x_lane + j * 64);
+  }
+  const int n_units = (o1 - o0 + UNIT - 1) / UNIT;
+  const bool timed = a.wait_cycles != nullptr && tid == 0;
+  unsigned long long waited = 0;
+  for (int seg0 = 0; seg0 < n_units; seg0 += SEG) {
+    const int seg1 = min(n_units, seg0 + SEG);
+    for (int u = seg0; u < seg1; ++u) {
+      float acc[4][4] = {};
+      const bool whole = o1 - (o0 + u * UNIT) >= UNIT;  // tensor-copied, swizzled
+#pragma unroll 1
+      for (int c = 0; c < CHUNKS; ++c, ++it) {
+        const int slot = it % STAGES;
+        const long long w0 = timed ? clock64() : 0;
+        if (!failed) failed = !mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
+        if (timed) waited += static_cast<unsigned long long>(clock64() - w0);
+        const int sk = u * CHUNKS + c;
+        if (a.stage_ns && tid == 0 && sk < 64) a.stage_ns[sk] = globaltimer_ns();
+        const uint32_t st_base = ring_base + static_cast<uint32_t>(slot * kGemvSlotBytes);
 #pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(stage + row * G::ROW_BYTES + (ci + j * TPR) * 16);
-          a0 = __ffma2_rn(make_float2(bf_lo(wv.x), bf_hi(wv.x)), make_float2(xr[j][0], xr[j][1]), a0);
-          a1 = __ffma2_rn(make_float2(bf_lo(wv.y), bf_hi(wv.y)), make_float2(xr[j][2], xr[j][3]), a1);
-          a0 = __ffma2_rn(make_float2(bf_lo(wv.z), bf_hi(wv.z)), make_float2(xr[j][4], xr[j][5]), a0);
-          a1 = __ffma2_rn(make_float2(bf_lo(wv.w), bf_hi(wv.w)), make_float2(xr[j][6], xr[j][7]), a1);
+        for (int j = 0; j < STEPS; ++j) {
+          uint32_t wb[4], xa[4];
+          const uint32_t sw = s_lane + static_cast<uint32_t>((j >> 1) * G::RPS * 128) + ((j & 1) ? s_odd : s_even);
+          ldmatrix_x4(wb, st_base + (whole ? sw : w_lane + j * 64));
+          if constexpr (CHUNKS == 1) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) xa[q] = xf[j][q];
+          } else {
+            ldmatrix_x4(xa, x_lane + static_cast<uint32_t>(c * G::KC * 2) + j * 64);
+          }
+          mma_x_rows(acc[(2 * j) & 3], xa[0], xa[1], wb[0], wb[1]);
+          mma_x_rows(acc[(2 * j + 1) & 3], xa[2], xa[3], wb[2], wb[3]);
         }
-        part[r] = (a0.x + a1.x) + (a0.y + a1.y);
+        __syncwarp();
+        if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
+        if (a.stage_ns && tid == 0 && sk < 64) a.stage_ns[64 + sk] = globaltimer_ns();
       }
-      __syncwarp();
-      if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
-      const float wsum = warp_reduce_rows<RPT>(part, lane);
-      if (warp_row_owner<RPT>(lane)) {
-        const int row = slotrow * RPT + warp_row_of_lane<RPT>(lane);
-        red[((st - seg0) * RPS + row) * WPR + (warp % WPR)] = wsum;
+      if (lane < 4) {
+        const int row = tile * 8 + 2 * lane;
+        float* dst = red + ((u - seg0) * RPS + row) * WPG + ks;
+        dst[0] = (acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]);
+        dst[WPG] = (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]);
       }
     }
     named_sync(1, kGemvConsumers);  // the segment's partials are in shared memory
     const int first = o0 + seg0 * UNIT;
     const int outs = min(o1, o0 + seg1 * UNIT) - first;
-    for (int u = tid; u < outs && !failed; u += kGemvConsumers) {
-      const int st = u / UNIT, r = u % UNIT;
-      const float* rr = red + (st * RPS + r) * WPR;
-      float v = 0.f;
+    for (int v = tid; v < outs && !failed; v += kGemvConsumers) {
+      const int un = v / UNIT, r = v % UNIT;
+      const float* rr = red + (un * RPS + r) * WPG;
+      float y = 0.f;
 #pragma unroll
-      for (int w = 0; w < WPR; ++w) v += rr[w];
-      const int out = first + u;
+      for (int w = 0; w < WPG; ++w) y += rr[w];
+      const int out = first + v;
       if constexpr (EPI == EPI_STORE) {
-        a.y[out] = __ushort_as_bfloat16(f2bf(v));
+        a.y[out] = __ushort_as_bfloat16(f2bf(y));
       } else if constexpr (EPI == EPI_STORE_F32) {
-        a.yf[out] = v;
+        a.yf[out] = y;
       } else if constexpr (EPI == EPI_RESID) {
-        const float s = __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)), rbf(v));
+        const float s = __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)), rbf(y));
         a.resid[out] = __ushort_as_bfloat16(f2bf(s));
         a.resid_sum[out] = s;
       } else if constexpr (EPI == EPI_SWIGLU) {
-        const float* ru = red + (st * RPS + r + PAIRS) * WPR;
+        const float* ru = red + (un * RPS + r + PAIRS) * WPG;
         float up = 0.f;
 #pragma unroll
-        for (int w = 0; w < WPR; ++w) up += ru[w];
-        const float g = rbf(v);
+        for (int w = 0; w < WPG; ++w) up += ru[w];
+        const float g = rbf(y);
         const float silu = g / (1.0f + __expf(-g));
         a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
       } else if constexpr (EPI == EPI_LOGITS_ARGMAX) {
-        a.yf[out] = v;
+        a.yf[out] = y;
         const unsigned long long packed =
-            (static_cast<unsigned long long>(order_key(v)) << 32) |
+            (static_cast<unsigned long long>(order_key(y)) << 32) |
             static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(out));
         best = best > packed ? best : packed;
       }
     }
     named_sync(1, kGemvConsumers);  // the next segment may overwrite `red`
   }
+  if (timed) *a.wait_cycles = waited;
 }
 
 // Argmax hand-off after the lm_head: the CTA maximum into the global
@@ -412,12 +452,12 @@ __device__ __forceinline__ void argmax_finish(const GemvArgs& a, unsigned long l
   }
 }
 
-template <int K, int STAGE_BYTES, int STAGES, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const GemvArgs a) {
-  using G = GemvGeom<K, STAGE_BYTES>;
+template <int K, int STAGES, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    gemv_stream_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kGemvSlotBytes);
   uint64_t* empty = full + STAGES;
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
   float* red8 = reinterpret_cast<float*>(cta_best + 1);   // [8]
@@ -443,18 +483,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
     // Weights do not depend on the previous kernel: stream before the wait.
     if (lane == 0) {
       int it = 0;
-      gemv_produce<K, STAGE_BYTES, STAGES, EPI == EPI_SWIGLU>(ring, full, empty, it, a.w, a.n_out, o0, o1,
-                                                          l2_policy_evict_first(), a.status);
+      gemv_produce<K, STAGES, EPI == EPI_SWIGLU>(ring, full, empty, it, &wmap, a.w, a.n_out, o0, o1,
+                                              l2_policy_evict_first(), a.status);
       ring_drain<STAGES>(full, it, a.status);
     }
   } else {
-    float xr[G::CPT][8];
     pdl_wait();
-    gemv_load_x<K, STAGE_BYTES, PRO>(a, xr, xs, red8);
+    gemv_stage_x<K, PRO>(a, xs, red8);
     int it = 0;
     unsigned long long best = 0ull;
     bool failed = false;
-    gemv_consume<K, STAGE_BYTES, STAGES, EPI>(ring, full, empty, it, a, o0, o1, xr, red, best, failed);
+    gemv_consume<K, STAGES, EPI>(ring, full, empty, it, a, o0, o1, xs, red, best, failed);
     if constexpr (EPI == EPI_LOGITS_ARGMAX) {
       if (best != 0ull) atomicMax(cta_best, best);
     }
@@ -465,9 +504,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream_kernel(const Gemv
   }
 }
 
-template <int K, int STAGE_BYTES, int STAGES>
+template <int K, int STAGES>
 constexpr size_t gemv_smem_bytes() {
-  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * sizeof(uint64_t) + 8 +
+  return static_cast<size_t>(STAGES) * kGemvSlotBytes + 2 * STAGES * sizeof(uint64_t) + 8 +
          (8 + kGemvRedFloats) * sizeof(float) + 128 + static_cast<size_t>(K) * 2 + 64;
 }
 

@@ -18,6 +18,7 @@
 #include "lcr_b200.h"
 #include "sampling.cuh"
 #include "small_kernels.cuh"
+#include "tmap.h"
 
 namespace lcrb {
 
@@ -283,6 +284,8 @@ extern "C" int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, in
     }
     const int per = gemv_outputs_per_chunk(in_features, epi);
     const int chunks = (out_features + per - 1) / per;
+    CUtensorMap map;
+    LCRB_TRY(make_weight_map(&map, w, out_features, in_features, false));
     for (int r = 0; r < rows; ++r) {
       GemvArgs a = {};
       a.w = cb(w);
@@ -290,8 +293,7 @@ extern "C" int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, in
       a.x_in = cb(x) + static_cast<size_t>(r) * in_features;
       if (y_fp32) a.yf = reinterpret_cast<float*>(y) + static_cast<size_t>(r) * out_features;
       else a.y = mb(y) + static_cast<size_t>(r) * out_features;
-      LCRB_TRY(gemv_launch(a, in_features, PRO_PLAIN, epi, false, std::min(chunks, sms), cs(stream),
-                           false));
+      LCRB_TRY(gemv_launch(a, map, in_features, PRO_PLAIN, epi, std::min(chunks, sms), cs(stream), false));
     }
     return LCR_OK;
   }

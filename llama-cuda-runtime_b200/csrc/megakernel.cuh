@@ -27,9 +27,10 @@
 
 namespace lcrb {
 
-constexpr int kMegaStageBytes = 32768;
+constexpr int kMegaStageBytes = kGemvSlotBytes;
 constexpr int kMegaStages = 6;
-constexpr int kMegaThreads = kGemvConsumers + 32;
+// 8 consumer warps, the ring producer (warp 8) and the L2 prefetcher (warp 9).
+constexpr int kMegaThreads = kGemvConsumers + 64;
 constexpr int kMegaWarps = kGemvConsumers / 32;
 
 struct MegaLayer {
@@ -48,6 +49,7 @@ struct MegaArgs {
   const bf16* final_norm;
   const bf16* lm_head;
   const MegaLayer* L;  // device array [layers]
+  const CUtensorMap* wmaps;  // device array: [layer * 4 + m] (qkv, o, gate/up, down), then lm_head
   const float* inv_freq;
   int32_t* state;      // [0] token, [1] position
   bf16* x;
@@ -77,8 +79,16 @@ struct MegaArgs {
   unsigned long long* trace;
 };
 
-constexpr int kMegaTraceEvents = 512;
+constexpr int kMegaTraceEvents = 1024;
 constexpr int kMegaTraceProducer = 256;
+// SM cycles consumer thread 0 waited on full stages in GEMV phase p, and the
+// producer waited on empty slots while issuing GEMV phase p.
+constexpr int kMegaTraceConsumerWait = 340;
+constexpr int kMegaTraceProducerWait = 424;
+// Per-stage timestamps of one layer's gate/up phase: producer issue [512 + s],
+// consumer thread 0 stage ready [576 + s] and released [640 + s].
+constexpr int kMegaTraceStageLayer = 8;
+constexpr int kMegaTraceStages = 512;
 
 enum : uint32_t { kStatusAbort = 1u << 8, kStatusTimeoutBarrier = 1u << 5 };
 
@@ -245,6 +255,16 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
   const int heads = a.num_kv * G;
   const int qd = heads * D, kvd = a.num_kv * D;
 
+  // The new position's K and V (this step's projection) are loaded with the
+  // query, so one L2 round trip covers both.
+  const bool has_new = pos >= item.begin && pos < item.end && grp == 0;
+  uint4 k_self = make_uint4(0, 0, 0, 0), k_other = k_self, v_raw = k_self;
+  if (has_new) {
+    const bf16* kh = a.qkv + qd + item.kvh * D;
+    k_self = ldg_cg16(kh + lig * 8);
+    k_other = ldg_cg16(kh + (lig * 8 < D / 2 ? lig * 8 + D / 2 : lig * 8 - D / 2));
+    v_raw = ldg_cg16(a.qkv + qd + kvd + item.kvh * D + lig * 8);
+  }
   float q[G][8], acc[G][8], m[G], l_[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -297,10 +317,10 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
   }
 
   // The new position (this step's token): rotate K, store K and V, attend.
-  if (pos >= item.begin && pos < item.end && grp == 0) {
+  if (has_new) {
     float kf[8], vf[8];
-    rope8<D>(a.qkv + qd + item.kvh * D, lig, cs, kf);
-    const uint4 vraw = ldg_cg16(a.qkv + qd + kvd + item.kvh * D + lig * 8);
+    rope8_from<D>(k_self, k_other, lig, cs, kf);
+    const uint4 vraw = v_raw;
     unpack8(vraw, vf);
     const long long off = kv_offset<PAGED>(a, l, item.kvh, pos, D);
     uint4 kw;
@@ -443,43 +463,56 @@ __device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos,
 // L2 prefetch window
 // ---------------------------------------------------------------------------
 
-// Walks this CTA's weight slices in schedule order -- per layer qkv, o, gate,
-// up, down, then the lm_head -- and keeps cp.async.bulk.prefetch.L2 up to
-// MegaArgs::prefetch_bytes ahead of what the producer has issued into the ring.
-// HBM then keeps streaming the next matrices while the consumers work through
-// barriers, attention and the small projections, and the ring refills from L2.
-constexpr unsigned kMegaPrefetchChunk = 32u << 10;
+// Walks this CTA's weight slices in the producer's order -- per layer qkv, o,
+// gate/up (gate and up rows alternating in 16 KB pieces, as the ring takes
+// them), down, then the lm_head -- prefetching them into L2 with the 32 lanes
+// of its own warp (warp 9), one 128-byte line per lane and instruction, on the
+// load/store path: a bulk prefetch would queue in the same TMA unit as the
+// ring's copies and delay them. It stays at most MegaArgs::prefetch_bytes
+// ahead of the bytes the producer has issued into the ring: while the
+// consumers sit in barriers, attention and the small projections and the ring
+// is full, HBM keeps streaming the next matrices into L2, and the ring
+// refills from there.
+constexpr unsigned kMegaPrefetchChunk = 16u << 10;
+// Value of the producer's progress word once it has issued everything (or
+// stopped on a failed wait): the prefetcher then stops.
+constexpr unsigned long long kMegaIssuedDone = ~0ull;
 
 template <int H, int QD, int F, int D>
 struct MegaPrefetch {
   const MegaArgs* a;
-  int slice;           // index into the schedule: 5 per layer, then lm_head
-  const char* ptr;     // next byte to prefetch in the current slice
-  unsigned long long left;  // bytes left in the current slice
-  unsigned long long done;  // bytes prefetched so far
+  int slice;                  // index into the schedule: 4 per layer, then lm_head
+  const char* ptr[2];         // next byte of each range of the slice
+  unsigned long long left[2]; // bytes left in each range
+  int turn;                   // range the next piece comes from
+  unsigned long long done;    // bytes prefetched so far
 
   __device__ __forceinline__ void open(int s) {
     slice = s;
-    left = 0;
+    left[0] = left[1] = 0;
+    turn = 0;
     const int c = blockIdx.x, n = gridDim.x;
-    if (s < 5 * a->layers) {
-      const MegaLayer& w = a->L[s / 5];
+    if (s < 4 * a->layers) {
+      const MegaLayer& w = a->L[s / 4];
       const int nqkv = QD + 2 * D * a->num_kv;
       int o0, o1, K;
       const bf16* base;
-      switch (s % 5) {
+      switch (s % 4) {
         case 0: o0 = gemv_share(nqkv, c, n); o1 = gemv_share(nqkv, c + 1, n); K = H; base = w.qkv; break;
         case 1: o0 = gemv_share(H, c, n); o1 = gemv_share(H, c + 1, n); K = QD; base = w.o; break;
         case 2: o0 = gemv_share(F, c, n); o1 = gemv_share(F, c + 1, n); K = H; base = w.gate_up; break;
-        case 3: o0 = F + gemv_share(F, c, n); o1 = F + gemv_share(F, c + 1, n); K = H; base = w.gate_up; break;
         default: o0 = gemv_share(H, c, n); o1 = gemv_share(H, c + 1, n); K = F; base = w.down; break;
       }
-      ptr = reinterpret_cast<const char*>(base + static_cast<size_t>(o0) * K);
-      left = static_cast<unsigned long long>(o1 - o0) * K * 2;
-    } else if (s == 5 * a->layers) {
+      ptr[0] = reinterpret_cast<const char*>(base + static_cast<size_t>(o0) * K);
+      left[0] = static_cast<unsigned long long>(o1 - o0) * K * 2;
+      if (s % 4 == 2) {  // the up rows of the same outputs
+        ptr[1] = reinterpret_cast<const char*>(base + (static_cast<size_t>(F) + o0) * K);
+        left[1] = left[0];
+      }
+    } else if (s == 4 * a->layers) {
       const int o0 = gemv_share(a->vocab, c, n), o1 = gemv_share(a->vocab, c + 1, n);
-      ptr = reinterpret_cast<const char*>(a->lm_head + static_cast<size_t>(o0) * H);
-      left = static_cast<unsigned long long>(o1 - o0) * H * 2;
+      ptr[0] = reinterpret_cast<const char*>(a->lm_head + static_cast<size_t>(o0) * H);
+      left[0] = static_cast<unsigned long long>(o1 - o0) * H * 2;
     }
   }
 
@@ -489,21 +522,68 @@ struct MegaPrefetch {
     open(0);
   }
 
-  __device__ __forceinline__ void top_up(unsigned long long issued) {
-    while (done < issued + a->prefetch_bytes) {
-      if (left == 0) {
-        if (slice >= 5 * a->layers) return;
-        open(slice + 1);
-        continue;
-      }
-      const unsigned bytes = static_cast<unsigned>(left < kMegaPrefetchChunk ? left : kMegaPrefetchChunk);
-      prefetch_l2(ptr, bytes);
-      ptr += bytes;
-      left -= bytes;
-      done += bytes;
+  // Issues one piece (every lane of the warp, with identical state); false
+  // once the schedule is exhausted.
+  __device__ __forceinline__ bool step(int lane) {
+    while (left[0] == 0 && left[1] == 0) {
+      if (slice >= 4 * a->layers) return false;
+      open(slice + 1);
     }
+    const bool second = left[0] == 0 || (turn == 1 && left[1] != 0);
+    const unsigned long long avail = second ? left[1] : left[0];
+    const unsigned bytes = static_cast<unsigned>(avail < kMegaPrefetchChunk ? avail : kMegaPrefetchChunk);
+    const char* p = second ? ptr[1] : ptr[0];
+    for (unsigned off = static_cast<unsigned>(lane) * 128u; off < bytes; off += 32u * 128u) prefetch_line_l2(p + off);
+    if (second) {
+      ptr[1] += bytes;
+      left[1] -= bytes;
+    } else {
+      ptr[0] += bytes;
+      left[0] -= bytes;
+    }
+    done += bytes;
+    turn = second ? 0 : 1;
+    return true;
   }
 };
+
+// The producer's side: publishes the weight bytes issued into the ring.
+struct MegaProgress {
+  volatile unsigned long long* word;
+  __device__ __forceinline__ void top_up(unsigned long long issued) { *word = issued; }
+};
+
+// Prefetcher loop (one whole warp, kept converged: lane 0 reads the
+// producer's progress and decides, the lanes follow). Every wait is bounded:
+// it gives up when the producer's progress has not moved for kWaitLimitNs.
+template <int H, int QD, int F, int D>
+__device__ __forceinline__ void mega_prefetch_loop(const MegaArgs& a, volatile unsigned long long* issued_word,
+                                                   int lane) {
+  MegaPrefetch<H, QD, F, D> pf;
+  pf.init(&a);
+  unsigned long long last = 0;
+  uint64_t since = globaltimer_ns();
+  for (;;) {
+    unsigned long long issued = lane == 0 ? *issued_word : 0ull;
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    if (issued == kMegaIssuedDone) return;
+    if (pf.done < issued + a.prefetch_bytes) {
+      if (!pf.step(lane)) return;
+      continue;
+    }
+    int give_up = 0;
+    if (lane == 0) {
+      if (issued != last) {
+        last = issued;
+        since = globaltimer_ns();
+      } else if (globaltimer_ns() - since > kWaitLimitNs) {
+        give_up = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, give_up, 0)) return;
+    __nanosleep(256);
+  }
+}
 
 // ---------------------------------------------------------------------------
 // The kernel
@@ -530,6 +610,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
   uint64_t* empty = full + STAGES;
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
   int* s_flags = reinterpret_cast<int*>(cta_best + 1);  // [0] abort, [1] last-CTA
+  // s_flags[2..3]: the producer's issued-bytes word read by the prefetcher
+  volatile unsigned long long* s_issued = reinterpret_cast<volatile unsigned long long*>(s_flags + 2);
   float* red8 = reinterpret_cast<float*>(s_flags + 4);
   float* red = red8 + 8;
   float* cs = red + Shape::RED_FLOATS;  // RoPE cos/sin [D]
@@ -545,6 +627,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     *cta_best = 0ull;
     s_flags[0] = 0;
     s_flags[1] = 0;
+    *s_issued = 0;
     mbar_fence_init();
     if (blockIdx.x == 0 && (pos < 0 || pos >= a.max_seq)) atomicOr(a.status, kStatusBadPosition);
   }
@@ -565,42 +648,52 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         ++phase;
         return true;
       };
-      MegaPrefetch<H, QD, F, D> pf_state;
-      pf_state.init(&a);
-      // A zero lead means no prefetching at all (a trailing prefetch would
-      // re-read lines the ring already consumed).
-      MegaPrefetch<H, QD, F, D>* pf = a.prefetch_bytes ? &pf_state : nullptr;
+      // Per-phase producer wait (written as the phase's slot; `phase` was
+      // advanced by mark(), so the current phase is phase - 1).
+      auto pwait = [&]() -> unsigned long long* {
+        if (!ptrace) return nullptr;
+        unsigned long long* w = ptrace + (kMegaTraceProducerWait - kMegaTraceProducer) + (phase - 1);
+        *w = 0;
+        return w;
+      };
+      MegaProgress progress{s_issued};
+      MegaProgress* pf = a.prefetch_bytes ? &progress : nullptr;
       unsigned long long issued = 0;
       for (int l = 0; l < a.layers && ok; ++l) {
         const MegaLayer& w = a.L[l];
         const int nqkv = QD + 2 * (D * a.num_kv);
-        ok = ok && mark() && gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, w.qkv, nqkv,
+        ok = ok && mark() && gemv_produce<H, STAGES, false>(ring, full, empty, it, a.wmaps + 4 * l, w.qkv, nqkv,
                                                      gemv_share(nqkv, blockIdx.x, ctas),
                                                      gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status,
-                                                     pf, &issued);
+                                                     pf, &issued, pwait());
         ok = ok && mark() && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
-        ok = ok && mark() && gemv_produce<QD, SB, STAGES, false>(ring, full, empty, it, w.o, H,
+        ok = ok && mark() && gemv_produce<QD, STAGES, false>(ring, full, empty, it, a.wmaps + 4 * l + 1, w.o, H,
                                                       gemv_share(H, blockIdx.x, ctas),
                                                       gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
-                                                      pf, &issued);
-        ok = ok && mark() && gemv_produce<H, SB, STAGES, true>(ring, full, empty, it, w.gate_up, F,
+                                                      pf, &issued, pwait());
+        ok = ok && mark() && gemv_produce<H, STAGES, true>(ring, full, empty, it, a.wmaps + 4 * l + 2, w.gate_up, F,
                                                     gemv_share(F, blockIdx.x, ctas),
                                                     gemv_share(F, blockIdx.x + 1, ctas), policy, a.status,
-                                                    pf, &issued);
-        ok = ok && mark() && gemv_produce<F, SB, STAGES, false>(ring, full, empty, it, w.down, H,
+                                                    pf, &issued, pwait(),
+                                                    (ptrace && l == kMegaTraceStageLayer) ? ptrace + (kMegaTraceStages - kMegaTraceProducer) : nullptr);
+        ok = ok && mark() && gemv_produce<F, STAGES, false>(ring, full, empty, it, a.wmaps + 4 * l + 3, w.down, H,
                                                      gemv_share(H, blockIdx.x, ctas),
                                                      gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
-                                                     pf, &issued);
+                                                     pf, &issued, pwait());
       }
       if (ok) {
         mark();
-        gemv_produce<H, SB, STAGES, false>(ring, full, empty, it, a.lm_head, a.vocab,
+        gemv_produce<H, STAGES, false>(ring, full, empty, it, a.wmaps + 4 * a.layers, a.lm_head, a.vocab,
                                           gemv_share(a.vocab, blockIdx.x, ctas),
                                           gemv_share(a.vocab, blockIdx.x + 1, ctas), policy, a.status,
-                                          pf, &issued);
+                                          pf, &issued, pwait());
       }
+      *s_issued = kMegaIssuedDone;
       ring_drain<STAGES>(full, it, a.status);
     }
+  } else if (warp == kMegaWarps + 1) {
+    // ---------------- L2 prefetcher (a zero lead means none)
+    if (a.prefetch_bytes) mega_prefetch_loop<H, QD, F, D>(a, s_issued, lane);
   } else {
     // ---------------- consumers
     int it = 0;
@@ -610,6 +703,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     unsigned long long* ctrace = a.trace ? a.trace + blockIdx.x * kMegaTraceEvents : nullptr;
     if (ctrace && tid == 0) ctrace[0] = globaltimer_ns();
     int phase_no = 0;
+    auto cwait = [&]() -> unsigned long long* {
+      return ctrace ? ctrace + kMegaTraceConsumerWait + (phase_no - 1) : nullptr;
+    };
     auto pro_done = [&]() {
       if (ctrace && tid == 0 && 163 + phase_no < kMegaTraceProducer - 1) ctrace[163 + phase_no] = globaltimer_ns();
       ++phase_no;
@@ -630,23 +726,23 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.eps = a.eps;
         g.norm_w = w.input_norm;
         g.y = a.qkv;
-        float xr[GemvGeom<H, SB>::CPT][8];
         if (l == 0) {
           g.embed = a.embed;
           g.token = a.state;
           g.vocab = a.vocab;
           g.x_out = a.x;
           g.xsum_out = a.xsum;
-          gemv_load_x<H, SB, PRO_EMBED_NORM>(g, xr, xs, red8);
+          gemv_stage_x<H, PRO_EMBED_NORM>(g, xs, red8);
         pro_done();
         } else {
           g.x_in = a.x;
           g.xsum = a.xsum;
-          gemv_load_x<H, SB, PRO_NORM>(g, xr, xs, red8);
+          gemv_stage_x<H, PRO_NORM>(g, xs, red8);
         pro_done();
         }
-        gemv_consume<H, SB, STAGES, EPI_STORE>(ring, full, empty, it, g, gemv_share(nqkv, blockIdx.x, ctas),
-                                               gemv_share(nqkv, blockIdx.x + 1, ctas), xr, red, best, failed);
+        g.wait_cycles = cwait();
+        gemv_consume<H, STAGES, EPI_STORE>(ring, full, empty, it, g, gemv_share(nqkv, blockIdx.x, ctas),
+                                               gemv_share(nqkv, blockIdx.x + 1, ctas), xs, red, best, failed);
       }
       if (!(run = sync())) break;
       pro_done();  // attention: no separate prologue
@@ -657,12 +753,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.status = a.status;
         g.resid = a.x;
         g.resid_sum = a.xsum;
-        float xr[GemvGeom<QD, SB>::CPT][8];
         mega_stage_attention<QD, D>(a, pos, xs);
-        gemv_x_regs<QD, SB>(xs, xr);
         pro_done();
-        gemv_consume<QD, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
-                                                gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
+        g.wait_cycles = cwait();
+        gemv_consume<QD, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
+                                                gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed);
       }
       if (!(run = sync())) break;
       {  // GU
@@ -673,11 +768,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.xsum = a.xsum;
         g.norm_w = w.post_norm;
         g.y = a.act;
-        float xr[GemvGeom<H, SB>::CPT][8];
-        gemv_load_x<H, SB, PRO_NORM>(g, xr, xs, red8);
+        gemv_stage_x<H, PRO_NORM>(g, xs, red8);
         pro_done();
-        gemv_consume<H, SB, STAGES, EPI_SWIGLU>(ring, full, empty, it, g, gemv_share(F, blockIdx.x, ctas),
-                                                gemv_share(F, blockIdx.x + 1, ctas), xr, red, best, failed);
+        g.wait_cycles = cwait();
+        g.stage_ns = (ctrace && l == kMegaTraceStageLayer) ? ctrace + kMegaTraceStages + 64 : nullptr;
+        gemv_consume<H, STAGES, EPI_SWIGLU>(ring, full, empty, it, g, gemv_share(F, blockIdx.x, ctas),
+                                                gemv_share(F, blockIdx.x + 1, ctas), xs, red, best, failed);
       }
       if (!(run = sync())) break;
       {  // DOWN
@@ -686,11 +782,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.x_in = a.act;
         g.resid = a.x;
         g.resid_sum = a.xsum;
-        float xr[GemvGeom<F, SB>::CPT][8];
-        gemv_load_x<F, SB, PRO_PLAIN>(g, xr, xs, red8);
+        gemv_stage_x<F, PRO_PLAIN>(g, xs, red8);
         pro_done();
-        gemv_consume<F, SB, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
-                                               gemv_share(H, blockIdx.x + 1, ctas), xr, red, best, failed);
+        g.wait_cycles = cwait();
+        gemv_consume<F, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
+                                               gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed);
       }
       if (!(run = sync())) break;
     }
@@ -702,12 +798,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       g.xsum = a.xsum;
       g.norm_w = a.final_norm;
       g.yf = a.logits;
-      float xr[GemvGeom<H, SB>::CPT][8];
-      gemv_load_x<H, SB, PRO_NORM>(g, xr, xs, red8);
+      gemv_stage_x<H, PRO_NORM>(g, xs, red8);
         pro_done();
-      gemv_consume<H, SB, STAGES, EPI_LOGITS_ARGMAX>(ring, full, empty, it, g,
+      g.wait_cycles = cwait();
+      gemv_consume<H, STAGES, EPI_LOGITS_ARGMAX>(ring, full, empty, it, g,
                                                      gemv_share(a.vocab, blockIdx.x, ctas),
-                                                     gemv_share(a.vocab, blockIdx.x + 1, ctas), xr, red,
+                                                     gemv_share(a.vocab, blockIdx.x + 1, ctas), xs, red,
                                                      best, failed);
       if (best != 0ull) atomicMax(cta_best, best);
       if (ctrace && tid == 0) ctrace[kMegaTraceProducer - 1] = globaltimer_ns();

@@ -27,10 +27,13 @@ MODELS = {"1b": ck.LLAMA_3_2_1B, "tiny": ck.TINY}
 PHASES = ("qkv", "attn", "o", "gate_up", "down")
 
 
-def print_trace(t: np.ndarray, layers: int) -> None:
+def print_trace(t: np.ndarray, layers: int, sm_mhz: float = 1965.0) -> None:
     """Phase timeline of one persistent decode step: per phase, the consumers'
     working time (previous barrier departure -> next barrier arrival) and the
-    barrier wait, averaged over layers (mean / max over CTAs, microseconds)."""
+    barrier wait, averaged over layers (mean / max over CTAs, microseconds);
+    for the matrix phases also the time consumer thread 0 waited on weight
+    stages to land and the producer waited on free ring slots (SM cycles at
+    `sm_mhz`)."""
     t = t.astype(np.int64)
     t0 = t[:, 0].min()
     nbar = 5 * layers
@@ -42,16 +45,20 @@ def print_trace(t: np.ndarray, layers: int) -> None:
     prod = t[:, 256:256 + nbar + 1]
     pro = t[:, 163:163 + nbar]
     prologue = (pro - start) / 1e3
+    cwait = t[:, 340:340 + nbar + 1] / sm_mhz
+    pwait = t[:, 424:424 + nbar + 1] / sm_mhz
     print(f"{'phase':8s} {'work mean':>10s} {'work max':>9s} {'prologue':>9s} {'wait mean':>10s} "
-          f"{'producer lead':>14s}  (us)")
+          f"{'producer lead':>14s} {'data wait':>10s} {'slot wait':>10s}  (us)")
     for k, name in enumerate(PHASES):
         cols = list(range(k, nbar, 5))
         lead = (start[:, cols] - prod[:, cols]) / 1e3  # >0: producer started this phase earlier
         print(f"{name:8s} {work[:, cols].mean():10.2f} {work[:, cols].max(axis=0).mean():9.2f} "
-              f"{prologue[:, cols].mean():9.2f} {wait[:, cols].mean():10.2f} {lead.mean():14.2f}")
+              f"{prologue[:, cols].mean():9.2f} {wait[:, cols].mean():10.2f} {lead.mean():14.2f} "
+              f"{cwait[:, cols].mean():10.2f} {pwait[:, cols].mean():10.2f}")
     lm = (t[:, 255] - depart[:, -1]) / 1e3
     total = (t[:, 255].max() - t0) / 1e3
-    print(f"lm_head  {lm.mean():10.2f} {lm.max():9.2f}")
+    print(f"lm_head  {lm.mean():10.2f} {lm.max():9.2f} {'':9s} {'':10s} {'':14s} "
+          f"{cwait[:, nbar].mean():10.2f} {pwait[:, nbar].mean():10.2f}")
     print(f"step (consumers start -> last CTA done): {total:.1f} us")
 
 
@@ -76,6 +83,8 @@ def main(argv=None) -> int:
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--trace", action="store_true",
                     help="per-phase timeline of the last decode step (persistent kernel)")
+    ap.add_argument("--trace-out", default=None,
+                    help="with --trace: also save the raw per-CTA timestamps (.npy)")
     args = ap.parse_args(argv)
 
     geom = MODELS[args.model]
@@ -130,7 +139,10 @@ def main(argv=None) -> int:
     report["bandwidth_utilization"] = (report["achieved_bandwidth_bytes_per_second"]
                                        / report["peak_bandwidth_bytes_per_second"])
     if args.trace:
-        print_trace(m.trace(), geom.num_layers)
+        t = m.trace()
+        print_trace(t, geom.num_layers)
+        if args.trace_out:
+            np.save(args.trace_out, t)
     if args.json:
         print(json.dumps(report))
     elif args.bench:

@@ -312,12 +312,12 @@ class Model:
         return ms.value
 
     def trace(self) -> np.ndarray:
-        """Per-CTA phase timestamps of the last step ([ctas][512] ns)."""
-        n = 1024 * 512
+        """Per-CTA phase timestamps of the last step ([ctas][1024] ns)."""
+        n = 1024 * 1024
         buf = np.zeros(n, dtype=np.uint64)
         got = ctypes.c_int()
         check(lib().lcr_copy_trace(self.ctx, buf.ctypes.data, n, ctypes.byref(got)))
-        return buf[:got.value].reshape(-1, 512)
+        return buf[:got.value].reshape(-1, 1024)
 
     def time_gemv(self, matrix: int, layer: int = 0, reps: int = 20) -> float:
         ms = ctypes.c_float()
