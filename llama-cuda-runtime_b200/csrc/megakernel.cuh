@@ -141,11 +141,14 @@ template <int D>
 struct MegaAttnGeom {
   static constexpr int LPP = D / 8;            // lanes per position
   static constexpr int GPW = 32 / LPP;         // positions per warp per pass
-  static constexpr int P = kMegaWarps * GPW;   // positions per stage
-  static constexpr int SUB = 16;               // positions per bulk copy
+  static constexpr int P = kMegaWarps * GPW;   // positions per pass of the 8 warps
   static constexpr int ROWB = D * 2;
-  static_assert(2 * P * D * 2 <= kMegaStageBytes, "KV stage must fit a ring stage");
-  static_assert(P % SUB == 0, "stage must be whole 16-position blocks");
+  // A ring stage carries STAGE_POS positions: K in its first 16 KB, V in the
+  // next, consumed in PASSES passes (128 positions at D = 64).
+  static constexpr int STAGE_POS = 16384 / ROWB;
+  static constexpr int PASSES = STAGE_POS / P;
+  static_assert(2 * STAGE_POS * ROWB <= kMegaStageBytes, "KV stage must fit a ring stage");
+  static_assert(PASSES >= 1 && STAGE_POS % P == 0, "a stage is whole passes");
 };
 
 __device__ __forceinline__ int mega_attn_chunk(int seq_len, int splits, int p) {
@@ -180,6 +183,60 @@ template <int D>
 constexpr int kMegaPartStride = D + 4;
 // Largest split count the persistent step uses.
 constexpr int kMegaMaxMergeSplits = 32;
+// Up to this many splits the O projection's prologue merges them (one round
+// of L2 loads); beyond it the last split of each KV head to finish merges its
+// heads once and the prologue loads the bf16 result.
+constexpr int kMegaPrologueMergeMax = 4;
+
+// Online logsumexp merge of the split records rec0[s * stride_s] for s in
+// [s_begin, s_end) stepping by `step`, dims d0..d0+7, into (M, L, acc) --
+// four records per round of L2 loads.
+template <int D>
+__device__ __forceinline__ void merge_split_records(const float* rec0, int s_begin, int s_end, int step, int d0,
+                                                    float& M, float& L, float (&acc)[8]) {
+  constexpr int B = 4;
+  for (int s0 = s_begin; s0 < s_end; s0 += B * step) {
+    float ms[B], ls[B];
+    float4 lo[B], hi[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int s = s0 + b * step;
+      const bool in = s < s_end;
+      const float* rec = rec0 + static_cast<size_t>(in ? s : s_begin) * kMegaPartStride<D>;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + D));
+      ms[b] = in ? ml.x : kNegBig;
+      ls[b] = in ? ml.y : 0.f;
+      lo[b] = __ldcg(reinterpret_cast<const float4*>(rec + d0));
+      hi[b] = __ldcg(reinterpret_cast<const float4*>(rec + d0 + 4));
+    }
+    float Mn = M;
+#pragma unroll
+    for (int b = 0; b < B; ++b) Mn = fmaxf(Mn, ms[b]);
+    const float keep = ex2_approx(M - Mn);
+    L *= keep;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= keep;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const float w = s0 + b * step < s_end ? ex2_approx(ms[b] - Mn) : 0.f;
+      L += ls[b] * w;
+      acc[0] += lo[b].x * w; acc[1] += lo[b].y * w; acc[2] += lo[b].z * w; acc[3] += lo[b].w * w;
+      acc[4] += hi[b].x * w; acc[5] += hi[b].y * w; acc[6] += hi[b].z * w; acc[7] += hi[b].w * w;
+    }
+    M = Mn;
+  }
+}
+
+// 8 dims of the merged output, rounded to bf16 as the reference stores attn_out.
+__device__ __forceinline__ uint4 merged_bf16x8(float L, const float (&acc)[8]) {
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  uint4 o;
+  o.x = pack_bf2(acc[0] * inv, acc[1] * inv);
+  o.y = pack_bf2(acc[2] * inv, acc[3] * inv);
+  o.z = pack_bf2(acc[4] * inv, acc[5] * inv);
+  o.w = pack_bf2(acc[6] * inv, acc[7] * inv);
+  return o;
+}
 
 template <int D>
 __device__ __forceinline__ AttnItem mega_attn_item(const MegaArgs& a, int pos) {
@@ -207,7 +264,7 @@ __device__ __forceinline__ AttnItem mega_attn_item(const MegaArgs& a, int pos) {
   it.begin = it.split * chunk;
   it.end = min(seq_len, it.begin + chunk);
   it.cache_end = min(it.end, pos);
-  it.nblocks = it.cache_end > it.begin ? (it.cache_end - it.begin + AG::P - 1) / AG::P : 0;
+  it.nblocks = it.cache_end > it.begin ? (it.cache_end - it.begin + AG::STAGE_POS - 1) / AG::STAGE_POS : 0;
   return it;
 }
 
@@ -222,17 +279,20 @@ __device__ __forceinline__ bool mega_attn_produce(uint8_t* ring, uint64_t* full,
         !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
       return false;
     }
-    const int p0 = item.begin + blk * AG::P;
-    // Only positions below cache_end are copied, in runs that never cross a
-    // 16-position (page-aligned) block.
-    const int nvalid = min(AG::P, item.cache_end - p0);
+    const int p0 = item.begin + blk * AG::STAGE_POS;
+    // Only positions below cache_end are copied: one run for the contiguous
+    // layout, one per page for the paged one.
+    const int nvalid = min(AG::STAGE_POS, item.cache_end - p0);
     uint8_t* dst = ring + slot * kMegaStageBytes;
     mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nvalid) * 2 * AG::ROWB);
-    for (int sb = 0; sb * AG::SUB < nvalid; ++sb) {
-      const uint32_t bytes = static_cast<uint32_t>(min(AG::SUB, nvalid - sb * AG::SUB)) * AG::ROWB;
-      const long long off = kv_offset<PAGED>(a, l, item.kvh, p0 + sb * AG::SUB, D);
-      bulk_g2s(dst + sb * AG::SUB * AG::ROWB, a.kpool + off, bytes, &full[slot]);
-      bulk_g2s(dst + AG::P * AG::ROWB + sb * AG::SUB * AG::ROWB, a.vpool + off, bytes, &full[slot]);
+    for (int n = 0; n < nvalid;) {
+      int run = nvalid - n;
+      if constexpr (PAGED) run = min(run, a.page_size - (p0 + n) % a.page_size);
+      const uint32_t bytes = static_cast<uint32_t>(run) * AG::ROWB;
+      const long long off = kv_offset<PAGED>(a, l, item.kvh, p0 + n, D);
+      bulk_g2s(dst + n * AG::ROWB, a.kpool + off, bytes, &full[slot]);
+      bulk_g2s(dst + AG::STAGE_POS * AG::ROWB + n * AG::ROWB, a.vpool + off, bytes, &full[slot]);
+      n += run;
     }
   }
   return true;
@@ -245,7 +305,8 @@ template <int D, int G, int STAGES, bool PAGED>
 __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t* full,
                                                   uint64_t* empty, int& it, const MegaArgs& a,
                                                   int l, int pos, const float* cs, float* scratch,
-                                                  int* s_last, bool& failed) {
+                                                  int* s_last, bool& failed,
+                                                  unsigned long long* wait_cycles = nullptr) {
   using AG = MegaAttnGeom<D>;
   constexpr int LPP = AG::LPP, GPW = AG::GPW, P = AG::P;
   const AttnItem item = mega_attn_item<D>(a, pos);
@@ -278,43 +339,54 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
     l_[g] = 0.f;
   }
 
+  const bool timed = wait_cycles != nullptr && tid == 0;
+  unsigned long long waited = 0;
   for (int blk = 0; blk < item.nblocks; ++blk, ++it) {
     const int slot = it % STAGES;
+    const long long w0 = timed ? clock64() : 0;
     if (!failed) failed = !mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
+    if (timed) waited += static_cast<unsigned long long>(clock64() - w0);
     const uint8_t* kst = ring + slot * kMegaStageBytes;
-    const uint8_t* vst = kst + P * AG::ROWB;
-    const bool live = !failed && item.begin + blk * P + grp < item.cache_end;
-    float kf[8], vf[8];
-    unpack8(*reinterpret_cast<const uint4*>(kst + grp * AG::ROWB + lig * 16), kf);
-    unpack8(*reinterpret_cast<const uint4*>(vst + grp * AG::ROWB + lig * 16), vf);
-    float sc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[e], s);
-      sc[g] = s;
-    }
-#pragma unroll
-    for (int off = LPP / 2; off >= 1; off >>= 1) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], off, LPP);
-    }
-    if (live) {
+    const uint8_t* vst = kst + AG::STAGE_POS * AG::ROWB;
+#pragma unroll 1
+    for (int pass = 0; pass < AG::PASSES; ++pass) {
+      const int row = pass * P + grp;
+      const int first = item.begin + blk * AG::STAGE_POS + pass * P;
+      if (first >= item.cache_end) break;  // uniform across the CTA
+      const bool live = !failed && first + grp < item.cache_end;
+      float kf[8], vf[8];
+      unpack8(*reinterpret_cast<const uint4*>(kst + row * AG::ROWB + lig * 16), kf);
+      unpack8(*reinterpret_cast<const uint4*>(vst + row * AG::ROWB + lig * 16), vf);
+      float sc[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float mn = fmaxf(m[g], sc[g]);
-        const float alpha = ex2_approx(m[g] - mn);
-        const float p = ex2_approx(sc[g] - mn);
-        l_[g] = l_[g] * alpha + p;
+        float s = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * alpha);
-        m[g] = mn;
+        for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[e], s);
+        sc[g] = s;
+      }
+#pragma unroll
+      for (int off = LPP / 2; off >= 1; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], off, LPP);
+      }
+      if (live) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float mn = fmaxf(m[g], sc[g]);
+          const float alpha = ex2_approx(m[g] - mn);
+          const float p = ex2_approx(sc[g] - mn);
+          l_[g] = l_[g] * alpha + p;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * alpha);
+          m[g] = mn;
+        }
       }
     }
     __syncwarp();
     if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
   }
+  if (timed) *wait_cycles = waited;
 
   // The new position (this step's token): rotate K, store K and V, attend.
   if (has_new) {
@@ -402,59 +474,66 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
       rec[D + 1] = L;
     }
   }
+  if (item.splits <= kMegaPrologueMergeMax) return;
+  // Many splits: the last split of this KV head to publish merges the head
+  // group once (8 threads per 8-dim chunk, splits strided over them) and
+  // writes the bf16 output; the counter resets for the next step.
+  __threadfence();
+  named_sync(1, kGemvConsumers);
+  unsigned* ctr = a.attn_ctr + static_cast<size_t>(l) * a.num_kv + item.kvh;
+  if (tid == 0) *s_last = atomicAdd(ctr, 1u) == static_cast<unsigned>(item.splits - 1);
+  named_sync(1, kGemvConsumers);
+  if (!*s_last) return;
+  __threadfence();
+  const int sg = lane & 7;
+  for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
+    const int g = c * 8 / D, d0 = c * 8 % D;
+    float M = kNegBig, L = 0.f;
+    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    merge_split_records<D>(part_base + static_cast<size_t>(g) * a.splits * kMegaPartStride<D>, sg, item.splits, 8,
+                           d0, M, L, acc8);
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, M, off);
+      const float ol = __shfl_xor_sync(0xffffffffu, L, off);
+      const float Mn = fmaxf(M, om);
+      const float ws = ex2_approx(M - Mn), wo = ex2_approx(om - Mn);
+      L = L * ws + ol * wo;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float oa = __shfl_xor_sync(0xffffffffu, acc8[e], off);
+        acc8[e] = acc8[e] * ws + oa * wo;
+      }
+      M = Mn;
+    }
+    if (sg == 0) {
+      *reinterpret_cast<uint4*>(a.attn + static_cast<size_t>(item.kvh * G + g) * D + d0) = merged_bf16x8(L, acc8);
+    }
+  }
+  if (tid == 0) *ctr = 0u;
 }
 
-// O-phase prologue: the attention output, merged from the step's split
-// partials with the logsumexp rule (an online merge over batches of four
-// splits, one round of L2 loads per batch), rounded to bf16 as the reference
-// stores attn_out, and staged in shared memory: each thread one 8-element
-// chunk. Uses named barrier 1; `xs` is complete on return.
+// O-phase prologue: the attention output staged in shared memory, each thread
+// one 8-element chunk. Up to kMegaPrologueMergeMax splits it is merged here
+// from the split partials with the logsumexp rule (merge_split_records) and
+// rounded to bf16 as the reference stores attn_out; beyond that the attention
+// phase has already merged it into `attn`. Uses named barrier 1; `xs` is
+// complete on return.
 template <int QD, int D>
 __device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos, bf16* xs) {
   const int splits = mega_attn_splits(pos + 1, a.splits, MegaAttnGeom<D>::P);
   for (int c = threadIdx.x; c < QD / 8; c += kGemvConsumers) {
     const int col = c * 8;
+    if (splits > kMegaPrologueMergeMax) {  // merged by the attention phase
+      reinterpret_cast<uint4*>(xs)[c] = ldg_cg16(a.attn + col);
+      continue;
+    }
     const int h = col / D, d0 = col % D;
-    const float* rec0 = a.partials + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>;
-    constexpr int B = 4;
     float M = kNegBig, L = 0.f;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < splits; s0 += B) {
-      float ms[B], ls[B];
-      float4 lo[B], hi[B];
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const int s = min(s0 + b, splits - 1);  // clamp: a repeat is masked below
-        const float* rec = rec0 + s * kMegaPartStride<D>;
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + D));
-        ms[b] = s0 + b < splits ? ml.x : kNegBig;
-        ls[b] = s0 + b < splits ? ml.y : 0.f;
-        lo[b] = __ldcg(reinterpret_cast<const float4*>(rec + d0));
-        hi[b] = __ldcg(reinterpret_cast<const float4*>(rec + d0 + 4));
-      }
-      float Mn = M;
-#pragma unroll
-      for (int b = 0; b < B; ++b) Mn = fmaxf(Mn, ms[b]);
-      const float keep = ex2_approx(M - Mn);
-      L *= keep;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] *= keep;
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const float w = s0 + b < splits ? ex2_approx(ms[b] - Mn) : 0.f;
-        L += ls[b] * w;
-        acc[0] += lo[b].x * w; acc[1] += lo[b].y * w; acc[2] += lo[b].z * w; acc[3] += lo[b].w * w;
-        acc[4] += hi[b].x * w; acc[5] += hi[b].y * w; acc[6] += hi[b].z * w; acc[7] += hi[b].w * w;
-      }
-      M = Mn;
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    uint4 o;
-    o.x = pack_bf2(acc[0] * inv, acc[1] * inv);
-    o.y = pack_bf2(acc[2] * inv, acc[3] * inv);
-    o.z = pack_bf2(acc[4] * inv, acc[5] * inv);
-    o.w = pack_bf2(acc[6] * inv, acc[7] * inv);
-    reinterpret_cast<uint4*>(xs)[c] = o;
+    merge_split_records<D>(a.partials + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>, 0, splits, 1, d0, M, L,
+                           acc);
+    reinterpret_cast<uint4*>(xs)[c] = merged_bf16x8(L, acc);
   }
   named_sync(1, kGemvConsumers);
 }
@@ -746,7 +825,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       }
       if (!(run = sync())) break;
       pro_done();  // attention: no separate prologue
-      mega_attn_consume<D, G, STAGES, PAGED>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed);
+      mega_attn_consume<D, G, STAGES, PAGED>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
+                                             cwait());
       if (!(run = sync())) break;
       {  // O
         GemvArgs g = {};

@@ -105,6 +105,35 @@ def test_step_variants_are_bit_identical(tiny, variant):
     assert ta.tolist() == tb.tolist()
 
 
+@pytest.mark.parametrize("paged", [False, True])
+def test_tiny_long_context_vs_oracle(tiny, paged):
+    """700 cached positions: several 128-position KV stages per attention
+    split and many splits per KV head, shuffled physical pages when paged --
+    the persistent step's long-context path (config 3's shape on the tiny
+    model) against the oracle."""
+    block, wdev = tiny
+    prompt = ck.prompt_ids(3, 700)
+    m = rt.Model(block, wdev, max_seq=760, paged=paged, page_size=16, page_order_seed=99)
+    ref32 = oracle.Model(block, 760)
+    ref16 = oracle.Model(block, 760)
+    m.prefill(prompt)
+    for pos, tok in enumerate(prompt):
+        l32 = ref32.decode(int(tok), pos, oracle.MODE_FP32)
+        l16 = ref16.decode(int(tok), pos, oracle.MODE_BF16)
+    got = m.logits_to_host()
+    pos = len(prompt)
+    for step in range(6):
+        assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS, step
+        assert np.abs(got - l16).max() <= 1e-2, step
+        tok = int(np.argmax(got))
+        assert tok == oracle.argmax(l16), f"step {step}: greedy id differs from the bf16 oracle"
+        m.decode(tok)
+        got = m.logits_to_host()
+        l32 = ref32.decode(tok, pos, oracle.MODE_FP32)
+        l16 = ref16.decode(tok, pos, oracle.MODE_BF16)
+        pos += 1
+
+
 def test_paged_block_tables_match_oracle_allocator(tiny):
     block, wdev = tiny
     g = block.geom
