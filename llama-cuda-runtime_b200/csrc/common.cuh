@@ -48,7 +48,9 @@ enum : uint32_t {
   kStatusBadToken = 1u << 2,      // token id outside the vocabulary
   kStatusBadPosition = 1u << 3,   // position outside the cache
   kStatusBadPage = 1u << 4,       // page table entry outside the pool
+  kStatusTimeoutBarrier = 1u << 5,  // a grid barrier gave up
   kStatusBadSmem = 1u << 6,       // ring not 1024-byte aligned for swizzled tensor copies
+  kStatusAbort = 1u << 8,         // a CTA stopped; the others stop at their next wait
 };
 
 // ---------------------------------------------------------------------------

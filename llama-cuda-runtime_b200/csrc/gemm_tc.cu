@@ -1,0 +1,56 @@
+// Instantiations and launch of the tcgen05 batched projection.
+#include "gemm_tc.h"
+
+namespace lcrb {
+namespace {
+
+template <int NB, int EPI>
+int launch_t(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, cudaStream_t s) {
+  auto kernel = gemm_tc_kernel<NB, EPI>;
+  constexpr size_t smem = gemm_tc_smem_bytes<NB>();
+  LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  const int tiles_n = EPI == EPI_SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
+  const int tiles_b = (a.rows + NB - 1) / NB;
+  dim3 grid(static_cast<unsigned>(tiles_n * tiles_b), static_cast<unsigned>(a.splits));
+  kernel<<<grid, kTcThreads, smem, s>>>(a, wmap, xmap);
+  return launch_status("tcgen05 projection");
+}
+
+template <int NB>
+int by_epi(const TcArgs& a, const CUtensorMap& w, const CUtensorMap& x, int epi, cudaStream_t s) {
+  switch (epi) {
+    case EPI_STORE: return launch_t<NB, EPI_STORE>(a, w, x, s);
+    case EPI_STORE_F32: return launch_t<NB, EPI_STORE_F32>(a, w, x, s);
+    case EPI_RESID: return launch_t<NB, EPI_RESID>(a, w, x, s);
+    case EPI_SWIGLU: return launch_t<NB, EPI_SWIGLU>(a, w, x, s);
+    default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: no epilogue %d", epi);
+  }
+}
+
+}  // namespace
+
+int gemm_tc_batch_tile(int rows) {
+  if (rows <= 16) return 16;
+  if (rows <= 32) return 32;
+  if (rows <= 64) return 64;
+  return 128;
+}
+
+int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi,
+                   cudaStream_t stream) {
+  LCRB_REQUIRE(a.K % kTcSlabK == 0 && a.K >= kTcSlabK && a.n_out > 0 && a.rows > 0, LCR_ERR_SHAPE,
+               "tcgen05 projection: unsupported %d x %d x %d", a.rows, a.n_out, a.K);
+  LCRB_REQUIRE(a.splits >= 1 && a.splits <= a.K / kTcSlabK, LCR_ERR_INVALID, "tcgen05 projection: %d splits",
+               a.splits);
+  LCRB_REQUIRE(a.splits == 1 || (a.work && a.counters), LCR_ERR_INVALID,
+               "tcgen05 projection: split-K needs workspace");
+  switch (nb) {
+    case 16: return by_epi<16>(a, wmap, xmap, epi, stream);
+    case 32: return by_epi<32>(a, wmap, xmap, epi, stream);
+    case 64: return by_epi<64>(a, wmap, xmap, epi, stream);
+    case 128: return by_epi<128>(a, wmap, xmap, epi, stream);
+    default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: batch tile %d", nb);
+  }
+}
+
+}  // namespace lcrb

@@ -1,0 +1,302 @@
+// Batched projection y[b][n] = sum_k x[b][k] w[n][k] on the 5th-generation
+// tensor cores (tcgen05): the reference's gemm_nt (src/model.cu:38-45) at
+// batch >= 16 -- batched decode and prefill chunks.
+//
+// A tile is 128 weight rows (the UMMA M side, operand A) x NB batch rows (the
+// N side, operand B), accumulated in fp32 in TMEM. Both operands stream
+// through a shared-memory ring in 64-column K slabs: TMA tensor copies
+// (make_kmajor_map, box {64, rows, 1}) land each slab K-major with the
+// 128-byte swizzle, which is the canonical SW128 K-major operand layout of
+// tcgen05.mma (8-row groups 1024 bytes apart). Per slab the MMA thread issues
+// four m128 x nNB x k16 MMAs, advancing both descriptors by 32 bytes, and
+// commits the slab's release to its empty barrier.
+//
+// Warps: 0 TMA producer (one lane), 1 TMEM allocation + MMA issue (one lane),
+// 2-5 epilogue: each reads its 32 TMEM lanes (= 32 weight rows) with
+// tcgen05.ld.32x32b, so the four epilogue warps cover the 128 rows.
+//
+// Split-K: with splits > 1 each CTA adds its partial tile to fp32 workspace
+// in its own slot, and the last of a tile's CTAs (counter) sums the slots in
+// split order -- the result does not depend on which CTA finishes last.
+// Every wait is bounded (status bit, then the CTA drains its copies and MMAs
+// and frees TMEM before returning).
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"  // GemvEpi, order_key
+
+namespace lcrb {
+
+constexpr int kTcTileM = 128;        // weight rows per tile
+constexpr int kTcSlabK = 64;         // K columns per ring stage (128-byte swizzle span)
+constexpr int kTcThreads = 192;      // 6 warps
+constexpr int kTcRingBytes = 196608; // ring budget (stage count derived from it)
+
+template <int NB>
+struct TcGeom {
+  static_assert(NB == 16 || NB == 32 || NB == 64 || NB == 128 || NB == 256, "batch tile");
+  static constexpr int W_BYTES = kTcTileM * kTcSlabK * 2;  // 16 KB
+  static constexpr int X_BYTES = NB * kTcSlabK * 2;
+  static constexpr int STAGE = W_BYTES + X_BYTES;  // a multiple of 1024
+  static constexpr int STAGES = (kTcRingBytes / STAGE) < 8 ? (kTcRingBytes / STAGE) : 8;
+  static constexpr int TMEM_COLS = NB < 32 ? 32 : NB;  // power of two >= 32
+  static_assert(STAGE % 1024 == 0 && STAGES >= 3, "stage geometry");
+};
+
+struct TcArgs {
+  int n_out;        // weight rows (SWIGLU: F, outputs; the matrix has 2F rows)
+  int K;
+  int rows;         // batch rows of x
+  int splits;       // K slabs are split over this many CTAs per tile
+  int ldy;          // row stride of y / yf / resid (elements)
+  bf16* y;          // STORE / SWIGLU
+  float* yf;        // STORE_F32
+  bf16* resid;      // RESID: resid = bf16(resid + bf16(out)), sums kept
+  float* resid_sum;
+  float* work;      // splits > 1: [tiles][splits][NB][128] fp32
+  unsigned* counters;  // splits > 1: [tiles], zero between launches
+  uint32_t* status;    // device status word, or nullptr
+};
+
+// UMMA shared-memory descriptor of a K-major, 128-byte swizzled tile whose
+// 8-row groups are 1024 bytes apart (start address in 16-byte units; version 1).
+__device__ __forceinline__ uint64_t tc_desc_sw128(uint32_t smem_addr) {
+  return static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+// Instruction descriptor: bf16 A and B, fp32 accumulator, both K-major,
+// M = 128, N = NB.
+template <int NB>
+__device__ __forceinline__ uint32_t tc_idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(NB >> 3) << 17) |
+         (static_cast<uint32_t>(kTcTileM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// One output element of the epilogue: row n of the weights, batch row b.
+template <int EPI>
+__device__ __forceinline__ void tc_store(const TcArgs& a, int b, int n, float v, float up) {
+  const size_t o = static_cast<size_t>(b) * a.ldy + n;
+  if constexpr (EPI == EPI_STORE) {
+    a.y[o] = __ushort_as_bfloat16(f2bf(v));
+  } else if constexpr (EPI == EPI_STORE_F32) {
+    a.yf[o] = v;
+  } else if constexpr (EPI == EPI_RESID) {
+    const float s = __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + o)), rbf(v));
+    a.resid[o] = __ushort_as_bfloat16(f2bf(s));
+    a.resid_sum[o] = s;
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    const float g = rbf(v);
+    const float silu = g / (1.0f + __expf(-g));
+    a.y[o] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
+  }
+}
+
+template <int NB, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap) {
+  using G = TcGeom<NB>;
+  constexpr bool SWIGLU = EPI == EPI_SWIGLU;
+  constexpr int STAGES = G::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * G::STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* drain = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* s_flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] last CTA of the tile
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tiles_n = SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
+  const int tile = blockIdx.x % tiles_n;
+  const int tile_b = blockIdx.x / tiles_n;
+  const int split = blockIdx.y;
+  const int slabs = a.K / kTcSlabK;
+  const int s0 = static_cast<int>(static_cast<long long>(split) * slabs / a.splits);
+  const int s1 = static_cast<int>(static_cast<long long>(split + 1) * slabs / a.splits);
+  const int n0 = SWIGLU ? tile * 64 : tile * kTcTileM;
+  const int b0 = tile_b * NB;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    s_flags[0] = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(G::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const bool aligned = (smem_addr(ring) & 1023u) == 0;
+
+  if (warp == 0) {
+    if (lane == 0 && aligned) {
+      const uint64_t policy = l2_policy_evict_first();
+      int it = 0;
+      for (int s = s0; s < s1; ++s, ++it) {
+        const int slot = it % STAGES;
+        if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) break;
+        uint8_t* st = ring + slot * G::STAGE;
+        mbar_arrive_expect_tx(&full[slot], G::STAGE);
+        if constexpr (SWIGLU) {
+          tma_load_4d(st, &wmap, 0, n0, 0, s, &full[slot], policy);
+        } else {
+          tma_load_3d(st, &wmap, 0, n0, s, &full[slot], policy);
+        }
+        tma_load_3d(st + G::W_BYTES, &xmap, 0, b0, s, &full[slot], policy);
+      }
+      ring_drain<STAGES>(full, it, a.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc<NB>();
+      int it = 0;
+      bool ok = aligned;
+      for (int s = s0; s < s1 && ok; ++s, ++it) {
+        const int slot = it % STAGES;
+        if (!mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_addr(ring + slot * G::STAGE);
+        const uint64_t adesc = tc_desc_sw128(st);
+        const uint64_t bdesc = tc_desc_sw128(st + G::W_BYTES);
+#pragma unroll
+        for (int k = 0; k < kTcSlabK / 16; ++k) {
+          // +32 bytes per 16 columns inside the 128-byte swizzle span
+          tc_mma(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (s > s0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&empty[slot]);
+      }
+      // Accumulator complete (or abandoned): release the epilogue, and make
+      // sure no MMA is still running before TMEM is freed.
+      tc_commit(acc_full);
+      tc_commit(drain);
+      mbar_wait(drain, 0, a.status, kStatusTimeoutFull);
+      if (!ok && a.status) atomicOr(a.status, kStatusAbort);
+    }
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;  // tile row 0..127
+    // (status is optional: the per-kernel entry points may pass none)
+    const bool mine = mbar_wait(acc_full, 0, a.status, kStatusTimeoutFull) &&
+                      !(a.status != nullptr && (__ldcg(a.status) & kStatusAbort));
+    // One decision for all 128 epilogue threads (the branches below hold
+    // 128-thread barriers).
+    const bool have = !named_sync_or(2, 128, !mine);
+    tc_fence_after();
+    float v[NB];
+    if (have) {
+#pragma unroll
+      for (int c = 0; c < NB; c += 16) {
+        float t[16];
+        tc_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c, t);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[c + i] = t[i];
+      }
+      tc_wait_ld();
+    }
+    bool final_ = a.splits == 1;
+    if (have && a.splits > 1) {
+      // This CTA's partial into its own slot, then the last CTA of the tile
+      // sums the slots in split order.
+      float* slotp = a.work + (static_cast<size_t>(blockIdx.x) * a.splits + split) * NB * kTcTileM;
+#pragma unroll
+      for (int b = 0; b < NB; ++b) slotp[b * kTcTileM + row] = v[b];
+      __threadfence();
+      named_sync(2, 128);
+      if (tid == 64) s_flags[0] = atomicAdd(&a.counters[blockIdx.x], 1u) == static_cast<unsigned>(a.splits - 1);
+      named_sync(2, 128);
+      final_ = s_flags[0] != 0;
+      if (final_) {
+        __threadfence();
+        const float* base = a.work + static_cast<size_t>(blockIdx.x) * a.splits * NB * kTcTileM;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) v[b] = 0.f;
+        for (int sp = 0; sp < a.splits; ++sp) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) v[b] += __ldcg(base + (static_cast<size_t>(sp) * NB + b) * kTcTileM + row);
+        }
+        if (tid == 64) a.counters[blockIdx.x] = 0u;
+      }
+    }
+    if (have && final_) {
+      if constexpr (SWIGLU) {
+        // Rows 0-63 are gate rows n0 + r, rows 64-127 the matching up rows:
+        // exchange through the (now idle) ring.
+        float* xch = reinterpret_cast<float*>(ring);
+        if (row >= 64) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) xch[b * 64 + (row - 64)] = v[b];
+        }
+        named_sync(2, 128);
+        if (row < 64 && n0 + row < a.n_out) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], xch[b * 64 + row]);
+          }
+        }
+      } else if (n0 + row < a.n_out) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], 0.f);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TMEM_COLS) : "memory");
+  }
+}
+
+template <int NB>
+constexpr size_t gemm_tc_smem_bytes() {
+  return static_cast<size_t>(TcGeom<NB>::STAGES) * TcGeom<NB>::STAGE + (2 * TcGeom<NB>::STAGES + 2) * 8 + 16 + 1024;
+}
+
+}  // namespace lcrb

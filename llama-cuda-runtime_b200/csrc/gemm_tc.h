@@ -1,0 +1,20 @@
+// Host-side launcher of the tcgen05 batched projection (gemm_tc.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "gemm_tc.cuh"
+
+namespace lcrb {
+
+// Smallest supported batch tile covering `rows` (16, 32, 64 or 128; larger
+// batches take several tiles of 128).
+int gemm_tc_batch_tile(int rows);
+// Launches y = x w^T for `a.rows` batch rows: wmap = make_kmajor_map(w, n_out
+// (2F for SWIGLU as two halves), K, halves, 128 (64 for SWIGLU), 1), xmap =
+// make_kmajor_map(x, rows, K, 1, nb, 1). a.splits > 1 needs a.work and
+// a.counters. One CTA per (weight tile, batch tile, split).
+int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi,
+                   cudaStream_t stream);
+
+}  // namespace lcrb

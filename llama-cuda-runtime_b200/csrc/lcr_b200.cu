@@ -18,6 +18,7 @@
 #include "lcr_b200.h"
 #include "sampling.cuh"
 #include "small_kernels.cuh"
+#include "gemm_tc.h"
 #include "tmap.h"
 
 namespace lcrb {
@@ -276,6 +277,22 @@ extern "C" int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, in
   LCRB_REQUIRE(y && x && w && rows > 0 && in_features > 0 && out_features > 0, LCR_ERR_INVALID,
                "gemm_nt: null pointer or non-positive size");
   const int epi = y_fp32 ? EPI_STORE_F32 : EPI_STORE;
+  if (rows >= 16 && in_features % kTcSlabK == 0 && aligned16(x) && aligned16(w)) {
+    // Batched: tcgen05 tiles of 128 weight rows x up to 128 batch rows.
+    const int nb = gemm_tc_batch_tile(rows);
+    CUtensorMap wmap, xmap;
+    LCRB_TRY(make_kmajor_map(&wmap, w, out_features, in_features, 1, kTcTileM, 1));
+    LCRB_TRY(make_kmajor_map(&xmap, x, rows, in_features, 1, nb, 1));
+    TcArgs a = {};
+    a.n_out = out_features;
+    a.K = in_features;
+    a.rows = rows;
+    a.splits = 1;
+    a.ldy = out_features;
+    if (y_fp32) a.yf = reinterpret_cast<float*>(y);
+    else a.y = mb(y);
+    return gemm_tc_launch(a, wmap, xmap, nb, epi, cs(stream));
+  }
   if (gemv_supported(in_features, PRO_PLAIN, epi) && aligned16(x) && aligned16(w)) {
     int sms = 148;
     int dev = 0;

@@ -90,7 +90,6 @@ constexpr int kMegaTraceProducerWait = 424;
 constexpr int kMegaTraceStageLayer = 8;
 constexpr int kMegaTraceStages = 512;
 
-enum : uint32_t { kStatusAbort = 1u << 8, kStatusTimeoutBarrier = 1u << 5 };
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;

@@ -16,4 +16,11 @@ namespace lcrb {
 // refuses the map.
 int make_weight_map(CUtensorMap* out, const void* w, int rows, int K, bool swiglu);
 
+// The general form: the same {64 columns, rows, [2 halves,] K / 64 chunks}
+// view (halves = 2: rows [0, rows) and [rows, 2 rows) of the matrix) with a
+// {64, box_rows, [2,] box_chunks} box. The tcgen05 GEMM uses box_chunks = 1:
+// one 64-column K-major slab, 128-byte swizzled, per copy.
+int make_kmajor_map(CUtensorMap* out, const void* base, int rows, int K, int halves, int box_rows,
+                    int box_chunks);
+
 }  // namespace lcrb

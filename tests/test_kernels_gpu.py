@@ -136,7 +136,11 @@ def test_rope_q():
 
 @pytest.mark.parametrize("rows,k,n,fp32", [(1, 2048, 3072, 0), (1, 8192, 2048, 0),
                                            (3, 2048, 1000, 1), (2, 256, 700, 0),
-                                           (1, 1024, 256, 1), (2, 768, 333, 0)])
+                                           (1, 1024, 256, 1), (2, 768, 333, 0),
+                                           # batched: the tcgen05 path (>= 16 rows)
+                                           (16, 2048, 3072, 1), (64, 2048, 2048, 0),
+                                           (100, 1024, 700, 1), (200, 512, 384, 0),
+                                           (32, 8192, 256, 1), (17, 64, 130, 1)])
 def test_gemm_nt(rows, k, n, fp32):
     x = bf(RNG.normal(size=(rows, k)))
     w = bf(RNG.normal(0, 0.02, size=(n, k)))
