@@ -289,6 +289,54 @@ LCR_API int lcr_time_steps(lcr_ctx* ctx, int steps, float* ms);
 LCR_API int lcr_copy_trace(lcr_ctx* ctx, unsigned long long* host, int capacity, int* count);
 LCR_API int lcr_time_gemv(lcr_ctx* ctx, int matrix, int layer, int reps, float* ms);
 
+/* ------------------------------------------------------------------------- */
+/* Batched decode -- no counterpart in the reference, whose Model decodes one  */
+/* sequence at a time (src/model.h:60-127). Continuous batching keeps up to    */
+/* max_batch sequences in slots; one step decodes one token of each of the     */
+/* first n slots with tensor-core (tcgen05) projections, the paged decode      */
+/* attention of every sequence, and per-slot sampling.                         */
+/* ------------------------------------------------------------------------- */
+
+typedef struct lcr_batch_options {
+  int device;
+  int max_batch;   /* slots (1..256) */
+  int max_seq;     /* positions per sequence */
+  int page_size;   /* positions per KV page, a multiple of 16 */
+  int pool_pages;  /* pages in the shared KV pool; a page holds every layer */
+  int flags;       /* bit 1: no CUDA graph */
+} lcr_batch_options;
+
+typedef struct lcr_batch lcr_batch;
+
+LCR_API int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* weights,
+                             const lcr_batch_options* options, lcr_batch** out);
+LCR_API void lcr_batch_destroy(lcr_batch* batch);
+/* Physical pool pages of slot `slot` for positions [0, count * page_size):
+ * page i holds positions [i * page_size, (i + 1) * page_size) in every layer.
+ * Entries in [0, pool_pages); staged to the device with the next step. */
+LCR_API int lcr_batch_set_pages(lcr_batch* batch, int slot, const int32_t* pages, int count);
+/* Sampling of slot `slot`: temperature 0 = greedy (lowest id on ties);
+ * otherwise top-k / top-p as lcr_sample with the uniform drawn by
+ * Philox4x32-10 from (seed, position). */
+LCR_API int lcr_batch_set_sampling(lcr_batch* batch, int slot, float temperature, int top_k,
+                                   float top_p, uint64_t seed);
+/* One step for slots [0, n): slot b decodes host tokens[b] at host
+ * positions[b] (its K/V are written at that position; it attends to
+ * positions 0..positions[b]), then samples its next token. Asynchronous. */
+LCR_API int lcr_batch_step(lcr_batch* batch, int n, const int32_t* tokens,
+                           const int32_t* positions);
+/* The last step's sampled ids of slots [0, n) into host memory (synchronous). */
+LCR_API int lcr_batch_read(lcr_batch* batch, int32_t* next_ids, int n);
+/* The last step's fp32 logits [vocab] of one slot into host memory (synchronous). */
+LCR_API int lcr_batch_logits(lcr_batch* batch, int slot, float* host);
+LCR_API int lcr_batch_sync(lcr_batch* batch);
+LCR_API lcr_stream_t lcr_batch_stream(lcr_batch* batch);
+/* Kernel launches in one step of n slots. */
+LCR_API int lcr_batch_step_launches(const lcr_batch* batch, int n);
+/* Replays the step of the last lcr_batch_step `steps` times (same tokens and
+ * positions) between CUDA events on the batch stream: ms in total. */
+LCR_API int lcr_batch_time_steps(lcr_batch* batch, int steps, float* ms);
+
 #ifdef __cplusplus
 }
 #endif

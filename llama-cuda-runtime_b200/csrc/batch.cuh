@@ -1,0 +1,92 @@
+// Row kernels of the batched decode step (batch_ctx.cu): the RMSNorm in
+// front of each projection, for every sequence of the batch at once.
+#pragma once
+
+#include "common.cuh"
+
+namespace lcrb {
+
+struct NormRowsArgs {
+  // EMBED: the token's embedding row is the residual stream (elementwise.cu:25-41)
+  const int32_t* tokens;  // [rows]
+  const bf16* embed;      // [vocab][H]
+  int vocab;
+  bf16* x;                // [rows][H] residual stream (bf16), written when EMBED
+  float* xsum;            // [rows][H] its unrounded sums, written when EMBED
+  const bf16* gain;       // [H]
+  float eps;
+  bf16* out;              // [rows][H] bf16(x * rsqrt(mean(xsum^2) + eps) * gain)
+  uint32_t* status;
+};
+
+constexpr int kNormThreads = 256;
+
+// One CTA per row; the rounding points are those of the single-sequence
+// step (rmsnorm.cu:21-119): the sum of squares over the unrounded residual
+// sums, the product from the bf16 residual, rounded to bf16.
+template <int H, bool EMBED>
+__global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const NormRowsArgs a) {
+  constexpr int CH = H / 8;                                   // 8-element chunks
+  constexpr int PER = (CH + kNormThreads - 1) / kNormThreads;  // per thread
+  __shared__ float red[kNormThreads / 32];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t row = static_cast<size_t>(b) * H;
+  const bf16* src = a.x + row;
+  if constexpr (EMBED) {
+    int tok = a.tokens[b];
+    if (tok < 0 || tok >= a.vocab) {
+      if (tid == 0 && a.status) atomicOr(a.status, kStatusBadToken);
+      tok = 0;
+    }
+    src = a.embed + static_cast<size_t>(tok) * H;
+  }
+  uint4 raw[PER], gain[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int c = tid + p * kNormThreads;
+    if (c < CH) {
+      raw[p] = ldg_cg16(src + c * 8);
+      gain[p] = ldg16(a.gain + c * 8);
+      float v[8];
+      if constexpr (EMBED) {
+        unpack8(raw[p], v);
+        *reinterpret_cast<uint4*>(a.x + row + c * 8) = raw[p];
+        *reinterpret_cast<float4*>(a.xsum + row + c * 8) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(a.xsum + row + c * 8 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
+        const float4 s0 = __ldcg(reinterpret_cast<const float4*>(a.xsum + row + c * 8));
+        const float4 s1 = __ldcg(reinterpret_cast<const float4*>(a.xsum + row + c * 8 + 4));
+        v[0] = s0.x; v[1] = s0.y; v[2] = s0.z; v[3] = s0.w;
+        v[4] = s1.x; v[5] = s1.y; v[6] = s1.z; v[7] = s1.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) total += red[w];
+  const float scale = rsqrtf(total / static_cast<float>(H) + a.eps);
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int c = tid + p * kNormThreads;
+    if (c < CH) {
+      float xv[8], gf[8];
+      unpack8(raw[p], xv);
+      unpack8(gain[p], gf);
+      uint4 o;
+      o.x = pack_bf2(__fmul_rn(__fmul_rn(xv[0], scale), gf[0]), __fmul_rn(__fmul_rn(xv[1], scale), gf[1]));
+      o.y = pack_bf2(__fmul_rn(__fmul_rn(xv[2], scale), gf[2]), __fmul_rn(__fmul_rn(xv[3], scale), gf[3]));
+      o.z = pack_bf2(__fmul_rn(__fmul_rn(xv[4], scale), gf[4]), __fmul_rn(__fmul_rn(xv[5], scale), gf[5]));
+      o.w = pack_bf2(__fmul_rn(__fmul_rn(xv[6], scale), gf[6]), __fmul_rn(__fmul_rn(xv[7], scale), gf[7]));
+      *reinterpret_cast<uint4*>(a.out + row + c * 8) = o;
+    }
+  }
+}
+
+}  // namespace lcrb

@@ -1,0 +1,610 @@
+// Batched decode context (include/lcr_b200.h, lcr_batch_*): continuous
+// batching of up to max_batch sequences, one token each per step.
+//
+// A step of n slots is, per layer:
+//   norm_rows_kernel        x -> xn (layer 0: the token embeddings)
+//   gemm_tc_kernel          qkv  = xn W_qkv^T           (split-K)
+//   attn_decode_kernel      RoPE, K/V write at each slot's position, paged
+//                           attention over 0..position, split merge -> attn
+//   gemm_tc_kernel          x   += attn W_o^T (residual epilogue, split-K)
+//   norm_rows_kernel        x -> xn
+//   gemm_tc_kernel          act  = silu(xn W_gate^T) * (xn W_up^T)
+//   gemm_tc_kernel          x   += act W_down^T (residual epilogue, split-K)
+// then the final norm, the lm_head into fp32 logits [n][vocab] and one
+// sampling row per slot (greedy or top-k/top-p with a Philox uniform of
+// (seed, position)). The sequence of launches for a given n is captured once
+// as a CUDA graph and replayed.
+//
+// KV cache: one pool per layer of pool_pages pages [kv_head][page_size][D];
+// a slot's page table (shared by all layers) maps its positions to pages.
+// The caller (the scheduler) owns page allocation through lcr_batch_set_pages.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <new>
+#include <vector>
+
+#include "attention.cuh"
+#include "batch.cuh"
+#include "common.cuh"
+#include "dispatch.h"
+#include "gemm_tc.h"
+#include "lcr_b200.h"
+#include "rope_table.h"
+#include "sampling.cuh"
+#include "tmap.h"
+
+using namespace lcrb;
+
+namespace {
+
+constexpr int kStaging = 16;  // pinned (tokens, positions) staging areas
+
+struct StepMaps {  // activation tensor maps for one batch tile size
+  CUtensorMap xn, attn, act;
+};
+
+}  // namespace
+
+struct lcr_batch {
+  int device = 0;
+  lcr_model_desc d{};
+  lcr_batch_options o{};
+  int sms = 148;
+  bool use_graph = true;
+  cudaStream_t stream = nullptr;
+
+  const bf16* embed = nullptr;
+  const bf16* final_norm = nullptr;
+  const bf16* lm_head = nullptr;
+  std::vector<lcr_layer_weights> layers;
+  std::vector<CUtensorMap> wmaps;  // [layer * 4 + m]: qkv, o, gate/up, down; then lm_head
+  std::map<int, StepMaps> xmaps;   // by batch tile
+
+  char* buf = nullptr;
+  bf16* x = nullptr;
+  float* xsum = nullptr;
+  bf16* xn = nullptr;
+  bf16* qkv = nullptr;
+  bf16* attn = nullptr;
+  bf16* act = nullptr;
+  float* logits = nullptr;
+  float* partials = nullptr;
+  unsigned* attn_ctr = nullptr;
+  float* work = nullptr;
+  unsigned* gemm_ctr = nullptr;
+  float* inv_freq = nullptr;
+  int32_t* tokens = nullptr;
+  int32_t* positions = nullptr;
+  int32_t* tables = nullptr;  // [max_batch][max_pages]
+  float* inv_temp = nullptr;
+  int32_t* top_k = nullptr;
+  float* top_p = nullptr;
+  unsigned long long* seed = nullptr;
+  int32_t* next = nullptr;
+  uint32_t* status = nullptr;
+  bf16* kpool = nullptr;
+  bf16* vpool = nullptr;
+  size_t layer_elems = 0;  // elements of one layer's pool
+  int max_pages = 0;
+  int attn_splits_cap = 1;
+  size_t work_floats = 0;
+
+  std::vector<int32_t> tables_host;
+  std::vector<float> inv_temp_host, top_p_host;
+  std::vector<int32_t> top_k_host;
+  std::vector<unsigned long long> seed_host;
+  bool tables_dirty = true, sampling_dirty = true;
+  int32_t* pinned = nullptr;  // [kStaging][2 * max_batch]
+  cudaEvent_t staged[kStaging] = {};
+  int staging_next = 0;
+
+  std::map<int, cudaGraphExec_t> graphs;
+  int last_n = 0;
+  int launches = 0;
+};
+
+namespace {
+
+void release(lcr_batch* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  for (auto& g : c->graphs) cudaGraphExecDestroy(g.second);
+  for (cudaEvent_t e : c->staged) {
+    if (e) cudaEventDestroy(e);
+  }
+  cudaFree(c->buf);
+  cudaFree(c->logits);
+  cudaFree(c->kpool);
+  cudaFree(c->vpool);
+  cudaFree(c->work);
+  cudaFreeHost(c->pinned);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+int check_status(lcr_batch* c) {
+  uint32_t st = 0;
+  LCRB_CUDA(cudaMemcpyAsync(&st, c->status, sizeof st, cudaMemcpyDeviceToHost, c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  if (st == 0) return LCR_OK;
+  LCRB_CUDA(cudaMemsetAsync(c->status, 0, sizeof st, c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  if (st & (kStatusTimeoutFull | kStatusTimeoutEmpty | kStatusTimeoutBarrier | kStatusAbort)) {
+    return fail(LCR_ERR_TIMEOUT, "a device-side wait gave up (status 0x%x)", st);
+  }
+  if (st & kStatusBadToken) return fail(LCR_ERR_INVALID, "token id outside the vocabulary (status 0x%x)", st);
+  if (st & kStatusBadPage) return fail(LCR_ERR_POOL, "page table entry outside the pool (status 0x%x)", st);
+  return fail(LCR_ERR_STATE, "position outside the KV cache (status 0x%x)", st);
+}
+
+int norm_launch(lcr_batch* c, int n, bool embed, const void* gain) {
+  NormRowsArgs a = {};
+  a.tokens = c->tokens;
+  a.embed = c->embed;
+  a.vocab = c->d.vocab_size;
+  a.x = c->x;
+  a.xsum = c->xsum;
+  a.gain = static_cast<const bf16*>(gain);
+  a.eps = c->d.rms_norm_eps;
+  a.out = c->xn;
+  a.status = c->status;
+  ++c->launches;
+  const dim3 grid(static_cast<unsigned>(n));
+  switch (c->d.hidden_size) {
+    case 2048:
+      if (embed) norm_rows_kernel<2048, true><<<grid, kNormThreads, 0, c->stream>>>(a);
+      else norm_rows_kernel<2048, false><<<grid, kNormThreads, 0, c->stream>>>(a);
+      break;
+    case 256:
+      if (embed) norm_rows_kernel<256, true><<<grid, kNormThreads, 0, c->stream>>>(a);
+      else norm_rows_kernel<256, false><<<grid, kNormThreads, 0, c->stream>>>(a);
+      break;
+    case 4096:
+      if (embed) norm_rows_kernel<4096, true><<<grid, kNormThreads, 0, c->stream>>>(a);
+      else norm_rows_kernel<4096, false><<<grid, kNormThreads, 0, c->stream>>>(a);
+      break;
+    default:
+      return fail(LCR_ERR_SHAPE, "batched RMSNorm has no kernel for hidden size %d", c->d.hidden_size);
+  }
+  return launch_status("batched rmsnorm");
+}
+
+// One projection: n rows of `x` (tensor map `xm`, batch tile nb) against
+// weight map `wm` ([n_out][K], or gate/up halves for SWIGLU).
+int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb, int n, int n_out, int K,
+              int epi, bf16* y, float* yf, int ldy) {
+  TcArgs a = {};
+  a.n_out = n_out;
+  a.K = K;
+  a.rows = n;
+  a.ldy = ldy;
+  a.y = y;
+  a.yf = yf;
+  a.resid = c->x;
+  a.resid_sum = c->xsum;
+  a.status = c->status;
+  const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
+  const int tiles = tiles_n * ((n + nb - 1) / nb);
+  const int slabs = K / kTcSlabK;
+  // Enough CTAs to cover the SMs, at least two slabs per split, within the
+  // workspace.
+  int splits = std::max(1, (c->sms + tiles - 1) / tiles);
+  splits = std::min(splits, std::max(1, slabs / 2));
+  while (splits > 1 && static_cast<size_t>(tiles) * splits * nb * kTcTileM > c->work_floats) --splits;
+  a.splits = splits;
+  a.work = c->work;
+  a.counters = c->gemm_ctr;
+  ++c->launches;
+  return gemm_tc_launch(a, wm, xm, nb, epi, c->stream);
+}
+
+int attention_launch_layer(lcr_batch* c, int layer, int n) {
+  const lcr_model_desc& d = c->d;
+  const int qd = d.num_heads * d.head_dim, kvd = d.num_kv_heads * d.head_dim;
+  AttnArgs a = {};
+  a.qkv = c->qkv;
+  a.qkv_stride = qd + 2 * kvd;
+  a.q_dim = qd;
+  a.kv_dim = kvd;
+  a.inv_freq = c->inv_freq;
+  a.kpool = c->kpool + static_cast<size_t>(layer) * c->layer_elems;
+  a.vpool = c->vpool + static_cast<size_t>(layer) * c->layer_elems;
+  a.tables = c->tables;
+  a.table_seq_stride = c->max_pages;
+  a.max_pages = c->max_pages;
+  a.pool_pages = c->o.pool_pages;
+  a.page_size = c->o.page_size;
+  a.page_stride = static_cast<long long>(d.num_kv_heads) * c->o.page_size * d.head_dim;
+  a.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
+  a.max_seq = c->o.max_seq;
+  a.positions = c->positions;
+  // Enough (sequence, KV head, split) CTAs for about two per SM.
+  a.splits = std::max(1, std::min(c->attn_splits_cap, (2 * c->sms + d.num_kv_heads * n - 1) /
+                                                          (d.num_kv_heads * n)));
+  a.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
+  a.out = c->attn;
+  a.partials = c->partials;
+  a.counters = c->attn_ctr;
+  a.status = c->status;
+  ++c->launches;
+  return attn_launch(a, true, d.head_dim, d.num_heads / d.num_kv_heads, true, d.num_kv_heads, n, c->stream,
+                     false);
+}
+
+int maps_for(lcr_batch* c, int nb, const StepMaps** out) {
+  auto it = c->xmaps.find(nb);
+  if (it == c->xmaps.end()) {
+    const lcr_model_desc& d = c->d;
+    StepMaps m;
+    const int qd = d.num_heads * d.head_dim;
+    LCRB_TRY(make_kmajor_map(&m.xn, c->xn, c->o.max_batch, d.hidden_size, 1, nb, 1));
+    LCRB_TRY(make_kmajor_map(&m.attn, c->attn, c->o.max_batch, qd, 1, nb, 1));
+    LCRB_TRY(make_kmajor_map(&m.act, c->act, c->o.max_batch, d.intermediate_size, 1, nb, 1));
+    it = c->xmaps.emplace(nb, m).first;
+  }
+  *out = &it->second;
+  return LCR_OK;
+}
+
+int enqueue_step(lcr_batch* c, int n) {
+  const lcr_model_desc& d = c->d;
+  const int H = d.hidden_size, F = d.intermediate_size;
+  const int qd = d.num_heads * d.head_dim, kvd = d.num_kv_heads * d.head_dim;
+  const int nb = gemm_tc_batch_tile(n);
+  const StepMaps* m = nullptr;
+  LCRB_TRY(maps_for(c, nb, &m));
+  c->launches = 0;
+  for (int l = 0; l < d.num_layers; ++l) {
+    const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+    const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
+    LCRB_TRY(norm_launch(c, n, l == 0, w.input_norm));
+    LCRB_TRY(gemm_node(c, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_STORE, c->qkv, nullptr, qd + 2 * kvd));
+    LCRB_TRY(attention_launch_layer(c, l, n));
+    LCRB_TRY(gemm_node(c, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(norm_launch(c, n, false, w.post_attention_norm));
+    LCRB_TRY(gemm_node(c, wm[2], m->xn, nb, n, F, H, EPI_SWIGLU, c->act, nullptr, F));
+    LCRB_TRY(gemm_node(c, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H));
+  }
+  LCRB_TRY(norm_launch(c, n, false, c->final_norm));
+  LCRB_TRY(gemm_node(c, c->wmaps.back(), m->xn, nb, n, d.vocab_size, H, EPI_STORE_F32, nullptr, c->logits,
+                     d.vocab_size));
+  SampleArgs s = {};
+  s.logits = c->logits;
+  s.row_stride = d.vocab_size;
+  s.vocab = d.vocab_size;
+  s.inv_temperature = c->inv_temp;
+  s.top_k = c->top_k;
+  s.top_p = c->top_p;
+  s.uniform = nullptr;
+  s.seed = c->seed;
+  s.counter = c->positions;
+  s.out = c->next;
+  ++c->launches;
+  return sample_launch(s, n, c->stream, false);
+}
+
+int launch_step(lcr_batch* c, int n) {
+  if (!c->use_graph) return enqueue_step(c, n);
+  auto it = c->graphs.find(n);
+  if (it == c->graphs.end()) {
+    cudaGraph_t g = nullptr;
+    LCRB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    const int st = enqueue_step(c, n);
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (st != LCR_OK) {
+      if (g) cudaGraphDestroy(g);
+      return st;
+    }
+    LCRB_CUDA(e);
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    LCRB_CUDA(ie);
+    it = c->graphs.emplace(n, exec).first;
+  }
+  LCRB_CUDA(cudaGraphLaunch(it->second, c->stream));
+  return LCR_OK;
+}
+
+}  // namespace
+
+extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* weights,
+                                const lcr_batch_options* options, lcr_batch** out) {
+  LCRB_REQUIRE(desc && weights && options && out, LCR_ERR_INVALID, "lcr_batch_create: null argument");
+  *out = nullptr;
+  const lcr_model_desc& d = *desc;
+  const lcr_batch_options& o = *options;
+  LCRB_REQUIRE(d.hidden_size > 0 && d.intermediate_size > 0 && d.num_layers > 0 && d.num_heads > 0 &&
+                   d.num_kv_heads > 0 && d.num_heads % d.num_kv_heads == 0 && d.vocab_size > 0,
+               LCR_ERR_INVALID, "bad model description");
+  LCRB_REQUIRE(d.head_dim == 64 || d.head_dim == 128, LCR_ERR_SHAPE,
+               "decode attention is compiled for head_dim 64 or 128, this model has %d", d.head_dim);
+  const int qd = d.num_heads * d.head_dim, kvd = d.num_kv_heads * d.head_dim;
+  LCRB_REQUIRE(d.hidden_size % kTcSlabK == 0 && qd % kTcSlabK == 0 && d.intermediate_size % kTcSlabK == 0,
+               LCR_ERR_SHAPE, "tensor-core projections need hidden, q_dim and ffn multiples of %d", kTcSlabK);
+  LCRB_REQUIRE(d.hidden_size == 256 || d.hidden_size == 2048 || d.hidden_size == 4096, LCR_ERR_SHAPE,
+               "batched RMSNorm has no kernel for hidden size %d", d.hidden_size);
+  LCRB_REQUIRE(o.max_batch >= 1 && o.max_batch <= 256, LCR_ERR_INVALID, "max_batch %d outside 1..256",
+               o.max_batch);
+  LCRB_REQUIRE(o.max_seq > 0 && o.page_size > 0 && o.page_size % 16 == 0 && o.pool_pages > 0, LCR_ERR_SHAPE,
+               "batched KV cache: max_seq, page_size (multiple of 16) and pool_pages must be positive");
+  LCRB_REQUIRE(weights->embedding && weights->final_norm && weights->layers, LCR_ERR_INVALID,
+               "lcr_weights: null embedding, final_norm or layers");
+  int devices = 0;
+  if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) {
+    cudaGetLastError();
+    return fail(LCR_ERR_NO_DEVICE, "no CUDA device");
+  }
+  LCRB_REQUIRE(o.device >= 0 && o.device < devices, LCR_ERR_INVALID, "device %d of %d", o.device, devices);
+  LCRB_CUDA(cudaSetDevice(o.device));
+  int major = 0;
+  LCRB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, o.device));
+  LCRB_REQUIRE(major == 10, LCR_ERR_NO_DEVICE, "this library is built for sm_100a; device %d is sm_%d", o.device,
+               major * 10);
+
+  lcr_batch* c = new (std::nothrow) lcr_batch();
+  LCRB_REQUIRE(c != nullptr, LCR_ERR_INVALID, "out of host memory");
+  c->device = o.device;
+  c->d = d;
+  c->o = o;
+  c->use_graph = (o.flags & 2) == 0;
+  cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, o.device);
+  c->embed = static_cast<const bf16*>(weights->embedding);
+  c->final_norm = static_cast<const bf16*>(weights->final_norm);
+  c->lm_head = static_cast<const bf16*>(weights->lm_head ? weights->lm_head : weights->embedding);
+  c->layers.assign(weights->layers, weights->layers + d.num_layers);
+  c->max_pages = (o.max_seq + o.page_size - 1) / o.page_size;
+
+  int st = LCR_OK;
+  auto cuda = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && st == LCR_OK) st = fail(LCR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  };
+  cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+
+  // Tensor maps of the weights (128 rows per tile; gate/up as two halves of 64).
+  c->wmaps.resize(static_cast<size_t>(4 * d.num_layers + 1));
+  for (int l = 0; l < d.num_layers && st == LCR_OK; ++l) {
+    const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+    if (!(w.input_norm && w.qkv_proj && w.o_proj && w.post_attention_norm && w.gate_up_proj && w.down_proj)) {
+      st = fail(LCR_ERR_INVALID, "lcr_layer_weights: null tensor pointer");
+      break;
+    }
+    CUtensorMap* m = &c->wmaps[static_cast<size_t>(4 * l)];
+    st = make_kmajor_map(m, w.qkv_proj, qd + 2 * kvd, d.hidden_size, 1, kTcTileM, 1);
+    if (st == LCR_OK) st = make_kmajor_map(m + 1, w.o_proj, d.hidden_size, qd, 1, kTcTileM, 1);
+    if (st == LCR_OK) st = make_kmajor_map(m + 2, w.gate_up_proj, d.intermediate_size, d.hidden_size, 2, 64, 1);
+    if (st == LCR_OK) st = make_kmajor_map(m + 3, w.down_proj, d.hidden_size, d.intermediate_size, 1, kTcTileM, 1);
+  }
+  if (st == LCR_OK) st = make_kmajor_map(&c->wmaps.back(), c->lm_head, d.vocab_size, d.hidden_size, 1, kTcTileM, 1);
+
+  // Attention split cap: the FUSED kernel's last-CTA merge staging.
+  const int group = d.num_heads / d.num_kv_heads;
+  c->attn_splits_cap = d.head_dim == 64 ? attn_max_staged_splits<64, kAttnStages>(group)
+                                        : attn_max_staged_splits<128, kAttnStages>(group);
+  c->attn_splits_cap = std::max(1, c->attn_splits_cap);
+
+  // Activations and per-slot state, one allocation.
+  const size_t B = static_cast<size_t>(o.max_batch);
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t at = off;
+    off = (off + bytes + 255) / 256 * 256;
+    return at;
+  };
+  const size_t o_x = carve(sizeof(bf16) * B * d.hidden_size);
+  const size_t o_xsum = carve(sizeof(float) * B * d.hidden_size);
+  const size_t o_xn = carve(sizeof(bf16) * B * d.hidden_size);
+  const size_t o_qkv = carve(sizeof(bf16) * B * (qd + 2 * kvd));
+  const size_t o_attn = carve(sizeof(bf16) * B * qd);
+  const size_t o_act = carve(sizeof(bf16) * B * d.intermediate_size);
+  const size_t o_part = carve(sizeof(float) * B * d.num_heads * c->attn_splits_cap * (2 + d.head_dim));
+  const size_t o_actr = carve(sizeof(unsigned) * B * d.num_kv_heads);
+  const size_t o_gctr = carve(sizeof(unsigned) * 4096);
+  const size_t o_freq = carve(sizeof(float) * d.head_dim / 2);
+  const size_t o_tok = carve(sizeof(int32_t) * B);
+  const size_t o_pos = carve(sizeof(int32_t) * B);
+  const size_t o_tab = carve(sizeof(int32_t) * B * c->max_pages);
+  const size_t o_temp = carve(sizeof(float) * B);
+  const size_t o_topk = carve(sizeof(int32_t) * B);
+  const size_t o_topp = carve(sizeof(float) * B);
+  const size_t o_seed = carve(sizeof(unsigned long long) * B);
+  const size_t o_next = carve(sizeof(int32_t) * B);
+  const size_t o_status = carve(sizeof(uint32_t));
+  if (st == LCR_OK) cuda(cudaMalloc(&c->buf, off), "cudaMalloc(batch activations)");
+  if (st == LCR_OK) cuda(cudaMemset(c->buf, 0, off), "cudaMemset(batch activations)");
+  if (st == LCR_OK) {
+    char* b = c->buf;
+    c->x = reinterpret_cast<bf16*>(b + o_x);
+    c->xsum = reinterpret_cast<float*>(b + o_xsum);
+    c->xn = reinterpret_cast<bf16*>(b + o_xn);
+    c->qkv = reinterpret_cast<bf16*>(b + o_qkv);
+    c->attn = reinterpret_cast<bf16*>(b + o_attn);
+    c->act = reinterpret_cast<bf16*>(b + o_act);
+    c->partials = reinterpret_cast<float*>(b + o_part);
+    c->attn_ctr = reinterpret_cast<unsigned*>(b + o_actr);
+    c->gemm_ctr = reinterpret_cast<unsigned*>(b + o_gctr);
+    c->inv_freq = reinterpret_cast<float*>(b + o_freq);
+    c->tokens = reinterpret_cast<int32_t*>(b + o_tok);
+    c->positions = reinterpret_cast<int32_t*>(b + o_pos);
+    c->tables = reinterpret_cast<int32_t*>(b + o_tab);
+    c->inv_temp = reinterpret_cast<float*>(b + o_temp);
+    c->top_k = reinterpret_cast<int32_t*>(b + o_topk);
+    c->top_p = reinterpret_cast<float*>(b + o_topp);
+    c->seed = reinterpret_cast<unsigned long long*>(b + o_seed);
+    c->next = reinterpret_cast<int32_t*>(b + o_next);
+    c->status = reinterpret_cast<uint32_t*>(b + o_status);
+    const std::vector<float> freq = rope_inv_freq(d);
+    cuda(cudaMemcpy(c->inv_freq, freq.data(), freq.size() * sizeof(float), cudaMemcpyHostToDevice),
+         "upload inv_freq");
+  }
+  if (st == LCR_OK) {
+    cuda(cudaMalloc(&c->logits, sizeof(float) * B * d.vocab_size), "cudaMalloc(logits)");
+  }
+  // Split-K workspace: at most two CTAs per SM's worth of partial tiles.
+  c->work_floats = static_cast<size_t>(2 * c->sms) * 128 * kTcTileM;
+  if (st == LCR_OK) cuda(cudaMalloc(&c->work, c->work_floats * sizeof(float)), "cudaMalloc(split-K workspace)");
+  // KV pools: [layer][page][kv_head][page_size][D].
+  c->layer_elems = static_cast<size_t>(o.pool_pages) * d.num_kv_heads * o.page_size * d.head_dim;
+  const size_t kv_elems = c->layer_elems * d.num_layers;
+  if (st == LCR_OK) cuda(cudaMalloc(&c->kpool, kv_elems * sizeof(bf16)), "cudaMalloc(K pool)");
+  if (st == LCR_OK) cuda(cudaMalloc(&c->vpool, kv_elems * sizeof(bf16)), "cudaMalloc(V pool)");
+  if (st == LCR_OK) cuda(cudaMemset(c->kpool, 0, kv_elems * sizeof(bf16)), "cudaMemset(K pool)");
+  if (st == LCR_OK) cuda(cudaMemset(c->vpool, 0, kv_elems * sizeof(bf16)), "cudaMemset(V pool)");
+  if (st == LCR_OK) {
+    cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * B * kStaging), "cudaMallocHost");
+  }
+  for (int i = 0; i < kStaging && st == LCR_OK; ++i) {
+    cuda(cudaEventCreateWithFlags(&c->staged[i], cudaEventDisableTiming), "cudaEventCreate");
+  }
+  c->tables_host.assign(B * c->max_pages, 0);
+  c->inv_temp_host.assign(B, 0.f);
+  c->top_k_host.assign(B, 0);
+  c->top_p_host.assign(B, 1.f);
+  c->seed_host.assign(B, 0ull);
+  if (st != LCR_OK) {
+    release(c);
+    return st;
+  }
+  *out = c;
+  return LCR_OK;
+}
+
+extern "C" void lcr_batch_destroy(lcr_batch* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  release(c);
+}
+
+extern "C" int lcr_batch_set_pages(lcr_batch* c, int slot, const int32_t* pages, int count) {
+  LCRB_REQUIRE(c && (pages || count == 0), LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d outside 0..%d", slot,
+               c->o.max_batch - 1);
+  LCRB_REQUIRE(count >= 0 && count <= c->max_pages, LCR_ERR_INVALID, "%d pages; a slot holds at most %d", count,
+               c->max_pages);
+  for (int i = 0; i < count; ++i) {
+    LCRB_REQUIRE(pages[i] >= 0 && pages[i] < c->o.pool_pages, LCR_ERR_POOL, "page %d outside the pool of %d",
+                 pages[i], c->o.pool_pages);
+  }
+  int32_t* row = c->tables_host.data() + static_cast<size_t>(slot) * c->max_pages;
+  std::memcpy(row, pages, sizeof(int32_t) * count);
+  std::fill(row + count, row + c->max_pages, 0);
+  c->tables_dirty = true;
+  return LCR_OK;
+}
+
+extern "C" int lcr_batch_set_sampling(lcr_batch* c, int slot, float temperature, int top_k, float top_p,
+                                      uint64_t seed) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null batch");
+  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d outside 0..%d", slot,
+               c->o.max_batch - 1);
+  LCRB_REQUIRE(temperature >= 0.f && top_p > 0.f && top_p <= 1.f, LCR_ERR_INVALID,
+               "bad sampling parameters (temperature %g, top_p %g)", temperature, top_p);
+  c->inv_temp_host[static_cast<size_t>(slot)] = temperature > 0.f ? 1.0f / temperature : 0.f;
+  c->top_k_host[static_cast<size_t>(slot)] = top_k;
+  c->top_p_host[static_cast<size_t>(slot)] = top_p;
+  c->seed_host[static_cast<size_t>(slot)] = seed;
+  c->sampling_dirty = true;
+  return LCR_OK;
+}
+
+extern "C" int lcr_batch_step(lcr_batch* c, int n, const int32_t* tokens, const int32_t* positions) {
+  LCRB_REQUIRE(c && tokens && positions, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(n >= 1 && n <= c->o.max_batch, LCR_ERR_INVALID, "batch of %d slots; this context holds %d", n,
+               c->o.max_batch);
+  for (int b = 0; b < n; ++b) {
+    LCRB_REQUIRE(positions[b] >= 0 && positions[b] < c->o.max_seq, LCR_ERR_STATE,
+                 "slot %d: position %d outside the cache built for %d", b, positions[b], c->o.max_seq);
+    LCRB_REQUIRE((positions[b] / c->o.page_size) < c->max_pages, LCR_ERR_STATE, "slot %d: no page for position %d",
+                 b, positions[b]);
+  }
+  LCRB_CUDA(cudaSetDevice(c->device));
+  const size_t B = static_cast<size_t>(c->o.max_batch);
+  if (c->tables_dirty) {
+    LCRB_CUDA(cudaMemcpyAsync(c->tables, c->tables_host.data(), sizeof(int32_t) * B * c->max_pages,
+                              cudaMemcpyHostToDevice, c->stream));
+    c->tables_dirty = false;
+  }
+  if (c->sampling_dirty) {
+    LCRB_CUDA(cudaMemcpyAsync(c->inv_temp, c->inv_temp_host.data(), sizeof(float) * B, cudaMemcpyHostToDevice,
+                              c->stream));
+    LCRB_CUDA(cudaMemcpyAsync(c->top_k, c->top_k_host.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice,
+                              c->stream));
+    LCRB_CUDA(cudaMemcpyAsync(c->top_p, c->top_p_host.data(), sizeof(float) * B, cudaMemcpyHostToDevice,
+                              c->stream));
+    LCRB_CUDA(cudaMemcpyAsync(c->seed, c->seed_host.data(), sizeof(unsigned long long) * B,
+                              cudaMemcpyHostToDevice, c->stream));
+    c->sampling_dirty = false;
+  }
+  // (token, position) staging: a pinned area is reused only after the copy
+  // that last read it has completed.
+  const int slot = c->staging_next;
+  c->staging_next = (slot + 1) % kStaging;
+  LCRB_CUDA(cudaEventSynchronize(c->staged[slot]));
+  int32_t* area = c->pinned + static_cast<size_t>(slot) * 2 * B;
+  std::memcpy(area, tokens, sizeof(int32_t) * n);
+  std::memcpy(area + B, positions, sizeof(int32_t) * n);
+  LCRB_CUDA(cudaMemcpyAsync(c->tokens, area, sizeof(int32_t) * n, cudaMemcpyHostToDevice, c->stream));
+  LCRB_CUDA(cudaMemcpyAsync(c->positions, area + B, sizeof(int32_t) * n, cudaMemcpyHostToDevice, c->stream));
+  LCRB_CUDA(cudaEventRecord(c->staged[slot], c->stream));
+  c->last_n = n;
+  return launch_step(c, n);
+}
+
+extern "C" int lcr_batch_read(lcr_batch* c, int32_t* next_ids, int n) {
+  LCRB_REQUIRE(c && next_ids, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(n >= 0 && n <= c->o.max_batch, LCR_ERR_INVALID, "bad count %d", n);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_CUDA(cudaMemcpyAsync(next_ids, c->next, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, c->stream));
+  return check_status(c);
+}
+
+extern "C" int lcr_batch_logits(lcr_batch* c, int slot, float* host) {
+  LCRB_REQUIRE(c && host, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d", slot);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_CUDA(cudaMemcpyAsync(host, c->logits + static_cast<size_t>(slot) * c->d.vocab_size,
+                            sizeof(float) * c->d.vocab_size, cudaMemcpyDeviceToHost, c->stream));
+  return check_status(c);
+}
+
+extern "C" int lcr_batch_sync(lcr_batch* c) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null batch");
+  LCRB_CUDA(cudaSetDevice(c->device));
+  return check_status(c);
+}
+
+extern "C" lcr_stream_t lcr_batch_stream(lcr_batch* c) {
+  return c ? reinterpret_cast<lcr_stream_t>(c->stream) : nullptr;
+}
+
+extern "C" int lcr_batch_step_launches(const lcr_batch* c, int n) {
+  if (!c) return 0;
+  (void)n;
+  return 7 * c->d.num_layers + 3;
+}
+
+extern "C" int lcr_batch_time_steps(lcr_batch* c, int steps, float* ms) {
+  LCRB_REQUIRE(c && ms && steps > 0 && c->last_n > 0, LCR_ERR_INVALID,
+               "time_steps needs a previous lcr_batch_step and a positive count");
+  LCRB_CUDA(cudaSetDevice(c->device));
+  cudaEvent_t e0, e1;
+  LCRB_CUDA(cudaEventCreate(&e0));
+  LCRB_CUDA(cudaEventCreate(&e1));
+  cudaEventRecord(e0, c->stream);
+  int st = LCR_OK;
+  for (int i = 0; i < steps && st == LCR_OK; ++i) st = launch_step(c, c->last_n);
+  cudaEventRecord(e1, c->stream);
+  cudaEventSynchronize(e1);
+  float t = 0.f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (st != LCR_OK) return st;
+  *ms = t;
+  return check_status(c);
+}

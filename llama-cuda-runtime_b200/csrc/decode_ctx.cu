@@ -32,24 +32,12 @@
 #include "common.cuh"
 #include "dispatch.h"
 #include "gemv_dispatch.h"
+#include "rope_table.h"
 #include "tmap.h"
 #include "lcr_b200.h"
 #include "mega_dispatch.h"
 
-using namespace lcrb;
-
-namespace {
-
-enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8 };
-constexpr int kPinnedRing = 256;
-constexpr int kTimingSlots = 128;
-
-uint64_t splitmix64(uint64_t* s) {
-  uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
+namespace lcrb {
 
 // The RoPE table of src/config.cpp:223-259 (double math, float table).
 std::vector<float> rope_inv_freq(const lcr_model_desc& d) {
@@ -80,6 +68,24 @@ std::vector<float> rope_inv_freq(const lcr_model_desc& d) {
   }
   return f;
 }
+
+}  // namespace lcrb
+
+using namespace lcrb;
+
+namespace {
+
+enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8 };
+constexpr int kPinnedRing = 256;
+constexpr int kTimingSlots = 128;
+
+uint64_t splitmix64(uint64_t* s) {
+  uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
 
 }  // namespace
 

@@ -18,7 +18,8 @@
 //         the M-th key, ties at it are taken lowest index first, and a bitonic
 //         sort under that total order fixes their sequence;
 //       * the uniform is the caller's, or Philox4x32-10 (Salmon et al., SC'11)
-//         of (seed, counter, stream): the top 24 bits of word 0 times 2^-24.
+//         of (seed, counter = position, stream 0): the top 24 bits of word 0
+//         times 2^-24.
 #pragma once
 
 #include "common.cuh"
@@ -290,8 +291,9 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
       if (a.uniform != nullptr) {
         u = a.uniform[row];
       } else {
-        u = philox_uniform(a.seed[row], static_cast<unsigned long long>(a.counter[row]),
-                           static_cast<uint32_t>(row));
+        // Stream 0: a sequence's draws depend on its seed and position only,
+        // not on the batch slot it occupies.
+        u = philox_uniform(a.seed[row], static_cast<unsigned long long>(a.counter[row]), 0u);
       }
       const float top_p = a.top_p[row];
       const float inv_total = __fdiv_rn(1.0f, total);

@@ -67,6 +67,11 @@ class Options(ctypes.Structure):
                 ("flags", ctypes.c_int)]
 
 
+class BatchOptions(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("max_batch", ctypes.c_int), ("max_seq", ctypes.c_int),
+                ("page_size", ctypes.c_int), ("pool_pages", ctypes.c_int), ("flags", ctypes.c_int)]
+
+
 class KvView(ctypes.Structure):
     _fields_ = [("keys", ctypes.c_void_p), ("values", ctypes.c_void_p),
                 ("page_table", ctypes.c_void_p), ("page_size", ctypes.c_int),
@@ -121,6 +126,17 @@ _SIGS = {
     "lcr_time_steps": (_I, [_V, _I, ctypes.POINTER(_F)]),
     "lcr_time_gemv": (_I, [_V, _I, _I, _I, ctypes.POINTER(_F)]),
     "lcr_copy_trace": (_I, [_V, _V, _I, ctypes.POINTER(_I)]),
+    "lcr_batch_create": (_I, [_V, _V, _V, ctypes.POINTER(_V)]),
+    "lcr_batch_destroy": (None, [_V]),
+    "lcr_batch_set_pages": (_I, [_V, _I, _V, _I]),
+    "lcr_batch_set_sampling": (_I, [_V, _I, _F, _I, _F, ctypes.c_uint64]),
+    "lcr_batch_step": (_I, [_V, _I, _V, _V]),
+    "lcr_batch_read": (_I, [_V, _V, _I]),
+    "lcr_batch_logits": (_I, [_V, _I, _V]),
+    "lcr_batch_sync": (_I, [_V]),
+    "lcr_batch_stream": (_V, [_V]),
+    "lcr_batch_step_launches": (_I, [_V, _I]),
+    "lcr_batch_time_steps": (_I, [_V, _I, ctypes.POINTER(_F)]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -322,4 +338,85 @@ class Model:
     def time_gemv(self, matrix: int, layer: int = 0, reps: int = 20) -> float:
         ms = ctypes.c_float()
         check(lib().lcr_time_gemv(self.ctx, int(matrix), int(layer), int(reps), ctypes.byref(ms)))
+        return ms.value
+
+
+class Batch:
+    """Batched decode over a device copy of a WeightBlock: up to ``max_batch``
+    sequences in slots, one token each per step (lcr_batch_*). KV pages come
+    from a pool of ``pool_pages`` pages of ``page_size`` positions; the caller
+    assigns them per slot (``set_pages``), as a continuous-batching scheduler
+    does."""
+
+    def __init__(self, block: ck.WeightBlock, weights_dev=None, *, device: int = 0,
+                 max_batch: int = 64, max_seq: int = 4096, page_size: int = 16,
+                 pool_pages: int = 1024, flags: int = 0):
+        self.geom = block.geom
+        self.block = block
+        self.device = device
+        self.weights_dev = weights_dev if weights_dev is not None else upload_block(block, device)
+        base = self.weights_dev.data_ptr()
+        g = self.geom
+        addr = lambda name: base + block.offsets[name][0] * 2
+        self._layers = (LayerWeights * g.num_layers)(*[
+            LayerWeights(*[addr(n) for n in block.layer_groups(l)]) for l in range(g.num_layers)])
+        self._weights = Weights(addr("embed"), addr("final_norm"), addr("embed"), self._layers)
+        self._desc = desc_of(g)
+        self.options = BatchOptions(device, max_batch, max_seq, page_size, pool_pages, flags)
+        h = ctypes.c_void_p()
+        check(lib().lcr_batch_create(ctypes.byref(self._desc), ctypes.byref(self._weights),
+                                     ctypes.byref(self.options), ctypes.byref(h)))
+        self.h = h
+        self.max_batch = max_batch
+        self.page_size = page_size
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lcr_batch_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_pages(self, slot: int, pages) -> None:
+        arr = np.ascontiguousarray(np.asarray(pages, dtype=np.int32))
+        check(lib().lcr_batch_set_pages(self.h, int(slot), arr.ctypes.data, int(arr.size)))
+
+    def set_sampling(self, slot: int, temperature: float = 0.0, top_k: int = 0,
+                     top_p: float = 1.0, seed: int = 0) -> None:
+        check(lib().lcr_batch_set_sampling(self.h, int(slot), float(temperature), int(top_k),
+                                           float(top_p), int(seed)))
+
+    def step(self, tokens, positions) -> None:
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.int32))
+        assert t.size == p.size
+        check(lib().lcr_batch_step(self.h, int(t.size), t.ctypes.data, p.ctypes.data))
+
+    def read(self, n: int) -> np.ndarray:
+        out = np.zeros(n, dtype=np.int32)
+        check(lib().lcr_batch_read(self.h, out.ctypes.data, int(n)))
+        return out
+
+    def logits(self, slot: int) -> np.ndarray:
+        out = np.zeros(self.geom.vocab_size, dtype=np.float32)
+        check(lib().lcr_batch_logits(self.h, int(slot), out.ctypes.data))
+        return out
+
+    def sync(self) -> None:
+        check(lib().lcr_batch_sync(self.h))
+
+    @property
+    def stream(self) -> int:
+        return lib().lcr_batch_stream(self.h)
+
+    def step_launches(self, n: int) -> int:
+        return lib().lcr_batch_step_launches(self.h, int(n))
+
+    def time_steps(self, steps: int) -> float:
+        ms = ctypes.c_float()
+        check(lib().lcr_batch_time_steps(self.h, int(steps), ctypes.byref(ms)))
         return ms.value
