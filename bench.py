@@ -23,6 +23,10 @@ Multi-GPU (torchrun): every rank decodes its own independent sequence on its
 own GPU with its own weight replica -- the reference has no collective on this
 path, so there is none; value = all ranks' tokens / the slowest rank's time.
 
+batched  config 4 on the batched context in the same run:
+         64 sequences kept in slots by continuous batching, tcgen05 projections;
+         decode steps timed with CUDA events (see batched_bench).
+
 --impl reference: the reference has no CPU implementation of the decode step,
 so its arm is the fp32 host evaluation (oracle port) of the same workload on
 the host cores, rank 0 only.
@@ -202,6 +206,89 @@ def run_reference(args, world, rank):
     print(json.dumps(line))
 
 
+BATCH = 64
+BATCH_TARGET = 128
+BATCH_MAX_CTX = 4096
+
+
+def batched_bench(block, weights_dev, local, world, steps, warmup):
+    """Config 4 on the batched context: 64 slots kept
+    full by continuous batching -- initial contexts uniform in [128, 4096]
+    (seed 3), Poisson(4) arrivals per step replacing finished sequences, 128
+    tokens each, temperature 0.8 / top-k 50 / top-p 0.9 with per-sequence
+    Philox seeds, paged KV (16-position pages, shuffled pool). Admitted
+    contexts get synthetic KV (lcr_batch_fill_kv; prefill is not built);
+    admissions happen between steps, and the timed unit is the decode step:
+    CUDA events on the batch stream around each step."""
+    import torch
+
+    from lcr_b200 import checkpoint as ck
+    from lcr_b200 import runtime as rt
+    from lcr_b200 import scheduler as sch
+
+    g = ck.LLAMA_3_2_1B
+    max_seq = BATCH_MAX_CTX + BATCH_TARGET + 16
+    per_seq = (max_seq + 15) // 16
+    pool_pages = (BATCH + 4) * per_seq
+    bt = rt.Batch(block, weights_dev, device=local, max_batch=BATCH, max_seq=max_seq, page_size=16,
+                  pool_pages=pool_pages)
+    cb = sch.ContinuousBatcher(bt, page_size=16, pool_pages=pool_pages, page_seed=3,
+                               temperature=0.8, top_k=50, top_p=0.9)
+    for q in sch.config4_workload(np.random.default_rng(3), BATCH, BATCH_TARGET, 128, BATCH_MAX_CTX):
+        cb.submit(q)
+    arrivals = np.random.default_rng(4003)
+    next_sid = BATCH
+
+    def admit():
+        nonlocal next_sid
+        new, next_sid = sch.config4_arrivals(arrivals, next_sid, 4.0, BATCH_TARGET, 128, BATCH_MAX_CTX)
+        for q in new:
+            cb.submit(q)
+        cb.fill()
+
+    for _ in range(warmup):
+        admit()
+        cb.step()
+    bt.sync()
+    stream = torch.cuda.ExternalStream(bt.stream, device=f"cuda:{local}")
+    events, tokens, kv_positions = [], 0, 0
+    barrier(world)
+    torch.cuda.synchronize()
+    for _ in range(steps):
+        admit()
+        n = cb.active()
+        kv_positions += sum(cb.slots[b].position for b in range(n))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        tokens += cb.step()
+        e1.record(stream)
+        events.append((e0, e1))
+    bt.sync()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = sum(a.elapsed_time(b) for a, b in events)
+    max_ms = reduce_max(world, ms)
+    per_step_ms = max_ms / steps
+    bytes_step = g.weight_bytes_per_token() + (kv_positions / steps) * g.kv_bytes_per_position()
+    peak, _ = measured_peaks()
+    out = {
+        "workload": "config4: Llama-3.2-1B, 64 slots, contexts U[128,4096] (seed 3), Poisson(4) "
+                    "arrivals/step replace finished sequences, 128 tokens each, temp 0.8 top-k 50 "
+                    "top-p 0.9, per-sequence Philox, paged KV 16 (shuffled pool)",
+        "value": round(world * tokens / (max_ms / 1000.0), 1), "unit": "tok/s",
+        "ms_per_step": round(per_step_ms, 4), "steps": steps, "warmup": warmup,
+        "mean_context": round(kv_positions / max(1, steps * BATCH), 1),
+        "bytes_per_step": int(bytes_step),
+        "hbm_gbs": round(bytes_step / (per_step_ms / 1000) / 1e9, 1),
+        "frac_of_peak": round(bytes_step / (per_step_ms / 1000) / 1e9 / peak, 4),
+        "gpu_launches_per_step": bt.step_launches(BATCH),
+        "finished_sequences": cb.finished,
+        "note": "admitted contexts get synthetic KV (prefill not built); decode steps timed",
+    }
+    bt.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -209,6 +296,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched measurement")
+    ap.add_argument("--batched-steps", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)
@@ -302,6 +391,11 @@ def main():
         ms = m.time_gemv(i, 0, 20)
         per_matrix[name] = {"us": round(ms * 1000, 2),
                             "gbs": round(bytes_of[name] / (ms / 1000) / 1e9, 1)}
+    batched = None
+    if not args.no_batched:
+        batched = batched_bench(block, m.weights_dev, local, world, args.batched_steps,
+                                max(3, args.warmup // 4))
+
     ms_per_step = max_ms / args.steps
     # positions 127..382 read 128..383 cached positions: mean 255.5
     ctx_mean = PROMPT + (WINDOW - 1) / 2
@@ -337,6 +431,7 @@ def main():
             "gpu_launches": args.steps * m.step_launches(),
             "clocks": clocks,
             "cpu_baseline": base,
+            "batched": batched,
         }
         print(json.dumps(line))
     m.close()

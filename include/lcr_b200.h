@@ -322,9 +322,16 @@ LCR_API int lcr_batch_set_sampling(lcr_batch* batch, int slot, float temperature
                                    float top_p, uint64_t seed);
 /* One step for slots [0, n): slot b decodes host tokens[b] at host
  * positions[b] (its K/V are written at that position; it attends to
- * positions 0..positions[b]), then samples its next token. Asynchronous. */
+ * positions 0..positions[b]), then samples its next token. tokens = NULL
+ * continues every slot with the id it sampled in the previous step (no host
+ * round trip). Asynchronous. */
 LCR_API int lcr_batch_step(lcr_batch* batch, int n, const int32_t* tokens,
                            const int32_t* positions);
+/* Writes a seeded synthetic context (approximately standard normal K and V,
+ * bf16) for positions [0, length) of slot `slot` in every layer, through its
+ * current page table: a stand-in for the prompt's prefill when a benchmark
+ * admits a sequence. Asynchronous. */
+LCR_API int lcr_batch_fill_kv(lcr_batch* batch, int slot, int length, uint64_t seed);
 /* The last step's sampled ids of slots [0, n) into host memory (synchronous). */
 LCR_API int lcr_batch_read(lcr_batch* batch, int32_t* next_ids, int n);
 /* The last step's fp32 logits [vocab] of one slot into host memory (synchronous). */

@@ -89,4 +89,54 @@ __global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const NormRowsA
   }
 }
 
+// Seeded synthetic K/V for positions [0, length) of one sequence in every
+// layer: each element is an approximately standard normal value (the sum of
+// four hashed uniforms, centred and scaled), rounded to bf16, written at the
+// sequence's pages. Stands in for the prompt's KV when a benchmark admits a
+// sequence without running its prefill.
+struct FillKvArgs {
+  bf16* kpool;
+  bf16* vpool;
+  size_t layer_elems;
+  int layers, kv_heads, head_dim, page_size, length;
+  const int32_t* pages;  // the slot's device page table [max_pages]
+  unsigned long long seed;
+};
+
+__device__ __forceinline__ uint32_t fill_hash(uint64_t x) {
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdull;
+  x ^= x >> 33;
+  x *= 0xc4ceb9fe1a85ec53ull;
+  x ^= x >> 33;
+  return static_cast<uint32_t>(x);
+}
+
+__global__ void fill_kv_kernel(const FillKvArgs a) {
+  const long long per_layer = static_cast<long long>(a.length) * a.kv_heads * a.head_dim;
+  const long long total = per_layer * a.layers;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int layer = static_cast<int>(i / per_layer);
+    long long r = i % per_layer;
+    const int pos = static_cast<int>(r / (a.kv_heads * a.head_dim));
+    r %= a.kv_heads * a.head_dim;
+    const int head = static_cast<int>(r / a.head_dim), dim = static_cast<int>(r % a.head_dim);
+    const size_t off = static_cast<size_t>(layer) * a.layer_elems +
+                       (static_cast<size_t>(a.pages[pos / a.page_size]) * a.kv_heads + head) * a.page_size * a.head_dim +
+                       static_cast<size_t>(pos % a.page_size) * a.head_dim + dim;
+    const uint64_t key = a.seed ^ (static_cast<uint64_t>(i) * 0x9E3779B97F4A7C15ull);
+    float kv[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      float u = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) u += (fill_hash(key + 4 * t + j) >> 8) * (1.0f / 16777216.0f);
+      kv[t] = (u - 2.0f) * 1.7320508f;
+    }
+    a.kpool[off] = __float2bfloat16_rn(kv[0]);
+    a.vpool[off] = __float2bfloat16_rn(kv[1]);
+  }
+}
+
 }  // namespace lcrb

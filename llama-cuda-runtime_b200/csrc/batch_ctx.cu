@@ -513,7 +513,7 @@ extern "C" int lcr_batch_set_sampling(lcr_batch* c, int slot, float temperature,
 }
 
 extern "C" int lcr_batch_step(lcr_batch* c, int n, const int32_t* tokens, const int32_t* positions) {
-  LCRB_REQUIRE(c && tokens && positions, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(c && positions, LCR_ERR_INVALID, "null argument");
   LCRB_REQUIRE(n >= 1 && n <= c->o.max_batch, LCR_ERR_INVALID, "batch of %d slots; this context holds %d", n,
                c->o.max_batch);
   for (int b = 0; b < n; ++b) {
@@ -546,13 +546,44 @@ extern "C" int lcr_batch_step(lcr_batch* c, int n, const int32_t* tokens, const 
   c->staging_next = (slot + 1) % kStaging;
   LCRB_CUDA(cudaEventSynchronize(c->staged[slot]));
   int32_t* area = c->pinned + static_cast<size_t>(slot) * 2 * B;
-  std::memcpy(area, tokens, sizeof(int32_t) * n);
   std::memcpy(area + B, positions, sizeof(int32_t) * n);
-  LCRB_CUDA(cudaMemcpyAsync(c->tokens, area, sizeof(int32_t) * n, cudaMemcpyHostToDevice, c->stream));
+  if (tokens) {
+    std::memcpy(area, tokens, sizeof(int32_t) * n);
+    LCRB_CUDA(cudaMemcpyAsync(c->tokens, area, sizeof(int32_t) * n, cudaMemcpyHostToDevice, c->stream));
+  } else {  // each slot continues with the id it sampled last step
+    LCRB_CUDA(cudaMemcpyAsync(c->tokens, c->next, sizeof(int32_t) * n, cudaMemcpyDeviceToDevice, c->stream));
+  }
   LCRB_CUDA(cudaMemcpyAsync(c->positions, area + B, sizeof(int32_t) * n, cudaMemcpyHostToDevice, c->stream));
   LCRB_CUDA(cudaEventRecord(c->staged[slot], c->stream));
   c->last_n = n;
   return launch_step(c, n);
+}
+
+extern "C" int lcr_batch_fill_kv(lcr_batch* c, int slot, int length, uint64_t seed) {
+  LCRB_REQUIRE(c, LCR_ERR_INVALID, "null batch");
+  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d", slot);
+  LCRB_REQUIRE(length >= 0 && length <= c->o.max_seq, LCR_ERR_STATE, "length %d outside the cache", length);
+  if (length == 0) return LCR_OK;
+  LCRB_CUDA(cudaSetDevice(c->device));
+  if (c->tables_dirty) {
+    LCRB_CUDA(cudaMemcpyAsync(c->tables, c->tables_host.data(),
+                              sizeof(int32_t) * static_cast<size_t>(c->o.max_batch) * c->max_pages,
+                              cudaMemcpyHostToDevice, c->stream));
+    c->tables_dirty = false;
+  }
+  FillKvArgs a = {};
+  a.kpool = c->kpool;
+  a.vpool = c->vpool;
+  a.layer_elems = c->layer_elems;
+  a.layers = c->d.num_layers;
+  a.kv_heads = c->d.num_kv_heads;
+  a.head_dim = c->d.head_dim;
+  a.page_size = c->o.page_size;
+  a.length = length;
+  a.pages = c->tables + static_cast<size_t>(slot) * c->max_pages;
+  a.seed = seed;
+  fill_kv_kernel<<<4 * c->sms, 256, 0, c->stream>>>(a);
+  return launch_status("fill_kv");
 }
 
 extern "C" int lcr_batch_read(lcr_batch* c, int32_t* next_ids, int n) {

@@ -132,6 +132,7 @@ _SIGS = {
     "lcr_batch_set_sampling": (_I, [_V, _I, _F, _I, _F, ctypes.c_uint64]),
     "lcr_batch_step": (_I, [_V, _I, _V, _V]),
     "lcr_batch_read": (_I, [_V, _V, _I]),
+    "lcr_batch_fill_kv": (_I, [_V, _I, _I, ctypes.c_uint64]),
     "lcr_batch_logits": (_I, [_V, _I, _V]),
     "lcr_batch_sync": (_I, [_V]),
     "lcr_batch_stream": (_V, [_V]),
@@ -391,10 +392,17 @@ class Batch:
                                            float(top_p), int(seed)))
 
     def step(self, tokens, positions) -> None:
-        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        """tokens=None continues each slot with its previous sample."""
         p = np.ascontiguousarray(np.asarray(positions, dtype=np.int32))
+        if tokens is None:
+            check(lib().lcr_batch_step(self.h, int(p.size), None, p.ctypes.data))
+            return
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         assert t.size == p.size
         check(lib().lcr_batch_step(self.h, int(t.size), t.ctypes.data, p.ctypes.data))
+
+    def fill_kv(self, slot: int, length: int, seed: int) -> None:
+        check(lib().lcr_batch_fill_kv(self.h, int(slot), int(length), int(seed)))
 
     def read(self, n: int) -> np.ndarray:
         out = np.zeros(n, dtype=np.int32)

@@ -122,3 +122,55 @@ def test_batch_rejects_bad_inputs(tiny):
     with pytest.raises(rt.LcrError):
         bt.step([1] * 5, [0] * 5)  # 5 slots in a batch of 4
     bt.close()
+
+
+def test_device_feedback_equals_host_round_trip(tiny):
+    """tokens=None (each slot continues with its last sample, on the device)
+    gives the same steps as reading the samples back and passing them in."""
+    block, wdev = tiny
+    slots, max_seq = 12, 48
+    runs = []
+    for feedback in (True, False):
+        bt = rt.Batch(block, wdev, max_batch=slots, max_seq=max_seq, page_size=PAGE,
+                      pool_pages=slots * (max_seq // PAGE))
+        for s in range(slots):
+            bt.set_pages(s, list(range(s * (max_seq // PAGE), (s + 1) * (max_seq // PAGE))))
+            bt.set_sampling(s, 0.9, 40, 0.95, 1234 + s)
+        bt.step([int(t) for t in ck.prompt_ids(77, slots)], [0] * slots)
+        ids = []
+        for t in range(1, 20):
+            if feedback:
+                bt.step(None, [t] * slots)
+            else:
+                bt.step(bt.read(slots), [t] * slots)
+            ids.append(bt.read(slots).copy())
+        runs.append((np.array(ids), bt.logits(slots - 1)))
+        bt.close()
+    assert np.array_equal(runs[0][0], runs[1][0])
+    assert np.array_equal(runs[0][1], runs[1][1])
+
+
+def test_scheduler_runs_config4_shape_on_tiny(tiny):
+    """The continuous batcher on the device: staggered sequences with
+    synthetic contexts, arrivals filling freed slots, sampled steps."""
+    from lcr_b200 import scheduler as sch
+    block, wdev = tiny
+    slots, max_seq = 16, 256
+    pool = (slots + 2) * (max_seq // PAGE)
+    bt = rt.Batch(block, wdev, max_batch=slots, max_seq=max_seq, page_size=PAGE, pool_pages=pool)
+    cb = sch.ContinuousBatcher(bt, page_size=PAGE, pool_pages=pool, page_seed=3)
+    rng = np.random.default_rng(3)
+    for q in sch.config4_workload(rng, slots, 24, 16, 200):
+        cb.submit(q)
+    sid = slots
+    decoded = 0
+    for _ in range(60):
+        new, sid = sch.config4_arrivals(rng, sid, 2.0, 24, 16, 200)
+        for q in new:
+            cb.submit(q)
+        cb.fill()
+        decoded += cb.step()
+    ids = bt.read(cb.active())
+    assert cb.finished >= 30 and decoded == 60 * slots
+    assert np.all((ids >= 0) & (ids < block.geom.vocab_size))
+    bt.close()
