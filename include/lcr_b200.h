@@ -338,7 +338,8 @@ LCR_API int lcr_batch_read(lcr_batch* batch, int32_t* next_ids, int n);
 LCR_API int lcr_batch_logits(lcr_batch* batch, int slot, float* host);
 LCR_API int lcr_batch_sync(lcr_batch* batch);
 LCR_API lcr_stream_t lcr_batch_stream(lcr_batch* batch);
-/* Kernel launches in one step of n slots. */
+/* Kernel launches in one step of n slots (split projections add a reduction
+ * launch each); 0 until a step of n slots has been issued. */
 LCR_API int lcr_batch_step_launches(const lcr_batch* batch, int n);
 /* Replays the step of the last lcr_batch_step `steps` times (same tokens and
  * positions) between CUDA events on the batch stream: ms in total. */

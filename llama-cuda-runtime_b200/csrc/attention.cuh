@@ -61,18 +61,19 @@ struct AttnArgs {
 
 constexpr int kAttnConsumerWarps = 4;
 constexpr int kAttnThreads = (kAttnConsumerWarps + 1) * 32;
-constexpr int kAttnBlock = 16;  // positions per stage
+constexpr int kAttnBlock = 16;      // positions per chunk unit (split boundaries, pages)
+constexpr int kAttnStagePos = 64;   // positions per ring stage
 
 // Largest split count whose partials for one (sequence, KV head) group fit the
 // stage ring, so the last CTA can merge them from shared memory.
 template <int D, int STAGES>
 constexpr int attn_max_staged_splits(int group) {
-  return (STAGES * 2 * kAttnBlock * D * 2) / (group * (2 + D) * 4);
+  return (STAGES * 2 * kAttnStagePos * D * 2) / (group * (2 + D) * 4);
 }
 
 template <int D, int STAGES>
 constexpr size_t attn_smem_bytes() {
-  return static_cast<size_t>(STAGES) * 2 * kAttnBlock * D * 2 + 2 * STAGES * 8 +
+  return static_cast<size_t>(STAGES) * 2 * kAttnStagePos * D * 2 + 2 * STAGES * 8 +
          static_cast<size_t>(kAttnConsumerWarps) * 8 * (D + 2) * 4 + 64;
 }
 
@@ -143,10 +144,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   constexpr int LPP = D / 8;                    // lanes per position
   constexpr int GPW = 32 / LPP;                 // position groups per warp
   constexpr int NG = kAttnConsumerWarps * GPW;  // groups per CTA
-  constexpr int PASSES = kAttnBlock / NG;
+  constexpr int PASSES = kAttnStagePos / NG;
   constexpr int ROWB = D * 2;                   // bytes per K (or V) row
-  constexpr int KB = kAttnBlock * ROWB;         // bytes of K per stage
-  static_assert(kAttnBlock % NG == 0, "positions per stage");
+  constexpr int KB = kAttnStagePos * ROWB;      // bytes of K per stage
+  static_assert(kAttnStagePos % NG == 0 && kAttnStagePos % kAttnBlock == 0, "positions per stage");
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   const int begin = split * chunk;
   const int end = valid ? min(seq_len, begin + chunk) : 0;
   const int cache_end = min(end, pos);  // positions read from the cache
-  const int nblocks = cache_end > begin ? (cache_end - begin + kAttnBlock - 1) / kAttnBlock : 0;
+  const int nblocks = cache_end > begin ? (cache_end - begin + kAttnStagePos - 1) / kAttnStagePos : 0;
 
   if constexpr (FUSED) {
     // The angles depend only on the position: one sincosf per pair per CTA,
@@ -202,27 +203,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
             !mbar_wait(&empty[slot], ((blk / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
           break;
         }
-        const int p0 = begin + blk * kAttnBlock;
-        long long off;
-        if constexpr (PAGED) {
-          int page = table[p0 / a.page_size];
-          if (page < 0 || page >= a.pool_pages) {
-            if (a.status) atomicOr(a.status, kStatusBadPage);
-            page = 0;
-          }
-          off = static_cast<long long>(page) * a.page_stride + kvh * a.head_stride +
-                static_cast<long long>(p0 % a.page_size) * D;
-        } else {
-          off = static_cast<long long>(b) * a.seq_stride + kvh * a.head_stride +
-                static_cast<long long>(p0) * D;
-        }
-        // Copy only positions below cache_end: the caller's cache may end
-        // inside this 16-position block.
-        const uint32_t bytes = static_cast<uint32_t>(min(kAttnBlock, cache_end - p0)) * ROWB;
+        const int p0 = begin + blk * kAttnStagePos;
+        // Copy only positions below cache_end (the caller's cache may end
+        // inside this stage), in runs that do not cross a page.
+        const int nvalid = min(kAttnStagePos, cache_end - p0);
         uint8_t* dst = ring + slot * 2 * KB;
-        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-        bulk_g2s(dst, a.kpool + off, bytes, &full[slot]);
-        bulk_g2s(dst + KB, a.vpool + off, bytes, &full[slot]);
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nvalid) * 2 * ROWB);
+        for (int n = 0; n < nvalid;) {
+          int run = nvalid - n;
+          long long off;
+          const int p = p0 + n;
+          if constexpr (PAGED) {
+            run = min(run, a.page_size - p % a.page_size);
+            int page = table[p / a.page_size];
+            if (page < 0 || page >= a.pool_pages) {
+              if (a.status) atomicOr(a.status, kStatusBadPage);
+              page = 0;
+            }
+            off = static_cast<long long>(page) * a.page_stride + kvh * a.head_stride +
+                  static_cast<long long>(p % a.page_size) * D;
+          } else {
+            off = static_cast<long long>(b) * a.seq_stride + kvh * a.head_stride + static_cast<long long>(p) * D;
+          }
+          const uint32_t bytes = static_cast<uint32_t>(run) * ROWB;
+          bulk_g2s(dst + n * ROWB, a.kpool + off, bytes, &full[slot]);
+          bulk_g2s(dst + KB + n * ROWB, a.vpool + off, bytes, &full[slot]);
+          n += run;
+        }
         issued = blk + 1;
       }
       // Never leave the CTA with a copy still writing its shared memory.
@@ -259,7 +266,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       if (!mbar_wait(&full[slot], (blk / STAGES) & 1, a.status, kStatusTimeoutFull)) break;
       const uint8_t* kst = ring + slot * 2 * KB;
       const uint8_t* vst = kst + KB;
-      const int p0 = begin + blk * kAttnBlock;
+      const int p0 = begin + blk * kAttnStagePos;
 #pragma unroll
       for (int pass = 0; pass < PASSES; ++pass) {
         const int pl = pass * NG + grp;

@@ -3,7 +3,7 @@
 //
 // A step of n slots is, per layer:
 //   norm_rows_kernel        x -> xn (layer 0: the token embeddings)
-//   gemm_tc_kernel          qkv  = xn W_qkv^T           (split-K)
+//   gemm_tc_kernel          qkv  = xn W_qkv^T           (split-K, + reduction)
 //   attn_decode_kernel      RoPE, K/V write at each slot's position, paged
 //                           attention over 0..position, split merge -> attn
 //   gemm_tc_kernel          x   += attn W_o^T (residual epilogue, split-K)
@@ -75,7 +75,6 @@ struct lcr_batch {
   float* partials = nullptr;
   unsigned* attn_ctr = nullptr;
   float* work = nullptr;
-  unsigned* gemm_ctr = nullptr;
   float* inv_freq = nullptr;
   int32_t* tokens = nullptr;
   int32_t* positions = nullptr;
@@ -103,6 +102,7 @@ struct lcr_batch {
   int staging_next = 0;
 
   std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, int> launches_by_n;  // kernels one step of n slots launches
   int last_n = 0;
   int launches = 0;
 };
@@ -194,11 +194,10 @@ int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb
   // workspace.
   int splits = std::max(1, (c->sms + tiles - 1) / tiles);
   splits = std::min(splits, std::max(1, slabs / 2));
-  while (splits > 1 && static_cast<size_t>(tiles) * splits * nb * kTcTileM > c->work_floats) --splits;
+  while (splits > 1 && gemm_tc_work_floats(n, n_out, epi, splits) > c->work_floats) --splits;
   a.splits = splits;
   a.work = c->work;
-  a.counters = c->gemm_ctr;
-  ++c->launches;
+  c->launches += splits > 1 ? 2 : 1;
   return gemm_tc_launch(a, wm, xm, nb, epi, c->stream);
 }
 
@@ -222,9 +221,12 @@ int attention_launch_layer(lcr_batch* c, int layer, int n) {
   a.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
   a.max_seq = c->o.max_seq;
   a.positions = c->positions;
-  // Enough (sequence, KV head, split) CTAs for about two per SM.
-  a.splits = std::max(1, std::min(c->attn_splits_cap, (2 * c->sms + d.num_kv_heads * n - 1) /
-                                                          (d.num_kv_heads * n)));
+  // Splits of at most ~512 cached positions each (so long contexts spread
+  // over many CTAs), and at least about two (sequence, KV head, split) CTAs
+  // per SM; short sequences get correspondingly short chunks.
+  const int by_length = (c->o.max_seq + 511) / 512;
+  const int by_sms = (2 * c->sms + d.num_kv_heads * n - 1) / (d.num_kv_heads * n);
+  a.splits = std::max(1, std::min(c->attn_splits_cap, std::max(by_length, by_sms)));
   a.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
   a.out = c->attn;
   a.partials = c->partials;
@@ -288,12 +290,17 @@ int enqueue_step(lcr_batch* c, int n) {
 }
 
 int launch_step(lcr_batch* c, int n) {
-  if (!c->use_graph) return enqueue_step(c, n);
+  if (!c->use_graph) {
+    LCRB_TRY(enqueue_step(c, n));
+    c->launches_by_n[n] = c->launches;
+    return LCR_OK;
+  }
   auto it = c->graphs.find(n);
   if (it == c->graphs.end()) {
     cudaGraph_t g = nullptr;
     LCRB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
     const int st = enqueue_step(c, n);
+    if (st == LCR_OK) c->launches_by_n[n] = c->launches;
     const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (st != LCR_OK) {
       if (g) cudaGraphDestroy(g);
@@ -403,7 +410,6 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   const size_t o_act = carve(sizeof(bf16) * B * d.intermediate_size);
   const size_t o_part = carve(sizeof(float) * B * d.num_heads * c->attn_splits_cap * (2 + d.head_dim));
   const size_t o_actr = carve(sizeof(unsigned) * B * d.num_kv_heads);
-  const size_t o_gctr = carve(sizeof(unsigned) * 4096);
   const size_t o_freq = carve(sizeof(float) * d.head_dim / 2);
   const size_t o_tok = carve(sizeof(int32_t) * B);
   const size_t o_pos = carve(sizeof(int32_t) * B);
@@ -426,7 +432,6 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
     c->act = reinterpret_cast<bf16*>(b + o_act);
     c->partials = reinterpret_cast<float*>(b + o_part);
     c->attn_ctr = reinterpret_cast<unsigned*>(b + o_actr);
-    c->gemm_ctr = reinterpret_cast<unsigned*>(b + o_gctr);
     c->inv_freq = reinterpret_cast<float*>(b + o_freq);
     c->tokens = reinterpret_cast<int32_t*>(b + o_tok);
     c->positions = reinterpret_cast<int32_t*>(b + o_pos);
@@ -444,8 +449,10 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   if (st == LCR_OK) {
     cuda(cudaMalloc(&c->logits, sizeof(float) * B * d.vocab_size), "cudaMalloc(logits)");
   }
-  // Split-K workspace: at most two CTAs per SM's worth of partial tiles.
-  c->work_floats = static_cast<size_t>(2 * c->sms) * 128 * kTcTileM;
+  // Split-K workspace, per batch row: two splits of the gate/up projection
+  // (2 x 2F columns), or 32768 columns of the others (e.g. 10 splits of the
+  // 1B model's QKV); a projection that would need more takes fewer splits.
+  c->work_floats = B * std::max<size_t>(32768, 4 * static_cast<size_t>(d.intermediate_size));
   if (st == LCR_OK) cuda(cudaMalloc(&c->work, c->work_floats * sizeof(float)), "cudaMalloc(split-K workspace)");
   // KV pools: [layer][page][kv_head][page_size][D].
   c->layer_elems = static_cast<size_t>(o.pool_pages) * d.num_kv_heads * o.page_size * d.head_dim;
@@ -615,8 +622,8 @@ extern "C" lcr_stream_t lcr_batch_stream(lcr_batch* c) {
 
 extern "C" int lcr_batch_step_launches(const lcr_batch* c, int n) {
   if (!c) return 0;
-  (void)n;
-  return 7 * c->d.num_layers + 3;
+  const auto it = c->launches_by_n.find(n);
+  return it == c->launches_by_n.end() ? 0 : it->second;
 }
 
 extern "C" int lcr_batch_time_steps(lcr_batch* c, int steps, float* ms) {

@@ -9,7 +9,7 @@
 
 namespace lcrb {
 
-constexpr int kAttnStages = 8;
+constexpr int kAttnStages = 4;
 
 int attn_launch(const AttnArgs& a, bool fused, int head_dim, int group, bool paged, int kv_heads,
                 int seqs, cudaStream_t s, bool pdl);

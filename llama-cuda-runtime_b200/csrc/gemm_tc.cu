@@ -1,6 +1,8 @@
 // Instantiations and launch of the tcgen05 batched projection.
 #include "gemm_tc.h"
 
+#include <algorithm>
+
 namespace lcrb {
 namespace {
 
@@ -13,7 +15,14 @@ int launch_t(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, 
   const int tiles_b = (a.rows + NB - 1) / NB;
   dim3 grid(static_cast<unsigned>(tiles_n * tiles_b), static_cast<unsigned>(a.splits));
   kernel<<<grid, kTcThreads, smem, s>>>(a, wmap, xmap);
-  return launch_status("tcgen05 projection");
+  LCRB_TRY(launch_status("tcgen05 projection"));
+  if (a.splits > 1) {
+    const long long total = static_cast<long long>(a.rows) * a.n_out;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 4096));
+    gemm_tc_reduce_kernel<EPI><<<blocks, 256, 0, s>>>(a);
+    LCRB_TRY(launch_status("tcgen05 split-K reduction"));
+  }
+  return LCR_OK;
 }
 
 template <int NB>
@@ -36,13 +45,18 @@ int gemm_tc_batch_tile(int rows) {
   return 128;
 }
 
+size_t gemm_tc_work_floats(int rows, int n_out, int epi, int splits) {
+  const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
+  return splits > 1 ? static_cast<size_t>(splits) * rows * tiles_n * kTcTileM : 0;
+}
+
 int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi,
                    cudaStream_t stream) {
   LCRB_REQUIRE(a.K % kTcSlabK == 0 && a.K >= kTcSlabK && a.n_out > 0 && a.rows > 0, LCR_ERR_SHAPE,
                "tcgen05 projection: unsupported %d x %d x %d", a.rows, a.n_out, a.K);
   LCRB_REQUIRE(a.splits >= 1 && a.splits <= a.K / kTcSlabK, LCR_ERR_INVALID, "tcgen05 projection: %d splits",
                a.splits);
-  LCRB_REQUIRE(a.splits == 1 || (a.work && a.counters), LCR_ERR_INVALID,
+  LCRB_REQUIRE(a.splits == 1 || a.work, LCR_ERR_INVALID,
                "tcgen05 projection: split-K needs workspace");
   switch (nb) {
     case 16: return by_epi<16>(a, wmap, xmap, epi, stream);

@@ -15,9 +15,10 @@
 // 2-5 epilogue: each reads its 32 TMEM lanes (= 32 weight rows) with
 // tcgen05.ld.32x32b, so the four epilogue warps cover the 128 rows.
 //
-// Split-K: with splits > 1 each CTA adds its partial tile to fp32 workspace
-// in its own slot, and the last of a tile's CTAs (counter) sums the slots in
-// split order -- the result does not depend on which CTA finishes last.
+// Split-K: with splits > 1 each CTA stores its partial tile in fp32
+// workspace [split][row][tile column], and gemm_tc_reduce_kernel sums the
+// splits in split order and applies the epilogue -- the result does not
+// depend on which CTA finishes first.
 // Every wait is bounded (status bit, then the CTA drains its copies and MMAs
 // and frees TMEM before returning).
 #pragma once
@@ -53,8 +54,7 @@ struct TcArgs {
   float* yf;        // STORE_F32
   bf16* resid;      // RESID: resid = bf16(resid + bf16(out)), sums kept
   float* resid_sum;
-  float* work;      // splits > 1: [tiles][splits][NB][128] fp32
-  unsigned* counters;  // splits > 1: [tiles], zero between launches
+  float* work;      // splits > 1: [splits][rows][tiles_n * 128] fp32 partials
   uint32_t* status;    // device status word, or nullptr
 };
 
@@ -134,7 +134,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  int* s_flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] last CTA of the tile
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles_n = SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
@@ -154,7 +153,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
-    s_flags[0] = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -238,31 +236,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_wait_ld();
     }
-    bool final_ = a.splits == 1;
     if (have && a.splits > 1) {
-      // This CTA's partial into its own slot, then the last CTA of the tile
-      // sums the slots in split order.
-      float* slotp = a.work + (static_cast<size_t>(blockIdx.x) * a.splits + split) * NB * kTcTileM;
+      // This CTA's partial; gemm_tc_reduce_kernel finishes the tile.
+      const size_t m_total = static_cast<size_t>(tiles_n) * kTcTileM;
+      float* part = a.work + static_cast<size_t>(split) * a.rows * m_total + static_cast<size_t>(tile) * kTcTileM + row;
 #pragma unroll
-      for (int b = 0; b < NB; ++b) slotp[b * kTcTileM + row] = v[b];
-      __threadfence();
-      named_sync(2, 128);
-      if (tid == 64) s_flags[0] = atomicAdd(&a.counters[blockIdx.x], 1u) == static_cast<unsigned>(a.splits - 1);
-      named_sync(2, 128);
-      final_ = s_flags[0] != 0;
-      if (final_) {
-        __threadfence();
-        const float* base = a.work + static_cast<size_t>(blockIdx.x) * a.splits * NB * kTcTileM;
-#pragma unroll
-        for (int b = 0; b < NB; ++b) v[b] = 0.f;
-        for (int sp = 0; sp < a.splits; ++sp) {
-#pragma unroll
-          for (int b = 0; b < NB; ++b) v[b] += __ldcg(base + (static_cast<size_t>(sp) * NB + b) * kTcTileM + row);
-        }
-        if (tid == 64) a.counters[blockIdx.x] = 0u;
+      for (int b = 0; b < NB; ++b) {
+        if (b0 + b < a.rows) part[static_cast<size_t>(b0 + b) * m_total] = v[b];
       }
     }
-    if (have && final_) {
+    if (have && a.splits == 1) {
       if constexpr (SWIGLU) {
         // Rows 0-63 are gate rows n0 + r, rows 64-127 the matching up rows:
         // exchange through the (now idle) ring.
@@ -291,6 +274,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TMEM_COLS) : "memory");
+  }
+}
+
+// Split-K epilogue: y[b][n] = EPI(sum over splits, in split order, of the
+// partials). SWIGLU output n takes gate column (n / 64) * 128 + n % 64 and the
+// up column 64 after it (the tile layout of gemm_tc_kernel).
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_tc_reduce_kernel(const TcArgs a) {
+  const int tiles_n = EPI == EPI_SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
+  const size_t m_total = static_cast<size_t>(tiles_n) * kTcTileM;
+  const size_t plane = static_cast<size_t>(a.rows) * m_total;
+  const size_t total = static_cast<size_t>(a.rows) * a.n_out;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / a.n_out), n = static_cast<int>(i % a.n_out);
+    const size_t col = EPI == EPI_SWIGLU ? static_cast<size_t>(n / 64) * kTcTileM + n % 64 : n;
+    const float* src = a.work + static_cast<size_t>(b) * m_total + col;
+    float v = 0.f, up = 0.f;
+    for (int sp = 0; sp < a.splits; ++sp) {
+      v = __fadd_rn(v, __ldcg(src + sp * plane));
+      if constexpr (EPI == EPI_SWIGLU) up = __fadd_rn(up, __ldcg(src + sp * plane + 64));
+    }
+    tc_store<EPI>(a, b, n, v, up);
   }
 }
 

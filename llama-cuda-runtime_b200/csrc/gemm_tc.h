@@ -12,8 +12,10 @@ namespace lcrb {
 int gemm_tc_batch_tile(int rows);
 // Launches y = x w^T for `a.rows` batch rows: wmap = make_kmajor_map(w, n_out
 // (2F for SWIGLU as two halves), K, halves, 128 (64 for SWIGLU), 1), xmap =
-// make_kmajor_map(x, rows, K, 1, nb, 1). a.splits > 1 needs a.work and
-// a.counters. One CTA per (weight tile, batch tile, split).
+// make_kmajor_map(x, rows, K, 1, nb, 1). One CTA per (weight tile, batch
+// tile, split); a.splits > 1 needs a.work of gemm_tc_work_floats() floats and
+// adds a second launch (gemm_tc_reduce_kernel).
+size_t gemm_tc_work_floats(int rows, int n_out, int epi, int splits);
 int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi,
                    cudaStream_t stream);
 

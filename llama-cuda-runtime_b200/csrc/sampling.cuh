@@ -14,9 +14,13 @@
 //       * the denominator is a fixed tree: thread t sums i = t, t+1024, ... in
 //         index order, then an xor butterfly per warp and over the 32 warps;
 //       * the candidates are exactly the first M = min(top_k or V, 1024)
-//         tokens in (s desc, index asc) order: a 4 x 8-bit radix select finds
-//         the M-th key, ties at it are taken lowest index first, and a bitonic
-//         sort under that total order fixes their sequence;
+//         tokens in (s desc, index asc) order. A 2048-bucket histogram of -s
+//         (monotone in s) names the bucket holding the M-th token; every
+//         token at or above that bucket is compacted and bitonic-sorted under
+//         the total order, and the first M kept. When that set exceeds
+//         kMaxBucketSet (a flat distribution), a 4 x 8-bit radix select over
+//         the vocabulary finds the M-th key instead, ties at it taken lowest
+//         index first;
 //       * the uniform is the caller's, or Philox4x32-10 (Salmon et al., SC'11)
 //         of (seed, counter = position, stream 0): the top 24 bits of word 0
 //         times 2^-24.
@@ -28,6 +32,10 @@ namespace lcrb {
 
 constexpr int kSampleThreads = 1024;
 constexpr int kMaxCandidates = 1024;
+constexpr int kSampleBuckets = 2048;  // buckets of -s over [0, kSampleRange)
+constexpr float kSampleRange = 32.0f;
+constexpr int kMaxBucketSet = 2048;   // tokens the bucket path may sort
+static_assert(kSampleBuckets == 2 * kSampleThreads, "two buckets per thread in the scan");
 
 __device__ __forceinline__ float det_expf(float x) {
   if (!(x > -88.0f)) return 0.0f;
@@ -123,14 +131,42 @@ __device__ __forceinline__ float block_tree_sum_1024(float v, float* red32) {
   return w;
 }
 
+// Bucket of a scaled logit s <= 0: non-decreasing in -s, so a lower bucket
+// holds only strictly larger logits (NaN and very negative s go last).
+__device__ __forceinline__ int sample_bucket(float s) {
+  const float d = __fmul_rn(-s, kSampleBuckets / kSampleRange);
+  return d < static_cast<float>(kSampleBuckets - 1) ? max(0, static_cast<int>(d)) : kSampleBuckets - 1;
+}
+
+// Bitonic sort of keys[0, n) (n a power of two) under (key desc, index asc).
+__device__ __forceinline__ void sort_candidates(uint32_t* keys, uint32_t* idx, int n) {
+  for (int span = 2; span <= n; span <<= 1) {
+    for (int step = span >> 1; step > 0; step >>= 1) {
+      for (int i = threadIdx.x; i < n; i += kSampleThreads) {
+        const int j = i ^ step;
+        if (j > i) {
+          const bool i_first = (keys[i] > keys[j]) || (keys[i] == keys[j] && idx[i] < idx[j]);
+          const bool ascending_block = (i & span) != 0;  // reverse order in this half
+          if (ascending_block ? i_first : !i_first) {
+            const uint32_t tk = keys[i], ti = idx[i];
+            keys[i] = keys[j]; idx[i] = idx[j];
+            keys[j] = tk; idx[j] = ti;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
 static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(const SampleArgs a) {
   __shared__ float red32[32];
   __shared__ unsigned long long best_s;
-  __shared__ int hist[256];
-  __shared__ uint32_t ckey[kMaxCandidates];
-  __shared__ uint32_t cidx[kMaxCandidates];
+  __shared__ int hist[kSampleBuckets];
+  __shared__ uint32_t ckey[kMaxBucketSet];
+  __shared__ uint32_t cidx[kMaxBucketSet];
   __shared__ uint32_t sel_prefix, sel_want;
-  __shared__ int n_gt;
+  __shared__ int n_gt, sel_bucket, sel_count;
   __shared__ int scan[kSampleThreads / 32];
 
   const int row = blockIdx.x, tid = threadIdx.x;
@@ -163,25 +199,79 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
     for (int i = tid; i < V; i += kSampleThreads) mx = fmaxf(mx, L[i]);
     mx = block_max_1024(mx, red32);
 
-    // Pass 2: the denominator and the top digit histogram.
-    for (int i = tid; i < 256; i += kSampleThreads) hist[i] = 0;
+    // Pass 2: the denominator and the bucket histogram.
+    for (int i = tid; i < kSampleBuckets; i += kSampleThreads) hist[i] = 0;
     __syncthreads();
     float acc = 0.0f;
     for (int i = tid; i < V; i += kSampleThreads) {
       const float s = __fmul_rn(__fsub_rn(L[i], mx), inv_t);
       acc = __fadd_rn(acc, det_expf(s));
-      atomicAdd(&hist[sample_key(s) >> 24], 1);
+      atomicAdd(&hist[sample_bucket(s)], 1);
     }
-    const float total = block_tree_sum_1024(acc, red32);
+    const float total = block_tree_sum_1024(acc, red32);  // synchronises hist too
 
     int k = a.top_k[row];
     int M = k > 0 ? k : V;
     M = min(M, min(kMaxCandidates, V));
 
-    // Radix select of the M-th largest key, eight bits at a time.
-    uint32_t prefix = 0u, mask = 0u, want = static_cast<uint32_t>(M);
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      if (shift < 24) {
+    // The bucket holding the M-th token: a block-wide inclusive scan of the
+    // histogram (two buckets per thread).
+    {
+      const int lane = tid & 31, warp = tid >> 5;
+      const int h0 = hist[2 * tid], h1 = hist[2 * tid + 1];
+      int incl = h0 + h1;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      if (lane == 31) scan[warp] = incl;
+      if (tid == 0) {
+        sel_bucket = kSampleBuckets - 1;
+        sel_count = V;
+      }
+      __syncthreads();
+      int before = 0;
+      for (int w = 0; w < warp; ++w) before += scan[w];
+      const int c1 = before + incl;   // tokens in buckets <= 2 tid + 1
+      const int c0 = c1 - h1;         // tokens in buckets <= 2 tid
+      const int prev = c0 - h0;       // tokens in buckets < 2 tid
+      if (prev < M && c0 >= M) {
+        sel_bucket = 2 * tid;
+        sel_count = c0;
+      } else if (c0 < M && c1 >= M) {
+        sel_bucket = 2 * tid + 1;
+        sel_count = c1;
+      }
+      if (tid == 0) n_gt = 0;
+      __syncthreads();
+    }
+    const int bucket = sel_bucket, count = sel_count;
+
+    if (count <= kMaxBucketSet) {
+      // Pass 3: compact every token in buckets <= bucket, then sort them.
+      for (int i = tid; i < V; i += kSampleThreads) {
+        const float s = __fmul_rn(__fsub_rn(L[i], mx), inv_t);
+        if (sample_bucket(s) <= bucket) {
+          const int slot = atomicAdd(&n_gt, 1);
+          if (slot < kMaxBucketSet) {
+            ckey[slot] = sample_key(s);
+            cidx[slot] = static_cast<uint32_t>(i);
+          }
+        }
+      }
+      int n = 32;
+      while (n < count) n <<= 1;
+      for (int i = count + tid; i < n; i += kSampleThreads) {
+        ckey[i] = 0u;
+        cidx[i] = 0x7fffffffu;
+      }
+      __syncthreads();
+      sort_candidates(ckey, cidx, n);
+    } else {
+      // Radix select of the M-th largest key, eight bits at a time.
+      uint32_t prefix = 0u, mask = 0u, want = static_cast<uint32_t>(M);
+      for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += kSampleThreads) hist[i] = 0;
         __syncthreads();
         for (int i = tid; i < V; i += kSampleThreads) {
@@ -189,102 +279,93 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
           if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
         }
         __syncthreads();
-      }
-      if (tid == 0) {
-        uint32_t w = want;
-        int digit = 0;
-        for (int d = 255; d >= 0; --d) {
-          const uint32_t c = static_cast<uint32_t>(hist[d]);
-          if (w <= c) {
-            digit = d;
-            break;
+        if (tid == 0) {
+          uint32_t w = want;
+          int digit = 0;
+          for (int d = 255; d >= 0; --d) {
+            const uint32_t c = static_cast<uint32_t>(hist[d]);
+            if (w <= c) {
+              digit = d;
+              break;
+            }
+            w -= c;
           }
-          w -= c;
-        }
-        sel_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
-        sel_want = w;
-      }
-      __syncthreads();
-      prefix = sel_prefix;
-      want = sel_want;
-      mask |= 255u << shift;
-      __syncthreads();
-    }
-    const uint32_t T = prefix;       // key of the M-th candidate
-    const int need_eq = static_cast<int>(want);  // ties at T to take, lowest ids first
-    const int n_greater = M - need_eq;
-
-    // Compaction: thread t scans a contiguous index range, so an exclusive
-    // scan of its tie count orders ties by index.
-    const int R = (V + kSampleThreads - 1) / kSampleThreads;
-    const int lo = min(V, tid * R), hi = min(V, lo + R);
-    int my_eq = 0;
-    for (int i = lo; i < hi; ++i) {
-      my_eq += sample_key(__fmul_rn(__fsub_rn(L[i], mx), inv_t)) == T;
-    }
-    // exclusive scan over 1024 threads
-    int incl = my_eq;
-    const int lane = tid & 31, warp = tid >> 5;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
-    }
-    if (lane == 31) scan[warp] = incl;
-    if (tid == 0) n_gt = 0;
-    __syncthreads();
-    if (warp == 0) {
-      int v = scan[lane];
-      int vi = v;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int o = __shfl_up_sync(0xffffffffu, vi, off);
-        if (lane >= off) vi += o;
-      }
-      scan[lane] = vi - v;  // exclusive warp offsets
-    }
-    __syncthreads();
-    int eq_rank = scan[warp] + incl - my_eq;
-    for (int i = tid; i < kMaxCandidates; i += kSampleThreads) {
-      ckey[i] = 0u;
-      cidx[i] = 0x7fffffffu;
-    }
-    __syncthreads();
-    for (int i = lo; i < hi; ++i) {
-      const uint32_t key = sample_key(__fmul_rn(__fsub_rn(L[i], mx), inv_t));
-      if (key > T) {
-        const int slot = atomicAdd(&n_gt, 1);
-        if (slot < n_greater) {
-          ckey[slot] = key;
-          cidx[slot] = static_cast<uint32_t>(i);
-        }
-      } else if (key == T) {
-        if (eq_rank < need_eq) {
-          ckey[n_greater + eq_rank] = key;
-          cidx[n_greater + eq_rank] = static_cast<uint32_t>(i);
-        }
-        ++eq_rank;
-      }
-    }
-    __syncthreads();
-
-    // Bitonic sort of 1024 (key desc, index asc); padding sorts last.
-    for (int span = 2; span <= kMaxCandidates; span <<= 1) {
-      for (int step = span >> 1; step > 0; step >>= 1) {
-        const int i = tid, j = tid ^ step;
-        if (j > i) {
-          const bool i_first = (ckey[i] > ckey[j]) || (ckey[i] == ckey[j] && cidx[i] < cidx[j]);
-          const bool ascending_block = (i & span) != 0;  // reverse order in this half
-          const bool swap = ascending_block ? i_first : !i_first;
-          if (swap) {
-            const uint32_t tk = ckey[i], ti = cidx[i];
-            ckey[i] = ckey[j]; cidx[i] = cidx[j];
-            ckey[j] = tk; cidx[j] = ti;
-          }
+          sel_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
+          sel_want = w;
         }
         __syncthreads();
+        prefix = sel_prefix;
+        want = sel_want;
+        mask |= 255u << shift;
+        __syncthreads();
       }
+      const uint32_t T = prefix;       // key of the M-th candidate
+      const int need_eq = static_cast<int>(want);  // ties at T to take, lowest ids first
+      const int n_greater = M - need_eq;
+
+      // Compaction: thread t scans a contiguous index range, so an exclusive
+      // scan of its tie count orders ties by index.
+      const int R = (V + kSampleThreads - 1) / kSampleThreads;
+      const int lo = min(V, tid * R), hi = min(V, lo + R);
+      int my_eq = 0;
+      for (int i = lo; i < hi; ++i) {
+        my_eq += sample_key(__fmul_rn(__fsub_rn(L[i], mx), inv_t)) == T;
+      }
+      // exclusive scan over 1024 threads
+      int incl = my_eq;
+      const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      if (lane == 31) scan[warp] = incl;
+      __syncthreads();
+      if (warp == 0) {
+        int v = scan[lane];
+        int vi = v;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int o = __shfl_up_sync(0xffffffffu, vi, off);
+          if (lane >= off) vi += o;
+        }
+        scan[lane] = vi - v;  // exclusive warp offsets
+      }
+      __syncthreads();
+      int eq_rank = scan[warp] + incl - my_eq;
+      for (int i = tid; i < kMaxCandidates; i += kSampleThreads) {
+        ckey[i] = 0u;
+        cidx[i] = 0x7fffffffu;
+      }
+      __syncthreads();
+      for (int i = lo; i < hi; ++i) {
+        const uint32_t key = sample_key(__fmul_rn(__fsub_rn(L[i], mx), inv_t));
+        if (key > T) {
+          const int slot = atomicAdd(&n_gt, 1);
+          if (slot < n_greater) {
+            ckey[slot] = key;
+            cidx[slot] = static_cast<uint32_t>(i);
+          }
+        } else if (key == T) {
+          if (eq_rank < need_eq) {
+            ckey[n_greater + eq_rank] = key;
+            cidx[n_greater + eq_rank] = static_cast<uint32_t>(i);
+          }
+          ++eq_rank;
+        }
+      }
+      __syncthreads();
+      sort_candidates(ckey, cidx, kMaxCandidates);
     }
+
+    // Each candidate's probability, computed in parallel; the walk below
+    // adds them in candidate order, as a serial loop would.
+    const float inv_total = __fdiv_rn(1.0f, total);
+    float* prob = reinterpret_cast<float*>(ckey);
+    for (int j = tid; j < M; j += kSampleThreads) {
+      prob[j] = __fmul_rn(det_expf(key_to_float(ckey[j])), inv_total);
+    }
+    __syncthreads();
 
     if (tid == 0) {
       float u;
@@ -296,11 +377,10 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
         u = philox_uniform(a.seed[row], static_cast<unsigned long long>(a.counter[row]), 0u);
       }
       const float top_p = a.top_p[row];
-      const float inv_total = __fdiv_rn(1.0f, total);
       int keep = 0;
       float kept = 0.0f;
       for (int j = 0; j < M; ++j) {
-        const float p = __fmul_rn(det_expf(key_to_float(ckey[j])), inv_total);
+        const float p = prob[j];
         kept = __fadd_rn(kept, p);
         ++keep;
         if (top_p < 1.0f && kept >= top_p) break;
@@ -309,7 +389,7 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
       float running = 0.0f;
       picked = static_cast<int>(cidx[0]);
       for (int j = 0; j < keep; ++j) {
-        const float p = __fmul_rn(det_expf(key_to_float(ckey[j])), inv_total);
+        const float p = prob[j];
         running = __fadd_rn(running, p);
         picked = static_cast<int>(cidx[j]);
         if (running >= target) break;

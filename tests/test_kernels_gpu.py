@@ -148,7 +148,10 @@ def test_gemm_nt(rows, k, n, fp32):
     run(L.lcr_gemm_nt(y.data_ptr(), fp32, dptr(x), dptr(w), rows, k, n, S()))
     got = y.cpu().numpy() if fp32 else fl(host_bf(y))
     want = np.concatenate([oracle.gemv(w, x[r]) for r in range(rows)])
-    expect_close(got, want, 1e-5 if fp32 else 1e-2, "gemm_nt")
+    # fp32 outputs: both sides accumulate in fp32, in different orders (the
+    # oracle left to right, the kernels in lane / tensor-core trees), so the
+    # rounding difference grows like sqrt(k).
+    expect_close(got, want, 1e-5 * max(1.0, np.sqrt(k / 2048)) if fp32 else 1e-2, "gemm_nt")
 
 
 # --- decode attention: the reference's 11 cases (tests/test_kernels.cu:417-440)
