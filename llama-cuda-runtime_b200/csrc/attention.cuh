@@ -57,6 +57,12 @@ struct AttnArgs {
   float* partials;           // [sequences][heads][splits][2 + D]
   unsigned* counters;        // FUSED: [sequences][kv_heads]
   uint32_t* status;
+  // attn_batch_kernel only: positions per work item (a multiple of 16), the
+  // sequences of the batch, and two work counters that are zero between
+  // launches (next item, finished CTAs).
+  int item_pos;
+  int seqs;
+  unsigned* work;
 };
 
 constexpr int kAttnConsumerWarps = 4;
@@ -137,6 +143,100 @@ __device__ __forceinline__ void softmax_merge(float& m, float& l, float (&acc)[G
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[g][e] = acc[g][e] * a + oacc[e] * b;
   m = mn;
+}
+
+// Finishes split `split` of `splits` of one (sequence, KV head) from the
+// consumer warps' (m, l, acc) records in `comb` ([warps][G][2 + D]): the
+// output itself when there is one split, else this split's partial (slot
+// `split` of `slots` per head), and -- FUSED, in the last CTA of the
+// (sequence, KV head) to finish -- the merge of every split, staged through
+// `stage` (stage_bytes of idle shared memory) when it fits, else read from
+// L2. Run by the 128 consumer threads (threadIdx.x 0..127) after `comb` is
+// complete; uses named barrier 1.
+template <int D, int G, bool FUSED>
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, const float* comb, uint8_t* stage, int stage_bytes,
+                                            int split, int splits, int slots, int kvh, int b, int num_kv,
+                                            int* s_last) {
+  const int tid = threadIdx.x;
+  const int heads = num_kv * G;
+  // Thread t of the 128 consumers finalises (head g, dims) pairs.
+  for (int idx = tid; idx < G * D; idx += kAttnConsumerWarps * 32) {
+    const int g = idx / D, d = idx % D;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < kAttnConsumerWarps; ++w) M = fmaxf(M, comb[(w * G + g) * (D + 2)]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnConsumerWarps; ++w) {
+      const float* c = comb + (w * G + g) * (D + 2);
+      const float sc = ex2_approx(c[0] - M);
+      L += c[1] * sc;
+      A += c[2 + d] * sc;
+    }
+    const int h = kvh * G + g;
+    if (splits == 1) {
+      a.out[static_cast<size_t>(b) * heads * D + h * D + d] =
+          __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
+    } else {
+      float* slotp = a.partials + ((static_cast<size_t>(b) * heads + h) * slots + split) * (2 + D);
+      if (d == 0) {
+        slotp[0] = M;
+        slotp[1] = L;
+      }
+      slotp[2 + d] = A;
+    }
+  }
+
+  if (FUSED && splits > 1) {
+    // Last CTA of this (sequence, KV head) merges every split: this
+    // thread's partial is visible device-wide before the count moves.
+    __threadfence();
+    named_sync(1, kAttnConsumerWarps * 32);
+    if (tid == 0) {
+      __threadfence();
+      const unsigned prev = atomicAdd(&a.counters[b * num_kv + kvh], 1u);
+      *s_last = (prev == static_cast<unsigned>(splits) - 1) ? 1 : 0;
+      if (*s_last) {
+        __threadfence();
+        a.counters[b * num_kv + kvh] = 0u;
+      }
+    }
+    named_sync(1, kAttnConsumerWarps * 32);
+    if (*s_last) {
+      // Stage the group's split partials -- one contiguous span of
+      // G * splits * (2 + D) floats -- into the idle stage memory with
+      // coalesced L2 loads, then merge from shared memory.
+      const int span = G * slots * (2 + D);
+      const float* src = a.partials + (static_cast<size_t>(b) * heads + kvh * G) * slots * (2 + D);
+      float* stg = reinterpret_cast<float*>(stage);
+      if (span * static_cast<int>(sizeof(float)) <= stage_bytes) {
+#pragma unroll 8
+        for (int i = tid; i < span; i += kAttnConsumerWarps * 32) stg[i] = __ldcg(src + i);
+        named_sync(1, kAttnConsumerWarps * 32);
+      } else {
+        stg = nullptr;  // too many splits to stage: merge straight from L2
+      }
+      for (int idx = tid; idx < G * D; idx += kAttnConsumerWarps * 32) {
+        const int g = idx / D, d = idx % D;
+        const int h = kvh * G + g;
+        const float* base = stg ? stg + g * slots * (2 + D)
+                                : src + g * slots * (2 + D);
+        float M = kNegBig;
+        for (int s = 0; s < splits; ++s) M = fmaxf(M, stg ? base[s * (2 + D)] : __ldcg(base + s * (2 + D)));
+        float L = 0.f, A = 0.f;
+        for (int s = 0; s < splits; ++s) {
+          const float m_s = stg ? base[s * (2 + D)] : __ldcg(base + s * (2 + D));
+          const float l_s = stg ? base[s * (2 + D) + 1] : __ldcg(base + s * (2 + D) + 1);
+          const float a_s = stg ? base[s * (2 + D) + 2 + d] : __ldcg(base + s * (2 + D) + 2 + d);
+          const float sc = ex2_approx(m_s - M);
+          L += l_s * sc;
+          A += a_s * sc;
+        }
+        a.out[static_cast<size_t>(b) * heads * D + h * D + d] =
+            __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
+      }
+    }
+  }
 }
 
 template <int D, int G, bool PAGED, bool FUSED, int STAGES>
@@ -240,7 +340,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   } else {
     const int lig = lane % LPP;    // lane within the position group
     const int grp = warp * GPW + lane / LPP;
-    const int heads = num_kv * G;
 
     float q[G][8], acc[G][8], m[G], l[G];
     pdl_wait();
@@ -386,83 +485,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       }
     }
     named_sync(1, kAttnConsumerWarps * 32);
-    // Thread t of the 128 consumers finalises (head g, dims) pairs.
-    for (int idx = tid; idx < G * D; idx += kAttnConsumerWarps * 32) {
-      const int g = idx / D, d = idx % D;
-      float M = kNegBig;
-#pragma unroll
-      for (int w = 0; w < kAttnConsumerWarps; ++w) M = fmaxf(M, comb[(w * G + g) * (D + 2)]);
-      float L = 0.f, A = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnConsumerWarps; ++w) {
-        const float* c = comb + (w * G + g) * (D + 2);
-        const float sc = ex2_approx(c[0] - M);
-        L += c[1] * sc;
-        A += c[2 + d] * sc;
-      }
-      const int h = kvh * G + g;
-      if (a.splits == 1) {
-        a.out[static_cast<size_t>(b) * heads * D + h * D + d] =
-            __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
-      } else {
-        float* slotp = a.partials + ((static_cast<size_t>(b) * heads + h) * a.splits + split) * (2 + D);
-        if (d == 0) {
-          slotp[0] = M;
-          slotp[1] = L;
-        }
-        slotp[2 + d] = A;
-        __threadfence();
-      }
-    }
-
-    if (FUSED && a.splits > 1) {
-      // Last CTA of this (sequence, KV head) merges every split.
-      named_sync(1, kAttnConsumerWarps * 32);
-      if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&a.counters[b * num_kv + kvh], 1u);
-        s_last = (prev == static_cast<unsigned>(a.splits) - 1) ? 1 : 0;
-        if (s_last) {
-          __threadfence();
-          a.counters[b * num_kv + kvh] = 0u;
-        }
-      }
-      named_sync(1, kAttnConsumerWarps * 32);
-      if (s_last) {
-        // Stage the group's split partials -- one contiguous span of
-        // G * splits * (2 + D) floats -- into the (now idle) ring with
-        // coalesced L2 loads, then merge from shared memory.
-        const int span = G * a.splits * (2 + D);
-        const float* src = a.partials + (static_cast<size_t>(b) * heads + kvh * G) * a.splits * (2 + D);
-        float* stg = reinterpret_cast<float*>(ring);
-        if (span * static_cast<int>(sizeof(float)) <= STAGES * 2 * KB) {
-#pragma unroll 8
-          for (int i = tid; i < span; i += kAttnConsumerWarps * 32) stg[i] = __ldcg(src + i);
-          named_sync(1, kAttnConsumerWarps * 32);
-        } else {
-          stg = nullptr;  // too many splits to stage: merge straight from L2
-        }
-        for (int idx = tid; idx < G * D; idx += kAttnConsumerWarps * 32) {
-          const int g = idx / D, d = idx % D;
-          const int h = kvh * G + g;
-          const float* base = stg ? stg + g * a.splits * (2 + D)
-                                  : src + g * a.splits * (2 + D);
-          float M = kNegBig;
-          for (int s = 0; s < a.splits; ++s) M = fmaxf(M, stg ? base[s * (2 + D)] : __ldcg(base + s * (2 + D)));
-          float L = 0.f, A = 0.f;
-          for (int s = 0; s < a.splits; ++s) {
-            const float m_s = stg ? base[s * (2 + D)] : __ldcg(base + s * (2 + D));
-            const float l_s = stg ? base[s * (2 + D) + 1] : __ldcg(base + s * (2 + D) + 1);
-            const float a_s = stg ? base[s * (2 + D) + 2 + d] : __ldcg(base + s * (2 + D) + 2 + d);
-            const float sc = ex2_approx(m_s - M);
-            L += l_s * sc;
-            A += a_s * sc;
-          }
-          a.out[static_cast<size_t>(b) * heads * D + h * D + d] =
-              __ushort_as_bfloat16(f2bf(L > 0.f ? A / L : 0.f));
-        }
-      }
-    }
+    attn_finish<D, G, FUSED>(a, comb, ring, STAGES * 2 * KB, split, a.splits, a.splits, kvh, b, num_kv, &s_last);
   }
 }
 

@@ -17,6 +17,12 @@ struct NormRowsArgs {
   float eps;
   bf16* out;              // [rows][H] bf16(x * rsqrt(mean(xsum^2) + eps) * gain)
   uint32_t* status;
+  // EMBED, optional: the step's RoPE table, rope[row][half] = (cos, sin) of
+  // float(positions[row]) * inv_freq[i] (sincosf, as src/kernels/rope.cu:50).
+  const int32_t* positions;
+  const float* inv_freq;
+  float2* rope;
+  int half;
 };
 
 constexpr int kNormThreads = 256;
@@ -33,6 +39,14 @@ __global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const NormRowsA
   const size_t row = static_cast<size_t>(b) * H;
   const bf16* src = a.x + row;
   if constexpr (EMBED) {
+    if (a.rope != nullptr) {
+      const float p = static_cast<float>(a.positions[b]);
+      for (int i = tid; i < a.half; i += kNormThreads) {
+        float sn, cs;
+        sincosf(p * a.inv_freq[i], &sn, &cs);
+        a.rope[static_cast<size_t>(b) * a.half + i] = make_float2(cs, sn);
+      }
+    }
     int tok = a.tokens[b];
     if (tok < 0 || tok >= a.vocab) {
       if (tid == 0 && a.status) atomicOr(a.status, kStatusBadToken);

@@ -3,9 +3,12 @@
 //
 // A step of n slots is, per layer:
 //   norm_rows_kernel        x -> xn (layer 0: the token embeddings)
-//   gemm_tc_kernel          qkv  = xn W_qkv^T           (split-K, + reduction)
-//   attn_decode_kernel      RoPE, K/V write at each slot's position, paged
-//                           attention over 0..position, split merge -> attn
+//   gemm_tc_kernel          qkv  = xn W_qkv^T, RoPE on q and k (the step's
+//                           cos/sin table, written by the layer-0 norm)
+//                           (split-K, + reduction)
+//   attn_batch_kernel       K/V write at each slot's position, paged
+//                           attention over 0..position on the tensor pipe,
+//                           split merge -> attn
 //   gemm_tc_kernel          x   += attn W_o^T (residual epilogue, split-K)
 //   norm_rows_kernel        x -> xn
 //   gemm_tc_kernel          act  = silu(xn W_gate^T) * (xn W_up^T)
@@ -28,6 +31,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "attn_batch.h"
 #include "batch.cuh"
 #include "common.cuh"
 #include "dispatch.h"
@@ -63,6 +67,7 @@ struct lcr_batch {
   std::vector<lcr_layer_weights> layers;
   std::vector<CUtensorMap> wmaps;  // [layer * 4 + m]: qkv, o, gate/up, down; then lm_head
   std::map<int, StepMaps> xmaps;   // by batch tile
+  std::vector<CUtensorMap> kvmaps; // [layer * 2 + {0: K, 1: V}] pool rows of head_dim
 
   char* buf = nullptr;
   bf16* x = nullptr;
@@ -73,9 +78,10 @@ struct lcr_batch {
   bf16* act = nullptr;
   float* logits = nullptr;
   float* partials = nullptr;
-  unsigned* attn_ctr = nullptr;
+  unsigned* attn_work = nullptr;
   float* work = nullptr;
   float* inv_freq = nullptr;
+  float2* rope = nullptr;  // [max_batch][head_dim / 2] (cos, sin) of this step
   int32_t* tokens = nullptr;
   int32_t* positions = nullptr;
   int32_t* tables = nullptr;  // [max_batch][max_pages]
@@ -89,7 +95,9 @@ struct lcr_batch {
   bf16* vpool = nullptr;
   size_t layer_elems = 0;  // elements of one layer's pool
   int max_pages = 0;
-  int attn_splits_cap = 1;
+  int attn_item_pos = 512;  // positions per attention work item
+  int attn_slots = 1;       // partial slots per head: ceil(max_seq / attn_item_pos)
+  int attn_ctas = 1;        // persistent attention CTAs
   size_t work_floats = 0;
 
   std::vector<int32_t> tables_host;
@@ -152,6 +160,12 @@ int norm_launch(lcr_batch* c, int n, bool embed, const void* gain) {
   a.eps = c->d.rms_norm_eps;
   a.out = c->xn;
   a.status = c->status;
+  if (embed) {
+    a.positions = c->positions;
+    a.inv_freq = c->inv_freq;
+    a.rope = c->rope;
+    a.half = c->d.head_dim / 2;
+  }
   ++c->launches;
   const dim3 grid(static_cast<unsigned>(n));
   switch (c->d.hidden_size) {
@@ -187,6 +201,9 @@ int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb
   a.resid = c->x;
   a.resid_sum = c->xsum;
   a.status = c->status;
+  a.rope = c->rope;
+  a.head_dim = c->d.head_dim;
+  a.rope_cols = (c->d.num_heads + c->d.num_kv_heads) * c->d.head_dim;
   const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
   const int tiles = tiles_n * ((n + nb - 1) / nb);
   const int slabs = K / kTcSlabK;
@@ -221,20 +238,19 @@ int attention_launch_layer(lcr_batch* c, int layer, int n) {
   a.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
   a.max_seq = c->o.max_seq;
   a.positions = c->positions;
-  // Splits of at most ~512 cached positions each (so long contexts spread
-  // over many CTAs), and at least about two (sequence, KV head, split) CTAs
-  // per SM; short sequences get correspondingly short chunks.
-  const int by_length = (c->o.max_seq + 511) / 512;
-  const int by_sms = (2 * c->sms + d.num_kv_heads * n - 1) / (d.num_kv_heads * n);
-  a.splits = std::max(1, std::min(c->attn_splits_cap, std::max(by_length, by_sms)));
+  // Work items of attn_item_pos positions per (sequence, KV head), spread
+  // over the persistent CTAs.
+  a.item_pos = c->attn_item_pos;
+  a.splits = c->attn_slots;
+  a.seqs = n;
+  a.work = c->attn_work;
   a.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
   a.out = c->attn;
   a.partials = c->partials;
-  a.counters = c->attn_ctr;
   a.status = c->status;
-  ++c->launches;
-  return attn_launch(a, true, d.head_dim, d.num_heads / d.num_kv_heads, true, d.num_kv_heads, n, c->stream,
-                     false);
+  c->launches += 2;
+  return attn_batch_launch(a, c->kvmaps[static_cast<size_t>(2 * layer)], c->kvmaps[static_cast<size_t>(2 * layer + 1)],
+                           d.head_dim, d.num_heads / d.num_kv_heads, c->attn_ctas, c->stream);
 }
 
 int maps_for(lcr_batch* c, int nb, const StepMaps** out) {
@@ -264,7 +280,7 @@ int enqueue_step(lcr_batch* c, int n) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
     const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
     LCRB_TRY(norm_launch(c, n, l == 0, w.input_norm));
-    LCRB_TRY(gemm_node(c, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_STORE, c->qkv, nullptr, qd + 2 * kvd));
+    LCRB_TRY(gemm_node(c, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_ROPE, c->qkv, nullptr, qd + 2 * kvd));
     LCRB_TRY(attention_launch_layer(c, l, n));
     LCRB_TRY(gemm_node(c, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H));
     LCRB_TRY(norm_launch(c, n, false, w.post_attention_norm));
@@ -388,11 +404,12 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   }
   if (st == LCR_OK) st = make_kmajor_map(&c->wmaps.back(), c->lm_head, d.vocab_size, d.hidden_size, 1, kTcTileM, 1);
 
-  // Attention split cap: the FUSED kernel's last-CTA merge staging.
+  // Attention work items: 512 positions, or more for very long caches so
+  // that a sequence has at most 64 partial slots per head.
   const int group = d.num_heads / d.num_kv_heads;
-  c->attn_splits_cap = d.head_dim == 64 ? attn_max_staged_splits<64, kAttnStages>(group)
-                                        : attn_max_staged_splits<128, kAttnStages>(group);
-  c->attn_splits_cap = std::max(1, c->attn_splits_cap);
+  c->attn_item_pos = std::max(512, ((o.max_seq + 63) / 64 + 15) / 16 * 16);
+  c->attn_slots = (o.max_seq + c->attn_item_pos - 1) / c->attn_item_pos;
+  if (st == LCR_OK) st = attn_batch_ctas(d.head_dim, group, o.max_batch, c->sms, &c->attn_ctas);
 
   // Activations and per-slot state, one allocation.
   const size_t B = static_cast<size_t>(o.max_batch);
@@ -408,9 +425,10 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   const size_t o_qkv = carve(sizeof(bf16) * B * (qd + 2 * kvd));
   const size_t o_attn = carve(sizeof(bf16) * B * qd);
   const size_t o_act = carve(sizeof(bf16) * B * d.intermediate_size);
-  const size_t o_part = carve(sizeof(float) * B * d.num_heads * c->attn_splits_cap * (2 + d.head_dim));
-  const size_t o_actr = carve(sizeof(unsigned) * B * d.num_kv_heads);
+  const size_t o_part = carve(sizeof(float) * B * d.num_heads * c->attn_slots * (2 + d.head_dim));
+  const size_t o_awork = carve(sizeof(unsigned) * 2);
   const size_t o_freq = carve(sizeof(float) * d.head_dim / 2);
+  const size_t o_rope = carve(sizeof(float2) * B * (d.head_dim / 2));
   const size_t o_tok = carve(sizeof(int32_t) * B);
   const size_t o_pos = carve(sizeof(int32_t) * B);
   const size_t o_tab = carve(sizeof(int32_t) * B * c->max_pages);
@@ -431,8 +449,9 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
     c->attn = reinterpret_cast<bf16*>(b + o_attn);
     c->act = reinterpret_cast<bf16*>(b + o_act);
     c->partials = reinterpret_cast<float*>(b + o_part);
-    c->attn_ctr = reinterpret_cast<unsigned*>(b + o_actr);
+    c->attn_work = reinterpret_cast<unsigned*>(b + o_awork);
     c->inv_freq = reinterpret_cast<float*>(b + o_freq);
+    c->rope = reinterpret_cast<float2*>(b + o_rope);
     c->tokens = reinterpret_cast<int32_t*>(b + o_tok);
     c->positions = reinterpret_cast<int32_t*>(b + o_pos);
     c->tables = reinterpret_cast<int32_t*>(b + o_tab);
@@ -461,6 +480,21 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   if (st == LCR_OK) cuda(cudaMalloc(&c->vpool, kv_elems * sizeof(bf16)), "cudaMalloc(V pool)");
   if (st == LCR_OK) cuda(cudaMemset(c->kpool, 0, kv_elems * sizeof(bf16)), "cudaMemset(K pool)");
   if (st == LCR_OK) cuda(cudaMemset(c->vpool, 0, kv_elems * sizeof(bf16)), "cudaMemset(V pool)");
+  // Tensor maps of each layer's pools as rows of head_dim, 16-row boxes.
+  const long long pool_rows = static_cast<long long>(o.pool_pages) * d.num_kv_heads * o.page_size;
+  if (st == LCR_OK && pool_rows > 0x7fffffffLL) {
+    st = fail(LCR_ERR_SHAPE, "KV pool of %lld rows per layer is too large", pool_rows);
+  }
+  c->kvmaps.resize(static_cast<size_t>(2 * d.num_layers));
+  for (int l = 0; l < d.num_layers && st == LCR_OK; ++l) {
+    const size_t at = static_cast<size_t>(l) * c->layer_elems;
+    st = make_kmajor_map(&c->kvmaps[static_cast<size_t>(2 * l)], c->kpool + at, static_cast<int>(pool_rows),
+                         d.head_dim, 1, kAbUnit, d.head_dim / 64);
+    if (st == LCR_OK) {
+      st = make_kmajor_map(&c->kvmaps[static_cast<size_t>(2 * l + 1)], c->vpool + at, static_cast<int>(pool_rows),
+                           d.head_dim, 1, kAbUnit, d.head_dim / 64);
+    }
+  }
   if (st == LCR_OK) {
     cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * B * kStaging), "cudaMallocHost");
   }

@@ -32,6 +32,7 @@ int by_epi(const TcArgs& a, const CUtensorMap& w, const CUtensorMap& x, int epi,
     case EPI_STORE_F32: return launch_t<NB, EPI_STORE_F32>(a, w, x, s);
     case EPI_RESID: return launch_t<NB, EPI_RESID>(a, w, x, s);
     case EPI_SWIGLU: return launch_t<NB, EPI_SWIGLU>(a, w, x, s);
+    case EPI_ROPE: return launch_t<NB, EPI_ROPE>(a, w, x, s);
     default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: no epilogue %d", epi);
   }
 }
@@ -56,6 +57,8 @@ int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& 
                "tcgen05 projection: unsupported %d x %d x %d", a.rows, a.n_out, a.K);
   LCRB_REQUIRE(a.splits >= 1 && a.splits <= a.K / kTcSlabK, LCR_ERR_INVALID, "tcgen05 projection: %d splits",
                a.splits);
+  LCRB_REQUIRE(epi != EPI_ROPE || (a.rope && (a.head_dim == 64 || a.head_dim == 128) && a.rope_cols % a.head_dim == 0),
+               LCR_ERR_SHAPE, "tcgen05 projection: RoPE epilogue needs a table and head_dim 64 or 128");
   LCRB_REQUIRE(a.splits == 1 || a.work, LCR_ERR_INVALID,
                "tcgen05 projection: split-K needs workspace");
   switch (nb) {

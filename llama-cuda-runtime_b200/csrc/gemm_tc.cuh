@@ -56,6 +56,11 @@ struct TcArgs {
   float* resid_sum;
   float* work;      // splits > 1: [splits][rows][tiles_n * 128] fp32 partials
   uint32_t* status;    // device status word, or nullptr
+  // ROPE: columns [0, rope_cols) are heads of head_dim (a power of two <= 128)
+  // rotated with rope[row][head_dim / 2] = (cos, sin) of the row's angles.
+  const float2* rope;
+  int head_dim;
+  int rope_cols;
 };
 
 // UMMA shared-memory descriptor of a K-major, 128-byte swizzled tile whose
@@ -103,6 +108,8 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // One output element of the epilogue: row n of the weights, batch row b.
+// `up` is SWIGLU's up-projection value, or ROPE's rotation partner (column
+// n ^ head_dim / 2).
 template <int EPI>
 __device__ __forceinline__ void tc_store(const TcArgs& a, int b, int n, float v, float up) {
   const size_t o = static_cast<size_t>(b) * a.ldy + n;
@@ -118,6 +125,18 @@ __device__ __forceinline__ void tc_store(const TcArgs& a, int b, int n, float v,
     const float g = rbf(v);
     const float silu = g / (1.0f + __expf(-g));
     a.y[o] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
+  } else if constexpr (EPI == EPI_ROPE) {
+    // The projection output is rounded to bf16, then rotated in fp32 and
+    // rounded again (rope_write_kv_kernel, src/kernels/rope.cu:58-87).
+    float r = rbf(v);
+    if (n < a.rope_cols) {
+      const int half = a.head_dim >> 1;
+      const int d = n & (a.head_dim - 1);
+      const float2 cs = a.rope[static_cast<size_t>(b) * half + (d & (half - 1))];
+      const float other = rbf(up);
+      r = rbf(d < half ? (r * cs.x - other * cs.y) : (r * cs.x + other * cs.y));
+    }
+    a.y[o] = __ushort_as_bfloat16(f2bf(r));
   }
 }
 
@@ -261,6 +280,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], xch[b * 64 + row]);
           }
         }
+      } else if constexpr (EPI == EPI_ROPE) {
+        // Rotation partners (tile row ^ head_dim / 2) through the idle ring.
+        float* xch = reinterpret_cast<float*>(ring);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) xch[b * kTcTileM + row] = v[b];
+        named_sync(2, 128);
+        if (n0 + row < a.n_out) {
+          const int prow = row ^ (a.head_dim >> 1);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], xch[b * kTcTileM + prow]);
+          }
+        }
       } else if (n0 + row < a.n_out) {
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
@@ -295,6 +327,12 @@ __global__ void __launch_bounds__(256) gemm_tc_reduce_kernel(const TcArgs a) {
     for (int sp = 0; sp < a.splits; ++sp) {
       v = __fadd_rn(v, __ldcg(src + sp * plane));
       if constexpr (EPI == EPI_SWIGLU) up = __fadd_rn(up, __ldcg(src + sp * plane + 64));
+    }
+    if constexpr (EPI == EPI_ROPE) {
+      if (n < a.rope_cols) {  // the partner's sum, in the same order
+        const float* par = a.work + static_cast<size_t>(b) * m_total + (n ^ (a.head_dim >> 1));
+        for (int sp = 0; sp < a.splits; ++sp) up = __fadd_rn(up, __ldcg(par + sp * plane));
+      }
     }
     tc_store<EPI>(a, b, n, v, up);
   }

@@ -41,7 +41,9 @@
 namespace lcrb {
 
 enum GemvPro { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
-enum GemvEpi { EPI_STORE = 0, EPI_STORE_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS_ARGMAX = 4 };
+// EPI_ROPE (tcgen05 projection only): bf16 store with the rotate-half RoPE
+// applied to the q and k columns of a QKV projection.
+enum GemvEpi { EPI_STORE = 0, EPI_STORE_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS_ARGMAX = 4, EPI_ROPE = 5 };
 
 struct GemvArgs {
   const bf16* w;      // [N][K]; SWIGLU: rows [0, F) gate, [F, 2F) up
