@@ -511,8 +511,10 @@ __global__ void __launch_bounds__(D) attn_batch_merge_kernel(const AttnArgs a) {
   if (splits == 1) return;
   const float* base = a.partials + (static_cast<size_t>(b) * heads + h) * a.splits * (2 + D);
   float M = kNegBig;
+#pragma unroll 4
   for (int q = 0; q < splits; ++q) M = fmaxf(M, base[q * (2 + D)]);
   float Lsum = 0.f, A = 0.f;
+#pragma unroll 4
   for (int q = 0; q < splits; ++q) {
     const float sc = ex2_approx(base[q * (2 + D)] - M);
     Lsum += base[q * (2 + D) + 1] * sc;

@@ -95,6 +95,7 @@ struct lcr_batch {
   bf16* vpool = nullptr;
   size_t layer_elems = 0;  // elements of one layer's pool
   int max_pages = 0;
+  int tc_chunks = 2;        // 64-column K chunks per projection stage (fits batch tiles to 128)
   int attn_item_pos = 512;  // positions per attention work item
   int attn_slots = 1;       // partial slots per head: ceil(max_seq / attn_item_pos)
   int attn_ctas = 1;        // persistent attention CTAs
@@ -206,16 +207,16 @@ int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb
   a.rope_cols = (c->d.num_heads + c->d.num_kv_heads) * c->d.head_dim;
   const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
   const int tiles = tiles_n * ((n + nb - 1) / nb);
-  const int slabs = K / kTcSlabK;
-  // Enough CTAs to cover the SMs, at least two slabs per split, within the
-  // workspace.
-  int splits = std::max(1, (c->sms + tiles - 1) / tiles);
-  splits = std::min(splits, std::max(1, slabs / 2));
+  const int steps = K / (kTcSlabK * c->tc_chunks);
+  // As many splits as fit the SMs in one wave (one CTA per SM), within the
+  // K stages and the workspace.
+  int splits = std::max(1, c->sms / tiles);
+  splits = std::min(splits, steps);
   while (splits > 1 && gemm_tc_work_floats(n, n_out, epi, splits) > c->work_floats) --splits;
   a.splits = splits;
   a.work = c->work;
   c->launches += splits > 1 ? 2 : 1;
-  return gemm_tc_launch(a, wm, xm, nb, epi, c->stream);
+  return gemm_tc_launch(a, wm, xm, nb, epi, c->tc_chunks, c->stream);
 }
 
 int attention_launch_layer(lcr_batch* c, int layer, int n) {
@@ -259,9 +260,10 @@ int maps_for(lcr_batch* c, int nb, const StepMaps** out) {
     const lcr_model_desc& d = c->d;
     StepMaps m;
     const int qd = d.num_heads * d.head_dim;
-    LCRB_TRY(make_kmajor_map(&m.xn, c->xn, c->o.max_batch, d.hidden_size, 1, nb, 1));
-    LCRB_TRY(make_kmajor_map(&m.attn, c->attn, c->o.max_batch, qd, 1, nb, 1));
-    LCRB_TRY(make_kmajor_map(&m.act, c->act, c->o.max_batch, d.intermediate_size, 1, nb, 1));
+    const int ch = c->tc_chunks;
+    LCRB_TRY(make_kmajor_map(&m.xn, c->xn, c->o.max_batch, d.hidden_size, 1, nb, ch));
+    LCRB_TRY(make_kmajor_map(&m.attn, c->attn, c->o.max_batch, qd, 1, nb, ch));
+    LCRB_TRY(make_kmajor_map(&m.act, c->act, c->o.max_batch, d.intermediate_size, 1, nb, ch));
     it = c->xmaps.emplace(nb, m).first;
   }
   *out = &it->second;
@@ -397,12 +399,15 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
       break;
     }
     CUtensorMap* m = &c->wmaps[static_cast<size_t>(4 * l)];
-    st = make_kmajor_map(m, w.qkv_proj, qd + 2 * kvd, d.hidden_size, 1, kTcTileM, 1);
-    if (st == LCR_OK) st = make_kmajor_map(m + 1, w.o_proj, d.hidden_size, qd, 1, kTcTileM, 1);
-    if (st == LCR_OK) st = make_kmajor_map(m + 2, w.gate_up_proj, d.intermediate_size, d.hidden_size, 2, 64, 1);
-    if (st == LCR_OK) st = make_kmajor_map(m + 3, w.down_proj, d.hidden_size, d.intermediate_size, 1, kTcTileM, 1);
+    const int ch = c->tc_chunks;
+    st = make_kmajor_map(m, w.qkv_proj, qd + 2 * kvd, d.hidden_size, 1, kTcTileM, ch);
+    if (st == LCR_OK) st = make_kmajor_map(m + 1, w.o_proj, d.hidden_size, qd, 1, kTcTileM, ch);
+    if (st == LCR_OK) st = make_kmajor_map(m + 2, w.gate_up_proj, d.intermediate_size, d.hidden_size, 2, 64, ch);
+    if (st == LCR_OK) st = make_kmajor_map(m + 3, w.down_proj, d.hidden_size, d.intermediate_size, 1, kTcTileM, ch);
   }
-  if (st == LCR_OK) st = make_kmajor_map(&c->wmaps.back(), c->lm_head, d.vocab_size, d.hidden_size, 1, kTcTileM, 1);
+  if (st == LCR_OK) {
+    st = make_kmajor_map(&c->wmaps.back(), c->lm_head, d.vocab_size, d.hidden_size, 1, kTcTileM, c->tc_chunks);
+  }
 
   // Attention work items: 512 positions, or more for very long caches so
   // that a sequence has at most 64 partial slots per head.

@@ -6,10 +6,10 @@
 namespace lcrb {
 namespace {
 
-template <int NB, int EPI>
+template <int NB, int EPI, int CH>
 int launch_t(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, cudaStream_t s) {
-  auto kernel = gemm_tc_kernel<NB, EPI>;
-  constexpr size_t smem = gemm_tc_smem_bytes<NB>();
+  auto kernel = gemm_tc_kernel<NB, EPI, CH>;
+  constexpr size_t smem = gemm_tc_smem_bytes<NB, CH>();
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   const int tiles_n = EPI == EPI_SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
   const int tiles_b = (a.rows + NB - 1) / NB;
@@ -25,15 +25,27 @@ int launch_t(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, 
   return LCR_OK;
 }
 
-template <int NB>
+template <int NB, int CH>
 int by_epi(const TcArgs& a, const CUtensorMap& w, const CUtensorMap& x, int epi, cudaStream_t s) {
   switch (epi) {
-    case EPI_STORE: return launch_t<NB, EPI_STORE>(a, w, x, s);
-    case EPI_STORE_F32: return launch_t<NB, EPI_STORE_F32>(a, w, x, s);
-    case EPI_RESID: return launch_t<NB, EPI_RESID>(a, w, x, s);
-    case EPI_SWIGLU: return launch_t<NB, EPI_SWIGLU>(a, w, x, s);
-    case EPI_ROPE: return launch_t<NB, EPI_ROPE>(a, w, x, s);
+    case EPI_STORE: return launch_t<NB, EPI_STORE, CH>(a, w, x, s);
+    case EPI_STORE_F32: return launch_t<NB, EPI_STORE_F32, CH>(a, w, x, s);
+    case EPI_RESID: return launch_t<NB, EPI_RESID, CH>(a, w, x, s);
+    case EPI_SWIGLU: return launch_t<NB, EPI_SWIGLU, CH>(a, w, x, s);
+    case EPI_ROPE: return launch_t<NB, EPI_ROPE, CH>(a, w, x, s);
     default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: no epilogue %d", epi);
+  }
+}
+
+template <int NB>
+int by_chunks(const TcArgs& a, const CUtensorMap& w, const CUtensorMap& x, int epi, int ch, cudaStream_t s) {
+  switch (ch) {
+    case 1: return by_epi<NB, 1>(a, w, x, epi, s);
+    case 2: return by_epi<NB, 2>(a, w, x, epi, s);
+    case 4:
+      if constexpr (NB <= 64) return by_epi<NB, 4>(a, w, x, epi, s);
+      [[fallthrough]];
+    default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: %d chunks per stage with batch tile %d", ch, NB);
   }
 }
 
@@ -46,26 +58,27 @@ int gemm_tc_batch_tile(int rows) {
   return 128;
 }
 
+int gemm_tc_max_chunks(int nb) { return nb <= 64 ? 4 : 2; }
+
 size_t gemm_tc_work_floats(int rows, int n_out, int epi, int splits) {
   const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
   return splits > 1 ? static_cast<size_t>(splits) * rows * tiles_n * kTcTileM : 0;
 }
 
-int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi,
+int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi, int ch,
                    cudaStream_t stream) {
-  LCRB_REQUIRE(a.K % kTcSlabK == 0 && a.K >= kTcSlabK && a.n_out > 0 && a.rows > 0, LCR_ERR_SHAPE,
-               "tcgen05 projection: unsupported %d x %d x %d", a.rows, a.n_out, a.K);
-  LCRB_REQUIRE(a.splits >= 1 && a.splits <= a.K / kTcSlabK, LCR_ERR_INVALID, "tcgen05 projection: %d splits",
-               a.splits);
+  LCRB_REQUIRE(ch >= 1 && a.K % (kTcSlabK * ch) == 0 && a.n_out > 0 && a.rows > 0, LCR_ERR_SHAPE,
+               "tcgen05 projection: unsupported %d x %d x %d (%d chunks per stage)", a.rows, a.n_out, a.K, ch);
+  LCRB_REQUIRE(a.splits >= 1 && a.splits <= a.K / (kTcSlabK * ch), LCR_ERR_INVALID,
+               "tcgen05 projection: %d splits", a.splits);
   LCRB_REQUIRE(epi != EPI_ROPE || (a.rope && (a.head_dim == 64 || a.head_dim == 128) && a.rope_cols % a.head_dim == 0),
                LCR_ERR_SHAPE, "tcgen05 projection: RoPE epilogue needs a table and head_dim 64 or 128");
-  LCRB_REQUIRE(a.splits == 1 || a.work, LCR_ERR_INVALID,
-               "tcgen05 projection: split-K needs workspace");
+  LCRB_REQUIRE(a.splits == 1 || a.work, LCR_ERR_INVALID, "tcgen05 projection: split-K needs workspace");
   switch (nb) {
-    case 16: return by_epi<16>(a, wmap, xmap, epi, stream);
-    case 32: return by_epi<32>(a, wmap, xmap, epi, stream);
-    case 64: return by_epi<64>(a, wmap, xmap, epi, stream);
-    case 128: return by_epi<128>(a, wmap, xmap, epi, stream);
+    case 16: return by_chunks<16>(a, wmap, xmap, epi, ch, stream);
+    case 32: return by_chunks<32>(a, wmap, xmap, epi, ch, stream);
+    case 64: return by_chunks<64>(a, wmap, xmap, epi, ch, stream);
+    case 128: return by_chunks<128>(a, wmap, xmap, epi, ch, stream);
     default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: batch tile %d", nb);
   }
 }

@@ -4,12 +4,15 @@
 //
 // A tile is 128 weight rows (the UMMA M side, operand A) x NB batch rows (the
 // N side, operand B), accumulated in fp32 in TMEM. Both operands stream
-// through a shared-memory ring in 64-column K slabs: TMA tensor copies
-// (make_kmajor_map, box {64, rows, 1}) land each slab K-major with the
-// 128-byte swizzle, which is the canonical SW128 K-major operand layout of
-// tcgen05.mma (8-row groups 1024 bytes apart). Per slab the MMA thread issues
-// four m128 x nNB x k16 MMAs, advancing both descriptors by 32 bytes, and
-// commits the slab's release to its empty barrier.
+// through a shared-memory ring in stages of CH 64-column K chunks: TMA tensor
+// copies (make_kmajor_map, box {64, rows, CH}) land each chunk K-major with
+// the 128-byte swizzle, which is the canonical SW128 K-major operand layout
+// of tcgen05.mma (8-row groups 1024 bytes apart), chunk after chunk. Per
+// chunk the MMA thread issues four m128 x nNB x k16 MMAs, advancing both
+// descriptors by 32 bytes, and commits the stage's release to its empty
+// barrier. Several chunks per copy give each weight row CH x 128 contiguous
+// bytes per request, which the DRAM streams far better than 128-byte pieces
+// 4 KB apart.
 //
 // Warps: 0 TMA producer (one lane), 1 TMEM allocation + MMA issue (one lane),
 // 2-5 epilogue: each reads its 32 TMEM lanes (= 32 weight rows) with
@@ -29,19 +32,21 @@
 namespace lcrb {
 
 constexpr int kTcTileM = 128;        // weight rows per tile
-constexpr int kTcSlabK = 64;         // K columns per ring stage (128-byte swizzle span)
+constexpr int kTcSlabK = 64;         // K columns per chunk (128-byte swizzle span)
 constexpr int kTcThreads = 192;      // 6 warps
 constexpr int kTcRingBytes = 196608; // ring budget (stage count derived from it)
 
-template <int NB>
+template <int NB, int CH>
 struct TcGeom {
   static_assert(NB == 16 || NB == 32 || NB == 64 || NB == 128 || NB == 256, "batch tile");
-  static constexpr int W_BYTES = kTcTileM * kTcSlabK * 2;  // 16 KB
-  static constexpr int X_BYTES = NB * kTcSlabK * 2;
+  static constexpr int W_CHUNK = kTcTileM * kTcSlabK * 2;  // 16 KB
+  static constexpr int X_CHUNK = NB * kTcSlabK * 2;
+  static constexpr int W_BYTES = CH * W_CHUNK;
+  static constexpr int X_BYTES = CH * X_CHUNK;
   static constexpr int STAGE = W_BYTES + X_BYTES;  // a multiple of 1024
   static constexpr int STAGES = (kTcRingBytes / STAGE) < 8 ? (kTcRingBytes / STAGE) : 8;
   static constexpr int TMEM_COLS = NB < 32 ? 32 : NB;  // power of two >= 32
-  static_assert(STAGE % 1024 == 0 && STAGES >= 3, "stage geometry");
+  static_assert(STAGE % 1024 == 0 && STAGES >= 2, "stage geometry");
 };
 
 struct TcArgs {
@@ -140,10 +145,10 @@ __device__ __forceinline__ void tc_store(const TcArgs& a, int b, int n, float v,
   }
 }
 
-template <int NB, int EPI>
+template <int NB, int EPI, int CH>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap) {
-  using G = TcGeom<NB>;
+  using G = TcGeom<NB, CH>;
   constexpr bool SWIGLU = EPI == EPI_SWIGLU;
   constexpr int STAGES = G::STAGES;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int tile = blockIdx.x % tiles_n;
   const int tile_b = blockIdx.x / tiles_n;
   const int split = blockIdx.y;
-  const int slabs = a.K / kTcSlabK;
+  const int slabs = a.K / (kTcSlabK * CH);  // ring stages over K
   const int s0 = static_cast<int>(static_cast<long long>(split) * slabs / a.splits);
   const int s1 = static_cast<int>(static_cast<long long>(split + 1) * slabs / a.splits);
   const int n0 = SWIGLU ? tile * 64 : tile * kTcTileM;
@@ -189,18 +194,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     if (lane == 0 && aligned) {
       const uint64_t policy = l2_policy_evict_first();
+      // Each tile walks its K range from its own starting stage, so CTAs
+      // running side by side read different slabs of x (not the same L2
+      // lines at once); the accumulation order is fixed per tile.
+      const int span = s1 - s0;
+      const int rot = span > 0 ? static_cast<int>(blockIdx.x % static_cast<unsigned>(span)) : 0;
       int it = 0;
-      for (int s = s0; s < s1; ++s, ++it) {
+      for (int q = 0; q < span; ++q, ++it) {
+        const int s = s0 + (q + rot < span ? q + rot : q + rot - span);
         const int slot = it % STAGES;
         if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) break;
         uint8_t* st = ring + slot * G::STAGE;
         mbar_arrive_expect_tx(&full[slot], G::STAGE);
         if constexpr (SWIGLU) {
-          tma_load_4d(st, &wmap, 0, n0, 0, s, &full[slot], policy);
+          tma_load_4d(st, &wmap, 0, n0, 0, s * CH, &full[slot], policy);
         } else {
-          tma_load_3d(st, &wmap, 0, n0, s, &full[slot], policy);
+          tma_load_3d(st, &wmap, 0, n0, s * CH, &full[slot], policy);
         }
-        tma_load_3d(st + G::W_BYTES, &xmap, 0, b0, s, &full[slot], policy);
+        tma_load_3d(st + G::W_BYTES, &xmap, 0, b0, s * CH, &full[slot], policy);
       }
       ring_drain<STAGES>(full, it, a.status);
     }
@@ -217,12 +228,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_after();
         const uint32_t st = smem_addr(ring + slot * G::STAGE);
-        const uint64_t adesc = tc_desc_sw128(st);
-        const uint64_t bdesc = tc_desc_sw128(st + G::W_BYTES);
 #pragma unroll
-        for (int k = 0; k < kTcSlabK / 16; ++k) {
-          // +32 bytes per 16 columns inside the 128-byte swizzle span
-          tc_mma(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (s > s0 || k > 0) ? 1u : 0u);
+        for (int c = 0; c < CH; ++c) {
+          const uint64_t adesc = tc_desc_sw128(st + c * G::W_CHUNK);
+          const uint64_t bdesc = tc_desc_sw128(st + G::W_BYTES + c * G::X_CHUNK);
+#pragma unroll
+          for (int k = 0; k < kTcSlabK / 16; ++k) {
+            // +32 bytes per 16 columns inside the 128-byte swizzle span
+            tc_mma(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (it > 0 || c > 0 || k > 0) ? 1u : 0u);
+          }
         }
         tc_commit(&empty[slot]);
       }
@@ -338,9 +352,10 @@ __global__ void __launch_bounds__(256) gemm_tc_reduce_kernel(const TcArgs a) {
   }
 }
 
-template <int NB>
+template <int NB, int CH>
 constexpr size_t gemm_tc_smem_bytes() {
-  return static_cast<size_t>(TcGeom<NB>::STAGES) * TcGeom<NB>::STAGE + (2 * TcGeom<NB>::STAGES + 2) * 8 + 16 + 1024;
+  using G = TcGeom<NB, CH>;
+  return static_cast<size_t>(G::STAGES) * G::STAGE + (2 * G::STAGES + 2) * 8 + 16 + 1024;
 }
 
 }  // namespace lcrb

@@ -10,13 +10,16 @@ namespace lcrb {
 // Smallest supported batch tile covering `rows` (16, 32, 64 or 128; larger
 // batches take several tiles of 128).
 int gemm_tc_batch_tile(int rows);
-// Launches y = x w^T for `a.rows` batch rows: wmap = make_kmajor_map(w, n_out
-// (2F for SWIGLU as two halves), K, halves, 128 (64 for SWIGLU), 1), xmap =
-// make_kmajor_map(x, rows, K, 1, nb, 1). One CTA per (weight tile, batch
-// tile, split); a.splits > 1 needs a.work of gemm_tc_work_floats() floats and
-// adds a second launch (gemm_tc_reduce_kernel).
+// Largest chunks per stage gemm_tc_launch takes with batch tile nb.
+int gemm_tc_max_chunks(int nb);
 size_t gemm_tc_work_floats(int rows, int n_out, int epi, int splits);
-int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi,
+// Launches y = x w^T for `a.rows` batch rows, each ring stage carrying `ch`
+// 64-column K chunks: wmap = make_kmajor_map(w, n_out (2F for SWIGLU as two
+// halves), K, halves, 128 (64 for SWIGLU), ch), xmap = make_kmajor_map(x,
+// rows, K, 1, nb, ch). One CTA per (weight tile, batch tile, split); a.splits
+// > 1 needs a.work of gemm_tc_work_floats() floats and adds a second launch
+// (gemm_tc_reduce_kernel).
+int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi, int ch,
                    cudaStream_t stream);
 
 }  // namespace lcrb
