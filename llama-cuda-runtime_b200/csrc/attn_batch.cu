@@ -9,10 +9,8 @@ int launch_t(const AttnArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap
   auto kernel = attn_batch_kernel<D, G>;
   const size_t smem = attn_batch_smem_bytes<D, G>(a.seqs);
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  kernel<<<ctas, kAbThreads, smem, s>>>(a, kmap, vmap);
-  LCRB_TRY(launch_status("batched decode attention"));
-  attn_batch_merge_kernel<D><<<a.seqs * (a.q_dim / D), D, 0, s>>>(a);
-  return launch_status("batched decode attention merge");
+  LCRB_TRY(launch_kernel(kernel, dim3(ctas), dim3(kAbThreads), smem, s, true, a, kmap, vmap));
+  return launch_kernel(attn_batch_merge_kernel<D>, dim3(a.seqs * (a.q_dim / D)), dim3(D), 0, s, true, a);
 }
 
 template <int D, int G>

@@ -212,7 +212,6 @@ __global__ void __launch_bounds__(kAbThreads, D == 64 ? 3 : 1)
     }
   }
   __syncthreads();
-  pdl_launch_next();
   const int total = cum[n];
 
   if (warp == kAttnConsumerWarps) {
@@ -294,6 +293,7 @@ __global__ void __launch_bounds__(kAbThreads, D == 64 ? 3 : 1)
       }
       cur = __shfl_sync(0xffffffffu, static_cast<int>(nxt), 0);
     }
+    pdl_launch_next();  // the merge kernel may start launching
     if (ok) {  // the end-of-work stage: no copies, a plain arrive
       const int slot = st % STAGES;
       if (lane == 0 && st >= STAGES) {
@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(kAbThreads, D == 64 ? 3 : 1)
   if (warp == kAttnConsumerWarps + 1) {
     // ---------------------------------------------------------------- finisher
     const int heads = num_kv * G;
+    pdl_wait();  // its outputs are read by kernels that ran before this one
     for (int k = 0;; ++k) {
       const int buf = k & 1;
       if (!mbar_wait(&rec_full[buf], (k >> 1) & 1, a.status, kStatusTimeoutFull)) break;
@@ -374,6 +375,7 @@ __global__ void __launch_bounds__(kAbThreads, D == 64 ? 3 : 1)
   float o[NT][4];
   float m_run = kNegBig, l_run = 0.f;
   int pos = 0, items = 0;
+  pdl_wait();  // the new key / value rows come from the QKV projection
 
   for (int st = 0;; ++st) {
     const int slot = st % STAGES;
@@ -505,6 +507,8 @@ template <int D>
 __global__ void __launch_bounds__(D) attn_batch_merge_kernel(const AttnArgs a) {
   const int heads = (a.q_dim / D);
   const int b = blockIdx.x / heads, h = blockIdx.x % heads, d = threadIdx.x;
+  pdl_wait();
+  pdl_launch_next();
   const int p = a.positions[b];
   if (!(p >= 0 && p < a.max_seq && p / a.page_size < a.max_pages)) return;
   const int splits = (p + a.item_pos) / a.item_pos;

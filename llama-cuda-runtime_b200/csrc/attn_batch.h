@@ -12,7 +12,7 @@ namespace lcrb {
 // `seqs` sequences on `sms` SMs (as many as fit at once).
 int attn_batch_ctas(int head_dim, int group, int seqs, int sms, int* ctas);
 // One layer's attention for a.seqs sequences (at most kAbMaxSeqs), two
-// launches (attention, then the merge of split partials): kmap /
+// programmatic launches (attention, then the merge of split partials): kmap /
 // vmap = make_kmajor_map of the layer's K / V pool as [pool_pages *
 // kv_heads * page_size][head_dim] rows with a {64, 16, head_dim / 64} box;
 // `a` as for attn_launch in FUSED paged mode (page_size a multiple of 16),

@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const NormRowsA
   constexpr int PER = (CH + kNormThreads - 1) / kNormThreads;  // per thread
   __shared__ float red[kNormThreads / 32];
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();  // the residual stream comes from the preceding projection
+  pdl_launch_next();
   const size_t row = static_cast<size_t>(b) * H;
   const bf16* src = a.x + row;
   if constexpr (EMBED) {

@@ -1,7 +1,10 @@
 // Batched decode context (include/lcr_b200.h, lcr_batch_*): continuous
 // batching of up to max_batch sequences, one token each per step.
 //
-// A step of n slots is, per layer:
+// Every kernel after the first launches programmatically (PDL): it starts
+// while its predecessor drains and waits (griddepcontrol.wait) before
+// reading that predecessor's outputs; the projections stream their first
+// weight stages before the wait. A step of n slots is, per layer:
 //   norm_rows_kernel        x -> xn (layer 0: the token embeddings)
 //   gemm_tc_kernel          qkv  = xn W_qkv^T, RoPE on q and k (the step's
 //                           cos/sin table, written by the layer-0 norm)
@@ -169,23 +172,17 @@ int norm_launch(lcr_batch* c, int n, bool embed, const void* gain) {
   }
   ++c->launches;
   const dim3 grid(static_cast<unsigned>(n));
+  void (*kernel)(NormRowsArgs) = nullptr;
   switch (c->d.hidden_size) {
-    case 2048:
-      if (embed) norm_rows_kernel<2048, true><<<grid, kNormThreads, 0, c->stream>>>(a);
-      else norm_rows_kernel<2048, false><<<grid, kNormThreads, 0, c->stream>>>(a);
-      break;
-    case 256:
-      if (embed) norm_rows_kernel<256, true><<<grid, kNormThreads, 0, c->stream>>>(a);
-      else norm_rows_kernel<256, false><<<grid, kNormThreads, 0, c->stream>>>(a);
-      break;
-    case 4096:
-      if (embed) norm_rows_kernel<4096, true><<<grid, kNormThreads, 0, c->stream>>>(a);
-      else norm_rows_kernel<4096, false><<<grid, kNormThreads, 0, c->stream>>>(a);
-      break;
+    case 256: kernel = embed ? norm_rows_kernel<256, true> : norm_rows_kernel<256, false>; break;
+    case 2048: kernel = embed ? norm_rows_kernel<2048, true> : norm_rows_kernel<2048, false>; break;
+    case 4096: kernel = embed ? norm_rows_kernel<4096, true> : norm_rows_kernel<4096, false>; break;
     default:
       return fail(LCR_ERR_SHAPE, "batched RMSNorm has no kernel for hidden size %d", c->d.hidden_size);
   }
-  return launch_status("batched rmsnorm");
+  // The step's first kernel follows the host copies of its inputs; the
+  // others launch programmatically after their predecessor.
+  return launch_kernel(kernel, grid, dim3(kNormThreads), 0, c->stream, !embed, a);
 }
 
 // One projection: n rows of `x` (tensor map `xm`, batch tile nb) against
@@ -216,7 +213,7 @@ int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb
   a.splits = splits;
   a.work = c->work;
   c->launches += splits > 1 ? 2 : 1;
-  return gemm_tc_launch(a, wm, xm, nb, epi, c->tc_chunks, c->stream);
+  return gemm_tc_launch(a, wm, xm, nb, epi, c->tc_chunks, c->stream, true);
 }
 
 int attention_launch_layer(lcr_batch* c, int layer, int n) {
@@ -304,7 +301,7 @@ int enqueue_step(lcr_batch* c, int n) {
   s.counter = c->positions;
   s.out = c->next;
   ++c->launches;
-  return sample_launch(s, n, c->stream, false);
+  return sample_launch(s, n, c->stream, true);
 }
 
 int launch_step(lcr_batch* c, int n) {

@@ -237,6 +237,27 @@ __device__ __forceinline__ void pdl_launch_next() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Launches kernel<<<grid, block, smem, stream>>>(args) -- with programmatic
+// stream serialization when `pdl`, so that the kernel may start while its
+// predecessor finishes (it must pdl_wait() before touching that
+// predecessor's outputs, or anything a still-running kernel writes).
+template <class... Params, class... Args>
+inline int launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                         Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  return e == cudaSuccess ? LCR_OK : fail(LCR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
 // Named barrier over the first `threads` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

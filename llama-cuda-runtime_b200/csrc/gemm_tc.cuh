@@ -145,6 +145,68 @@ __device__ __forceinline__ void tc_store(const TcArgs& a, int b, int n, float v,
   }
 }
 
+// Outputs n .. n + 7 of batch row b (fewer at the matrix edge): one 16-byte
+// access per bf16 vector where the row is 16-byte aligned, else per element.
+template <int EPI>
+__device__ __forceinline__ void tc_store8(const TcArgs& a, int b, int n, const float (&v)[8], const float (&aux)[8]) {
+  const size_t o = static_cast<size_t>(b) * a.ldy + n;
+  const bool whole = n + 8 <= a.n_out;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if constexpr (EPI == EPI_STORE || EPI == EPI_SWIGLU || EPI == EPI_ROPE) {
+    if (whole && al16(a.y + o)) {
+      float r[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if constexpr (EPI == EPI_STORE) {
+          r[e] = v[e];
+        } else if constexpr (EPI == EPI_SWIGLU) {
+          const float g = rbf(v[e]);
+          r[e] = (g / (1.0f + __expf(-g))) * rbf(aux[e]);
+        } else {
+          r[e] = rbf(v[e]);
+          if (n + e < a.rope_cols) {
+            const int half = a.head_dim >> 1;
+            const int d = (n + e) & (a.head_dim - 1);
+            const float2 cs = a.rope[static_cast<size_t>(b) * half + (d & (half - 1))];
+            const float other = rbf(aux[e]);
+            r[e] = d < half ? (r[e] * cs.x - other * cs.y) : (r[e] * cs.x + other * cs.y);
+          }
+        }
+      }
+      uint4 w;
+      w.x = pack_bf2(r[0], r[1]);
+      w.y = pack_bf2(r[2], r[3]);
+      w.z = pack_bf2(r[4], r[5]);
+      w.w = pack_bf2(r[6], r[7]);
+      *reinterpret_cast<uint4*>(a.y + o) = w;
+      return;
+    }
+  } else if constexpr (EPI == EPI_STORE_F32) {
+    if (whole && al16(a.yf + o)) {
+      *reinterpret_cast<float4*>(a.yf + o) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(a.yf + o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      return;
+    }
+  } else if constexpr (EPI == EPI_RESID) {
+    if (whole && al16(a.resid + o) && al16(a.resid_sum + o)) {
+      float x[8], s8[8];
+      unpack8(ldg_cg16(a.resid + o), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s8[e] = __fadd_rn(x[e], rbf(v[e]));
+      uint4 w;
+      w.x = pack_bf2(s8[0], s8[1]);
+      w.y = pack_bf2(s8[2], s8[3]);
+      w.z = pack_bf2(s8[4], s8[5]);
+      w.w = pack_bf2(s8[6], s8[7]);
+      *reinterpret_cast<uint4*>(a.resid + o) = w;
+      *reinterpret_cast<float4*>(a.resid_sum + o) = make_float4(s8[0], s8[1], s8[2], s8[3]);
+      *reinterpret_cast<float4*>(a.resid_sum + o + 4) = make_float4(s8[4], s8[5], s8[6], s8[7]);
+      return;
+    }
+  }
+  for (int e = 0; e < 8 && n + e < a.n_out; ++e) tc_store<EPI>(a, b, n + e, v[e], aux[e]);
+}
+
 template <int NB, int EPI, int CH>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap) {
@@ -199,19 +261,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // lines at once); the accumulation order is fixed per tile.
       const int span = s1 - s0;
       const int rot = span > 0 ? static_cast<int>(blockIdx.x % static_cast<unsigned>(span)) : 0;
-      int it = 0;
-      for (int q = 0; q < span; ++q, ++it) {
-        const int s = s0 + (q + rot < span ? q + rot : q + rot - span);
+      auto k_stage = [&](int q) { return s0 + (q + rot < span ? q + rot : q + rot - span); };
+      auto load_w = [&](int q, uint8_t* st, uint64_t* bar) {
+        if constexpr (SWIGLU) {
+          tma_load_4d(st, &wmap, 0, n0, 0, k_stage(q) * CH, bar, policy);
+        } else {
+          tma_load_3d(st, &wmap, 0, n0, k_stage(q) * CH, bar, policy);
+        }
+      };
+      // The weights do not depend on the preceding kernel: the first ring's
+      // worth streams before the wait for its output (x).
+      const int pre = span < STAGES ? span : STAGES;
+      for (int q = 0; q < pre; ++q) {
+        mbar_arrive_expect_tx(&full[q], G::STAGE);
+        load_w(q, ring + q * G::STAGE, &full[q]);
+      }
+      pdl_wait();
+      for (int q = 0; q < pre; ++q) {
+        tma_load_3d(ring + q * G::STAGE + G::W_BYTES, &xmap, 0, b0, k_stage(q) * CH, &full[q], policy);
+      }
+      int it = pre;
+      for (int q = pre; q < span; ++q, ++it) {
         const int slot = it % STAGES;
-        if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) break;
+        if (!mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) break;
         uint8_t* st = ring + slot * G::STAGE;
         mbar_arrive_expect_tx(&full[slot], G::STAGE);
-        if constexpr (SWIGLU) {
-          tma_load_4d(st, &wmap, 0, n0, 0, s * CH, &full[slot], policy);
-        } else {
-          tma_load_3d(st, &wmap, 0, n0, s * CH, &full[slot], policy);
-        }
-        tma_load_3d(st + G::W_BYTES, &xmap, 0, b0, s * CH, &full[slot], policy);
+        load_w(q, st, &full[slot]);
+        tma_load_3d(st + G::W_BYTES, &xmap, 0, b0, k_stage(q) * CH, &full[slot], policy);
       }
       ring_drain<STAGES>(full, it, a.status);
     }
@@ -240,8 +316,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_commit(&empty[slot]);
       }
-      // Accumulator complete (or abandoned): release the epilogue, and make
-      // sure no MMA is still running before TMEM is freed.
+      // Accumulator complete (or abandoned): the next kernel may start
+      // launching; release the epilogue, and make sure no MMA is still
+      // running before TMEM is freed.
+      pdl_launch_next();
       tc_commit(acc_full);
       tc_commit(drain);
       mbar_wait(drain, 0, a.status, kStatusTimeoutFull);
@@ -251,6 +329,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
     const int quad = warp & 3;
     const int row = quad * 32 + lane;  // tile row 0..127
+    pdl_wait();  // the residual stream and RoPE table come from earlier kernels
     // (status is optional: the per-kernel entry points may pass none)
     const bool mine = mbar_wait(acc_full, 0, a.status, kStatusTimeoutFull) &&
                       !(a.status != nullptr && (__ldcg(a.status) & kStatusAbort));
@@ -279,39 +358,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     if (have && a.splits == 1) {
-      if constexpr (SWIGLU) {
-        // Rows 0-63 are gate rows n0 + r, rows 64-127 the matching up rows:
-        // exchange through the (now idle) ring.
-        float* xch = reinterpret_cast<float*>(ring);
-        if (row >= 64) {
+      // Transpose the tile through the idle ring (rows padded to NB + 1
+      // floats), then each thread finishes 8 consecutive outputs of one
+      // batch row at a time: vector loads and stores, and every epilogue
+      // warp shares the work (SWIGLU: rows 0-63 gate, 64-127 up; ROPE: the
+      // partner of tile row r is r ^ head_dim / 2).
+      float* T = reinterpret_cast<float*>(ring);
 #pragma unroll
-          for (int b = 0; b < NB; ++b) xch[b * 64 + (row - 64)] = v[b];
-        }
-        named_sync(2, 128);
-        if (row < 64 && n0 + row < a.n_out) {
+      for (int b = 0; b < NB; ++b) T[row * (NB + 1) + b] = v[b];
+      named_sync(2, 128);
+      constexpr int NOUT = SWIGLU ? 64 : kTcTileM;
+      for (int c = tid - 64; c < (NOUT / 8) * NB; c += 128) {
+        const int n8 = c / NB, b = c % NB;
+        const int nl = n8 * 8;
+        if (b0 + b >= a.rows || n0 + nl >= a.n_out) continue;
+        float val[8], aux[8];
 #pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], xch[b * 64 + row]);
+        for (int e = 0; e < 8; ++e) {
+          val[e] = T[(nl + e) * (NB + 1) + b];
+          if constexpr (SWIGLU) {
+            aux[e] = T[(64 + nl + e) * (NB + 1) + b];
+          } else if constexpr (EPI == EPI_ROPE) {
+            aux[e] = T[((nl + e) ^ (a.head_dim >> 1)) * (NB + 1) + b];
+          } else {
+            aux[e] = 0.f;
           }
         }
-      } else if constexpr (EPI == EPI_ROPE) {
-        // Rotation partners (tile row ^ head_dim / 2) through the idle ring.
-        float* xch = reinterpret_cast<float*>(ring);
-#pragma unroll
-        for (int b = 0; b < NB; ++b) xch[b * kTcTileM + row] = v[b];
-        named_sync(2, 128);
-        if (n0 + row < a.n_out) {
-          const int prow = row ^ (a.head_dim >> 1);
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], xch[b * kTcTileM + prow]);
-          }
-        }
-      } else if (n0 + row < a.n_out) {
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          if (b0 + b < a.rows) tc_store<EPI>(a, b0 + b, n0 + row, v[b], 0.f);
-        }
+        tc_store8<EPI>(a, b0 + b, n0 + nl, val, aux);
       }
     }
   }
@@ -332,6 +405,8 @@ __global__ void __launch_bounds__(256) gemm_tc_reduce_kernel(const TcArgs a) {
   const size_t m_total = static_cast<size_t>(tiles_n) * kTcTileM;
   const size_t plane = static_cast<size_t>(a.rows) * m_total;
   const size_t total = static_cast<size_t>(a.rows) * a.n_out;
+  pdl_wait();
+  pdl_launch_next();
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const int b = static_cast<int>(i / a.n_out), n = static_cast<int>(i % a.n_out);

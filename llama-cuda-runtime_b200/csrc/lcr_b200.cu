@@ -291,7 +291,7 @@ extern "C" int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, in
     a.ldy = out_features;
     if (y_fp32) a.yf = reinterpret_cast<float*>(y);
     else a.y = mb(y);
-    return gemm_tc_launch(a, wmap, xmap, nb, epi, 1, cs(stream));
+    return gemm_tc_launch(a, wmap, xmap, nb, epi, 1, cs(stream), false);
   }
   if (gemv_supported(in_features, PRO_PLAIN, epi) && aligned16(x) && aligned16(w)) {
     int sms = 148;

@@ -170,6 +170,8 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
   __shared__ int scan[kSampleThreads / 32];
 
   const int row = blockIdx.x, tid = threadIdx.x;
+  pdl_wait();  // the logits come from the preceding kernel
+  pdl_launch_next();
   const float* L = a.logits + static_cast<long long>(row) * a.row_stride;
   const int V = a.vocab;
   const float inv_t = a.inv_temperature[row];
