@@ -332,6 +332,18 @@ LCR_API int lcr_batch_step(lcr_batch* batch, int n, const int32_t* tokens,
  * current page table: a stand-in for the prompt's prefill when a benchmark
  * admits a sequence. Asynchronous. */
 LCR_API int lcr_batch_fill_kv(lcr_batch* batch, int slot, int length, uint64_t seed);
+/* Chunked prefill, Model::prefill (src/model.cu:308-345 with the attention of
+ * model.cu:509-560): `count` prompt tokens of slot `slot` at positions
+ * start .. start + count - 1, through the projections as tcgen05 GEMMs over
+ * the chunk's rows and causal flash attention over the slot's pages (which
+ * must cover start + count positions; earlier positions come from earlier
+ * chunks or steps). Writes the chunk's K/V into the cache, the last row's
+ * logits into the slot's logits (lcr_batch_logits) and its sample, with the
+ * slot's sampling parameters and Philox counter start + count - 1, into the
+ * slot's next id (lcr_batch_read). The slot then decodes from position
+ * start + count. Asynchronous; the first call (or a longer chunk) allocates
+ * the chunk's activations. */
+LCR_API int lcr_batch_prefill(lcr_batch* batch, int slot, const int32_t* tokens, int count, int start);
 /* The last step's sampled ids of slots [0, n) into host memory (synchronous). */
 LCR_API int lcr_batch_read(lcr_batch* batch, int32_t* next_ids, int n);
 /* The last step's fp32 logits [vocab] of one slot into host memory (synchronous). */

@@ -1,0 +1,45 @@
+// Instantiations and launch of the causal prefill attention.
+#include "attn_prefill.h"
+
+namespace lcrb {
+namespace {
+
+template <int D, int G>
+int launch_t(const PrefillAttnArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap, int kv_heads,
+             cudaStream_t s) {
+  auto kernel = attn_prefill_kernel<D, G>;
+  constexpr size_t smem = attn_prefill_smem_bytes<D>();
+  LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  const int pairs = (a.count + 15) / 16 * G;
+  const dim3 grid(static_cast<unsigned>((pairs + kAttnConsumerWarps - 1) / kAttnConsumerWarps),
+                  static_cast<unsigned>(kv_heads));
+  return launch_kernel(kernel, grid, dim3(kAttnThreads), smem, s, true, a, kmap, vmap);
+}
+
+template <int D>
+int by_group(const PrefillAttnArgs& a, const CUtensorMap& k, const CUtensorMap& v, int group, int kv_heads,
+             cudaStream_t s) {
+  switch (group) {
+    case 1: return launch_t<D, 1>(a, k, v, kv_heads, s);
+    case 2: return launch_t<D, 2>(a, k, v, kv_heads, s);
+    case 4: return launch_t<D, 4>(a, k, v, kv_heads, s);
+    case 8: return launch_t<D, 8>(a, k, v, kv_heads, s);
+    default:
+      return fail(LCR_ERR_SHAPE,
+                  "prefill attention is compiled for 1, 2, 4 or 8 query heads per KV head, this model has %d",
+                  group);
+  }
+}
+
+}  // namespace
+
+int attn_prefill_launch(const PrefillAttnArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap, int head_dim,
+                        int group, int kv_heads, cudaStream_t s) {
+  LCRB_REQUIRE(a.count >= 1 && a.start >= 0 && a.page_size % kAbUnit == 0, LCR_ERR_SHAPE,
+               "prefill attention: unsupported chunk (%d rows at %d, page size %d)", a.count, a.start, a.page_size);
+  if (head_dim == 64) return by_group<64>(a, kmap, vmap, group, kv_heads, s);
+  if (head_dim == 128) return by_group<128>(a, kmap, vmap, group, kv_heads, s);
+  return fail(LCR_ERR_SHAPE, "prefill attention is compiled for head_dim 64 or 128, this model has %d", head_dim);
+}
+
+}  // namespace lcrb

@@ -105,6 +105,50 @@ __global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const NormRowsA
   }
 }
 
+// Prefill: the chunk's rotated K rows and V rows (from the QKV projection)
+// into the sequence's pages at positions start .. start + count - 1, one CTA
+// per position; CTAs past the chunk, up to the next multiple of 16, zero
+// those slots, so that a 16-position unit read by attn_prefill_kernel holds
+// finite values everywhere (decode overwrites them later).
+struct KvWriteArgs {
+  const bf16* qkv;
+  int qkv_stride, q_dim, kv_dim, head_dim, kv_heads;
+  bf16* kpool;  // this layer's pools
+  bf16* vpool;
+  const int32_t* table;
+  int page_size, pool_pages;
+  long long page_stride, head_stride;
+  int start, count;
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(128) kv_write_kernel(const KvWriteArgs a) {
+  pdl_wait();  // the rows come from the preceding projection
+  pdl_launch_next();
+  const int r = blockIdx.x;
+  const int pos = a.start + r;
+  int page = a.table[pos / a.page_size];
+  if (page < 0 || page >= a.pool_pages) {
+    if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusBadPage);
+    return;
+  }
+  const int pieces = a.head_dim / 8;
+  const long long base = static_cast<long long>(page) * a.page_stride +
+                         static_cast<long long>(pos % a.page_size) * a.head_dim;
+  for (int i = threadIdx.x; i < a.kv_heads * pieces; i += blockDim.x) {
+    const int h = i / pieces, piece = i % pieces;
+    uint4 k = make_uint4(0u, 0u, 0u, 0u), v = k;
+    if (r < a.count) {
+      const bf16* row = a.qkv + static_cast<size_t>(r) * a.qkv_stride + a.q_dim + h * a.head_dim + piece * 8;
+      k = ldg_cg16(row);
+      v = ldg_cg16(row + a.kv_dim);
+    }
+    const long long off = base + h * a.head_stride + piece * 8;
+    *reinterpret_cast<uint4*>(a.kpool + off) = k;
+    *reinterpret_cast<uint4*>(a.vpool + off) = v;
+  }
+}
+
 // Seeded synthetic K/V for positions [0, length) of one sequence in every
 // layer: each element is an approximately standard normal value (the sum of
 // four hashed uniforms, centred and scaled), rounded to bf16, written at the

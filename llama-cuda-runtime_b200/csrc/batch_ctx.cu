@@ -35,6 +35,7 @@
 
 #include "attention.cuh"
 #include "attn_batch.h"
+#include "attn_prefill.h"
 #include "batch.cuh"
 #include "common.cuh"
 #include "dispatch.h"
@@ -52,6 +53,20 @@ constexpr int kStaging = 16;  // pinned (tokens, positions) staging areas
 
 struct StepMaps {  // activation tensor maps for one batch tile size
   CUtensorMap xn, attn, act;
+};
+
+// One set of activation rows: the step's (max_batch rows) or a prefill
+// chunk's.
+struct Acts {
+  int32_t* tokens;
+  int32_t* positions;
+  bf16* x;       // residual stream (bf16)
+  float* xsum;   // its unrounded sums
+  bf16* xn;      // normalised rows
+  bf16* qkv;
+  bf16* attn;
+  bf16* act;
+  float2* rope;  // [rows][head_dim / 2] (cos, sin)
 };
 
 }  // namespace
@@ -113,6 +128,10 @@ struct lcr_batch {
   cudaEvent_t staged[kStaging] = {};
   int staging_next = 0;
 
+  char* pre_buf = nullptr;  // prefill activations, grown to the largest chunk
+  int pre_rows = 0;
+  Acts pre{};
+
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, int> launches_by_n;  // kernels one step of n slots launches
   int last_n = 0;
@@ -133,6 +152,7 @@ void release(lcr_batch* c) {
   cudaFree(c->kpool);
   cudaFree(c->vpool);
   cudaFree(c->work);
+  cudaFree(c->pre_buf);
   cudaFreeHost(c->pinned);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -153,21 +173,25 @@ int check_status(lcr_batch* c) {
   return fail(LCR_ERR_STATE, "position outside the KV cache (status 0x%x)", st);
 }
 
-int norm_launch(lcr_batch* c, int n, bool embed, const void* gain) {
+Acts step_acts(const lcr_batch* c) {
+  return Acts{c->tokens, c->positions, c->x, c->xsum, c->xn, c->qkv, c->attn, c->act, c->rope};
+}
+
+int norm_launch(lcr_batch* c, const Acts& v, int n, bool embed, const void* gain) {
   NormRowsArgs a = {};
-  a.tokens = c->tokens;
+  a.tokens = v.tokens;
   a.embed = c->embed;
   a.vocab = c->d.vocab_size;
-  a.x = c->x;
-  a.xsum = c->xsum;
+  a.x = v.x;
+  a.xsum = v.xsum;
   a.gain = static_cast<const bf16*>(gain);
   a.eps = c->d.rms_norm_eps;
-  a.out = c->xn;
+  a.out = v.xn;
   a.status = c->status;
   if (embed) {
-    a.positions = c->positions;
+    a.positions = v.positions;
     a.inv_freq = c->inv_freq;
-    a.rope = c->rope;
+    a.rope = v.rope;
     a.half = c->d.head_dim / 2;
   }
   ++c->launches;
@@ -187,8 +211,8 @@ int norm_launch(lcr_batch* c, int n, bool embed, const void* gain) {
 
 // One projection: n rows of `x` (tensor map `xm`, batch tile nb) against
 // weight map `wm` ([n_out][K], or gate/up halves for SWIGLU).
-int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb, int n, int n_out, int K,
-              int epi, bf16* y, float* yf, int ldy) {
+int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensorMap& xm, int nb, int n, int n_out,
+              int K, int epi, bf16* y, float* yf, int ldy) {
   TcArgs a = {};
   a.n_out = n_out;
   a.K = K;
@@ -196,10 +220,10 @@ int gemm_node(lcr_batch* c, const CUtensorMap& wm, const CUtensorMap& xm, int nb
   a.ldy = ldy;
   a.y = y;
   a.yf = yf;
-  a.resid = c->x;
-  a.resid_sum = c->xsum;
+  a.resid = v.x;
+  a.resid_sum = v.xsum;
   a.status = c->status;
-  a.rope = c->rope;
+  a.rope = v.rope;
   a.head_dim = c->d.head_dim;
   a.rope_cols = (c->d.num_heads + c->d.num_kv_heads) * c->d.head_dim;
   const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
@@ -275,19 +299,20 @@ int enqueue_step(lcr_batch* c, int n) {
   const StepMaps* m = nullptr;
   LCRB_TRY(maps_for(c, nb, &m));
   c->launches = 0;
+  const Acts v = step_acts(c);
   for (int l = 0; l < d.num_layers; ++l) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
     const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
-    LCRB_TRY(norm_launch(c, n, l == 0, w.input_norm));
-    LCRB_TRY(gemm_node(c, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_ROPE, c->qkv, nullptr, qd + 2 * kvd));
+    LCRB_TRY(norm_launch(c, v, n, l == 0, w.input_norm));
+    LCRB_TRY(gemm_node(c, v, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd));
     LCRB_TRY(attention_launch_layer(c, l, n));
-    LCRB_TRY(gemm_node(c, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H));
-    LCRB_TRY(norm_launch(c, n, false, w.post_attention_norm));
-    LCRB_TRY(gemm_node(c, wm[2], m->xn, nb, n, F, H, EPI_SWIGLU, c->act, nullptr, F));
-    LCRB_TRY(gemm_node(c, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(gemm_node(c, v, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(norm_launch(c, v, n, false, w.post_attention_norm));
+    LCRB_TRY(gemm_node(c, v, wm[2], m->xn, nb, n, F, H, EPI_SWIGLU, v.act, nullptr, F));
+    LCRB_TRY(gemm_node(c, v, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H));
   }
-  LCRB_TRY(norm_launch(c, n, false, c->final_norm));
-  LCRB_TRY(gemm_node(c, c->wmaps.back(), m->xn, nb, n, d.vocab_size, H, EPI_STORE_F32, nullptr, c->logits,
+  LCRB_TRY(norm_launch(c, v, n, false, c->final_norm));
+  LCRB_TRY(gemm_node(c, v, c->wmaps.back(), m->xn, nb, n, d.vocab_size, H, EPI_STORE_F32, nullptr, c->logits,
                      d.vocab_size));
   SampleArgs s = {};
   s.logits = c->logits;
@@ -302,6 +327,28 @@ int enqueue_step(lcr_batch* c, int n) {
   s.out = c->next;
   ++c->launches;
   return sample_launch(s, n, c->stream, true);
+}
+
+// Uploads changed page tables and sampling parameters (on the stream).
+int upload_slot_state(lcr_batch* c) {
+  const size_t B = static_cast<size_t>(c->o.max_batch);
+  if (c->tables_dirty) {
+    LCRB_CUDA(cudaMemcpyAsync(c->tables, c->tables_host.data(), sizeof(int32_t) * B * c->max_pages,
+                              cudaMemcpyHostToDevice, c->stream));
+    c->tables_dirty = false;
+  }
+  if (c->sampling_dirty) {
+    LCRB_CUDA(cudaMemcpyAsync(c->inv_temp, c->inv_temp_host.data(), sizeof(float) * B, cudaMemcpyHostToDevice,
+                              c->stream));
+    LCRB_CUDA(cudaMemcpyAsync(c->top_k, c->top_k_host.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice,
+                              c->stream));
+    LCRB_CUDA(cudaMemcpyAsync(c->top_p, c->top_p_host.data(), sizeof(float) * B, cudaMemcpyHostToDevice,
+                              c->stream));
+    LCRB_CUDA(cudaMemcpyAsync(c->seed, c->seed_host.data(), sizeof(unsigned long long) * B,
+                              cudaMemcpyHostToDevice, c->stream));
+    c->sampling_dirty = false;
+  }
+  return LCR_OK;
 }
 
 int launch_step(lcr_batch* c, int n) {
@@ -567,22 +614,7 @@ extern "C" int lcr_batch_step(lcr_batch* c, int n, const int32_t* tokens, const 
   }
   LCRB_CUDA(cudaSetDevice(c->device));
   const size_t B = static_cast<size_t>(c->o.max_batch);
-  if (c->tables_dirty) {
-    LCRB_CUDA(cudaMemcpyAsync(c->tables, c->tables_host.data(), sizeof(int32_t) * B * c->max_pages,
-                              cudaMemcpyHostToDevice, c->stream));
-    c->tables_dirty = false;
-  }
-  if (c->sampling_dirty) {
-    LCRB_CUDA(cudaMemcpyAsync(c->inv_temp, c->inv_temp_host.data(), sizeof(float) * B, cudaMemcpyHostToDevice,
-                              c->stream));
-    LCRB_CUDA(cudaMemcpyAsync(c->top_k, c->top_k_host.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice,
-                              c->stream));
-    LCRB_CUDA(cudaMemcpyAsync(c->top_p, c->top_p_host.data(), sizeof(float) * B, cudaMemcpyHostToDevice,
-                              c->stream));
-    LCRB_CUDA(cudaMemcpyAsync(c->seed, c->seed_host.data(), sizeof(unsigned long long) * B,
-                              cudaMemcpyHostToDevice, c->stream));
-    c->sampling_dirty = false;
-  }
+  LCRB_TRY(upload_slot_state(c));
   // (token, position) staging: a pinned area is reused only after the copy
   // that last read it has completed.
   const int slot = c->staging_next;
@@ -627,6 +659,141 @@ extern "C" int lcr_batch_fill_kv(lcr_batch* c, int slot, int length, uint64_t se
   a.seed = seed;
   fill_kv_kernel<<<4 * c->sms, 256, 0, c->stream>>>(a);
   return launch_status("fill_kv");
+}
+
+namespace {
+
+// Grows the prefill activations to at least `rows` rows (a multiple of 128).
+int prefill_reserve(lcr_batch* c, int rows) {
+  if (rows <= c->pre_rows) return LCR_OK;
+  const lcr_model_desc& d = c->d;
+  const size_t R = static_cast<size_t>((rows + 127) / 128 * 128);
+  const int qd = d.num_heads * d.head_dim, kvd = d.num_kv_heads * d.head_dim;
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t at = off;
+    off = (off + bytes + 255) / 256 * 256;
+    return at;
+  };
+  const size_t o_tok = carve(sizeof(int32_t) * R), o_pos = carve(sizeof(int32_t) * R);
+  const size_t o_x = carve(sizeof(bf16) * R * d.hidden_size), o_xsum = carve(sizeof(float) * R * d.hidden_size);
+  const size_t o_xn = carve(sizeof(bf16) * R * d.hidden_size), o_qkv = carve(sizeof(bf16) * R * (qd + 2 * kvd));
+  const size_t o_attn = carve(sizeof(bf16) * R * qd), o_act = carve(sizeof(bf16) * R * d.intermediate_size);
+  const size_t o_rope = carve(sizeof(float2) * R * (d.head_dim / 2));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));  // the old buffers may still be in use
+  cudaFree(c->pre_buf);
+  c->pre_buf = nullptr;
+  c->pre_rows = 0;
+  LCRB_CUDA(cudaMalloc(&c->pre_buf, off));
+  char* b = c->pre_buf;
+  c->pre = Acts{reinterpret_cast<int32_t*>(b + o_tok), reinterpret_cast<int32_t*>(b + o_pos),
+                reinterpret_cast<bf16*>(b + o_x),       reinterpret_cast<float*>(b + o_xsum),
+                reinterpret_cast<bf16*>(b + o_xn),      reinterpret_cast<bf16*>(b + o_qkv),
+                reinterpret_cast<bf16*>(b + o_attn),    reinterpret_cast<bf16*>(b + o_act),
+                reinterpret_cast<float2*>(b + o_rope)};
+  c->pre_rows = static_cast<int>(R);
+  return LCR_OK;
+}
+
+}  // namespace
+
+extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, int count, int start) {
+  LCRB_REQUIRE(c && tokens, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d outside 0..%d", slot,
+               c->o.max_batch - 1);
+  LCRB_REQUIRE(count >= 1 && start >= 0 && start + count <= c->o.max_seq, LCR_ERR_STATE,
+               "prefill of %d positions at %d outside the cache built for %d", count, start, c->o.max_seq);
+  const lcr_model_desc& d = c->d;
+  for (int i = 0; i < count; ++i) {
+    LCRB_REQUIRE(tokens[i] >= 0 && tokens[i] < d.vocab_size, LCR_ERR_INVALID, "token %d: id %d outside the vocabulary",
+                 i, tokens[i]);
+  }
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(upload_slot_state(c));
+  LCRB_TRY(prefill_reserve(c, count));
+  const Acts& v = c->pre;
+  const int H = d.hidden_size, F = d.intermediate_size;
+  const int qd = d.num_heads * d.head_dim, kvd = d.num_kv_heads * d.head_dim;
+  // Inputs of the chunk (pageable sources are staged by the copy itself).
+  std::vector<int32_t> pos(static_cast<size_t>(count));
+  for (int i = 0; i < count; ++i) pos[static_cast<size_t>(i)] = start + i;
+  LCRB_CUDA(cudaMemcpyAsync(v.tokens, tokens, sizeof(int32_t) * count, cudaMemcpyHostToDevice, c->stream));
+  LCRB_CUDA(cudaMemcpyAsync(v.positions, pos.data(), sizeof(int32_t) * count, cudaMemcpyHostToDevice, c->stream));
+  // Activation tensor maps for this chunk's batch tile.
+  const int nb = gemm_tc_batch_tile(count);
+  StepMaps m;
+  LCRB_TRY(make_kmajor_map(&m.xn, v.xn, c->pre_rows, H, 1, nb, c->tc_chunks));
+  LCRB_TRY(make_kmajor_map(&m.attn, v.attn, c->pre_rows, qd, 1, nb, c->tc_chunks));
+  LCRB_TRY(make_kmajor_map(&m.act, v.act, c->pre_rows, F, 1, nb, c->tc_chunks));
+  const int32_t* table = c->tables + static_cast<size_t>(slot) * c->max_pages;
+  const int group = d.num_heads / d.num_kv_heads;
+  const int pad_rows = (start + count + 15) / 16 * 16 - start;
+  for (int l = 0; l < d.num_layers; ++l) {
+    const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+    const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
+    LCRB_TRY(norm_launch(c, v, count, l == 0, w.input_norm));
+    LCRB_TRY(gemm_node(c, v, wm[0], m.xn, nb, count, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd));
+    KvWriteArgs kw = {};
+    kw.qkv = v.qkv;
+    kw.qkv_stride = qd + 2 * kvd;
+    kw.q_dim = qd;
+    kw.kv_dim = kvd;
+    kw.head_dim = d.head_dim;
+    kw.kv_heads = d.num_kv_heads;
+    kw.kpool = c->kpool + static_cast<size_t>(l) * c->layer_elems;
+    kw.vpool = c->vpool + static_cast<size_t>(l) * c->layer_elems;
+    kw.table = table;
+    kw.page_size = c->o.page_size;
+    kw.pool_pages = c->o.pool_pages;
+    kw.page_stride = static_cast<long long>(d.num_kv_heads) * c->o.page_size * d.head_dim;
+    kw.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
+    kw.start = start;
+    kw.count = count;
+    kw.status = c->status;
+    LCRB_TRY(launch_kernel(kv_write_kernel, dim3(static_cast<unsigned>(pad_rows)), dim3(128), 0, c->stream, true, kw));
+    PrefillAttnArgs pa = {};
+    pa.qkv = v.qkv;
+    pa.qkv_stride = qd + 2 * kvd;
+    pa.q_dim = qd;
+    pa.kv_dim = kvd;
+    pa.table = table;
+    pa.page_size = c->o.page_size;
+    pa.pool_pages = c->o.pool_pages;
+    pa.start = start;
+    pa.count = count;
+    pa.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
+    pa.out = v.attn;
+    pa.status = c->status;
+    LCRB_TRY(attn_prefill_launch(pa, c->kvmaps[static_cast<size_t>(2 * l)], c->kvmaps[static_cast<size_t>(2 * l + 1)],
+                                 d.head_dim, group, d.num_kv_heads, c->stream));
+    LCRB_TRY(gemm_node(c, v, wm[1], m.attn, nb, count, H, qd, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(norm_launch(c, v, count, false, w.post_attention_norm));
+    LCRB_TRY(gemm_node(c, v, wm[2], m.xn, nb, count, F, H, EPI_SWIGLU, v.act, nullptr, F));
+    LCRB_TRY(gemm_node(c, v, wm[3], m.act, nb, count, H, F, EPI_RESID, nullptr, nullptr, H));
+  }
+  // The last row only: final norm, lm_head into this slot's logits, sample
+  // with this slot's parameters and Philox counter = the last position.
+  Acts last = v;
+  last.x += static_cast<size_t>(count - 1) * H;
+  last.xsum += static_cast<size_t>(count - 1) * H;
+  LCRB_TRY(norm_launch(c, last, 1, false, c->final_norm));
+  CUtensorMap xlast;
+  LCRB_TRY(make_kmajor_map(&xlast, v.xn, c->pre_rows, H, 1, 16, c->tc_chunks));
+  float* logits = c->logits + static_cast<size_t>(slot) * d.vocab_size;
+  LCRB_TRY(gemm_node(c, last, c->wmaps.back(), xlast, 16, 1, d.vocab_size, H, EPI_STORE_F32, nullptr, logits,
+                     d.vocab_size));
+  SampleArgs s = {};
+  s.logits = logits;
+  s.row_stride = d.vocab_size;
+  s.vocab = d.vocab_size;
+  s.inv_temperature = c->inv_temp + slot;
+  s.top_k = c->top_k + slot;
+  s.top_p = c->top_p + slot;
+  s.uniform = nullptr;
+  s.seed = c->seed + slot;
+  s.counter = v.positions + (count - 1);
+  s.out = c->next + slot;
+  return sample_launch(s, 1, c->stream, true);
 }
 
 extern "C" int lcr_batch_read(lcr_batch* c, int32_t* next_ids, int n) {

@@ -133,6 +133,7 @@ _SIGS = {
     "lcr_batch_step": (_I, [_V, _I, _V, _V]),
     "lcr_batch_read": (_I, [_V, _V, _I]),
     "lcr_batch_fill_kv": (_I, [_V, _I, _I, ctypes.c_uint64]),
+    "lcr_batch_prefill": (_I, [_V, _I, _V, _I, _I]),
     "lcr_batch_logits": (_I, [_V, _I, _V]),
     "lcr_batch_sync": (_I, [_V]),
     "lcr_batch_stream": (_V, [_V]),
@@ -403,6 +404,13 @@ class Batch:
 
     def fill_kv(self, slot: int, length: int, seed: int) -> None:
         check(lib().lcr_batch_fill_kv(self.h, int(slot), int(length), int(seed)))
+
+    def prefill(self, slot: int, tokens, start: int = 0) -> None:
+        """Prefill `tokens` for `slot` at positions start .. (tcgen05 GEMMs
+        and causal flash attention); the slot's logits / next id then hold
+        the last row's."""
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        check(lib().lcr_batch_prefill(self.h, int(slot), ids.ctypes.data, int(ids.size), int(start)))
 
     def read(self, n: int) -> np.ndarray:
         out = np.zeros(n, dtype=np.int32)

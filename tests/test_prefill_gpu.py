@@ -1,0 +1,125 @@
+"""Chunked prefill (lcr_batch_prefill: tcgen05 projections over the chunk's
+rows, causal flash attention over the slot's pages) through the C ABI
+against the oracle, which evaluates the same prompt one position at a time
+(Model::prefill's maths): the last row's logits after each chunk, then
+decode steps that read the K/V the prefill wrote. Tolerances are the
+north-star ones used for the batched path: max-abs 3e-2 and cosine 0.999
+against fp32, 2e-2 against the bf16-rounding oracle."""
+import numpy as np
+import pytest
+
+import oracle
+from lcr_b200 import checkpoint as ck
+from lcr_b200 import runtime as rt
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+MAX_ABS = 3e-2
+MIN_COS = 0.999
+PAGE = 16
+
+# tiny (head_dim 64, 2 query heads per KV head) and a wide-head geometry
+# (head_dim 128, 8 query heads per KV head) that the 1B model does not cover
+WIDE = ck.small_geometry(layers=2, hidden=256, heads=8, kv_heads=1, head_dim=128, ffn=1024, vocab=4096,
+                         name="wide")
+
+
+def cos(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+@pytest.fixture(scope="module", params=["tiny", "wide"])
+def model(request):
+    geom = ck.TINY if request.param == "tiny" else WIDE
+    block = ck.cached(geom, 0) if request.param == "tiny" else ck.generate(geom, 5)
+    return request.param, block, rt.upload_block(block)
+
+
+def _check(got, l32, l16, what):
+    abs32 = float(np.abs(got - l32).max())
+    abs16 = float(np.abs(got - l16).max())
+    c = cos(got, l32)
+    assert abs32 <= MAX_ABS and c >= MIN_COS and abs16 <= 2e-2, (what, abs32, c, abs16)
+
+
+@pytest.mark.parametrize("chunks", [(24, 16), (150,), (7, 33, 1)])
+def test_prefill_chunks_then_decode_match_oracle(model, chunks):
+    name, block, wdev = model
+    total = sum(chunks)
+    max_seq = 224
+    per = max_seq // PAGE
+    pool = 3 * per
+    bt = rt.Batch(block, wdev, max_batch=4, max_seq=max_seq, page_size=PAGE, pool_pages=pool)
+    slot = 2
+    bt.set_pages(slot, oracle.page_permutation(pool, 17)[:per])
+    bt.set_sampling(slot, 0.0)
+    vocab = block.geom.vocab_size
+    prompt = np.asarray(ck.prompt_ids(300 + total, total + 8), dtype=np.int64) % vocab
+    r16 = oracle.Model(block, max_seq)
+    r32 = oracle.Model(block, max_seq)
+    start = 0
+    for n in chunks:
+        bt.prefill(slot, prompt[start:start + n], start)
+        for p in range(start, start + n):
+            l16 = r16.decode(int(prompt[p]), p, oracle.MODE_BF16)
+            l32 = r32.decode(int(prompt[p]), p, oracle.MODE_FP32)
+        got = bt.logits(slot)
+        _check(got, l32, l16, f"{name} chunk ending at {start + n}")
+        ids = bt.read(4)
+        assert int(ids[slot]) == int(np.argmax(got))
+        start += n
+    # Decode on from the prefilled cache: a one-slot step is row 0 and reads
+    # slot 0's page table, so slot 0 gets the prefilled pages.
+    bt.set_pages(0, oracle.page_permutation(pool, 17)[:per])
+    bt.set_sampling(0, 0.0)
+    for p in range(total, total + 4):
+        bt.step([int(prompt[p])], [p])
+        l16 = r16.decode(int(prompt[p]), p, oracle.MODE_BF16)
+        l32 = r32.decode(int(prompt[p]), p, oracle.MODE_FP32)
+        _check(bt.logits(0), l32, l16, f"{name} decode at {p}")
+    bt.close()
+
+
+def test_batched_decode_wide_heads_match_oracle(model):
+    """The batched decode step (tensor-pipe attention, persistent work items)
+    on both geometries: staggered slots, shuffled pages, per-sequence parity."""
+    name, block, wdev = model
+    slots, max_seq, steps = 6, 96, 40
+    per = max_seq // PAGE
+    pool = slots * per + 3
+    bt = rt.Batch(block, wdev, max_batch=slots, max_seq=max_seq, page_size=PAGE, pool_pages=pool)
+    order = oracle.page_permutation(pool, 23)
+    vocab = block.geom.vocab_size
+    seqs = []
+    for s in range(slots):
+        bt.set_pages(s, order[s * per:(s + 1) * per])
+        bt.set_sampling(s, 0.0)
+        seqs.append(np.asarray(ck.prompt_ids(500 + s, max_seq), dtype=np.int64) % vocab)
+    for t in range(steps):
+        n = min(slots, t + 1)
+        bt.step([int(seqs[s][t - s]) for s in range(n)], [t - s for s in range(n)])
+    for s in range(slots):
+        r16 = oracle.Model(block, max_seq)
+        r32 = oracle.Model(block, max_seq)
+        for p in range(steps - s):
+            l16 = r16.decode(int(seqs[s][p]), p, oracle.MODE_BF16)
+            l32 = r32.decode(int(seqs[s][p]), p, oracle.MODE_FP32)
+        _check(bt.logits(s), l32, l16, f"{name} slot {s}")
+    bt.close()
+
+
+def test_prefill_rejects_bad_inputs(model):
+    name, block, wdev = model
+    bt = rt.Batch(block, wdev, max_batch=2, max_seq=32, page_size=PAGE, pool_pages=4)
+    with pytest.raises(rt.LcrError):
+        bt.prefill(0, [1, 2, 3], 30)  # positions 30..32 outside max_seq 32
+    with pytest.raises(rt.LcrError):
+        bt.prefill(2, [1], 0)  # slot 2 of 2
+    with pytest.raises(rt.LcrError):
+        bt.prefill(0, [block.geom.vocab_size], 0)  # token outside the vocabulary
+    bt.close()
