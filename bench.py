@@ -217,9 +217,10 @@ def batched_bench(block, weights_dev, local, world, steps, warmup):
     (seed 3), Poisson(4) arrivals per step replacing finished sequences, 128
     tokens each, temperature 0.8 / top-k 50 / top-p 0.9 with per-sequence
     Philox seeds, paged KV (16-position pages, shuffled pool). Admitted
-    contexts get synthetic KV (lcr_batch_fill_kv; prefill is not built);
-    admissions happen between steps, and the timed unit is the decode step:
-    CUDA events on the batch stream around each step."""
+    contexts get synthetic KV (lcr_batch_fill_kv, untimed: config 4 measures
+    decode; the prefill chunk is measured by prefill_bench); admissions
+    happen between steps, and the timed unit is the decode step: CUDA events
+    on the batch stream around each step."""
     import torch
 
     from lcr_b200 import checkpoint as ck
@@ -283,10 +284,73 @@ def batched_bench(block, weights_dev, local, world, steps, warmup):
         "frac_of_peak": round(bytes_step / (per_step_ms / 1000) / 1e9 / peak, 4),
         "gpu_launches_per_step": bt.step_launches(BATCH),
         "finished_sequences": cb.finished,
-        "note": "admitted contexts get synthetic KV (prefill not built); decode steps timed",
+        "note": "admitted contexts get synthetic KV (seeded fill, untimed); decode steps timed",
     }
     bt.close()
     return out
+
+
+PREFILL_CHUNK = 2048
+
+
+def measured_bf16_tflops():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_bench(block, weights_dev, local, reps=5):
+    """Config 5's prefill chunk on one GPU: 2048 prompt
+    tokens (seed 5) into an empty paged sequence (16-position pages, shuffled)
+    through lcr_batch_prefill -- tcgen05 projections over the 2048 rows,
+    causal flash attention, the last row's lm_head and sample. FLOPs per
+    chunk: 2 x (non-embedding weights) x 2048 for the projections plus
+    4 x heads x head_dim x 2048 x 2049 / 2 per layer for causal QK^T and PV,
+    plus the one-row lm_head. CUDA events on the batch stream around each
+    chunk, after two warm-up chunks; the chunk rewrites the same pages."""
+    import torch
+
+    from lcr_b200 import checkpoint as ck
+    from lcr_b200 import runtime as rt
+
+    g = ck.LLAMA_3_2_1B
+    P = PREFILL_CHUNK
+    pages = P // 16
+    bt = rt.Batch(block, weights_dev, device=local, max_batch=1, max_seq=P, page_size=16, pool_pages=pages)
+    bt.set_pages(0, np.random.default_rng(5).permutation(pages).astype(np.int32))
+    bt.set_sampling(0, 0.0)
+    ids = ck.prompt_ids(5, P)
+    for _ in range(2):
+        bt.prefill(0, ids, 0)
+    bt.sync()
+    stream = torch.cuda.ExternalStream(bt.stream, device=f"cuda:{local}")
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        bt.prefill(0, ids, 0)
+        e1.record(stream)
+        times.append((e0, e1))
+    bt.sync()
+    torch.cuda.synchronize()
+    ms = sorted(a.elapsed_time(b) for a, b in times)[len(times) // 2]
+    h, f, q, kv = g.hidden_size, g.intermediate_size, g.q_dim, g.kv_dim
+    layer_params = (q + 2 * kv) * h + h * q + 2 * f * h + f * h
+    proj = 2.0 * layer_params * g.num_layers * P
+    attn = 4.0 * g.num_heads * g.head_dim * P * (P + 1) / 2 * g.num_layers
+    head = 2.0 * g.vocab_size * h
+    flops = proj + attn + head
+    peak, kind = measured_bf16_tflops()
+    tflops = flops / (ms / 1000) / 1e12
+    bt.close()
+    return {"workload": f"config5 prefill chunk: {P} prompt tokens (seed 5), Llama-3.2-1B, empty paged "
+                        "sequence (16-position pages, shuffled)",
+            "ms_per_chunk": round(ms, 3), "tok_per_s": round(P / (ms / 1000), 1),
+            "flops_per_chunk": flops, "tflops": round(tflops, 1),
+            "peak_tflops": peak, "peak_source": kind, "frac_of_peak": round(tflops / peak, 4),
+            "reps": reps, "statistic": "median"}
 
 
 def main():
@@ -391,10 +455,11 @@ def main():
         ms = m.time_gemv(i, 0, 20)
         per_matrix[name] = {"us": round(ms * 1000, 2),
                             "gbs": round(bytes_of[name] / (ms / 1000) / 1e9, 1)}
-    batched = None
+    batched = prefill = None
     if not args.no_batched:
         batched = batched_bench(block, m.weights_dev, local, world, args.batched_steps,
                                 max(3, args.warmup // 4))
+        prefill = prefill_bench(block, m.weights_dev, local)
 
     ms_per_step = max_ms / args.steps
     # positions 127..382 read 128..383 cached positions: mean 255.5
@@ -432,6 +497,7 @@ def main():
             "clocks": clocks,
             "cpu_baseline": base,
             "batched": batched,
+            "prefill": prefill,
         }
         print(json.dumps(line))
     m.close()

@@ -84,6 +84,7 @@ struct lcr_batch {
   const bf16* lm_head = nullptr;
   std::vector<lcr_layer_weights> layers;
   std::vector<CUtensorMap> wmaps;  // [layer * 4 + m]: qkv, o, gate/up, down; then lm_head
+  std::vector<CUtensorMap> wmaps1; // the same with one 64-column chunk per copy (prefill chunks)
   std::map<int, StepMaps> xmaps;   // by batch tile
   std::vector<CUtensorMap> kvmaps; // [layer * 2 + {0: K, 1: V}] pool rows of head_dim
 
@@ -212,7 +213,7 @@ int norm_launch(lcr_batch* c, const Acts& v, int n, bool embed, const void* gain
 // One projection: n rows of `x` (tensor map `xm`, batch tile nb) against
 // weight map `wm` ([n_out][K], or gate/up halves for SWIGLU).
 int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensorMap& xm, int nb, int n, int n_out,
-              int K, int epi, bf16* y, float* yf, int ldy) {
+              int K, int epi, bf16* y, float* yf, int ldy, int ch) {
   TcArgs a = {};
   a.n_out = n_out;
   a.K = K;
@@ -228,7 +229,7 @@ int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensor
   a.rope_cols = (c->d.num_heads + c->d.num_kv_heads) * c->d.head_dim;
   const int tiles_n = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + kTcTileM - 1) / kTcTileM;
   const int tiles = tiles_n * ((n + nb - 1) / nb);
-  const int steps = K / (kTcSlabK * c->tc_chunks);
+  const int steps = K / (kTcSlabK * ch);
   // As many splits as fit the SMs in one wave (one CTA per SM), within the
   // K stages and the workspace.
   int splits = std::max(1, c->sms / tiles);
@@ -237,7 +238,7 @@ int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensor
   a.splits = splits;
   a.work = c->work;
   c->launches += splits > 1 ? 2 : 1;
-  return gemm_tc_launch(a, wm, xm, nb, epi, c->tc_chunks, c->stream, true);
+  return gemm_tc_launch(a, wm, xm, nb, epi, ch, c->stream, true);
 }
 
 int attention_launch_layer(lcr_batch* c, int layer, int n) {
@@ -304,16 +305,17 @@ int enqueue_step(lcr_batch* c, int n) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
     const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
     LCRB_TRY(norm_launch(c, v, n, l == 0, w.input_norm));
-    LCRB_TRY(gemm_node(c, v, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd));
+    const int ch = c->tc_chunks;
+    LCRB_TRY(gemm_node(c, v, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd, ch));
     LCRB_TRY(attention_launch_layer(c, l, n));
-    LCRB_TRY(gemm_node(c, v, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(gemm_node(c, v, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H, ch));
     LCRB_TRY(norm_launch(c, v, n, false, w.post_attention_norm));
-    LCRB_TRY(gemm_node(c, v, wm[2], m->xn, nb, n, F, H, EPI_SWIGLU, v.act, nullptr, F));
-    LCRB_TRY(gemm_node(c, v, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(gemm_node(c, v, wm[2], m->xn, nb, n, F, H, EPI_SWIGLU, v.act, nullptr, F, ch));
+    LCRB_TRY(gemm_node(c, v, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H, ch));
   }
   LCRB_TRY(norm_launch(c, v, n, false, c->final_norm));
   LCRB_TRY(gemm_node(c, v, c->wmaps.back(), m->xn, nb, n, d.vocab_size, H, EPI_STORE_F32, nullptr, c->logits,
-                     d.vocab_size));
+                     d.vocab_size, c->tc_chunks));
   SampleArgs s = {};
   s.logits = c->logits;
   s.row_stride = d.vocab_size;
@@ -451,6 +453,15 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   }
   if (st == LCR_OK) {
     st = make_kmajor_map(&c->wmaps.back(), c->lm_head, d.vocab_size, d.hidden_size, 1, kTcTileM, c->tc_chunks);
+  }
+  c->wmaps1.resize(static_cast<size_t>(4 * d.num_layers));
+  for (int l = 0; l < d.num_layers && st == LCR_OK; ++l) {
+    const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
+    CUtensorMap* m = &c->wmaps1[static_cast<size_t>(4 * l)];
+    st = make_kmajor_map(m, w.qkv_proj, qd + 2 * kvd, d.hidden_size, 1, kTcTileM, 1);
+    if (st == LCR_OK) st = make_kmajor_map(m + 1, w.o_proj, d.hidden_size, qd, 1, kTcTileM, 1);
+    if (st == LCR_OK) st = make_kmajor_map(m + 2, w.gate_up_proj, d.intermediate_size, d.hidden_size, 2, 64, 1);
+    if (st == LCR_OK) st = make_kmajor_map(m + 3, w.down_proj, d.hidden_size, d.intermediate_size, 1, kTcTileM, 1);
   }
 
   // Attention work items: 512 positions, or more for very long caches so
@@ -720,19 +731,20 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
   LCRB_CUDA(cudaMemcpyAsync(v.tokens, tokens, sizeof(int32_t) * count, cudaMemcpyHostToDevice, c->stream));
   LCRB_CUDA(cudaMemcpyAsync(v.positions, pos.data(), sizeof(int32_t) * count, cudaMemcpyHostToDevice, c->stream));
   // Activation tensor maps for this chunk's batch tile.
+  // One chunk per stage: 128-row tiles then run two CTAs per SM.
   const int nb = gemm_tc_batch_tile(count);
   StepMaps m;
-  LCRB_TRY(make_kmajor_map(&m.xn, v.xn, c->pre_rows, H, 1, nb, c->tc_chunks));
-  LCRB_TRY(make_kmajor_map(&m.attn, v.attn, c->pre_rows, qd, 1, nb, c->tc_chunks));
-  LCRB_TRY(make_kmajor_map(&m.act, v.act, c->pre_rows, F, 1, nb, c->tc_chunks));
+  LCRB_TRY(make_kmajor_map(&m.xn, v.xn, c->pre_rows, H, 1, nb, 1));
+  LCRB_TRY(make_kmajor_map(&m.attn, v.attn, c->pre_rows, qd, 1, nb, 1));
+  LCRB_TRY(make_kmajor_map(&m.act, v.act, c->pre_rows, F, 1, nb, 1));
   const int32_t* table = c->tables + static_cast<size_t>(slot) * c->max_pages;
   const int group = d.num_heads / d.num_kv_heads;
   const int pad_rows = (start + count + 15) / 16 * 16 - start;
   for (int l = 0; l < d.num_layers; ++l) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
-    const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
+    const CUtensorMap* wm = &c->wmaps1[static_cast<size_t>(4 * l)];
     LCRB_TRY(norm_launch(c, v, count, l == 0, w.input_norm));
-    LCRB_TRY(gemm_node(c, v, wm[0], m.xn, nb, count, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd));
+    LCRB_TRY(gemm_node(c, v, wm[0], m.xn, nb, count, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd, 1));
     KvWriteArgs kw = {};
     kw.qkv = v.qkv;
     kw.qkv_stride = qd + 2 * kvd;
@@ -766,10 +778,10 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     pa.status = c->status;
     LCRB_TRY(attn_prefill_launch(pa, c->kvmaps[static_cast<size_t>(2 * l)], c->kvmaps[static_cast<size_t>(2 * l + 1)],
                                  d.head_dim, group, d.num_kv_heads, c->stream));
-    LCRB_TRY(gemm_node(c, v, wm[1], m.attn, nb, count, H, qd, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(gemm_node(c, v, wm[1], m.attn, nb, count, H, qd, EPI_RESID, nullptr, nullptr, H, 1));
     LCRB_TRY(norm_launch(c, v, count, false, w.post_attention_norm));
-    LCRB_TRY(gemm_node(c, v, wm[2], m.xn, nb, count, F, H, EPI_SWIGLU, v.act, nullptr, F));
-    LCRB_TRY(gemm_node(c, v, wm[3], m.act, nb, count, H, F, EPI_RESID, nullptr, nullptr, H));
+    LCRB_TRY(gemm_node(c, v, wm[2], m.xn, nb, count, F, H, EPI_SWIGLU, v.act, nullptr, F, 1));
+    LCRB_TRY(gemm_node(c, v, wm[3], m.act, nb, count, H, F, EPI_RESID, nullptr, nullptr, H, 1));
   }
   // The last row only: final norm, lm_head into this slot's logits, sample
   // with this slot's parameters and Philox counter = the last position.
@@ -781,7 +793,7 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
   LCRB_TRY(make_kmajor_map(&xlast, v.xn, c->pre_rows, H, 1, 16, c->tc_chunks));
   float* logits = c->logits + static_cast<size_t>(slot) * d.vocab_size;
   LCRB_TRY(gemm_node(c, last, c->wmaps.back(), xlast, 16, 1, d.vocab_size, H, EPI_STORE_F32, nullptr, logits,
-                     d.vocab_size));
+                     d.vocab_size, c->tc_chunks));
   SampleArgs s = {};
   s.logits = logits;
   s.row_stride = d.vocab_size;

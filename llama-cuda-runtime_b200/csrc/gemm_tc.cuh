@@ -35,6 +35,10 @@ constexpr int kTcTileM = 128;        // weight rows per tile
 constexpr int kTcSlabK = 64;         // K columns per chunk (128-byte swizzle span)
 constexpr int kTcThreads = 192;      // 6 warps
 constexpr int kTcRingBytes = 196608; // ring budget (stage count derived from it)
+// 128-row batch tiles with one chunk per stage (prefill chunks) take half of
+// it, so that two CTAs share an SM and one's epilogue overlaps the other's
+// main loop.
+constexpr int kTcRingBytesPaired = 98304;
 
 template <int NB, int CH>
 struct TcGeom {
@@ -44,7 +48,8 @@ struct TcGeom {
   static constexpr int W_BYTES = CH * W_CHUNK;
   static constexpr int X_BYTES = CH * X_CHUNK;
   static constexpr int STAGE = W_BYTES + X_BYTES;  // a multiple of 1024
-  static constexpr int STAGES = (kTcRingBytes / STAGE) < 8 ? (kTcRingBytes / STAGE) : 8;
+  static constexpr int RING = (NB == 128 && CH == 1) ? kTcRingBytesPaired : kTcRingBytes;
+  static constexpr int STAGES = (RING / STAGE) < 8 ? (RING / STAGE) : 8;
   static constexpr int TMEM_COLS = NB < 32 ? 32 : NB;  // power of two >= 32
   static_assert(STAGE % 1024 == 0 && STAGES >= 2, "stage geometry");
 };
