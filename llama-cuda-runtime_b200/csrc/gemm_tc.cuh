@@ -228,8 +228,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles_n = SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
-  const int tile = blockIdx.x % tiles_n;
-  const int tile_b = blockIdx.x / tiles_n;
+  // Batch tiles vary fastest: the CTAs of one weight tile run side by side,
+  // so each weight tile leaves DRAM once however many batch tiles there are.
+  const int tiles_b = (a.rows + NB - 1) / NB;
+  const int tile = blockIdx.x / tiles_b;
+  const int tile_b = blockIdx.x % tiles_b;
   const int split = blockIdx.y;
   const int slabs = a.K / (kTcSlabK * CH);  // ring stages over K
   const int s0 = static_cast<int>(static_cast<long long>(split) * slabs / a.splits);
