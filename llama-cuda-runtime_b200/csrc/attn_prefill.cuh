@@ -42,17 +42,24 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Three ring stages (two for head_dim 128): the warps spend longer per stage
+// than the decode kernel's, and a smaller ring lets four CTAs share an SM.
+template <int D>
+constexpr int attn_prefill_stages() {
+  return D == 64 ? 3 : 2;
+}
+
 template <int D>
 constexpr size_t attn_prefill_smem_bytes() {
-  return 1024 + static_cast<size_t>(AbGeom<D>::RING) + 2 * AbGeom<D>::STAGES * 8;
+  return 1024 + static_cast<size_t>(attn_prefill_stages<D>()) * AbGeom<D>::STAGE + 2 * attn_prefill_stages<D>() * 8;
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const PrefillAttnArgs a,
+__global__ void __launch_bounds__(kAttnThreads, D == 64 ? 4 : 2) attn_prefill_kernel(const PrefillAttnArgs a,
                                                                     const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap) {
   using Geo = AbGeom<D>;
-  constexpr int STAGES = Geo::STAGES;
+  constexpr int STAGES = attn_prefill_stages<D>();
   constexpr int UNIT = Geo::UNIT;
   constexpr int KSTEPS = D / 16;
   constexpr int NT = D / 8;
@@ -60,7 +67,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const Prefil
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = align_smem<uint8_t>(smem_raw, 1024);
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + Geo::RING);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + STAGES * Geo::STAGE);
   uint64_t* empty = full + STAGES;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -224,12 +231,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const Prefil
       l_b = l_b * alpha_b + sumb;
       m_a = na;
       m_b = nb;
+      // Most units leave every row's maximum where it was: skip the rescale
+      // then (warp-uniform test).
+      if (__any_sync(0xffffffffu, alpha_a != 1.0f || alpha_b != 1.0f)) {
 #pragma unroll
-      for (int nn = 0; nn < NT; ++nn) {
-        o[nn][0] *= alpha_a;
-        o[nn][1] *= alpha_a;
-        o[nn][2] *= alpha_b;
-        o[nn][3] *= alpha_b;
+        for (int nn = 0; nn < NT; ++nn) {
+          o[nn][0] *= alpha_a;
+          o[nn][1] *= alpha_a;
+          o[nn][2] *= alpha_b;
+          o[nn][3] *= alpha_b;
+        }
       }
       const uint32_t p0 = pack_bf2(pa[0][0], pa[0][1]), p1 = pack_bf2(pb[0][0], pb[0][1]);
       const uint32_t p2 = pack_bf2(pa[1][0], pa[1][1]), p3 = pack_bf2(pb[1][0], pb[1][1]);
