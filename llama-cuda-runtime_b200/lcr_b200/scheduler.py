@@ -12,6 +12,7 @@ from __future__ import annotations
 
 from collections import deque
 from dataclasses import dataclass, field
+from typing import Optional
 
 import numpy as np
 
@@ -47,6 +48,8 @@ class Sequence:
     seed: int             # Philox key of its sampling
     generated: int = 0
     pages: list = field(default_factory=list)
+    prompt: Optional[np.ndarray] = None  # context token ids, for a real prefill
+    tokens: list = field(default_factory=list)  # sampled ids, when recorded
 
     @property
     def position(self) -> int:  # position decoded by the next step
@@ -59,12 +62,16 @@ class Sequence:
 
 class ContinuousBatcher:
     """Keeps the slots of a runtime.Batch full: admits waiting sequences into
-    free slots (pages reserved, context written by lcr_batch_fill_kv as a
-    stand-in for prefill, sampling set), steps every slot with device token
-    feedback, and retires sequences that reached their target."""
+    free slots (pages reserved, sampling set, the context prefilled in chunks
+    of `prefill_chunk` tokens through lcr_batch_prefill when the sequence has
+    a prompt, else written by lcr_batch_fill_kv as a synthetic stand-in),
+    steps every slot with device token feedback, and retires sequences that
+    reached their target. With `record`, every sampled id is read back and
+    kept on its sequence (one host round trip per step)."""
 
     def __init__(self, batch, *, page_size: int, pool_pages: int, page_seed: int = 0,
-                 temperature: float = 0.8, top_k: int = 50, top_p: float = 0.9):
+                 temperature: float = 0.8, top_k: int = 50, top_p: float = 0.9,
+                 prefill_chunk: int = 2048, record: bool = False):
         self.batch = batch
         self.page_size = page_size
         self.pool = PagePool(pool_pages, page_seed)
@@ -73,6 +80,8 @@ class ContinuousBatcher:
         self.sampling = (temperature, top_k, top_p)
         self.finished = 0
         self.admitted = 0
+        self.prefill_chunk = prefill_chunk
+        self.record = record
 
     def submit(self, seq: Sequence) -> None:
         self.waiting.append(seq)
@@ -81,11 +90,20 @@ class ContinuousBatcher:
         need = (seq.context + seq.target + self.page_size - 1) // self.page_size
         seq.pages = self.pool.take(need)
         self.batch.set_pages(slot, seq.pages)
-        # Positions below seq.position hold its context (and any tokens it is
-        # assumed to have decoded already).
-        self.batch.fill_kv(slot, seq.position, seq.seed)
         t, k, p = self.sampling
         self.batch.set_sampling(slot, t, k, p, seq.seed)
+        if seq.prompt is not None:
+            # The prompt through the prefill path; its last row's sample is the
+            # slot's next token, which the first step feeds back.
+            assert len(seq.prompt) == seq.context and seq.generated == 0
+            for at in range(0, seq.context, self.prefill_chunk):
+                self.batch.prefill(slot, seq.prompt[at:at + self.prefill_chunk], at)
+            if self.record:
+                seq.tokens.append(int(self.batch.read(slot + 1)[slot]))
+        else:
+            # Positions below seq.position hold its context (and any tokens it
+            # is assumed to have decoded already).
+            self.batch.fill_kv(slot, seq.position, seq.seed)
         self.slots[slot] = seq
         self.admitted += 1
 
@@ -130,9 +148,12 @@ class ContinuousBatcher:
         if n == 0:
             return 0
         self.batch.step(tokens, [self.slots[b].position for b in range(n)])
+        ids = self.batch.read(n) if self.record else None
         for b in range(n):
             seq = self.slots[b]
             seq.generated += 1
+            if ids is not None:
+                seq.tokens.append(int(ids[b]))
             if seq.done:
                 self.pool.give(seq.pages)
                 self.slots[b] = None

@@ -123,3 +123,43 @@ def test_prefill_rejects_bad_inputs(model):
     with pytest.raises(rt.LcrError):
         bt.prefill(0, [block.geom.vocab_size], 0)  # token outside the vocabulary
     bt.close()
+
+
+def test_batcher_with_prefill_generates_oracle_greedy_ids(model):
+    """Continuous batching end to end: sequences admitted into 2 slots with
+    their prompts prefilled in 32-token chunks, greedy decoding with device
+    token feedback, retirement and slot compaction; every sequence's ids
+    (the prefill's sample, then one per step) are the oracle's greedy
+    continuation of its prompt -- up to a near tie, after which the two
+    continuations may legitimately part."""
+    from lcr_b200 import scheduler as sch
+    name, block, wdev = model
+    vocab = block.geom.vocab_size
+    lengths, target, max_seq = [40, 70, 25, 33], 5, 96
+    per = max_seq // PAGE
+    bt = rt.Batch(block, wdev, max_batch=2, max_seq=max_seq, page_size=PAGE, pool_pages=2 * per + 2)
+    cb = sch.ContinuousBatcher(bt, page_size=PAGE, pool_pages=2 * per + 2, page_seed=9, temperature=0.0,
+                               prefill_chunk=32, record=True)
+    seqs = []
+    for i, n in enumerate(lengths):
+        prompt = (np.asarray(ck.prompt_ids(700 + i, n), dtype=np.int64) % vocab).astype(np.int32)
+        seqs.append(sch.Sequence(sid=i, context=n, target=target, seed=i, prompt=prompt))
+        cb.submit(seqs[-1])
+    for _ in range(40):
+        cb.fill()
+        if cb.step() == 0 and not cb.waiting:
+            break
+    assert cb.finished == len(lengths)
+    for q in seqs:
+        assert len(q.tokens) == target + 1
+        r = oracle.Model(block, max_seq)
+        for p in range(q.context):
+            logits = r.decode(int(q.prompt[p]), p, oracle.MODE_BF16)
+        for k, got in enumerate(q.tokens):
+            want = int(np.argmax(logits))
+            if got != want:
+                top2 = np.sort(logits)[-2:]
+                assert top2[1] - top2[0] < 2e-2, (name, q.sid, k, got, want)
+                break
+            logits = r.decode(got, q.context + k, oracle.MODE_BF16)
+    bt.close()
