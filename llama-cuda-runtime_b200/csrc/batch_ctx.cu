@@ -212,8 +212,12 @@ int norm_launch(lcr_batch* c, const Acts& v, int n, bool embed, const void* gain
 
 // One projection: n rows of `x` (tensor map `xm`, batch tile nb) against
 // weight map `wm` ([n_out][K], or gate/up halves for SWIGLU).
+// With `norm_gain` (a RESID projection), the RMSNorm of the updated rows into
+// v.xn is fused into the split-K reduction when the projection splits;
+// *normed says whether it was, so the caller launches the norm otherwise.
 int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensorMap& xm, int nb, int n, int n_out,
-              int K, int epi, bf16* y, float* yf, int ldy, int ch) {
+              int K, int epi, bf16* y, float* yf, int ldy, int ch, const void* norm_gain = nullptr,
+              bool* normed = nullptr) {
   TcArgs a = {};
   a.n_out = n_out;
   a.K = K;
@@ -237,6 +241,13 @@ int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensor
   while (splits > 1 && gemm_tc_work_floats(n, n_out, epi, splits) > c->work_floats) --splits;
   a.splits = splits;
   a.work = c->work;
+  const bool fuse = norm_gain != nullptr && epi == EPI_RESID && splits > 1;
+  if (fuse) {
+    a.norm_gain = static_cast<const bf16*>(norm_gain);
+    a.norm_eps = c->d.rms_norm_eps;
+    a.norm_out = v.xn;
+  }
+  if (normed) *normed = fuse;
   c->launches += splits > 1 ? 2 : 1;
   return gemm_tc_launch(a, wm, xm, nb, epi, ch, c->stream, true);
 }
@@ -301,19 +312,22 @@ int enqueue_step(lcr_batch* c, int n) {
   LCRB_TRY(maps_for(c, nb, &m));
   c->launches = 0;
   const Acts v = step_acts(c);
+  bool normed = false;  // the previous down projection already wrote xn
   for (int l = 0; l < d.num_layers; ++l) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
     const CUtensorMap* wm = &c->wmaps[static_cast<size_t>(4 * l)];
-    LCRB_TRY(norm_launch(c, v, n, l == 0, w.input_norm));
+    if (!normed) LCRB_TRY(norm_launch(c, v, n, l == 0, w.input_norm));
     const int ch = c->tc_chunks;
     LCRB_TRY(gemm_node(c, v, wm[0], m->xn, nb, n, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd, ch));
     LCRB_TRY(attention_launch_layer(c, l, n));
-    LCRB_TRY(gemm_node(c, v, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H, ch));
-    LCRB_TRY(norm_launch(c, v, n, false, w.post_attention_norm));
+    LCRB_TRY(gemm_node(c, v, wm[1], m->attn, nb, n, H, qd, EPI_RESID, nullptr, nullptr, H, ch,
+                       w.post_attention_norm, &normed));
+    if (!normed) LCRB_TRY(norm_launch(c, v, n, false, w.post_attention_norm));
     LCRB_TRY(gemm_node(c, v, wm[2], m->xn, nb, n, F, H, EPI_SWIGLU, v.act, nullptr, F, ch));
-    LCRB_TRY(gemm_node(c, v, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H, ch));
+    const void* next_gain = l + 1 < d.num_layers ? c->layers[static_cast<size_t>(l + 1)].input_norm : c->final_norm;
+    LCRB_TRY(gemm_node(c, v, wm[3], m->act, nb, n, H, F, EPI_RESID, nullptr, nullptr, H, ch, next_gain, &normed));
   }
-  LCRB_TRY(norm_launch(c, v, n, false, c->final_norm));
+  if (!normed) LCRB_TRY(norm_launch(c, v, n, false, c->final_norm));
   LCRB_TRY(gemm_node(c, v, c->wmaps.back(), m->xn, nb, n, d.vocab_size, H, EPI_STORE_F32, nullptr, c->logits,
                      d.vocab_size, c->tc_chunks));
   SampleArgs s = {};

@@ -16,6 +16,16 @@ int launch_t(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, 
   dim3 grid(static_cast<unsigned>(tiles_n * tiles_b), static_cast<unsigned>(a.splits));
   LCRB_TRY(launch_kernel(kernel, grid, dim3(kTcThreads), smem, s, pdl, a, wmap, xmap));
   if (a.splits > 1) {
+    if constexpr (EPI == EPI_RESID) {
+      if (a.norm_out != nullptr) {
+        void (*fused)(TcArgs) = a.n_out == 2048   ? gemm_tc_reduce_norm_kernel<2048>
+                                : a.n_out == 256  ? gemm_tc_reduce_norm_kernel<256>
+                                : a.n_out == 4096 ? gemm_tc_reduce_norm_kernel<4096>
+                                                  : nullptr;
+        LCRB_REQUIRE(fused != nullptr, LCR_ERR_SHAPE, "fused residual RMSNorm has no kernel for width %d", a.n_out);
+        return launch_kernel(fused, dim3(static_cast<unsigned>(a.rows)), dim3(256), 0, s, pdl, a);
+      }
+    }
     const long long total = static_cast<long long>(a.rows) * a.n_out;
     const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 4096));
     LCRB_TRY(launch_kernel(gemm_tc_reduce_kernel<EPI>, dim3(blocks), dim3(256), 0, s, pdl, a));

@@ -71,6 +71,12 @@ struct TcArgs {
   const float2* rope;
   int head_dim;
   int rope_cols;
+  // RESID with splits > 1, optional: the RMSNorm of the updated residual rows
+  // into norm_out (bf16 [rows][n_out]) with gain norm_gain, fused into the
+  // reduction (gemm_tc_reduce_norm_kernel).
+  const bf16* norm_gain;
+  float norm_eps;
+  bf16* norm_out;
 };
 
 // UMMA shared-memory descriptor of a K-major, 128-byte swizzled tile whose
@@ -432,6 +438,83 @@ __global__ void __launch_bounds__(256) gemm_tc_reduce_kernel(const TcArgs a) {
       }
     }
     tc_store<EPI>(a, b, n, v, up);
+  }
+}
+
+// Split-K residual epilogue fused with the RMSNorm that follows it: one CTA
+// of 256 threads per batch row, thread t owning 8-column chunks t, t + 256,
+// .. as norm_rows_kernel does. Per chunk: the split sum in split order (as
+// gemm_tc_reduce_kernel), s = resid + bf16(sum), stored as bf16 and as the
+// unrounded fp32 sum; then the sum of squares of the fp32 sums over the same
+// tree as norm_rows_kernel, and out = bf16(bf16(s) * scale * gain) --
+// bit-identical to the two launches it replaces.
+template <int H>
+__global__ void __launch_bounds__(256) gemm_tc_reduce_norm_kernel(const TcArgs a) {
+  constexpr int CHUNKS = H / 8;
+  constexpr int PER = (CHUNKS + 255) / 256;
+  __shared__ float red[8];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  pdl_launch_next();
+  const size_t plane = static_cast<size_t>(a.rows) * H;  // m_total = H for RESID
+  const size_t row = static_cast<size_t>(b) * H;
+  float xs[PER][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int c = tid + p * 256;
+    if (c < CHUNKS) {
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int sp = 0; sp < a.splits; ++sp) {
+        const float* src = a.work + sp * plane + row + c * 8;
+        const float4 lo = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + 4));
+        v[0] = __fadd_rn(v[0], lo.x); v[1] = __fadd_rn(v[1], lo.y);
+        v[2] = __fadd_rn(v[2], lo.z); v[3] = __fadd_rn(v[3], lo.w);
+        v[4] = __fadd_rn(v[4], hi.x); v[5] = __fadd_rn(v[5], hi.y);
+        v[6] = __fadd_rn(v[6], hi.z); v[7] = __fadd_rn(v[7], hi.w);
+      }
+      float x[8];
+      unpack8(ldg_cg16(a.resid + row + c * 8), x);
+      float s8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s8[e] = __fadd_rn(x[e], rbf(v[e]));
+      uint4 w;
+      w.x = pack_bf2(s8[0], s8[1]);
+      w.y = pack_bf2(s8[2], s8[3]);
+      w.z = pack_bf2(s8[4], s8[5]);
+      w.w = pack_bf2(s8[6], s8[7]);
+      *reinterpret_cast<uint4*>(a.resid + row + c * 8) = w;
+      *reinterpret_cast<float4*>(a.resid_sum + row + c * 8) = make_float4(s8[0], s8[1], s8[2], s8[3]);
+      *reinterpret_cast<float4*>(a.resid_sum + row + c * 8 + 4) = make_float4(s8[4], s8[5], s8[6], s8[7]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ss = fmaf(s8[e], s8[e], ss);
+        xs[p][e] = rbf(s8[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) total += red[w];
+  const float scale = rsqrtf(total / static_cast<float>(H) + a.norm_eps);
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int c = tid + p * 256;
+    if (c < CHUNKS) {
+      float gf[8];
+      unpack8(ldg16(a.norm_gain + c * 8), gf);
+      uint4 o;
+      o.x = pack_bf2(__fmul_rn(__fmul_rn(xs[p][0], scale), gf[0]), __fmul_rn(__fmul_rn(xs[p][1], scale), gf[1]));
+      o.y = pack_bf2(__fmul_rn(__fmul_rn(xs[p][2], scale), gf[2]), __fmul_rn(__fmul_rn(xs[p][3], scale), gf[3]));
+      o.z = pack_bf2(__fmul_rn(__fmul_rn(xs[p][4], scale), gf[4]), __fmul_rn(__fmul_rn(xs[p][5], scale), gf[5]));
+      o.w = pack_bf2(__fmul_rn(__fmul_rn(xs[p][6], scale), gf[6]), __fmul_rn(__fmul_rn(xs[p][7], scale), gf[7]));
+      *reinterpret_cast<uint4*>(a.norm_out + row + c * 8) = o;
+    }
   }
 }
 

@@ -18,7 +18,9 @@ size_t gemm_tc_work_floats(int rows, int n_out, int epi, int splits);
 // halves), K, halves, 128 (64 for SWIGLU), ch), xmap = make_kmajor_map(x,
 // rows, K, 1, nb, ch). One CTA per (weight tile, batch tile, split); a.splits
 // > 1 needs a.work of gemm_tc_work_floats() floats and adds a second launch
-// (gemm_tc_reduce_kernel). With `pdl` both launch programmatically: the
+// (gemm_tc_reduce_kernel; for RESID with a.norm_out, the reduction fused
+// with the RMSNorm of the updated rows). With `pdl` both launch
+// programmatically: the
 // first ring's weights stream before the wait for the preceding kernel.
 int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi, int ch,
                    cudaStream_t stream, bool pdl);
