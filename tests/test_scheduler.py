@@ -89,3 +89,18 @@ def test_config4_workload_is_steady_and_seeded():
     for _ in range(40):
         cb.step()
     assert 18 <= cb.finished <= 22
+
+
+def test_config5_requests_and_sharding():
+    """Config 5's request set: lognormal contexts (median 2048) clipped to
+    [512, 32768], seeded; the longest-processing-time split puts every
+    request on exactly one shard with near-equal expected bytes."""
+    from lcr_b200 import serve
+    c = serve.config5_requests(512, 1.0)
+    assert np.array_equal(c, serve.config5_requests(512, 1.0))
+    assert c.min() >= 512 and c.max() <= 32768 and 1800 <= np.median(c) <= 2300
+    for shards in (1, 2, 4, 8):
+        parts = [serve.shard_requests(c, k, shards, 256) for k in range(shards)]
+        assert sorted(i for p in parts for i in p) == list(range(512))
+        loads = [sum(int(c[i]) + 256 for i in p) for p in parts]
+        assert max(loads) - min(loads) <= int(c.max()) + 256
