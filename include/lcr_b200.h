@@ -344,6 +344,8 @@ LCR_API int lcr_batch_fill_kv(lcr_batch* batch, int slot, int length, uint64_t s
  * start + count. Asynchronous; the first call (or a longer chunk) allocates
  * the chunk's activations. */
 LCR_API int lcr_batch_prefill(lcr_batch* batch, int slot, const int32_t* tokens, int count, int start);
+/* (lcr_batch_step, lcr_batch_fill_kv and lcr_batch_prefill reject positions
+ * beyond the pages set for the slot with LCR_ERR_STATE.) */
 /* The last step's sampled ids of slots [0, n) into host memory (synchronous). */
 LCR_API int lcr_batch_read(lcr_batch* batch, int32_t* next_ids, int n);
 /* The last step's fp32 logits [vocab] of one slot into host memory (synchronous). */

@@ -121,6 +121,7 @@ struct lcr_batch {
   size_t work_floats = 0;
 
   std::vector<int32_t> tables_host;
+  std::vector<int> pages_set;  // pages each slot's table holds (lcr_batch_set_pages)
   std::vector<float> inv_temp_host, top_p_host;
   std::vector<int32_t> top_k_host;
   std::vector<unsigned long long> seed_host;
@@ -576,6 +577,7 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
     cuda(cudaEventCreateWithFlags(&c->staged[i], cudaEventDisableTiming), "cudaEventCreate");
   }
   c->tables_host.assign(B * c->max_pages, 0);
+  c->pages_set.assign(B, 0);
   c->inv_temp_host.assign(B, 0.f);
   c->top_k_host.assign(B, 0);
   c->top_p_host.assign(B, 1.f);
@@ -608,6 +610,7 @@ extern "C" int lcr_batch_set_pages(lcr_batch* c, int slot, const int32_t* pages,
   int32_t* row = c->tables_host.data() + static_cast<size_t>(slot) * c->max_pages;
   std::memcpy(row, pages, sizeof(int32_t) * count);
   std::fill(row + count, row + c->max_pages, 0);
+  c->pages_set[static_cast<size_t>(slot)] = count;
   c->tables_dirty = true;
   return LCR_OK;
 }
@@ -634,8 +637,9 @@ extern "C" int lcr_batch_step(lcr_batch* c, int n, const int32_t* tokens, const 
   for (int b = 0; b < n; ++b) {
     LCRB_REQUIRE(positions[b] >= 0 && positions[b] < c->o.max_seq, LCR_ERR_STATE,
                  "slot %d: position %d outside the cache built for %d", b, positions[b], c->o.max_seq);
-    LCRB_REQUIRE((positions[b] / c->o.page_size) < c->max_pages, LCR_ERR_STATE, "slot %d: no page for position %d",
-                 b, positions[b]);
+    LCRB_REQUIRE(positions[b] / c->o.page_size < c->pages_set[static_cast<size_t>(b)], LCR_ERR_STATE,
+                 "slot %d: no page for position %d (its table holds %d pages)", b, positions[b],
+                 c->pages_set[static_cast<size_t>(b)]);
   }
   LCRB_CUDA(cudaSetDevice(c->device));
   const size_t B = static_cast<size_t>(c->o.max_batch);
@@ -663,6 +667,9 @@ extern "C" int lcr_batch_fill_kv(lcr_batch* c, int slot, int length, uint64_t se
   LCRB_REQUIRE(c, LCR_ERR_INVALID, "null batch");
   LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d", slot);
   LCRB_REQUIRE(length >= 0 && length <= c->o.max_seq, LCR_ERR_STATE, "length %d outside the cache", length);
+  LCRB_REQUIRE((length + c->o.page_size - 1) / c->o.page_size <= c->pages_set[static_cast<size_t>(slot)],
+               LCR_ERR_STATE, "slot %d: %d positions need more than its %d pages", slot, length,
+               c->pages_set[static_cast<size_t>(slot)]);
   if (length == 0) return LCR_OK;
   LCRB_CUDA(cudaSetDevice(c->device));
   if (c->tables_dirty) {
@@ -728,6 +735,9 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
                c->o.max_batch - 1);
   LCRB_REQUIRE(count >= 1 && start >= 0 && start + count <= c->o.max_seq, LCR_ERR_STATE,
                "prefill of %d positions at %d outside the cache built for %d", count, start, c->o.max_seq);
+  LCRB_REQUIRE((start + count - 1) / c->o.page_size < c->pages_set[static_cast<size_t>(slot)], LCR_ERR_STATE,
+               "slot %d: no page for position %d (its table holds %d pages)", slot, start + count - 1,
+               c->pages_set[static_cast<size_t>(slot)]);
   const lcr_model_desc& d = c->d;
   for (int i = 0; i < count; ++i) {
     LCRB_REQUIRE(tokens[i] >= 0 && tokens[i] < d.vocab_size, LCR_ERR_INVALID, "token %d: id %d outside the vocabulary",

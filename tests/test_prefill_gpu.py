@@ -122,6 +122,14 @@ def test_prefill_rejects_bad_inputs(model):
         bt.prefill(2, [1], 0)  # slot 2 of 2
     with pytest.raises(rt.LcrError):
         bt.prefill(0, [block.geom.vocab_size], 0)  # token outside the vocabulary
+    with pytest.raises(rt.LcrError):
+        bt.prefill(0, [1, 2, 3], 0)  # slot 0 has no pages yet
+    bt.set_pages(1, [2])
+    with pytest.raises(rt.LcrError):
+        bt.prefill(1, list(range(1, 18)), 0)  # 17 positions, one 16-position page
+    bt.prefill(1, list(range(1, 17)), 0)
+    with pytest.raises(rt.LcrError):
+        bt.step([1, 1], [16, 16])  # row 0 (slot 0) has no pages, row 1's page ends at 15
     bt.close()
 
 
