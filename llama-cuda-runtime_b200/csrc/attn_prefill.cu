@@ -11,8 +11,8 @@ int launch_t(const PrefillAttnArgs& a, const CUtensorMap& kmap, const CUtensorMa
   constexpr size_t smem = attn_prefill_smem_bytes<D>();
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   const int pairs = (a.count + 15) / 16 * G;
-  const dim3 grid(static_cast<unsigned>((pairs + kAttnConsumerWarps - 1) / kAttnConsumerWarps),
-                  static_cast<unsigned>(kv_heads));
+  const dim3 grid(static_cast<unsigned>(kv_heads),
+                  static_cast<unsigned>((pairs + kAttnConsumerWarps - 1) / kAttnConsumerWarps));
   return launch_kernel(kernel, grid, dim3(kAttnThreads), smem, s, true, a, kmap, vmap);
 }
 

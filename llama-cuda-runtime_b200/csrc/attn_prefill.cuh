@@ -7,14 +7,15 @@
 //
 // The chunk's rotated K/V rows are in the cache already (kv_write_kernel), so
 // every key -- the cached prefix and the chunk itself -- comes from the pool.
-// Grid (CTAs per KV head, kv_heads); each consumer warp owns one (query head,
+// Grid (kv_heads, CTAs per KV head); each consumer warp owns one (query head,
 // 16-query tile) pair of the KV head's group, four pairs per CTA, heaviest
 // tiles first. The producer warp streams the keys 0 .. (last query of the
 // CTA) in stages of four 16-position units: K and V as 128-byte-swizzled TMA
-// boxes, the layout attn_batch_kernel reads (AbGeom). Per unit a warp
-// computes S = Q K^T (m16n8k16, 16 queries x 16 keys, bf16 operands, fp32
-// sums), the causal mask and an online softmax per query row in the log2
-// domain, then O += P V with P rounded to bf16; the output is O / l.
+// boxes, the layout attn_batch_kernel reads (AbGeom). Per stage a warp
+// computes S = Q K^T for the stage's 64 keys (m16n8k16, 16 queries x 8 keys
+// per tile, bf16 operands, fp32 sums), the causal mask and one online-softmax
+// update per query row in the log2 domain, then O += P V with P rounded to
+// bf16 (l sums the unrounded weights); the output is O / l.
 #pragma once
 
 #include "attn_batch.cuh"
@@ -42,11 +43,12 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Three ring stages (two for head_dim 128): the warps spend longer per stage
-// than the decode kernel's, and a smaller ring lets four CTAs share an SM.
+// Four ring stages for head_dim 64 (three CTAs share an SM: the per-stage
+// softmax of 64 keys needs more than the 96 registers a thread of four
+// resident CTAs gets), two for head_dim 128.
 template <int D>
 constexpr int attn_prefill_stages() {
-  return D == 64 ? 3 : 2;
+  return D == 64 ? 4 : 2;
 }
 
 template <int D>
@@ -55,7 +57,7 @@ constexpr size_t attn_prefill_smem_bytes() {
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnThreads, D == 64 ? 4 : 2) attn_prefill_kernel(const PrefillAttnArgs a,
+__global__ void __launch_bounds__(kAttnThreads, D == 64 ? 3 : 2) attn_prefill_kernel(const PrefillAttnArgs a,
                                                                     const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap) {
   using Geo = AbGeom<D>;
@@ -71,11 +73,13 @@ __global__ void __launch_bounds__(kAttnThreads, D == 64 ? 4 : 2) attn_prefill_ke
   uint64_t* empty = full + STAGES;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kvh = blockIdx.y, num_kv = gridDim.y;
+  // KV heads vary fastest in the grid, so every head's heaviest tiles are
+  // dispatched first.
+  const int kvh = blockIdx.x, num_kv = gridDim.x;
   const int tiles = (a.count + 15) / 16;
   const int pairs = tiles * G;
-  // This CTA's pairs 4 * blockIdx.x + w, taken from the last query tile down.
-  const int p_first = W * static_cast<int>(blockIdx.x);
+  // This CTA's pairs 4 * blockIdx.y + w, taken from the last query tile down.
+  const int p_first = W * static_cast<int>(blockIdx.y);
   const int qt_max = tiles - 1 - p_first / G;
   const int key_end = a.start + min(a.count, (qt_max + 1) * 16);  // keys 0 .. key_end - 1
   const int units = (key_end + kAbUnit - 1) / kAbUnit;
@@ -182,57 +186,96 @@ __global__ void __launch_bounds__(kAttnThreads, D == 64 ? 4 : 2) attn_prefill_ke
     const int slot = st % STAGES;
     if (!mbar_wait(&full[slot], (st / STAGES) & 1, a.status, kStatusTimeoutFull)) break;
     const int u0 = st * W;
-    const int cnt = min(W, units - u0);
-    for (int u = 0; u < cnt; ++u) {
-      const int kp0 = (u0 + u) * kAbUnit;
-      if (kp0 > warp_last) break;  // every later key is masked for this warp
-      const uint32_t ks = smem_addr(ring + slot * Geo::STAGE + u * UNIT);
-      const uint32_t vs = smem_addr(ring + slot * Geo::STAGE + (W + u) * UNIT);
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int kp0 = u0 * kAbUnit;
+    // Units of this stage that hold a key this warp needs (warp-uniform);
+    // the rest stay untouched: their bytes may be another stage's.
+    const int live = warp_last < kp0 ? 0 : min(min(W, units - u0), (warp_last - kp0) / kAbUnit + 1);
+    if (live > 0) {
+      const uint32_t ks = smem_addr(ring + slot * Geo::STAGE);
+      const uint32_t vs = ks + W * UNIT;
+      // S = Q K^T over the stage's keys: eight independent accumulator
+      // chains (unit u, 8-key half j), KSTEPS deep.
+      float s[W][2][4];
+#pragma unroll
+      for (int u = 0; u < W; ++u) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) s[u][j][0] = s[u][j][1] = s[u][j][2] = s[u][j][3] = 0.f;
+      }
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
-        uint32_t kb[4];
-        ldmatrix_x4(kb, ks + ab_offset(k_row, 2 * kk + (mi & 1)));
-        mma_16816(s[0], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], kb[0], kb[1]);
-        mma_16816(s[1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], kb[2], kb[3]);
-      }
-      // Causal mask and online softmax for rows g (regs 0, 1) and g + 8 (2, 3).
-      float mxa = kNegBig, mxb = kNegBig;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int kp = kp0 + 8 * j + 2 * t + e;
-          s[j][e] = (ra && kp <= pos_a) ? s[j][e] * a.scale_log2 : kNegBig;
-          s[j][2 + e] = (rb && kp <= pos_b) ? s[j][2 + e] * a.scale_log2 : kNegBig;
-          mxa = fmaxf(mxa, s[j][e]);
-          mxb = fmaxf(mxb, s[j][2 + e]);
+        for (int u = 0; u < W; ++u) {
+          if (u < live) {
+            uint32_t kb[4];
+            ldmatrix_x4(kb, ks + u * UNIT + ab_offset(k_row, 2 * kk + (mi & 1)));
+            mma_16816(s[u][0], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], kb[0], kb[1]);
+            mma_16816(s[u][1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], kb[2], kb[3]);
+          }
         }
       }
+      // Causal mask (only a stage that reaches past the tile's first query,
+      // or holds units past the keys, needs one), then one online-softmax
+      // update per query row for all the stage's keys: rows g (regs 0, 1)
+      // and g + 8 (2, 3). Maxima are taken on the raw scores (the scale is
+      // positive) and the scale is folded into the exponent's FMA; the
+      // running maximum m is kept in the scaled log2 domain.
+      if (kp0 + live * kAbUnit - 1 > a.start + q0 || live < W) {
+        const int lim_a = pos_a - kp0 - 2 * t, lim_b = pos_b - kp0 - 2 * t;
+#pragma unroll
+        for (int u = 0; u < W; ++u) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int off = kAbUnit * u + 8 * j + e;
+              if (u >= live || off > lim_a) s[u][j][e] = kNegBig;
+              if (u >= live || off > lim_b) s[u][j][2 + e] = kNegBig;
+            }
+          }
+        }
+      }
+      float ua[W], ub[W];
+#pragma unroll
+      for (int u = 0; u < W; ++u) {
+        ua[u] = fmaxf(fmaxf(s[u][0][0], s[u][0][1]), fmaxf(s[u][1][0], s[u][1][1]));
+        ub[u] = fmaxf(fmaxf(s[u][0][2], s[u][0][3]), fmaxf(s[u][1][2], s[u][1][3]));
+      }
+      static_assert(W == 4, "the stage maximum below is a tree over four units");
+      float mxa = fmaxf(fmaxf(ua[0], ua[1]), fmaxf(ua[2], ua[3]));
+      float mxb = fmaxf(fmaxf(ub[0], ub[1]), fmaxf(ub[2], ub[3]));
       mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
-      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
       mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
       mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
-      const float na = fmaxf(m_a, mxa), nb = fmaxf(m_b, mxb);
+      // (every row has an unmasked key 0 in the first stage, so m is finite
+      // from there on and masked scores give exp2(-huge) = 0)
+      const float na = fmaxf(m_a, mxa * a.scale_log2), nb = fmaxf(m_b, mxb * a.scale_log2);
       const float alpha_a = ex2_approx(m_a - na), alpha_b = ex2_approx(m_b - nb);
-      float pa[2][2], pb[2][2];
-      float suma = 0.f, sumb = 0.f;
+      uint32_t pf[W][4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int u = 0; u < W; ++u) {
+        float pa[2][2], pb[2][2];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          pa[j][e] = s[j][e] > kNegBig ? rbf(ex2_approx(s[j][e] - na)) : 0.f;
-          pb[j][e] = s[j][2 + e] > kNegBig ? rbf(ex2_approx(s[j][2 + e] - nb)) : 0.f;
-          suma += pa[j][e];
-          sumb += pb[j][e];
+        for (int j = 0; j < 2; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            pa[j][e] = ex2_approx(fmaf(s[u][j][e], a.scale_log2, -na));
+            pb[j][e] = ex2_approx(fmaf(s[u][j][2 + e], a.scale_log2, -nb));
+          }
         }
+        ua[u] = (pa[0][0] + pa[0][1]) + (pa[1][0] + pa[1][1]);
+        ub[u] = (pb[0][0] + pb[0][1]) + (pb[1][0] + pb[1][1]);
+        pf[u][0] = pack_bf2(pa[0][0], pa[0][1]);
+        pf[u][1] = pack_bf2(pb[0][0], pb[0][1]);
+        pf[u][2] = pack_bf2(pa[1][0], pa[1][1]);
+        pf[u][3] = pack_bf2(pb[1][0], pb[1][1]);
       }
-      l_a = l_a * alpha_a + suma;
-      l_b = l_b * alpha_b + sumb;
+      l_a = fmaf(l_a, alpha_a, (ua[0] + ua[1]) + (ua[2] + ua[3]));
+      l_b = fmaf(l_b, alpha_b, (ub[0] + ub[1]) + (ub[2] + ub[3]));
       m_a = na;
       m_b = nb;
-      // Most units leave every row's maximum where it was: skip the rescale
-      // then (warp-uniform test).
+      // Most stages leave every row's maximum where it was: skip the
+      // rescale then (warp-uniform test).
       if (__any_sync(0xffffffffu, alpha_a != 1.0f || alpha_b != 1.0f)) {
 #pragma unroll
         for (int nn = 0; nn < NT; ++nn) {
@@ -242,14 +285,18 @@ __global__ void __launch_bounds__(kAttnThreads, D == 64 ? 4 : 2) attn_prefill_ke
           o[nn][3] *= alpha_b;
         }
       }
-      const uint32_t p0 = pack_bf2(pa[0][0], pa[0][1]), p1 = pack_bf2(pb[0][0], pb[0][1]);
-      const uint32_t p2 = pack_bf2(pa[1][0], pa[1][1]), p3 = pack_bf2(pb[1][0], pb[1][1]);
+      // O += P V, one 16-key k-step per live unit.
 #pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        uint32_t vb[4];
-        ldmatrix_x4_trans(vb, vs + ab_offset(v_row, 2 * c + (mi >> 1)));
-        mma_16816(o[2 * c], p0, p1, p2, p3, vb[0], vb[1]);
-        mma_16816(o[2 * c + 1], p0, p1, p2, p3, vb[2], vb[3]);
+      for (int u = 0; u < W; ++u) {
+        if (u < live) {
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t vb[4];
+            ldmatrix_x4_trans(vb, vs + u * UNIT + ab_offset(v_row, 2 * c + (mi >> 1)));
+            mma_16816(o[2 * c], pf[u][0], pf[u][1], pf[u][2], pf[u][3], vb[0], vb[1]);
+            mma_16816(o[2 * c + 1], pf[u][0], pf[u][1], pf[u][2], pf[u][3], vb[2], vb[3]);
+          }
+        }
       }
     }
     __syncwarp();
