@@ -303,7 +303,9 @@ typedef struct lcr_batch_options {
   int max_seq;     /* positions per sequence */
   int page_size;   /* positions per KV page, a multiple of 16 */
   int pool_pages;  /* pages in the shared KV pool; a page holds every layer */
-  int flags;       /* bit 1: no CUDA graph */
+  int flags;       /* bit 1: no CUDA graph; bit 2: projections of 128-row
+                      batch tiles (prefill chunks) one CTA per tile instead of
+                      the persistent kernel (same results) */
 } lcr_batch_options;
 
 typedef struct lcr_batch lcr_batch;

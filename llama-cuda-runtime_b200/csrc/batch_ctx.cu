@@ -77,6 +77,7 @@ struct lcr_batch {
   lcr_batch_options o{};
   int sms = 148;
   bool use_graph = true;
+  bool persist_gemm = true;  // 128-row projection tiles on gemm_tc_persist_kernel
   cudaStream_t stream = nullptr;
 
   const bf16* embed = nullptr;
@@ -242,6 +243,7 @@ int gemm_node(lcr_batch* c, const Acts& v, const CUtensorMap& wm, const CUtensor
   while (splits > 1 && gemm_tc_work_floats(n, n_out, epi, splits) > c->work_floats) --splits;
   a.splits = splits;
   a.work = c->work;
+  a.ctas = c->persist_gemm ? c->sms : 0;
   const bool fuse = norm_gain != nullptr && epi == EPI_RESID && splits > 1;
   if (fuse) {
     a.norm_gain = static_cast<const bf16*>(norm_gain);
@@ -438,6 +440,7 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   c->d = d;
   c->o = o;
   c->use_graph = (o.flags & 2) == 0;
+  c->persist_gemm = (o.flags & 4) == 0;
   cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, o.device);
   c->embed = static_cast<const bf16*>(weights->embedding);
   c->final_norm = static_cast<const bf16*>(weights->final_norm);
@@ -754,13 +757,34 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
   for (int i = 0; i < count; ++i) pos[static_cast<size_t>(i)] = start + i;
   LCRB_CUDA(cudaMemcpyAsync(v.tokens, tokens, sizeof(int32_t) * count, cudaMemcpyHostToDevice, c->stream));
   LCRB_CUDA(cudaMemcpyAsync(v.positions, pos.data(), sizeof(int32_t) * count, cudaMemcpyHostToDevice, c->stream));
-  // Activation tensor maps for this chunk's batch tile.
-  // One chunk per stage: 128-row tiles then run two CTAs per SM.
+  // Activation tensor maps for this chunk's batch tiles (one 64-column chunk
+  // per stage), and the tile of each projection.
   const int nb = gemm_tc_batch_tile(count);
-  StepMaps m;
+  StepMaps m, m2;
   LCRB_TRY(make_kmajor_map(&m.xn, v.xn, c->pre_rows, H, 1, nb, 1));
   LCRB_TRY(make_kmajor_map(&m.attn, v.attn, c->pre_rows, qd, 1, nb, 1));
   LCRB_TRY(make_kmajor_map(&m.act, v.act, c->pre_rows, F, 1, nb, 1));
+  // 256-row tiles (persistent kernel; a third fewer shared-memory operand
+  // bytes per FLOP, modelled as 1.36x the rate of 128-row tiles) where they
+  // need no split-K and their last round of tiles idles no more SMs than
+  // that saves.
+  auto wide = [&](int weight_tiles) {
+    if (nb != 128 || !c->persist_gemm) return false;
+    const long long t128 = static_cast<long long>(weight_tiles) * ((count + 127) / 128);
+    const long long t256 = static_cast<long long>(weight_tiles) * ((count + 255) / 256);
+    if (2 * t256 <= c->sms) return false;
+    const long long r128 = (t128 + c->sms - 1) / c->sms, r256 = (t256 + c->sms - 1) / c->sms;
+    return r256 * 376 <= r128 * 256;
+  };
+  const bool wide_qkv = wide((qd + 2 * kvd + kTcTileM - 1) / kTcTileM);
+  const bool wide_o = wide((H + kTcTileM - 1) / kTcTileM);
+  const bool wide_gu = wide((F + 63) / 64);
+  const bool wide_down = wide((H + kTcTileM - 1) / kTcTileM);
+  if (wide_qkv || wide_o || wide_gu || wide_down) {
+    LCRB_TRY(make_kmajor_map(&m2.xn, v.xn, c->pre_rows, H, 1, 256, 1));
+    LCRB_TRY(make_kmajor_map(&m2.attn, v.attn, c->pre_rows, qd, 1, 256, 1));
+    LCRB_TRY(make_kmajor_map(&m2.act, v.act, c->pre_rows, F, 1, 256, 1));
+  }
   const int32_t* table = c->tables + static_cast<size_t>(slot) * c->max_pages;
   const int group = d.num_heads / d.num_kv_heads;
   const int pad_rows = (start + count + 15) / 16 * 16 - start;
@@ -768,7 +792,8 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
     const CUtensorMap* wm = &c->wmaps1[static_cast<size_t>(4 * l)];
     LCRB_TRY(norm_launch(c, v, count, l == 0, w.input_norm));
-    LCRB_TRY(gemm_node(c, v, wm[0], m.xn, nb, count, qd + 2 * kvd, H, EPI_ROPE, v.qkv, nullptr, qd + 2 * kvd, 1));
+    LCRB_TRY(gemm_node(c, v, wm[0], wide_qkv ? m2.xn : m.xn, wide_qkv ? 256 : nb, count, qd + 2 * kvd, H, EPI_ROPE,
+                       v.qkv, nullptr, qd + 2 * kvd, 1));
     KvWriteArgs kw = {};
     kw.qkv = v.qkv;
     kw.qkv_stride = qd + 2 * kvd;
@@ -802,10 +827,13 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     pa.status = c->status;
     LCRB_TRY(attn_prefill_launch(pa, c->kvmaps[static_cast<size_t>(2 * l)], c->kvmaps[static_cast<size_t>(2 * l + 1)],
                                  d.head_dim, group, d.num_kv_heads, c->stream));
-    LCRB_TRY(gemm_node(c, v, wm[1], m.attn, nb, count, H, qd, EPI_RESID, nullptr, nullptr, H, 1));
+    LCRB_TRY(gemm_node(c, v, wm[1], wide_o ? m2.attn : m.attn, wide_o ? 256 : nb, count, H, qd, EPI_RESID, nullptr,
+                       nullptr, H, 1));
     LCRB_TRY(norm_launch(c, v, count, false, w.post_attention_norm));
-    LCRB_TRY(gemm_node(c, v, wm[2], m.xn, nb, count, F, H, EPI_SWIGLU, v.act, nullptr, F, 1));
-    LCRB_TRY(gemm_node(c, v, wm[3], m.act, nb, count, H, F, EPI_RESID, nullptr, nullptr, H, 1));
+    LCRB_TRY(gemm_node(c, v, wm[2], wide_gu ? m2.xn : m.xn, wide_gu ? 256 : nb, count, F, H, EPI_SWIGLU, v.act, nullptr,
+                       F, 1));
+    LCRB_TRY(gemm_node(c, v, wm[3], wide_down ? m2.act : m.act, wide_down ? 256 : nb, count, H, F, EPI_RESID, nullptr,
+                       nullptr, H, 1));
   }
   // The last row only: final norm, lm_head into this slot's logits, sample
   // with this slot's parameters and Philox counter = the last position.

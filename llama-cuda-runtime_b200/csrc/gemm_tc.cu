@@ -6,8 +6,22 @@
 namespace lcrb {
 namespace {
 
+template <int NB, int EPI>
+int launch_persist(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, cudaStream_t s, bool pdl) {
+  auto kernel = gemm_tc_persist_kernel<NB, EPI>;
+  constexpr size_t smem = gemm_tc_persist_smem_bytes<NB>();
+  LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  const int tiles_n = EPI == EPI_SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
+  const int tiles = tiles_n * ((a.rows + NB - 1) / NB);
+  return launch_kernel(kernel, dim3(static_cast<unsigned>(std::min(tiles, a.ctas))), dim3(kTcThreads), smem, s, pdl,
+                       a, wmap, xmap);
+}
+
 template <int NB, int EPI, int CH>
 int launch_t(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, cudaStream_t s, bool pdl) {
+  if constexpr (NB == 128 && CH == 1) {
+    if (a.splits == 1 && a.ctas > 0) return launch_persist<128, EPI>(a, wmap, xmap, s, pdl);
+  }
   auto kernel = gemm_tc_kernel<NB, EPI, CH>;
   constexpr size_t smem = gemm_tc_smem_bytes<NB, CH>();
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -88,6 +102,18 @@ int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& 
     case 32: return by_chunks<32>(a, wmap, xmap, epi, ch, stream, pdl);
     case 64: return by_chunks<64>(a, wmap, xmap, epi, ch, stream, pdl);
     case 128: return by_chunks<128>(a, wmap, xmap, epi, ch, stream, pdl);
+    case 256:
+      // Persistent kernel only (one 64-column chunk per stage, no split-K).
+      LCRB_REQUIRE(ch == 1 && a.splits == 1 && a.ctas > 0, LCR_ERR_SHAPE,
+                   "tcgen05 projection: 256-row batch tiles run persistent, one chunk per stage, without split-K");
+      switch (epi) {
+        case EPI_STORE: return launch_persist<256, EPI_STORE>(a, wmap, xmap, stream, pdl);
+        case EPI_STORE_F32: return launch_persist<256, EPI_STORE_F32>(a, wmap, xmap, stream, pdl);
+        case EPI_RESID: return launch_persist<256, EPI_RESID>(a, wmap, xmap, stream, pdl);
+        case EPI_SWIGLU: return launch_persist<256, EPI_SWIGLU>(a, wmap, xmap, stream, pdl);
+        case EPI_ROPE: return launch_persist<256, EPI_ROPE>(a, wmap, xmap, stream, pdl);
+        default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: no epilogue %d", epi);
+      }
     default: return fail(LCR_ERR_SHAPE, "tcgen05 projection: batch tile %d", nb);
   }
 }

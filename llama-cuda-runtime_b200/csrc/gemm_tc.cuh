@@ -71,6 +71,9 @@ struct TcArgs {
   const float2* rope;
   int head_dim;
   int rope_cols;
+  // 128-row batch tiles without split-K: run gemm_tc_persist_kernel on this
+  // many CTAs (at most one per tile); 0 launches one CTA per tile instead.
+  int ctas;
   // RESID with splits > 1, optional: the RMSNorm of the updated residual rows
   // into norm_out (bf16 [rows][n_out]) with gain norm_gain, fused into the
   // reduction (gemm_tc_reduce_norm_kernel).
@@ -270,11 +273,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     if (lane == 0 && aligned) {
       const uint64_t policy = l2_policy_evict_first();
-      // Each tile walks its K range from its own starting stage, so CTAs
-      // running side by side read different slabs of x (not the same L2
-      // lines at once); the accumulation order is fixed per tile.
+      // Each weight tile walks its K range from its own starting stage, so
+      // CTAs of neighbouring weight tiles read different slabs of x (not the
+      // same L2 lines at once); the accumulation order is fixed per weight
+      // tile, whatever the batch tiling.
       const int span = s1 - s0;
-      const int rot = span > 0 ? static_cast<int>(blockIdx.x % static_cast<unsigned>(span)) : 0;
+      const int rot = span > 0 ? tile % span : 0;
       auto k_stage = [&](int q) { return s0 + (q + rot < span ? q + rot : q + rot - span); };
       auto load_w = [&](int q, uint8_t* st, uint64_t* bar) {
         if constexpr (SWIGLU) {
@@ -516,6 +520,245 @@ __global__ void __launch_bounds__(256) gemm_tc_reduce_norm_kernel(const TcArgs a
       *reinterpret_cast<uint4*>(a.norm_out + row + c * 8) = o;
     }
   }
+}
+
+// Persistent form for prefill chunks (128- or 256-row batch tiles, no
+// split-K). One CTA per SM walks the tiles blockIdx.x, blockIdx.x +
+// gridDim.x, ... (batch tiles fastest, as in gemm_tc_kernel); the producer
+// streams their stages through one ring without a break, the MMA thread
+// alternates between two TMEM accumulators, and the epilogue of one tile runs
+// while the next tile's MMAs do. The epilogue reads the accumulator in
+// 64-column passes (batch rows), each transposed through a padded staging
+// buffer T[batch row][tile row], so that a thread finishes 8 consecutive
+// outputs of one batch row and a warp's stores cover whole rows. Per tile the
+// K order (rotated by the weight tile's index) and the accumulation are those
+// of gemm_tc_kernel<128, EPI, 1>, so the outputs do not depend on the tile
+// size or on the kernel.
+//
+// Why 256-row tiles: an m128 x n x k16 MMA reads (128 + n) x 32 bytes of
+// operands from shared memory and the ring is written with as many, so at
+// n = 128 an SM moves 16 KB per 64-clock MMA -- twice what its shared memory
+// delivers at the tensor pipe's full rate; n = 256 moves 24 KB per 128 clocks.
+constexpr int kTcpHalf = 64;                  // batch rows per epilogue pass
+constexpr int kTcpPitch = kTcTileM + 4;       // staging row pitch (floats)
+constexpr int kTcpStaging = kTcpHalf * kTcpPitch * 4;
+template <int NB>
+constexpr int tcp_stages() {
+  return NB == 128 ? 6 : 4;  // 192 KB of ring either way
+}
+
+template <int NB, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_persist_kernel(const TcArgs a,
+                                                                        const __grid_constant__ CUtensorMap wmap,
+                                                                        const __grid_constant__ CUtensorMap xmap) {
+  static_assert(NB == 128 || NB == 256, "persistent batch tile");
+  using G = TcGeom<NB, 1>;
+  constexpr int STAGES = tcp_stages<NB>();
+  constexpr bool SWIGLU = EPI == EPI_SWIGLU;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ring = smem;
+  float* T = reinterpret_cast<float*>(smem + STAGES * G::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * G::STAGE + kTcpStaging);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tiles_n = SWIGLU ? (a.n_out + 63) / 64 : (a.n_out + kTcTileM - 1) / kTcTileM;
+  const int tiles_b = (a.rows + NB - 1) / NB;
+  const int tiles = tiles_n * tiles_b;
+  const int span = a.K / kTcSlabK;
+  const int first = static_cast<int>(blockIdx.x), stride = static_cast<int>(gridDim.x);
+  const int mine = tiles > first ? (tiles - 1 - first) / stride + 1 : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(2 * NB)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const bool aligned = (smem_addr(ring) & 1023u) == 0;
+
+  if (warp == 0) {
+    if (lane == 0 && aligned) {
+      const uint64_t policy = l2_policy_evict_first();
+      // Stage q of tile t: weight rows of tile t / tiles_b, batch rows of
+      // tile t % tiles_b, K slab (q + t / tiles_b) mod span.
+      auto slab = [&](int t, int q) { return (q + (t / tiles_b) % span) % span; };
+      auto load_w = [&](int t, int q, uint8_t* st, uint64_t* bar) {
+        const int tile = t / tiles_b;
+        if constexpr (SWIGLU) {
+          tma_load_4d(st, &wmap, 0, tile * 64, 0, slab(t, q), bar, policy);
+        } else {
+          tma_load_3d(st, &wmap, 0, tile * kTcTileM, slab(t, q), bar, policy);
+        }
+      };
+      auto load_x = [&](int t, int q, uint8_t* st, uint64_t* bar) {
+        tma_load_3d(st + G::W_BYTES, &xmap, 0, (t % tiles_b) * NB, slab(t, q), bar, policy);
+      };
+      // The weights do not depend on the preceding kernel: the first ring's
+      // worth streams before the wait for its output (x).
+      const int pre = mine > 0 ? (span < STAGES ? span : STAGES) : 0;
+      for (int q = 0; q < pre; ++q) {
+        mbar_arrive_expect_tx(&full[q], G::STAGE);
+        load_w(first, q, ring + q * G::STAGE, &full[q]);
+      }
+      pdl_wait();
+      for (int q = 0; q < pre; ++q) load_x(first, q, ring + q * G::STAGE, &full[q]);
+      int it = pre;
+      bool ok = true;
+      for (int i = 0; i < mine && ok; ++i) {
+        const int t = first + i * stride;
+        for (int q = i == 0 ? pre : 0; q < span; ++q, ++it) {
+          const int slot = it % STAGES;
+          if (!mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ring + slot * G::STAGE;
+          mbar_arrive_expect_tx(&full[slot], G::STAGE);
+          load_w(t, q, st, &full[slot]);
+          load_x(t, q, st, &full[slot]);
+        }
+      }
+      ring_drain<STAGES>(full, it, a.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc<NB>();
+      int it = 0;
+      bool ok = aligned;
+      for (int i = 0; i < mine && ok; ++i) {
+        const int buf = i & 1;
+        // The epilogue has finished with this accumulator's previous tile.
+        if (i >= 2 && !mbar_wait(&acc_empty[buf], ((i >> 1) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * NB);
+        for (int q = 0; q < span; ++q, ++it) {
+          const int slot = it % STAGES;
+          if (!mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_addr(ring + slot * G::STAGE);
+          const uint64_t adesc = tc_desc_sw128(st);
+          const uint64_t bdesc = tc_desc_sw128(st + G::W_BYTES);
+#pragma unroll
+          for (int k = 0; k < kTcSlabK / 16; ++k) {
+            tc_mma(d, adesc + 2 * k, bdesc + 2 * k, idesc, (q > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[slot]);
+        }
+        if (!ok && a.status) atomicOr(a.status, kStatusAbort);
+        // Accumulator complete (or abandoned: the epilogue sees the abort).
+        tc_commit(&acc_full[buf]);
+      }
+      pdl_launch_next();
+      tc_commit(drain);
+      mbar_wait(drain, 0, a.status, kStatusTimeoutFull);
+      if (!ok && a.status) atomicOr(a.status, kStatusAbort);
+    }
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 = tile rows.
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;  // tile row 0..127
+    const int et = tid - 64;           // 0..127
+    constexpr int NOUT = SWIGLU ? 64 : kTcTileM;
+    constexpr int N8 = NOUT / 8;
+    pdl_wait();  // the residual stream and RoPE table come from earlier kernels
+    for (int i = 0; i < mine; ++i) {
+      const int buf = i & 1;
+      const int t = first + i * stride;
+      const int n0 = SWIGLU ? (t / tiles_b) * 64 : (t / tiles_b) * kTcTileM;
+      const int b0 = (t % tiles_b) * NB;
+      const bool got = mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kStatusTimeoutFull) &&
+                       !(a.status != nullptr && (__ldcg(a.status) & kStatusAbort));
+      // One decision for all 128 epilogue threads (the loop holds 128-thread
+      // barriers).
+      if (named_sync_or(2, 128, !got)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int h = 0; h < NB / kTcpHalf; ++h) {
+        float v[kTcpHalf];
+#pragma unroll
+        for (int c = 0; c < kTcpHalf; c += 16) {
+          float t16[16];
+          tc_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NB + h * kTcpHalf + c),
+                  t16);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[c + e] = t16[e];
+        }
+        tc_wait_ld();
+        if (h == NB / kTcpHalf - 1) {
+          // This warp is done with the accumulator: the MMA thread may reuse it.
+          tc_fence_before();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+#pragma unroll
+        for (int bb = 0; bb < kTcpHalf; ++bb) T[bb * kTcpPitch + row] = v[bb];
+        named_sync(2, 128);
+        // Item c: outputs 8 * (c % N8) .. + 7 of batch row c / N8 of the half
+        // (SWIGLU: gate rows 0-63, up rows 64-127; ROPE: the partner of tile
+        // row r is r ^ head_dim / 2).
+        for (int c = et; c < N8 * kTcpHalf; c += 128) {
+          const int nl = (c % N8) * 8, bb = c / N8;
+          const int brow = b0 + h * kTcpHalf + bb;
+          if (brow >= a.rows || n0 + nl >= a.n_out) continue;
+          const float* tr = T + bb * kTcpPitch;
+          float val[8], aux[8];
+          *reinterpret_cast<float4*>(val) = *reinterpret_cast<const float4*>(tr + nl);
+          *reinterpret_cast<float4*>(val + 4) = *reinterpret_cast<const float4*>(tr + nl + 4);
+          if constexpr (SWIGLU) {
+            *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + 64 + nl);
+            *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + 64 + nl + 4);
+          } else if constexpr (EPI == EPI_ROPE) {
+            const int pn = nl ^ (a.head_dim >> 1);  // 8-aligned: the partners of nl .. nl + 7 are pn .. pn + 7
+            *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + pn);
+            *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + pn + 4);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) aux[e] = 0.f;
+          }
+          tc_store8<EPI>(a, brow, n0 + nl, val, aux);
+        }
+        named_sync(2, 128);  // T is read before the next half or tile overwrites it
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NB) : "memory");
+  }
+}
+
+template <int NB>
+constexpr size_t gemm_tc_persist_smem_bytes() {
+  return static_cast<size_t>(tcp_stages<NB>()) * TcGeom<NB, 1>::STAGE + kTcpStaging + (2 * tcp_stages<NB>() + 5) * 8 +
+         16;
 }
 
 template <int NB, int CH>

@@ -19,9 +19,11 @@ size_t gemm_tc_work_floats(int rows, int n_out, int epi, int splits);
 // rows, K, 1, nb, ch). One CTA per (weight tile, batch tile, split); a.splits
 // > 1 needs a.work of gemm_tc_work_floats() floats and adds a second launch
 // (gemm_tc_reduce_kernel; for RESID with a.norm_out, the reduction fused
-// with the RMSNorm of the updated rows). With `pdl` both launch
-// programmatically: the
-// first ring's weights stream before the wait for the preceding kernel.
+// with the RMSNorm of the updated rows). nb = 128 with ch = 1, a.splits = 1
+// and a.ctas > 0 runs gemm_tc_persist_kernel on min(tiles, a.ctas) CTAs;
+// nb = 256 (prefill chunks) runs only there. With `pdl` the kernels launch
+// programmatically: the first ring's weights stream before the wait for the
+// preceding kernel.
 int gemm_tc_launch(const TcArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, int nb, int epi, int ch,
                    cudaStream_t stream, bool pdl);
 

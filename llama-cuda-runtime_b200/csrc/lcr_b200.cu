@@ -289,6 +289,9 @@ extern "C" int lcr_gemm_nt(void* y, int y_fp32, const void* x, const void* w, in
     a.rows = rows;
     a.splits = 1;
     a.ldy = out_features;
+    a.ctas = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&a.ctas, cudaDevAttrMultiProcessorCount, dev);
     if (y_fp32) a.yf = reinterpret_cast<float*>(y);
     else a.y = mb(y);
     return gemm_tc_launch(a, wmap, xmap, nb, epi, 1, cs(stream), false);

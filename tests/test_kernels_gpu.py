@@ -140,7 +140,11 @@ def test_rope_q():
                                            # batched: the tcgen05 path (>= 16 rows)
                                            (16, 2048, 3072, 1), (64, 2048, 2048, 0),
                                            (100, 1024, 700, 1), (200, 512, 384, 0),
-                                           (32, 8192, 256, 1), (17, 64, 130, 1)])
+                                           (32, 8192, 256, 1), (17, 64, 130, 1),
+                                           # persistent 128-row tiles: CTAs walk
+                                           # several tiles (one K slab each in
+                                           # the second case)
+                                           (300, 256, 8192, 0), (257, 64, 20000, 1)])
 def test_gemm_nt(rows, k, n, fp32):
     x = bf(RNG.normal(size=(rows, k)))
     w = bf(RNG.normal(0, 0.02, size=(n, k)))

@@ -171,3 +171,34 @@ def test_batcher_with_prefill_generates_oracle_greedy_ids(model):
                 break
             logits = r.decode(got, q.context + k, oracle.MODE_BF16)
     bt.close()
+
+
+def test_persistent_projections_match_per_tile_kernel():
+    """Prefill chunks of a 2-layer model with the 1B geometry: 1300 rows
+    (every projection on 256-row tiles of the persistent kernel, the last one
+    partial), then 199 rows (gate/up on one 256-row tile, the rest split-K).
+    The persistent projection kernel (two TMEM accumulators, one CTA per SM
+    walking tiles) and the one-CTA-per-tile kernel with 128-row tiles (option
+    bit 4) must give bit-identical logits, through the second chunk and a
+    decode step that read the first chunk's K/V."""
+    import dataclasses
+    geom = dataclasses.replace(ck.LLAMA_3_2_1B, num_layers=2)
+    block = ck.generate(geom, 3)
+    wdev = rt.upload_block(block)
+    max_seq = 1536
+    per = max_seq // PAGE
+    prompt = np.asarray(ck.prompt_ids(41, 1500), dtype=np.int64) % geom.vocab_size
+    got = []
+    for flags in (0, 4):
+        bt = rt.Batch(block, wdev, max_batch=1, max_seq=max_seq, page_size=PAGE, pool_pages=per, flags=flags)
+        bt.set_pages(0, oracle.page_permutation(per, 5))
+        bt.set_sampling(0, 0.0)
+        bt.prefill(0, prompt[:1300], 0)
+        first = bt.logits(0).copy()
+        bt.prefill(0, prompt[1300:1499], 1300)
+        second = bt.logits(0).copy()
+        bt.step([int(prompt[1499])], [1499])
+        got.append((first, second, bt.logits(0).copy()))
+        bt.close()
+    for a, b, what in zip(got[0], got[1], ("first chunk", "second chunk", "decode")):
+        assert np.isfinite(a).all() and np.array_equal(a, b), what
