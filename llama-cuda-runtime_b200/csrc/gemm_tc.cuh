@@ -126,6 +126,15 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// The rotation of one RoPE pair in fp32 with explicit roundings (no
+// contraction into an FMA, which the compiler may or may not do depending on
+// the surroundings), so every epilogue computes the same bits: dimension d <
+// head_dim / 2 gives r cos - other sin, the upper half r cos + other sin.
+__device__ __forceinline__ float rope_rot(float r, float other, float2 cs, bool lower) {
+  const float rc = __fmul_rn(r, cs.x), os = __fmul_rn(other, cs.y);
+  return lower ? __fsub_rn(rc, os) : __fadd_rn(rc, os);
+}
+
 // One output element of the epilogue: row n of the weights, batch row b.
 // `up` is SWIGLU's up-projection value, or ROPE's rotation partner (column
 // n ^ head_dim / 2).
@@ -153,7 +162,7 @@ __device__ __forceinline__ void tc_store(const TcArgs& a, int b, int n, float v,
       const int d = n & (a.head_dim - 1);
       const float2 cs = a.rope[static_cast<size_t>(b) * half + (d & (half - 1))];
       const float other = rbf(up);
-      r = rbf(d < half ? (r * cs.x - other * cs.y) : (r * cs.x + other * cs.y));
+      r = rbf(rope_rot(r, other, cs, d < half));
     }
     a.y[o] = __ushort_as_bfloat16(f2bf(r));
   }
@@ -183,7 +192,7 @@ __device__ __forceinline__ void tc_store8(const TcArgs& a, int b, int n, const f
             const int d = (n + e) & (a.head_dim - 1);
             const float2 cs = a.rope[static_cast<size_t>(b) * half + (d & (half - 1))];
             const float other = rbf(aux[e]);
-            r[e] = d < half ? (r[e] * cs.x - other * cs.y) : (r[e] * cs.x + other * cs.y);
+            r[e] = rope_rot(r[e], other, cs, d < half);
           }
         }
       }
@@ -721,27 +730,106 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_persist_kernel(const Tc
         named_sync(2, 128);
         // Item c: outputs 8 * (c % N8) .. + 7 of batch row c / N8 of the half
         // (SWIGLU: gate rows 0-63, up rows 64-127; ROPE: the partner of tile
-        // row r is r ^ head_dim / 2).
-        for (int c = et; c < N8 * kTcpHalf; c += 128) {
-          const int nl = (c % N8) * 8, bb = c / N8;
-          const int brow = b0 + h * kTcpHalf + bb;
-          if (brow >= a.rows || n0 + nl >= a.n_out) continue;
-          const float* tr = T + bb * kTcpPitch;
-          float val[8], aux[8];
-          *reinterpret_cast<float4*>(val) = *reinterpret_cast<const float4*>(tr + nl);
-          *reinterpret_cast<float4*>(val + 4) = *reinterpret_cast<const float4*>(tr + nl + 4);
-          if constexpr (SWIGLU) {
-            *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + 64 + nl);
-            *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + 64 + nl + 4);
-          } else if constexpr (EPI == EPI_ROPE) {
-            const int pn = nl ^ (a.head_dim >> 1);  // 8-aligned: the partners of nl .. nl + 7 are pn .. pn + 7
-            *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + pn);
-            *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + pn + 4);
-          } else {
+        // row r is r ^ head_dim / 2). The global inputs of a group of items
+        // (RESID: the residual rows; ROPE: the rows' angles) are loaded before
+        // any of the group is stored: the stores may alias them as far as the
+        // compiler knows, so a load inside the store loop would wait out a
+        // whole memory latency per item.
+        constexpr int ITEMS = N8 * kTcpHalf / 128;
+        constexpr int GROUP = EPI == EPI_ROPE ? 4 : ITEMS;
+        constexpr int PRE = EPI == EPI_ROPE ? 4 : 1;  // 16-byte inputs per item
+        static_assert(ITEMS * 128 == N8 * kTcpHalf && ITEMS % GROUP == 0, "epilogue items");
 #pragma unroll
-            for (int e = 0; e < 8; ++e) aux[e] = 0.f;
+        for (int g0 = 0; g0 < ITEMS; g0 += GROUP) {
+          uint4 pre[GROUP][PRE];
+          bool fast[GROUP];
+#pragma unroll
+          for (int j = 0; j < GROUP; ++j) {
+            const int c = et + 128 * (g0 + j);
+            const int n = n0 + (c % N8) * 8, brow = b0 + h * kTcpHalf + c / N8;
+            const size_t o = static_cast<size_t>(brow) * a.ldy + n;
+            const bool live = brow < a.rows && n + 8 <= a.n_out;
+            fast[j] = false;
+            if constexpr (EPI == EPI_RESID) {
+              fast[j] = live && ((reinterpret_cast<uintptr_t>(a.resid + o) | reinterpret_cast<uintptr_t>(a.resid_sum + o)) &
+                                 15u) == 0;
+              if (fast[j]) pre[j][0] = ldg_cg16(a.resid + o);
+            } else if constexpr (EPI == EPI_ROPE) {
+              // 8 consecutive outputs of one rotated head: angles d .. d + 7
+              // of the half the head's dimension d falls in.
+              fast[j] = live && n + 8 <= a.rope_cols && (reinterpret_cast<uintptr_t>(a.y + o) & 15u) == 0;
+              if (fast[j]) {
+                const int half = a.head_dim >> 1;
+                const uint4* cs = reinterpret_cast<const uint4*>(a.rope + static_cast<size_t>(brow) * half +
+                                                                 (n & (half - 1)));
+#pragma unroll
+                for (int q = 0; q < 4; ++q) pre[j][q] = ldg_cg16(cs + q);
+              }
+            }
           }
-          tc_store8<EPI>(a, brow, n0 + nl, val, aux);
+#pragma unroll
+          for (int j = 0; j < GROUP; ++j) {
+            const int c = et + 128 * (g0 + j);
+            const int nl = (c % N8) * 8, bb = c / N8;
+            const int brow = b0 + h * kTcpHalf + bb;
+            if (brow >= a.rows || n0 + nl >= a.n_out) continue;
+            const float* tr = T + bb * kTcpPitch;
+            float val[8], aux[8];
+            *reinterpret_cast<float4*>(val) = *reinterpret_cast<const float4*>(tr + nl);
+            *reinterpret_cast<float4*>(val + 4) = *reinterpret_cast<const float4*>(tr + nl + 4);
+            if constexpr (SWIGLU) {
+              *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + 64 + nl);
+              *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + 64 + nl + 4);
+            } else if constexpr (EPI == EPI_ROPE) {
+              const int pn = nl ^ (a.head_dim >> 1);  // 8-aligned: the partners of nl .. nl + 7 are pn .. pn + 7
+              *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + pn);
+              *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + pn + 4);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) aux[e] = 0.f;
+            }
+            const size_t o = static_cast<size_t>(brow) * a.ldy + n0 + nl;
+            if constexpr (EPI == EPI_RESID) {
+              if (fast[j]) {
+                // tc_store8's residual update with the row loaded above
+                float x[8], s8[8];
+                unpack8(pre[j][0], x);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s8[e] = __fadd_rn(x[e], rbf(val[e]));
+                uint4 w;
+                w.x = pack_bf2(s8[0], s8[1]);
+                w.y = pack_bf2(s8[2], s8[3]);
+                w.z = pack_bf2(s8[4], s8[5]);
+                w.w = pack_bf2(s8[6], s8[7]);
+                *reinterpret_cast<uint4*>(a.resid + o) = w;
+                *reinterpret_cast<float4*>(a.resid_sum + o) = make_float4(s8[0], s8[1], s8[2], s8[3]);
+                *reinterpret_cast<float4*>(a.resid_sum + o + 4) = make_float4(s8[4], s8[5], s8[6], s8[7]);
+                continue;
+              }
+            } else if constexpr (EPI == EPI_ROPE) {
+              if (fast[j]) {
+                // tc_store8's rotation with the angles loaded above
+                const float2* cs = reinterpret_cast<const float2*>(pre[j]);
+                const int half = a.head_dim >> 1;
+                float r[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  r[e] = rbf(val[e]);
+                  const int d = (n0 + nl + e) & (a.head_dim - 1);
+                  const float other = rbf(aux[e]);
+                  r[e] = rope_rot(r[e], other, cs[e], d < half);
+                }
+                uint4 w;
+                w.x = pack_bf2(r[0], r[1]);
+                w.y = pack_bf2(r[2], r[3]);
+                w.z = pack_bf2(r[4], r[5]);
+                w.w = pack_bf2(r[6], r[7]);
+                *reinterpret_cast<uint4*>(a.y + o) = w;
+                continue;
+              }
+            }
+            tc_store8<EPI>(a, brow, n0 + nl, val, aux);
+          }
         }
         named_sync(2, 128);  // T is read before the next half or tile overwrites it
       }
