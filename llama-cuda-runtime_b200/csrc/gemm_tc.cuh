@@ -551,6 +551,18 @@ __global__ void __launch_bounds__(256) gemm_tc_reduce_norm_kernel(const TcArgs a
 constexpr int kTcpHalf = 64;                  // batch rows per epilogue pass
 constexpr int kTcpPitch = kTcTileM + 4;       // staging row pitch (floats)
 constexpr int kTcpStaging = kTcpHalf * kTcpPitch * 4;
+// Staging column of tile row r: r with bit 2 flipped where bit 5 is set, so
+// the eight 32-byte row pieces that eight lanes read at once (m = 0, 8, .., 56)
+// start in eight different 4-bank groups; a warp's writes (32 consecutive
+// rows) stay a permutation of 32 consecutive words.
+__device__ __forceinline__ int tcp_swz(int r) { return r ^ (((r >> 5) & 1) << 2); }
+// Tile rows m .. m + 7 (m a multiple of 8) of one staging row.
+__device__ __forceinline__ void tcp_ld8(const float* tr, int m, float* out) {
+  const int f = ((m >> 5) & 1) << 2;
+  *reinterpret_cast<float4*>(out) = *reinterpret_cast<const float4*>(tr + (m ^ f));
+  *reinterpret_cast<float4*>(out + 4) = *reinterpret_cast<const float4*>(tr + ((m + 4) ^ f));
+}
+
 template <int NB>
 constexpr int tcp_stages() {
   return NB == 128 ? 6 : 4;  // 192 KB of ring either way
@@ -726,7 +738,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_persist_kernel(const Tc
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
 #pragma unroll
-        for (int bb = 0; bb < kTcpHalf; ++bb) T[bb * kTcpPitch + row] = v[bb];
+        for (int bb = 0; bb < kTcpHalf; ++bb) T[bb * kTcpPitch + tcp_swz(row)] = v[bb];
         named_sync(2, 128);
         // Item c: outputs 8 * (c % N8) .. + 7 of batch row c / N8 of the half
         // (SWIGLU: gate rows 0-63, up rows 64-127; ROPE: the partner of tile
@@ -775,15 +787,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_persist_kernel(const Tc
             if (brow >= a.rows || n0 + nl >= a.n_out) continue;
             const float* tr = T + bb * kTcpPitch;
             float val[8], aux[8];
-            *reinterpret_cast<float4*>(val) = *reinterpret_cast<const float4*>(tr + nl);
-            *reinterpret_cast<float4*>(val + 4) = *reinterpret_cast<const float4*>(tr + nl + 4);
+            tcp_ld8(tr, nl, val);
             if constexpr (SWIGLU) {
-              *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + 64 + nl);
-              *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + 64 + nl + 4);
+              tcp_ld8(tr, 64 + nl, aux);
             } else if constexpr (EPI == EPI_ROPE) {
               const int pn = nl ^ (a.head_dim >> 1);  // 8-aligned: the partners of nl .. nl + 7 are pn .. pn + 7
-              *reinterpret_cast<float4*>(aux) = *reinterpret_cast<const float4*>(tr + pn);
-              *reinterpret_cast<float4*>(aux + 4) = *reinterpret_cast<const float4*>(tr + pn + 4);
+              tcp_ld8(tr, pn, aux);
             } else {
 #pragma unroll
               for (int e = 0; e < 8; ++e) aux[e] = 0.f;
