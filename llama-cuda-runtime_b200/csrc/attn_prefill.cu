@@ -1,5 +1,6 @@
 // Instantiations and launch of the causal prefill attention.
 #include "attn_prefill.h"
+#include "attn_prefill_tc.cuh"
 
 namespace lcrb {
 namespace {
@@ -14,6 +15,19 @@ int launch_t(const PrefillAttnArgs& a, const CUtensorMap& kmap, const CUtensorMa
   const dim3 grid(static_cast<unsigned>(kv_heads),
                   static_cast<unsigned>((pairs + kAttnConsumerWarps - 1) / kAttnConsumerWarps));
   return launch_kernel(kernel, grid, dim3(kAttnThreads), smem, s, true, a, kmap, vmap);
+}
+
+// head_dim 64: the tcgen05 kernel, 128 query rows (128 / G queries x G heads)
+// per CTA, heaviest blocks first.
+template <int G>
+int launch_tc(const PrefillAttnArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap, int kv_heads,
+              cudaStream_t s) {
+  auto kernel = attn_prefill_tc_kernel<G>;
+  constexpr size_t smem = attn_prefill_tc_smem_bytes();
+  LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  constexpr int QB = 128 / G;
+  const dim3 grid(static_cast<unsigned>(kv_heads), static_cast<unsigned>((a.count + QB - 1) / QB));
+  return launch_kernel(kernel, grid, dim3(kApTcThreads), smem, s, true, a, kmap, vmap);
 }
 
 template <int D>
@@ -37,7 +51,15 @@ int attn_prefill_launch(const PrefillAttnArgs& a, const CUtensorMap& kmap, const
                         int group, int kv_heads, cudaStream_t s) {
   LCRB_REQUIRE(a.count >= 1 && a.start >= 0 && a.page_size % kAbUnit == 0, LCR_ERR_SHAPE,
                "prefill attention: unsupported chunk (%d rows at %d, page size %d)", a.count, a.start, a.page_size);
-  if (head_dim == 64) return by_group<64>(a, kmap, vmap, group, kv_heads, s);
+  if (head_dim == 64) {
+    switch (group) {
+      case 1: return launch_tc<1>(a, kmap, vmap, kv_heads, s);
+      case 2: return launch_tc<2>(a, kmap, vmap, kv_heads, s);
+      case 4: return launch_tc<4>(a, kmap, vmap, kv_heads, s);
+      case 8: return launch_tc<8>(a, kmap, vmap, kv_heads, s);
+      default: return by_group<64>(a, kmap, vmap, group, kv_heads, s);
+    }
+  }
   if (head_dim == 128) return by_group<128>(a, kmap, vmap, group, kv_heads, s);
   return fail(LCR_ERR_SHAPE, "prefill attention is compiled for head_dim 64 or 128, this model has %d", head_dim);
 }
