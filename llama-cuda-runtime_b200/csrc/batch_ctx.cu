@@ -429,6 +429,8 @@ extern "C" int lcr_batch_create(const lcr_model_desc* desc, const lcr_weights* w
   }
   LCRB_REQUIRE(o.device >= 0 && o.device < devices, LCR_ERR_INVALID, "device %d of %d", o.device, devices);
   LCRB_CUDA(cudaSetDevice(o.device));
+  LCRB_REQUIRE(on_device(weights->embedding, o.device) && on_device(weights->final_norm, o.device), LCR_ERR_INVALID,
+               "lcr_weights: the weights are not in device %d's memory", o.device);
   int major = 0;
   LCRB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, o.device));
   LCRB_REQUIRE(major == 10, LCR_ERR_NO_DEVICE, "this library is built for sm_100a; device %d is sm_%d", o.device,

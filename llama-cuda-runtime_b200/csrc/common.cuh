@@ -35,6 +35,19 @@ int launch_status(const char* what);
                           cudaGetErrorString(e_), __FILE__, __LINE__);      \
   } while (0)
 
+// Whether `p` is memory that device `device` may read: device memory of that
+// device (or managed / host-mapped memory). Weights on another GPU would
+// otherwise surface as an illegal access inside the first kernel.
+inline bool on_device(const void* p, int device) {
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (attr.type == cudaMemoryTypeDevice) return attr.device == device;
+  return attr.type == cudaMemoryTypeManaged || attr.type == cudaMemoryTypeHost;
+}
+
 #define LCRB_TRY(expr)            \
   do {                            \
     int s_ = (expr);              \

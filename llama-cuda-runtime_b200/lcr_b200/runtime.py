@@ -197,6 +197,14 @@ def upload_block(block: ck.WeightBlock, device: int = 0):
     return host.to(f"cuda:{device}")
 
 
+def _check_weights_device(weights_dev, device: int) -> None:
+    """The context's kernels read the weights directly: they must be in that
+    device's memory (the C ABI rejects them otherwise; this says so first)."""
+    where = getattr(weights_dev, "device", None)
+    if where is not None and where.type == "cuda" and where.index != device:
+        raise ValueError(f"weights are on cuda:{where.index}, the context is on cuda:{device}")
+
+
 def desc_of(geom: ck.Geometry) -> ModelDesc:
     return ModelDesc(geom.hidden_size, geom.intermediate_size, geom.num_layers, geom.num_heads,
                      geom.num_kv_heads, geom.head_dim, geom.vocab_size, geom.rms_norm_eps,
@@ -218,6 +226,7 @@ class Model:
         self.block = block
         self.device = device
         self.weights_dev = weights_dev if weights_dev is not None else upload_block(block, device)
+        _check_weights_device(self.weights_dev, device)
         base = self.weights_dev.data_ptr()
         g = self.geom
         addr = lambda name: base + block.offsets[name][0] * 2
@@ -357,6 +366,7 @@ class Batch:
         self.block = block
         self.device = device
         self.weights_dev = weights_dev if weights_dev is not None else upload_block(block, device)
+        _check_weights_device(self.weights_dev, device)
         base = self.weights_dev.data_ptr()
         g = self.geom
         addr = lambda name: base + block.offsets[name][0] * 2

@@ -51,7 +51,7 @@ def main(argv=None) -> int:
     if args.layers:
         geom = dataclasses.replace(geom, num_layers=args.layers)
     block = ck.generate(geom, 1)
-    wdev = rt.upload_block(block)
+    wdev = rt.upload_block(block, args.device)
     if args.config5:
         report = config5(block, wdev, args)
     elif args.prefill:

@@ -174,3 +174,18 @@ def test_scheduler_runs_config4_shape_on_tiny(tiny):
     assert cb.finished >= 30 and decoded == 60 * slots
     assert np.all((ids >= 0) & (ids < block.geom.vocab_size))
     bt.close()
+
+
+def test_weights_outside_the_device_are_rejected():
+    """A context reads its weights directly, so lcr_batch_create refuses
+    weights that are not in its device's memory (here: pageable host memory)
+    instead of letting the first kernel fault; with two GPUs, weights on the
+    other GPU are refused too."""
+    block = ck.cached(ck.TINY, 0)
+    host = torch.from_numpy(block.data.view(np.int16))
+    with pytest.raises(rt.LcrError):
+        rt.Batch(block, host, max_batch=2, max_seq=64, page_size=16, pool_pages=8)
+    if torch.cuda.device_count() >= 2:
+        w0 = rt.upload_block(block, 0)
+        with pytest.raises(ValueError):
+            rt.Batch(block, w0, device=1, max_batch=2, max_seq=64, page_size=16, pool_pages=8)
