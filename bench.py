@@ -26,6 +26,9 @@ path, so there is none; value = all ranks' tokens / the slowest rank's time.
 batched  config 4 on the batched context in the same run:
          64 sequences kept in slots by continuous batching, tcgen05 projections;
          decode steps timed with CUDA events (see batched_bench).
+prefill  config 5's 2048-token prefill chunk on tcgen05 (see prefill_bench).
+long_context  config 3: bs1 decode after an 8192-id
+         prompt over shuffled 16-position pages (see long_context_bench).
 
 --impl reference: the reference has no CPU implementation of the decode step,
 so its arm is the fp32 host evaluation (oracle port) of the same workload on
@@ -290,6 +293,66 @@ def batched_bench(block, weights_dev, local, world, steps, warmup):
     return out
 
 
+LONG_PROMPT = 8192
+LONG_DECODE = 256
+
+
+def long_context_bench(block, weights_dev, local, short_ms_per_step, warmup=16):
+    """Config 3 on the bs1 persistent step: an 8192-id
+    prompt (seed 2) through lcr_prefill (untimed: it runs the prompt as decode
+    steps), then 256 greedy tokens at positions 8191..8446 over a paged KV
+    cache of 16-position pages in a seeded shuffled physical order (seed 2).
+    The 256 steps are timed with CUDA events on the context's stream after
+    `warmup` steps from the same position. Bytes per step are the weights plus
+    the KV read at the window's mean context (reference main.cu:195-220).
+
+    The attention shares: by bytes, the KV read over the step's bytes; by
+    time, the step time added over config 2's (whose context is ~32x shorter)
+    over this step time -- an estimate from the two measurements, since the
+    step is one persistent launch."""
+    import torch
+
+    from lcr_b200 import checkpoint as ck
+    from lcr_b200 import runtime as rt
+
+    g = ck.LLAMA_3_2_1B
+    m = rt.Model(block, weights_dev, device=local, max_seq=LONG_PROMPT + LONG_DECODE + 16, paged=True,
+                 page_size=16, page_order_seed=2)
+    prompt = ck.prompt_ids(2, LONG_PROMPT)
+    m.prefill(prompt[:-1])
+    pinned = torch.empty(2, dtype=torch.int32, pin_memory=True)
+    pinned[0] = int(prompt[-1])
+    m.set_token(pinned.data_ptr(), LONG_PROMPT - 1)
+    m.enqueue_steps(warmup)
+    m.sync()
+    stream = torch.cuda.ExternalStream(m.stream, device=f"cuda:{local}")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    m.set_token(pinned.data_ptr(), LONG_PROMPT - 1)
+    e0.record(stream)
+    m.enqueue_steps(LONG_DECODE)
+    e1.record(stream)
+    m.sync()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / LONG_DECODE
+    ctx_mean = LONG_PROMPT + (LONG_DECODE - 1) / 2
+    kv_bytes = ctx_mean * g.kv_bytes_per_position()
+    step_bytes = g.weight_bytes_per_token() + kv_bytes
+    peak, kind = measured_peaks()
+    gbs = step_bytes / (ms / 1000) / 1e9
+    out = {"workload": f"config3: Llama-3.2-1B bs1 greedy, {LONG_PROMPT}-id prompt (seed 2), "
+                       f"{LONG_DECODE} tokens at positions {LONG_PROMPT - 1}..{LONG_PROMPT + LONG_DECODE - 2}, "
+                       "paged KV 16 (seeded shuffled page order)",
+           "value": round(1000.0 / ms, 2), "unit": "tok/s", "ms_per_step": round(ms, 5),
+           "steps": LONG_DECODE, "warmup": warmup,
+           "bytes_per_step": int(step_bytes), "hbm_gbs": round(gbs, 1),
+           "frac_of_peak": round(gbs / peak, 4), "peak_source": kind,
+           "attention_byte_share": round(kv_bytes / step_bytes, 4),
+           "attention_time_share_est": round(max(0.0, ms - short_ms_per_step) / ms, 4)}
+    m.close()
+    return out
+
+
 PREFILL_CHUNK = 2048
 
 
@@ -362,6 +425,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched measurement")
     ap.add_argument("--batched-steps", type=int, default=64)
+    ap.add_argument("--no-long-context", action="store_true",
+                    help="skip the config-3 long-context measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)
@@ -462,6 +527,9 @@ def main():
         prefill = prefill_bench(block, m.weights_dev, local)
 
     ms_per_step = max_ms / args.steps
+    long_ctx = None
+    if not args.no_long_context:
+        long_ctx = long_context_bench(block, m.weights_dev, local, ms_per_step)
     # positions 127..382 read 128..383 cached positions: mean 255.5
     ctx_mean = PROMPT + (WINDOW - 1) / 2
     step_bytes = g.weight_bytes_per_token() + ctx_mean * g.kv_bytes_per_position()
@@ -498,6 +566,7 @@ def main():
             "cpu_baseline": base,
             "batched": batched,
             "prefill": prefill,
+            "long_context": long_ctx,
         }
         print(json.dumps(line))
     m.close()

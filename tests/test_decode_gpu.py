@@ -237,3 +237,35 @@ def test_1b_config2_teacher_forced_vs_oracle():
     assert worst["rms32"] <= SLACK * worst["ref_rms32"]
     assert worst["abs32"] <= SLACK * worst["ref_abs32"]
     assert near_ties <= steps // 10
+
+
+def test_1b_config3_paged_shuffled_matches_contiguous():
+    """Config 3's shape at full size: Llama-3.2-1B (seed 1), an 8192-id prompt
+    (seed 2), then greedy steps. A paged cache of 16-position pages in a
+    shuffled physical order (page_order_seed 2) and a contiguous cache of the
+    same length must give bit-identical logits and token ids: the page table
+    only moves where a position's K/V rows live, and both contexts use the
+    same split count (same max_seq), so the summation order is the same."""
+    g = ck.LLAMA_3_2_1B
+    block = ck.cached(g, 1)
+    wdev = rt.upload_block(block, 0)
+    prompt = ck.prompt_ids(2, 8192)
+    max_seq = 8192 + 32
+    paged = rt.Model(block, wdev, max_seq=max_seq, paged=True, page_size=16, page_order_seed=2)
+    flat = rt.Model(block, wdev, max_seq=max_seq)
+    paged.prefill(prompt)
+    flat.prefill(prompt)
+    a, b = paged.logits_to_host(), flat.logits_to_host()
+    assert np.all(np.isfinite(a))
+    assert np.array_equal(a, b)
+    tables, mapped = paged.page_tables()
+    assert mapped == g.num_layers * (8192 // 16)
+    first = tables[0][tables[0] >= 0]
+    assert len(first) == 8192 // 16 and len(set(first.tolist())) == len(first)
+    assert not np.array_equal(first, np.sort(first)), "the physical page order is not shuffled"
+    ta = paged.generate_greedy(int(np.argmax(a)), 16)
+    tb = flat.generate_greedy(int(np.argmax(b)), 16)
+    assert ta.tolist() == tb.tolist()
+    assert np.array_equal(paged.logits_to_host(), flat.logits_to_host())
+    paged.close()
+    flat.close()
