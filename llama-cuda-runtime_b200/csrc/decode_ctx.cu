@@ -75,7 +75,9 @@ using namespace lcrb;
 
 namespace {
 
-enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8 };
+// Bit 4: the persistent step with fp32 activations instead of the
+// reference's bf16 storage rounding (closer to the fp32 evaluation, slower).
+enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8, kFlagFp32Act = 16 };
 constexpr int kPinnedRing = 256;
 constexpr int kTimingSlots = 128;
 
@@ -98,6 +100,7 @@ struct lcr_ctx {
   bool pdl = true;
   bool use_graph = true;
   bool persistent = false;  // the whole step as one cooperative kernel
+  bool f32 = false;         // persistent step: fp32 activations
 
   const bf16* embed = nullptr;
   const bf16* final_norm = nullptr;
@@ -110,6 +113,9 @@ struct lcr_ctx {
   bf16* qkv = nullptr;
   bf16* attn = nullptr;
   bf16* act = nullptr;
+  float* qkv_f = nullptr;   // fp32 activations of the persistent step
+  float* attn_f = nullptr;
+  float* act_f = nullptr;
   float* logits = nullptr;
   float* partials = nullptr;
   unsigned* attn_ctr = nullptr;
@@ -231,6 +237,9 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.qkv = c->qkv;
   a.attn = c->attn;
   a.act = c->act;
+  a.qkv_f = c->qkv_f;
+  a.attn_f = c->attn_f;
+  a.act_f = c->act_f;
   a.logits = c->logits;
   a.partials = c->partials;
   a.attn_ctr = c->attn_ctr;
@@ -257,7 +266,7 @@ int enqueue_persistent_step(lcr_ctx* c) {
   }
   c->launches = 1;
   return mega_launch(a, d.hidden_size, d.num_heads * d.head_dim, d.intermediate_size, d.head_dim,
-                     d.num_heads / d.num_kv_heads, c->o.paged != 0, c->sms, c->stream);
+                     d.num_heads / d.num_kv_heads, c->o.paged != 0, c->f32, c->sms, c->stream);
 }
 
 // Launches one decode step on the context's stream.
@@ -501,6 +510,7 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   }
   c->persistent = (o.flags & kFlagNoPersistent) == 0 &&
                   mega_supported(d.hidden_size, qd, d.intermediate_size, d.head_dim, group);
+  c->f32 = (o.flags & kFlagFp32Act) != 0;
   // Split-K width: about 128 cached positions per split at max_seq (short
   // caches merge fewer partials; measured at config 2: 4 splits 1615 tok/s
   // against 1590 for 8..18), at most one (kv_head, split) CTA per SM.
@@ -534,6 +544,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   const size_t o_qkv = carve(sizeof(bf16) * (qd + 2 * kvd));
   const size_t o_attn = carve(sizeof(bf16) * qd);
   const size_t o_act = carve(sizeof(bf16) * d.intermediate_size);
+  const size_t o_qkvf = carve(sizeof(float) * (qd + 2 * kvd));
+  const size_t o_attnf = carve(sizeof(float) * qd);
+  const size_t o_actf = carve(sizeof(float) * d.intermediate_size);
   const size_t o_logits = carve(sizeof(float) * d.vocab_size);
   // Split partial records: (2 + D) floats in the multi-kernel step, (D + 4) in
   // the persistent one.
@@ -556,6 +569,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     c->qkv = reinterpret_cast<bf16*>(b + o_qkv);
     c->attn = reinterpret_cast<bf16*>(b + o_attn);
     c->act = reinterpret_cast<bf16*>(b + o_act);
+    c->qkv_f = reinterpret_cast<float*>(b + o_qkvf);
+    c->attn_f = reinterpret_cast<float*>(b + o_attnf);
+    c->act_f = reinterpret_cast<float*>(b + o_actf);
     c->logits = reinterpret_cast<float*>(b + o_logits);
     c->partials = reinterpret_cast<float*>(b + o_part);
     c->attn_ctr = reinterpret_cast<unsigned*>(b + o_actr);

@@ -43,7 +43,25 @@ namespace lcrb {
 enum GemvPro { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
 // EPI_ROPE (tcgen05 projection only): bf16 store with the rotate-half RoPE
 // applied to the q and k columns of a QKV projection.
-enum GemvEpi { EPI_STORE = 0, EPI_STORE_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS_ARGMAX = 4, EPI_ROPE = 5 };
+// Persistent step only: EPI_ACC64 adds y, as a 2^-32 fixed-point integer, into
+// an int64 accumulator shared by every CTA (a split-K partial; integer adds
+// commute, so the sum is the same whatever order the CTAs arrive in);
+// EPI_SWIGLU_F32 stores act = silu(gate) * up as fp32 (rounded through bf16
+// when round_out, as the reference stores it).
+enum GemvEpi { EPI_STORE = 0, EPI_STORE_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS_ARGMAX = 4, EPI_ROPE = 5,
+               EPI_ACC64 = 6, EPI_SWIGLU_F32 = 7 };
+
+// Fixed-point scale of the split-K accumulators (EPI_ACC64): 2^32.
+constexpr float kFixScale = 4294967296.0f;
+constexpr double kFixInv = 1.0 / 4294967296.0;
+
+__device__ __forceinline__ void red_add_fixed(unsigned long long* acc, float y) {
+  const long long v = __float2ll_rn(y * kFixScale);
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(acc), "l"(v) : "memory");
+}
+__device__ __forceinline__ float fixed_to_float(unsigned long long v) {
+  return static_cast<float>(static_cast<double>(static_cast<long long>(v)) * kFixInv);
+}
 
 struct GemvArgs {
   const bf16* w;      // [N][K]; SWIGLU: rows [0, F) gate, [F, 2F) up
@@ -72,6 +90,10 @@ struct GemvArgs {
   int32_t* history;       //   history[pos] = next token (nullable)
   int history_len;
   int advance;
+  unsigned long long* acc64;  // ACC64: fixed-point accumulators, indexed by output
+  int round_out;              // STORE_F32 / SWIGLU_F32: round through bf16 as the reference stores
+  int exact_resid;            // RESID: resid_sum += y in fp32 (resid = its bf16 copy), no bf16 rounding of y
+  int32_t* state_gen;         // LOGITS_ARGMAX: step generation, advanced by one (nullable)
   unsigned long long* wait_cycles;  // trace: SM cycles thread 0 waited on full stages (nullable)
   unsigned long long* stage_ns;     // trace: [s] stage s ready, [64 + s] released (nullable)
 };
@@ -151,10 +173,14 @@ __device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint
                                              int o0, int o1, uint64_t policy, uint32_t* status,
                                              PF* pf = nullptr, unsigned long long* issued = nullptr,
                                              unsigned long long* wait_cycles = nullptr,
-                                             unsigned long long* issue_ns = nullptr) {
+                                             unsigned long long* issue_ns = nullptr, int ld = 0,
+                                             int chunk0 = 0) {
   using G = GemvGeom<K>;
   constexpr int UNIT = SWIGLU ? G::RPS / 2 : G::RPS;
   constexpr int CHUNK_STEP = G::KC / 64;  // tensor-map chunk coordinate per stage
+  // A column tile of a wider matrix: rows `ld` elements apart, the tile
+  // starting at 64-column chunk `chunk0`.
+  const size_t row_pitch = static_cast<size_t>(ld > 0 ? ld : K);
   if ((smem_addr(ring) & 1023u) != 0) {
     if (status) atomicOr(status, kStatusBadSmem);
     return false;
@@ -181,20 +207,20 @@ __device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint
         bytes = G::TILE_BYTES;
         mbar_arrive_expect_tx(&full[slot], G::TILE_BYTES);
         if constexpr (SWIGLU) {
-          tma_load_4d(dst, map, 0, first, 0, c * CHUNK_STEP, &full[slot], policy);
+          tma_load_4d(dst, map, 0, first, 0, chunk0 + c * CHUNK_STEP, &full[slot], policy);
         } else {
-          tma_load_3d(dst, map, 0, first, c * CHUNK_STEP, &full[slot], policy);
+          tma_load_3d(dst, map, 0, first, chunk0 + c * CHUNK_STEP, &full[slot], policy);
         }
       } else {
         bytes = static_cast<unsigned long long>(SWIGLU ? 2 : 1) * rows * G::SEG_BYTES;
         mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(bytes));
-        const char* src = wbase + (static_cast<size_t>(first) * K + c * G::KC) * 2;
+        const char* src = wbase + (static_cast<size_t>(first) * row_pitch + chunk0 * 64 + c * G::KC) * 2;
         for (int r = 0; r < rows; ++r) {
-          bulk_g2s(dst + r * G::PITCH, src + static_cast<size_t>(r) * G::ROW_BYTES, G::SEG_BYTES,
+          bulk_g2s(dst + r * G::PITCH, src + static_cast<size_t>(r) * row_pitch * 2, G::SEG_BYTES,
                    &full[slot], policy);
           if constexpr (SWIGLU) {
             bulk_g2s(dst + (UNIT + r) * G::PITCH,
-                     src + (static_cast<size_t>(n_out) + r) * G::ROW_BYTES, G::SEG_BYTES, &full[slot],
+                     src + (static_cast<size_t>(n_out) + r) * row_pitch * 2, G::SEG_BYTES, &full[slot],
                      policy);
           }
         }
@@ -318,21 +344,35 @@ __device__ __forceinline__ void mma_x_rows(float (&d)[4], uint32_t a0, uint32_t 
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
+// d += A B with A rows 0-7 the bf16 x (high part) and rows 8-15 its bf16
+// remainder x - hi (low part): d[0], d[1] collect W x_hi and d[2], d[3]
+// W x_lo, so their sum is the product with x to about 16 significant bits
+// at no extra MMA (the rows are otherwise zero).
+__device__ __forceinline__ void mma_x_hilo(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Consumers (256 threads): dot products of the streamed rows [o0, o1) with
 // the staged input `xs` (bf16 [K] in shared memory, 16-byte aligned) on the
 // tensor pipe, partials of the WPG warps sharing a row tile combined through
 // `red` (kGemvRedFloats floats) once per segment, then the epilogue.
 // LOGITS_ARGMAX folds the packed (order key, ~index) maximum into `best`.
-// Uses named barrier 1.
-template <int K, int STAGES, int EPI>
+// Uses named barrier 1. With `xs_lo` (LO) the input is xs + xs_lo, the bf16
+// pair of an fp32 vector (mma_x_hilo).
+template <int K, int STAGES, int EPI, bool LO = false>
 __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full, uint64_t* empty,
                                              int& it, const GemvArgs& a, int o0, int o1,
                                              const bf16* xs, float* red, unsigned long long& best,
-                                             bool& failed) {
+                                             bool& failed, const bf16* xs_lo = nullptr) {
   using G = GemvGeom<K>;
   constexpr int RPS = G::RPS, WPG = G::WPG, STEPS = G::STEPS, CHUNKS = G::CHUNKS;
   constexpr int PAIRS = RPS / 2;
-  constexpr int UNIT = (EPI == EPI_SWIGLU) ? PAIRS : RPS;
+  constexpr int UNIT = (EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_F32) ? PAIRS : RPS;
   constexpr int SEG = G::SEG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = warp / WPG, ks = warp % WPG;
@@ -348,11 +388,16 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
   const uint32_t s_odd = static_cast<uint32_t>(((4 + piece) ^ r8) << 4);
   const uint32_t x_lane = smem_addr(xs) + static_cast<uint32_t>((ks * G::KW + (lane >> 3) * 8) * 2);
   const uint32_t ring_base = smem_addr(ring);
+  const uint32_t xl_lane = LO ? smem_addr(xs_lo) + (x_lane - smem_addr(xs)) : 0u;
   // With one stage per group the warp's x fragments never change.
   uint32_t xf[CHUNKS == 1 ? STEPS : 1][4];
+  uint32_t xl[(CHUNKS == 1 && LO) ? STEPS : 1][4];
   if constexpr (CHUNKS == 1) {
 #pragma unroll
-    for (int j = 0; j < STEPS; ++j) ldmatrix_x4(xf[j], x_lane + j * 64);
+    for (int j = 0; j < STEPS; ++j) {
+      ldmatrix_x4(xf[j], x_lane + j * 64);
+      if constexpr (LO) ldmatrix_x4(xl[j], xl_lane + j * 64);
+    }
   }
   const int n_units = (o1 - o0 + UNIT - 1) / UNIT;
   const bool timed = a.wait_cycles != nullptr && tid == 0;
@@ -373,17 +418,26 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
         const uint32_t st_base = ring_base + static_cast<uint32_t>(slot * kGemvSlotBytes);
 #pragma unroll
         for (int j = 0; j < STEPS; ++j) {
-          uint32_t wb[4], xa[4];
+          uint32_t wb[4], xa[4], xb[4];
           const uint32_t sw = s_lane + static_cast<uint32_t>((j >> 1) * G::RPS * 128) + ((j & 1) ? s_odd : s_even);
           ldmatrix_x4(wb, st_base + (whole ? sw : w_lane + j * 64));
           if constexpr (CHUNKS == 1) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) xa[q] = xf[j][q];
+            for (int q = 0; q < 4; ++q) {
+              xa[q] = xf[j][q];
+              if constexpr (LO) xb[q] = xl[j][q];
+            }
           } else {
             ldmatrix_x4(xa, x_lane + static_cast<uint32_t>(c * G::KC * 2) + j * 64);
+            if constexpr (LO) ldmatrix_x4(xb, xl_lane + static_cast<uint32_t>(c * G::KC * 2) + j * 64);
           }
-          mma_x_rows(acc[(2 * j) & 3], xa[0], xa[1], wb[0], wb[1]);
-          mma_x_rows(acc[(2 * j + 1) & 3], xa[2], xa[3], wb[2], wb[3]);
+          if constexpr (LO) {
+            mma_x_hilo(acc[(2 * j) & 3], xa[0], xb[0], xa[1], xb[1], wb[0], wb[1]);
+            mma_x_hilo(acc[(2 * j + 1) & 3], xa[2], xb[2], xa[3], xb[3], wb[2], wb[3]);
+          } else {
+            mma_x_rows(acc[(2 * j) & 3], xa[0], xa[1], wb[0], wb[1]);
+            mma_x_rows(acc[(2 * j + 1) & 3], xa[2], xa[3], wb[2], wb[3]);
+          }
         }
         __syncwarp();
         if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
@@ -392,8 +446,15 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
       if (lane < 4) {
         const int row = tile * 8 + 2 * lane;
         float* dst = red + ((u - seg0) * RPS + row) * WPG + ks;
-        dst[0] = (acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]);
-        dst[WPG] = (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]);
+        if constexpr (LO) {
+          dst[0] = ((acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0])) +
+                   ((acc[0][2] + acc[1][2]) + (acc[2][2] + acc[3][2]));
+          dst[WPG] = ((acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1])) +
+                     ((acc[0][3] + acc[1][3]) + (acc[2][3] + acc[3][3]));
+        } else {
+          dst[0] = (acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]);
+          dst[WPG] = (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]);
+        }
       }
     }
     named_sync(1, kGemvConsumers);  // the segment's partials are in shared memory
@@ -409,9 +470,11 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
       if constexpr (EPI == EPI_STORE) {
         a.y[out] = __ushort_as_bfloat16(f2bf(y));
       } else if constexpr (EPI == EPI_STORE_F32) {
-        a.yf[out] = y;
+        a.yf[out] = a.round_out ? rbf(y) : y;
       } else if constexpr (EPI == EPI_RESID) {
-        const float s = __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)), rbf(y));
+        const float s = a.exact_resid
+                            ? __fadd_rn(__ldcg(a.resid_sum + out), y)
+                            : __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)), rbf(y));
         a.resid[out] = __ushort_as_bfloat16(f2bf(s));
         a.resid_sum[out] = s;
       } else if constexpr (EPI == EPI_SWIGLU) {
@@ -422,6 +485,19 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
         const float g = rbf(y);
         const float silu = g / (1.0f + __expf(-g));
         a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
+      } else if constexpr (EPI == EPI_SWIGLU_F32) {
+        const float* ru = red + (un * RPS + r + PAIRS) * WPG;
+        float up = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPG; ++w) up += ru[w];
+        if (a.round_out) {
+          const float g = rbf(y);
+          a.yf[out] = rbf(g / (1.0f + __expf(-g)) * rbf(up));
+        } else {
+          a.yf[out] = y / (1.0f + __expf(-y)) * up;
+        }
+      } else if constexpr (EPI == EPI_ACC64) {
+        red_add_fixed(a.acc64 + out, y);
       } else if constexpr (EPI == EPI_LOGITS_ARGMAX) {
         a.yf[out] = y;
         const unsigned long long packed =
@@ -451,6 +527,7 @@ __device__ __forceinline__ void argmax_finish(const GemvArgs& a, unsigned long l
     *a.state_token = next;
     if (a.history != nullptr && pos >= 0 && pos < a.history_len) a.history[pos] = next;
     if (a.advance) *a.state_pos = pos + 1;
+    if (a.state_gen) *a.state_gen += 1;
   }
 }
 

@@ -4,10 +4,10 @@
 namespace lcrb {
 namespace {
 
-template <int H, int QD, int F, int D, int G, bool PAGED>
+template <int H, int QD, int F, int D, int G, bool PAGED, bool F32>
 int launch_t(const MegaArgs& a, int ctas, cudaStream_t stream) {
-  auto kernel = decode_step_kernel<H, QD, F, D, G, PAGED>;
-  constexpr size_t smem = MegaShape<H, QD, F, D, G, PAGED>::SMEM;
+  auto kernel = decode_step_kernel<H, QD, F, D, G, PAGED, F32>;
+  constexpr size_t smem = MegaShape<H, QD, F, D, G, PAGED, F32>::SMEM;
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)));
   int per_sm = 0;
@@ -28,6 +28,16 @@ int launch_t(const MegaArgs& a, int ctas, cudaStream_t stream) {
   return LCR_OK;
 }
 
+template <int H, int QD, int F, int D, int G>
+int launch_g(const MegaArgs& a, bool paged, bool f32, int ctas, cudaStream_t stream) {
+  if (paged) {
+    return f32 ? launch_t<H, QD, F, D, G, true, true>(a, ctas, stream)
+               : launch_t<H, QD, F, D, G, true, false>(a, ctas, stream);
+  }
+  return f32 ? launch_t<H, QD, F, D, G, false, true>(a, ctas, stream)
+             : launch_t<H, QD, F, D, G, false, false>(a, ctas, stream);
+}
+
 }  // namespace
 
 bool mega_supported(int hidden, int q_dim, int ffn, int head_dim, int group) {
@@ -38,16 +48,14 @@ bool mega_supported(int hidden, int q_dim, int ffn, int head_dim, int group) {
 int mega_max_splits(int ctas, int num_kv) { return ctas / num_kv; }
 
 int mega_launch(const MegaArgs& a, int hidden, int q_dim, int ffn, int head_dim, int group,
-                bool paged, int ctas, cudaStream_t stream) {
+                bool paged, bool f32, int ctas, cudaStream_t stream) {
   LCRB_REQUIRE(a.num_kv * a.splits <= ctas, LCR_ERR_SHAPE,
                "%d KV heads x %d splits exceed %d persistent CTAs", a.num_kv, a.splits, ctas);
   if (hidden == 2048 && q_dim == 2048 && ffn == 8192 && head_dim == 64 && group == 4) {
-    return paged ? launch_t<2048, 2048, 8192, 64, 4, true>(a, ctas, stream)
-                 : launch_t<2048, 2048, 8192, 64, 4, false>(a, ctas, stream);
+    return launch_g<2048, 2048, 8192, 64, 4>(a, paged, f32, ctas, stream);
   }
   if (hidden == 256 && q_dim == 256 && ffn == 1024 && head_dim == 64 && group == 2) {
-    return paged ? launch_t<256, 256, 1024, 64, 2, true>(a, ctas, stream)
-                 : launch_t<256, 256, 1024, 64, 2, false>(a, ctas, stream);
+    return launch_g<256, 256, 1024, 64, 2>(a, paged, f32, ctas, stream);
   }
   return fail(LCR_ERR_SHAPE, "no persistent decode kernel for hidden %d / q_dim %d / ffn %d", hidden,
               q_dim, ffn);

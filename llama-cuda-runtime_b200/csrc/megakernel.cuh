@@ -12,7 +12,21 @@
 //   GU    gate/up row pairs: RMSNorm prologue, SwiGLU epilogue
 //   DOWN  rows of down_proj, residual epilogue
 //
-// then the lm_head rows with the final norm and the argmax hand-off. Between
+// then the lm_head rows with the final norm and the argmax hand-off.
+//
+// Two arithmetic modes (template F32):
+//   F32 = true   activations stay fp32 end to end, as in the fp32 host
+//                evaluation: GEMV inputs are split into a bf16 pair hi + lo
+//                fed to the two halves of one m16n8k16 A operand (gemv.cuh,
+//                mma_x_hilo); q, k, v, the attention output, the residual
+//                stream and SwiGLU stay fp32. Only the KV cache holds bf16 (the
+//                reference's KvCacheView format). The ring has 5 stages: the
+//                staged input's low half takes the sixth stage's shared memory.
+//   F32 = false  the reference's storage rounding (src/model.cu:370-484):
+//                bf16 normed inputs, qkv, roped q/k, attention output,
+//                projections, residual stream and SwiGLU output, with the
+//                unrounded residual sum feeding the norm.
+// Between
 // phases the consumers meet at a grid barrier (an arrival counter with a
 // bounded acquire spin). The producer never waits at barriers: it walks the
 // same schedule -- this CTA's rows of every matrix, and the KV blocks of its
@@ -28,7 +42,9 @@
 namespace lcrb {
 
 constexpr int kMegaStageBytes = kGemvSlotBytes;
-constexpr int kMegaStages = 6;
+// Ring stages: 6, or 5 with fp32 activations.
+template <bool F32>
+constexpr int kMegaStages = F32 ? 5 : 6;
 // 8 consumer warps, the ring producer (warp 8) and the L2 prefetcher (warp 9).
 constexpr int kMegaThreads = kGemvConsumers + 64;
 constexpr int kMegaWarps = kGemvConsumers / 32;
@@ -53,10 +69,13 @@ struct MegaArgs {
   const float* inv_freq;
   int32_t* state;      // [0] token, [1] position
   bf16* x;
-  float* xsum;
+  float* xsum;         // unrounded residual sums (with fp32 activations: the residual stream)
   bf16* qkv;
   bf16* attn;
   bf16* act;
+  float* qkv_f;        // fp32 activations: q;k;v, the merged attention output, SwiGLU
+  float* attn_f;
+  float* act_f;
   float* logits;
   float* partials;     // [heads][splits][2 + D]
   unsigned* attn_ctr;  // [layers][num_kv]
@@ -130,6 +149,127 @@ __device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, u
   }
   named_sync(1, kGemvConsumers);
   return *s_abort == 0;
+}
+
+// ---------------------------------------------------------------------------
+// fp32-activation staging
+// ---------------------------------------------------------------------------
+
+// 8 fp32 values -> their bf16 pair (hi, lo = bf16(v - hi)) at chunk c.
+__device__ __forceinline__ void store_hilo8(const float (&v)[8], bf16* xs, bf16* xs_lo, int c) {
+  uint4 hi;
+  hi.x = pack_bf2(v[0], v[1]);
+  hi.y = pack_bf2(v[2], v[3]);
+  hi.z = pack_bf2(v[4], v[5]);
+  hi.w = pack_bf2(v[6], v[7]);
+  reinterpret_cast<uint4*>(xs)[c] = hi;
+  float h[8];
+  unpack8(hi, h);
+  uint4 lo;
+  lo.x = pack_bf2(v[0] - h[0], v[1] - h[1]);
+  lo.y = pack_bf2(v[2] - h[2], v[3] - h[3]);
+  lo.z = pack_bf2(v[4] - h[4], v[5] - h[5]);
+  lo.w = pack_bf2(v[6] - h[6], v[7] - h[7]);
+  reinterpret_cast<uint4*>(xs_lo)[c] = lo;
+}
+
+// RMSNorm of the fp32 residual stream `xsum` (or, when `embed` is given, of
+// the device token's embedding row, which CTA 0 also stores as the stream)
+// times `gain`, staged as the bf16 pair xs + xs_lo, every value fp32 up to the
+// pair's ~16 significant bits. Uses named barrier 1; complete on return.
+template <int K>
+__device__ __forceinline__ void mega_stage_norm_f32(const float* xsum, const bf16* embed, const int32_t* token,
+                                                    int vocab, uint32_t* status, bf16* x_out, float* xsum_out,
+                                                    const bf16* gain, float eps, bf16* xs, bf16* xs_lo,
+                                                    float* red8) {
+  constexpr int NC = K / 8;
+  constexpr int PER = (NC + kGemvConsumers - 1) / kGemvConsumers;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bf16* erow = nullptr;
+  if (embed != nullptr) {
+    int tok = __ldcg(token);
+    if (tok < 0 || tok >= vocab) {
+      if (tid == 0) atomicOr(status, kStatusBadToken);
+      tok = 0;
+    }
+    erow = embed + static_cast<size_t>(tok) * K;
+  }
+  float v[PER][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int c = tid + p * kGemvConsumers;
+    if (c >= NC) break;
+    if (erow != nullptr) {
+      const uint4 raw = ldg_cg16(erow + c * 8);
+      unpack8(raw, v[p]);
+      if (blockIdx.x == 0) {
+        *reinterpret_cast<uint4*>(x_out + c * 8) = raw;
+        *reinterpret_cast<float4*>(xsum_out + c * 8) = make_float4(v[p][0], v[p][1], v[p][2], v[p][3]);
+        *reinterpret_cast<float4*>(xsum_out + c * 8 + 4) = make_float4(v[p][4], v[p][5], v[p][6], v[p][7]);
+      }
+    } else {
+      const float4 a0 = __ldcg(reinterpret_cast<const float4*>(xsum + c * 8));
+      const float4 a1 = __ldcg(reinterpret_cast<const float4*>(xsum + c * 8 + 4));
+      v[p][0] = a0.x; v[p][1] = a0.y; v[p][2] = a0.z; v[p][3] = a0.w;
+      v[p][4] = a1.x; v[p][5] = a1.y; v[p][6] = a1.z; v[p][7] = a1.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(v[p][e], v[p][e], ss);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0) red8[warp] = ss;
+  named_sync(1, kGemvConsumers);
+  float total = 0.f;
+#pragma unroll
+  for (int w = 0; w < kGemvConsumers / 32; ++w) total += red8[w];
+  const float scale = rsqrtf(total / static_cast<float>(K) + eps);
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int c = tid + p * kGemvConsumers;
+    if (c >= NC) break;
+    float gf[8], n[8];
+    unpack8(ldg16(gain + c * 8), gf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) n[e] = __fmul_rn(__fmul_rn(v[p][e], scale), gf[e]);
+    store_hilo8(n, xs, xs_lo, c);
+  }
+  named_sync(1, kGemvConsumers);  // xs complete (and red8 free again)
+}
+
+// An fp32 vector of n values (a multiple of 8) staged as the bf16 pair
+// xs + xs_lo. Uses named barrier 1; complete on return.
+__device__ __forceinline__ void mega_stage_vec_f32(const float* src, int n, bf16* xs, bf16* xs_lo) {
+  for (int c = threadIdx.x; c < n / 8; c += kGemvConsumers) {
+    const float4 a0 = __ldcg(reinterpret_cast<const float4*>(src + c * 8));
+    const float4 a1 = __ldcg(reinterpret_cast<const float4*>(src + c * 8 + 4));
+    const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    store_hilo8(v, xs, xs_lo, c);
+  }
+  named_sync(1, kGemvConsumers);
+}
+
+// 8 fp32 dims of one head from this step's fp32 qkv row with the rotate-half
+// RoPE applied from the step's cos/sin table, kept in fp32.
+template <int D>
+__device__ __forceinline__ void rope8f(const float* head, int lig, const float* cs, float* outv) {
+  constexpr int HALF = D / 2;
+  const int d0 = lig * 8;
+  const int p0 = d0 < HALF ? d0 + HALF : d0 - HALF;
+  const float4 s0 = __ldcg(reinterpret_cast<const float4*>(head + d0));
+  const float4 s1 = __ldcg(reinterpret_cast<const float4*>(head + d0 + 4));
+  const float4 o0 = __ldcg(reinterpret_cast<const float4*>(head + p0));
+  const float4 o1 = __ldcg(reinterpret_cast<const float4*>(head + p0 + 4));
+  const float self[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  const float other[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+  const bool lo = d0 < HALF;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int i = (d0 + e) % HALF;
+    const float c = cs[i], s = cs[HALF + i];
+    outv[e] = lo ? (self[e] * c - other[e] * s) : (self[e] * c + other[e] * s);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -300,7 +440,7 @@ __device__ __forceinline__ bool mega_attn_produce(uint8_t* ring, uint64_t* full,
 // Consumers: one (KV head, split) item -> partials (or the output when there
 // is a single split); the last CTA of a KV head merges its splits.
 // `cs` is the step's RoPE table, `scratch` >= kMegaWarps * G * (D + 2) floats.
-template <int D, int G, int STAGES, bool PAGED>
+template <int D, int G, int STAGES, bool PAGED, bool F32>
 __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t* full,
                                                   uint64_t* empty, int& it, const MegaArgs& a,
                                                   int l, int pos, const float* cs, float* scratch,
@@ -319,16 +459,30 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
   // query, so one L2 round trip covers both.
   const bool has_new = pos >= item.begin && pos < item.end && grp == 0;
   uint4 k_self = make_uint4(0, 0, 0, 0), k_other = k_self, v_raw = k_self;
+  float k_newf[8], v_newf[8];
   if (has_new) {
-    const bf16* kh = a.qkv + qd + item.kvh * D;
-    k_self = ldg_cg16(kh + lig * 8);
-    k_other = ldg_cg16(kh + (lig * 8 < D / 2 ? lig * 8 + D / 2 : lig * 8 - D / 2));
-    v_raw = ldg_cg16(a.qkv + qd + kvd + item.kvh * D + lig * 8);
+    if constexpr (F32) {
+      rope8f<D>(a.qkv_f + qd + item.kvh * D, lig, cs, k_newf);
+      const float* vh = a.qkv_f + qd + kvd + item.kvh * D + lig * 8;
+      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(vh));
+      const float4 v1 = __ldcg(reinterpret_cast<const float4*>(vh + 4));
+      v_newf[0] = v0.x; v_newf[1] = v0.y; v_newf[2] = v0.z; v_newf[3] = v0.w;
+      v_newf[4] = v1.x; v_newf[5] = v1.y; v_newf[6] = v1.z; v_newf[7] = v1.w;
+    } else {
+      const bf16* kh = a.qkv + qd + item.kvh * D;
+      k_self = ldg_cg16(kh + lig * 8);
+      k_other = ldg_cg16(kh + (lig * 8 < D / 2 ? lig * 8 + D / 2 : lig * 8 - D / 2));
+      v_raw = ldg_cg16(a.qkv + qd + kvd + item.kvh * D + lig * 8);
+    }
   }
   float q[G][8], acc[G][8], m[G], l_[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, q[g]);
+    if constexpr (F32) {
+      rope8f<D>(a.qkv_f + (item.kvh * G + g) * D, lig, cs, q[g]);
+    } else {
+      rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, q[g]);
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       q[g][e] *= a.scale_log2;
@@ -389,10 +543,23 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
 
   // The new position (this step's token): rotate K, store K and V, attend.
   if (has_new) {
+    // The cache holds bf16; with fp32 activations this step attends to the
+    // unrounded K and V.
     float kf[8], vf[8];
-    rope8_from<D>(k_self, k_other, lig, cs, kf);
-    const uint4 vraw = v_raw;
-    unpack8(vraw, vf);
+    uint4 vraw;
+    if constexpr (F32) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kf[e] = k_newf[e];
+        vf[e] = v_newf[e];
+      }
+      vraw.x = pack_bf2(vf[0], vf[1]); vraw.y = pack_bf2(vf[2], vf[3]);
+      vraw.z = pack_bf2(vf[4], vf[5]); vraw.w = pack_bf2(vf[6], vf[7]);
+    } else {
+      rope8_from<D>(k_self, k_other, lig, cs, kf);
+      vraw = v_raw;
+      unpack8(vraw, vf);
+    }
     const long long off = kv_offset<PAGED>(a, l, item.kvh, pos, D);
     uint4 kw;
     kw.x = pack_bf2(kf[0], kf[1]); kw.y = pack_bf2(kf[2], kf[3]);
@@ -506,7 +673,14 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
       M = Mn;
     }
     if (sg == 0) {
-      *reinterpret_cast<uint4*>(a.attn + static_cast<size_t>(item.kvh * G + g) * D + d0) = merged_bf16x8(L, acc8);
+      if constexpr (F32) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        float* dst = a.attn_f + static_cast<size_t>(item.kvh * G + g) * D + d0;
+        *reinterpret_cast<float4*>(dst) = make_float4(acc8[0] * inv, acc8[1] * inv, acc8[2] * inv, acc8[3] * inv);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc8[4] * inv, acc8[5] * inv, acc8[6] * inv, acc8[7] * inv);
+      } else {
+        *reinterpret_cast<uint4*>(a.attn + static_cast<size_t>(item.kvh * G + g) * D + d0) = merged_bf16x8(L, acc8);
+      }
     }
   }
   if (tid == 0) *ctr = 0u;
@@ -518,13 +692,22 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
 // rounded to bf16 as the reference stores attn_out; beyond that the attention
 // phase has already merged it into `attn`. Uses named barrier 1; `xs` is
 // complete on return.
-template <int QD, int D>
-__device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos, bf16* xs) {
+// With fp32 activations the output is staged unrounded, as the bf16 pair
+// xs + xs_lo.
+template <int QD, int D, bool F32>
+__device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos, bf16* xs, bf16* xs_lo) {
   const int splits = mega_attn_splits(pos + 1, a.splits, MegaAttnGeom<D>::P);
   for (int c = threadIdx.x; c < QD / 8; c += kGemvConsumers) {
     const int col = c * 8;
     if (splits > kMegaPrologueMergeMax) {  // merged by the attention phase
-      reinterpret_cast<uint4*>(xs)[c] = ldg_cg16(a.attn + col);
+      if constexpr (F32) {
+        const float4 a0 = __ldcg(reinterpret_cast<const float4*>(a.attn_f + col));
+        const float4 a1 = __ldcg(reinterpret_cast<const float4*>(a.attn_f + col + 4));
+        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        store_hilo8(v, xs, xs_lo, c);
+      } else {
+        reinterpret_cast<uint4*>(xs)[c] = ldg_cg16(a.attn + col);
+      }
       continue;
     }
     const int h = col / D, d0 = col % D;
@@ -532,7 +715,15 @@ __device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos,
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     merge_split_records<D>(a.partials + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>, 0, splits, 1, d0, M, L,
                            acc);
-    reinterpret_cast<uint4*>(xs)[c] = merged_bf16x8(L, acc);
+    if constexpr (F32) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = acc[e] * inv;
+      store_hilo8(v, xs, xs_lo, c);
+    } else {
+      reinterpret_cast<uint4*>(xs)[c] = merged_bf16x8(L, acc);
+    }
   }
   named_sync(1, kGemvConsumers);
 }
@@ -667,20 +858,21 @@ __device__ __forceinline__ void mega_prefetch_loop(const MegaArgs& a, volatile u
 // The kernel
 // ---------------------------------------------------------------------------
 
-template <int H, int QD, int F, int D, int G, bool PAGED>
+template <int H, int QD, int F, int D, int G, bool PAGED, bool F32>
 struct MegaShape {
+  static constexpr int STAGES = kMegaStages<F32>;
   static constexpr int RED_FLOATS = kGemvRedFloats + 512;  // GEMV segments, attention scratch
   static_assert(kMegaWarps * G * (D + 2) <= RED_FLOATS, "attention scratch");
   static constexpr int XS = (H > F ? H : F) > QD ? (H > F ? H : F) : QD;
-  static constexpr size_t SMEM = static_cast<size_t>(kMegaStages) * kMegaStageBytes +
-                                 2 * kMegaStages * 8 + 64 + (RED_FLOATS + 8 + D) * 4 + 128 +
-                                 static_cast<size_t>(XS) * 2 + 64;
+  static constexpr size_t SMEM = static_cast<size_t>(STAGES) * kMegaStageBytes +
+                                 2 * STAGES * 8 + 64 + (RED_FLOATS + 8 + D) * 4 + 128 +
+                                 static_cast<size_t>(XS) * 2 * (F32 ? 2 : 1) + 64;
 };
 
-template <int H, int QD, int F, int D, int G, bool PAGED>
+template <int H, int QD, int F, int D, int G, bool PAGED, bool F32>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const MegaArgs a) {
-  using Shape = MegaShape<H, QD, F, D, G, PAGED>;
-  constexpr int STAGES = kMegaStages;
+  using Shape = MegaShape<H, QD, F, D, G, PAGED, F32>;
+  constexpr int STAGES = Shape::STAGES;
   constexpr int SB = kMegaStageBytes;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem;
@@ -694,6 +886,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
   float* red = red8 + 8;
   float* cs = red + Shape::RED_FLOATS;  // RoPE cos/sin [D]
   bf16* xs = align_smem<bf16>(cs + D, 128);  // staged input vector [max(H, QD, F)], 16-byte access
+  bf16* xs_lo = F32 ? xs + Shape::XS : nullptr;  // its low bf16 half (fp32 activations)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pos = __ldcg(a.state + 1);
@@ -804,39 +997,45 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.eps = a.eps;
         g.norm_w = w.input_norm;
         g.y = a.qkv;
-        if (l == 0) {
+        g.yf = a.qkv_f;
+        if constexpr (F32) {
+          mega_stage_norm_f32<H>(a.xsum, l == 0 ? a.embed : nullptr, a.state, a.vocab, a.status, a.x, a.xsum,
+                                 w.input_norm, a.eps, xs, xs_lo, red8);
+        } else if (l == 0) {
           g.embed = a.embed;
           g.token = a.state;
           g.vocab = a.vocab;
           g.x_out = a.x;
           g.xsum_out = a.xsum;
           gemv_stage_x<H, PRO_EMBED_NORM>(g, xs, red8);
-        pro_done();
         } else {
           g.x_in = a.x;
           g.xsum = a.xsum;
           gemv_stage_x<H, PRO_NORM>(g, xs, red8);
-        pro_done();
         }
+        pro_done();
         g.wait_cycles = cwait();
-        gemv_consume<H, STAGES, EPI_STORE>(ring, full, empty, it, g, gemv_share(nqkv, blockIdx.x, ctas),
-                                               gemv_share(nqkv, blockIdx.x + 1, ctas), xs, red, best, failed);
+        gemv_consume<H, STAGES, F32 ? EPI_STORE_F32 : EPI_STORE, F32>(ring, full, empty, it, g,
+                                                                      gemv_share(nqkv, blockIdx.x, ctas),
+                                                                      gemv_share(nqkv, blockIdx.x + 1, ctas), xs, red,
+                                                                      best, failed, xs_lo);
       }
       if (!(run = sync())) break;
       pro_done();  // attention: no separate prologue
-      mega_attn_consume<D, G, STAGES, PAGED>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
-                                             cwait());
+      mega_attn_consume<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
+                                                  cwait());
       if (!(run = sync())) break;
       {  // O
         GemvArgs g = {};
         g.status = a.status;
         g.resid = a.x;
         g.resid_sum = a.xsum;
-        mega_stage_attention<QD, D>(a, pos, xs);
+        g.exact_resid = F32 ? 1 : 0;
+        mega_stage_attention<QD, D, F32>(a, pos, xs, xs_lo);
         pro_done();
         g.wait_cycles = cwait();
-        gemv_consume<QD, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
-                                                gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed);
+        gemv_consume<QD, STAGES, EPI_RESID, F32>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
+                                                 gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed, xs_lo);
       }
       if (!(run = sync())) break;
       {  // GU
@@ -847,12 +1046,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.xsum = a.xsum;
         g.norm_w = w.post_norm;
         g.y = a.act;
-        gemv_stage_x<H, PRO_NORM>(g, xs, red8);
+        g.yf = a.act_f;
+        if constexpr (F32) {
+          mega_stage_norm_f32<H>(a.xsum, nullptr, nullptr, 0, a.status, nullptr, nullptr, w.post_norm, a.eps, xs,
+                                 xs_lo, red8);
+        } else {
+          gemv_stage_x<H, PRO_NORM>(g, xs, red8);
+        }
         pro_done();
         g.wait_cycles = cwait();
         g.stage_ns = (ctrace && l == kMegaTraceStageLayer) ? ctrace + kMegaTraceStages + 64 : nullptr;
-        gemv_consume<H, STAGES, EPI_SWIGLU>(ring, full, empty, it, g, gemv_share(F, blockIdx.x, ctas),
-                                                gemv_share(F, blockIdx.x + 1, ctas), xs, red, best, failed);
+        gemv_consume<H, STAGES, F32 ? EPI_SWIGLU_F32 : EPI_SWIGLU, F32>(ring, full, empty, it, g,
+                                                                        gemv_share(F, blockIdx.x, ctas),
+                                                                        gemv_share(F, blockIdx.x + 1, ctas), xs, red,
+                                                                        best, failed, xs_lo);
       }
       if (!(run = sync())) break;
       {  // DOWN
@@ -861,11 +1068,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.x_in = a.act;
         g.resid = a.x;
         g.resid_sum = a.xsum;
-        gemv_stage_x<F, PRO_PLAIN>(g, xs, red8);
+        g.exact_resid = F32 ? 1 : 0;
+        if constexpr (F32) {
+          mega_stage_vec_f32(a.act_f, F, xs, xs_lo);
+        } else {
+          gemv_stage_x<F, PRO_PLAIN>(g, xs, red8);
+        }
         pro_done();
         g.wait_cycles = cwait();
-        gemv_consume<F, STAGES, EPI_RESID>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
-                                               gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed);
+        gemv_consume<F, STAGES, EPI_RESID, F32>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
+                                                gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed, xs_lo);
       }
       if (!(run = sync())) break;
     }
@@ -877,13 +1089,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       g.xsum = a.xsum;
       g.norm_w = a.final_norm;
       g.yf = a.logits;
-      gemv_stage_x<H, PRO_NORM>(g, xs, red8);
-        pro_done();
+      if constexpr (F32) {
+        mega_stage_norm_f32<H>(a.xsum, nullptr, nullptr, 0, a.status, nullptr, nullptr, a.final_norm, a.eps, xs,
+                               xs_lo, red8);
+      } else {
+        gemv_stage_x<H, PRO_NORM>(g, xs, red8);
+      }
+      pro_done();
       g.wait_cycles = cwait();
-      gemv_consume<H, STAGES, EPI_LOGITS_ARGMAX>(ring, full, empty, it, g,
-                                                     gemv_share(a.vocab, blockIdx.x, ctas),
-                                                     gemv_share(a.vocab, blockIdx.x + 1, ctas), xs, red,
-                                                     best, failed);
+      gemv_consume<H, STAGES, EPI_LOGITS_ARGMAX, F32>(ring, full, empty, it, g,
+                                                      gemv_share(a.vocab, blockIdx.x, ctas),
+                                                      gemv_share(a.vocab, blockIdx.x + 1, ctas), xs, red,
+                                                      best, failed, xs_lo);
       if (best != 0ull) atomicMax(cta_best, best);
       if (ctrace && tid == 0) ctrace[kMegaTraceProducer - 1] = globaltimer_ns();
     }

@@ -81,6 +81,11 @@ def main(argv=None) -> int:
     ap.add_argument("--peak-bandwidth", type=float, default=8000.0, help="GB/s")
     ap.add_argument("--bench", action="store_true")
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--fp32-act", action="store_true",
+                    help="persistent step with fp32 activations (default: the reference's "
+                         "bf16 storage rounding)")
+    ap.add_argument("--no-persistent", action="store_true",
+                    help="the multi-kernel step instead of the persistent kernel")
     ap.add_argument("--trace", action="store_true",
                     help="per-phase timeline of the last decode step (persistent kernel)")
     ap.add_argument("--trace-out", default=None,
@@ -99,7 +104,9 @@ def main(argv=None) -> int:
     m = rt.Model(block, device=args.device, max_seq=max_seq, paged=args.paged,
                  page_size=args.page_size, attention_splits=args.splits,
                  page_order_seed=args.page_order_seed,
-                 flags=rt.FLAG_TRACE if args.trace else 0)
+                 flags=(rt.FLAG_TRACE if args.trace else 0)
+                 | (rt.FLAG_FP32_ACT if args.fp32_act else 0)
+                 | (rt.FLAG_NO_PERSISTENT if args.no_persistent else 0))
     load_ms = (time.perf_counter() - t0) * 1000
 
     t0 = time.perf_counter()

@@ -28,6 +28,11 @@ FLAG_NO_PDL = 1
 FLAG_NO_GRAPH = 2
 FLAG_NO_PERSISTENT = 4
 FLAG_TRACE = 8
+# The persistent step with fp32 activations (bf16 hi/lo GEMV inputs, fp32
+# q/k/v, attention output, residual stream and SwiGLU) instead of the
+# reference's bf16 storage rounding: closer to the fp32 host evaluation, about
+# 10 % slower.
+FLAG_FP32_ACT = 16
 
 
 class LcrError(RuntimeError):

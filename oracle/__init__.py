@@ -19,6 +19,7 @@ REF_LIB_PATH = os.path.join(HERE, "_ref", "libref_host.so")
 MODE_FP32 = 0
 MODE_BF16 = 1
 MODE_BF16_REORDERED = 2
+MODE_FP32_KV_BF16 = 3
 
 
 def build(ref: bool = False) -> None:
@@ -96,6 +97,9 @@ def lib() -> ctypes.CDLL:
                                     ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.orc_gemv.argtypes = [_f32p, _u16p, _u16p, ctypes.c_int, ctypes.c_int]
         L.orc_set_threads.argtypes = [ctypes.c_int]
+        L.orc_prefill.restype = ctypes.c_int
+        L.orc_prefill.argtypes = [_P(_Config), _P(_Weights), ctypes.c_void_p, _P(ctypes.c_int32),
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
         _lib = L
     return _lib
 
@@ -161,6 +165,18 @@ class Model:
         if rc != 0:
             raise ValueError(f"oracle decode rejected token {token} at position {position}")
         return (logits, tp) if taps else logits
+
+    def prefill(self, tokens, start: int, mode: int = MODE_FP32, logits: bool = True):
+        """Tokens at positions start..start+len-1 as one chunk (orc_prefill):
+        appends their K/V to the cache and returns the last row's logits."""
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.empty(self.geom.vocab_size, dtype=np.float32) if logits else None
+        rc = lib().orc_prefill(ctypes.byref(self.cfg), ctypes.byref(self.w), self.state,
+                               _ptr(ids, ctypes.c_int32), int(ids.size), int(start), int(mode),
+                               _ptr(out, ctypes.c_float) if logits else None)
+        if rc != 0:
+            raise ValueError(f"oracle prefill rejected {ids.size} tokens at position {start} (rc {rc})")
+        return out
 
 
 def argmax(logits: np.ndarray) -> int:

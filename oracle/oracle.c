@@ -325,6 +325,7 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
                int token, int position, int mode, float* logits, float* taps) {
   if (token < 0 || token >= c->vocab || position < 0 || position >= s->max_seq) return 1;
   const int bf = (mode == ORC_MODE_BF16 || mode == ORC_MODE_BF16_REORDERED);
+  const int kvbf = bf || mode == ORC_MODE_FP32_KV_BF16; /* the cache stores bf16 */
   void (*gemv)(float*, const uint16_t*, const float*, int, int) =
       mode == ORC_MODE_BF16_REORDERED ? gemv_f_reordered : gemv_f;
   const int H = c->hidden, F = c->ffn, d = c->head_dim;
@@ -367,8 +368,9 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
       rope_head(kr, qkv + qd + (size_t)h * d, s->inv_freq, position, d);
       const size_t base = (((size_t)l * c->kv_heads + h) * s->max_seq + position) * d;
       for (int i = 0; i < d; ++i) {
-        s->k[base + i] = bf ? rb(kr[i]) : kr[i];
-        s->v[base + i] = qkv[qd + kvd + (size_t)h * d + i];
+        s->k[base + i] = kvbf ? rb(kr[i]) : kr[i];
+        const float v = qkv[qd + kvd + (size_t)h * d + i];
+        s->v[base + i] = kvbf ? rb(v) : v;
       }
     }
 
@@ -437,6 +439,216 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
 
   free(x); free(xsum); free(normed); free(qkv); free(qr); free(attn);
   free(proj); free(gu); free(act); free(sc);
+  return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Chunked prefill: Model::prefill -> run_layers(n, start)                   */
+/* (src/model.cu:308-345, 370-484, attention 509-560)                        */
+/* ------------------------------------------------------------------------ */
+
+#include <immintrin.h>
+
+static inline float hsum8(__m256 v) {
+  float t[8];
+  _mm256_storeu_ps(t, v);
+  double s = 0.0;
+  for (int i = 0; i < 8; ++i) s += t[i];
+  return (float)s;
+}
+
+/* Y[t * ldy + r] = sum_k W[r][k] X[t][k] for n rows of X (cols a multiple of
+ * 8): the chunk's projection as one GEMM, gemm_nt of src/model.cu:38-45 with
+ * fp32 accumulation. Weight rows are widened once per 8-row block; each
+ * (2 tokens x 2 rows) tile keeps eight fp32 lanes per product and sums the
+ * lanes in double. */
+static void gemm_f(float* Y, int ldy, const uint16_t* W, const float* X, int n,
+                   int rows, int cols) {
+#pragma omp parallel
+  {
+    float* wf = (float*)aligned_alloc(32, sizeof(float) * 8 * (size_t)cols);
+#pragma omp for schedule(dynamic, 1)
+    for (int r0 = 0; r0 < rows; r0 += 8) {
+      const int nr = rows - r0 < 8 ? rows - r0 : 8;
+      for (int r = 0; r < nr; ++r) {
+        const uint16_t* src = W + (size_t)(r0 + r) * cols;
+        for (int k = 0; k < cols; ++k) wf[(size_t)r * cols + k] = orc_bf16_to_float(src[k]);
+      }
+      for (int t = 0; t < n; t += 2) {
+        const int nt = n - t < 2 ? n - t : 2;
+        const float* x0 = X + (size_t)t * cols;
+        const float* x1 = X + (size_t)(t + nt - 1) * cols;
+        for (int r = 0; r < nr; r += 2) {
+          const int r1 = r + 1 < nr ? r + 1 : r;
+          const float* w0 = wf + (size_t)r * cols;
+          const float* w1 = wf + (size_t)r1 * cols;
+          __m256 a00 = _mm256_setzero_ps(), a01 = a00, a10 = a00, a11 = a00;
+          for (int k = 0; k < cols; k += 8) {
+            const __m256 xv0 = _mm256_loadu_ps(x0 + k), xv1 = _mm256_loadu_ps(x1 + k);
+            const __m256 wv0 = _mm256_load_ps(w0 + k), wv1 = _mm256_load_ps(w1 + k);
+            a00 = _mm256_fmadd_ps(xv0, wv0, a00);
+            a01 = _mm256_fmadd_ps(xv0, wv1, a01);
+            a10 = _mm256_fmadd_ps(xv1, wv0, a10);
+            a11 = _mm256_fmadd_ps(xv1, wv1, a11);
+          }
+          Y[(size_t)t * ldy + r0 + r] = hsum8(a00);
+          if (r1 != r) Y[(size_t)t * ldy + r0 + r1] = hsum8(a01);
+          if (nt == 2) {
+            Y[(size_t)(t + 1) * ldy + r0 + r] = hsum8(a10);
+            if (r1 != r) Y[(size_t)(t + 1) * ldy + r0 + r1] = hsum8(a11);
+          }
+        }
+      }
+    }
+    free(wf);
+  }
+}
+
+static inline float dot8n(const float* a, const float* b, int d) {
+  __m256 acc = _mm256_setzero_ps();
+  for (int i = 0; i < d; i += 8) acc = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), acc);
+  return hsum8(acc);
+}
+
+int orc_prefill(const orc_config* c, const orc_weights* w, orc_state* s,
+                const int32_t* tokens, int n, int start, int mode,
+                float* last_logits) {
+  if (n <= 0 || start < 0 || start + n > s->max_seq) return 1;
+  if (mode != ORC_MODE_FP32 && mode != ORC_MODE_BF16 && mode != ORC_MODE_FP32_KV_BF16) return 2;
+  for (int t = 0; t < n; ++t) {
+    if (tokens[t] < 0 || tokens[t] >= c->vocab) return 1;
+  }
+  const int bf = mode == ORC_MODE_BF16;
+  const int kvbf = bf || mode == ORC_MODE_FP32_KV_BF16;
+  const int H = c->hidden, F = c->ffn, d = c->head_dim;
+  const int qd = c->heads * d, kvd = c->kv_heads * d, group = c->heads / c->kv_heads;
+  const int nqkv = qd + 2 * kvd;
+  if (H % 8 || F % 8 || d % 8 || qd % 8) return 2;
+  const float scale = 1.0f / sqrtf((float)d);
+  const size_t N = (size_t)n;
+
+  float* x = (float*)malloc(sizeof(float) * N * H);
+  float* xsum = (float*)malloc(sizeof(float) * N * H);
+  float* normed = (float*)malloc(sizeof(float) * N * (H > qd ? H : qd));
+  float* qkv = (float*)malloc(sizeof(float) * N * nqkv);
+  float* qr = (float*)malloc(sizeof(float) * N * qd);
+  float* attn = (float*)malloc(sizeof(float) * N * qd);
+  float* proj = (float*)malloc(sizeof(float) * N * H);
+  float* gu = (float*)malloc(sizeof(float) * N * 2 * F);
+  float* act = (float*)malloc(sizeof(float) * N * F);
+
+  for (size_t t = 0; t < N; ++t) {
+    for (int i = 0; i < H; ++i) x[t * H + i] = orc_bf16_to_float(w->embed[(size_t)tokens[t] * H + i]);
+  }
+  memcpy(xsum, x, sizeof(float) * N * H);
+
+  for (int l = 0; l < c->layers; ++l) {
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < n; ++t) {
+      rmsnorm_f(normed + (size_t)t * H, x + (size_t)t * H, xsum + (size_t)t * H, w->input_norm[l], H, c->eps, bf);
+    }
+    gemm_f(qkv, nqkv, w->qkv[l], normed, n, nqkv, H);
+    if (bf) orc_round_bf16_inplace(qkv, N * nqkv);
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < n; ++t) {
+      const int pos = start + t;
+      const float* row = qkv + (size_t)t * nqkv;
+      for (int h = 0; h < c->heads; ++h) {
+        rope_head(qr + (size_t)t * qd + (size_t)h * d, row + (size_t)h * d, s->inv_freq, pos, d);
+      }
+      float kr[256];
+      for (int h = 0; h < c->kv_heads; ++h) {
+        rope_head(kr, row + qd + (size_t)h * d, s->inv_freq, pos, d);
+        const size_t base = (((size_t)l * c->kv_heads + h) * s->max_seq + pos) * d;
+        for (int i = 0; i < d; ++i) {
+          s->k[base + i] = kvbf ? rb(kr[i]) : kr[i];
+          const float v = row[qd + kvd + (size_t)h * d + i];
+          s->v[base + i] = kvbf ? rb(v) : v;
+        }
+      }
+    }
+    if (bf) orc_round_bf16_inplace(qr, N * qd);
+    /* causal GQA attention of every chunk row over the cache up to its own
+       position, q scaled once, fp32 softmax */
+#pragma omp parallel
+    {
+      float* sc = (float*)malloc(sizeof(float) * (size_t)(start + n));
+      float qs[256], acc[256];
+#pragma omp for schedule(dynamic, 4) collapse(2)
+      for (int t = 0; t < n; ++t) {
+        for (int h = 0; h < c->heads; ++h) {
+          const int seq = start + t + 1, kv = h / group;
+          const float* kb = s->k + (((size_t)l * c->kv_heads + kv) * s->max_seq) * d;
+          const float* vb = s->v + (((size_t)l * c->kv_heads + kv) * s->max_seq) * d;
+          for (int i = 0; i < d; ++i) qs[i] = qr[(size_t)t * qd + (size_t)h * d + i] * scale;
+          float mx = -INFINITY;
+          for (int p = 0; p < seq; ++p) {
+            sc[p] = dot8n(qs, kb + (size_t)p * d, d);
+            if (sc[p] > mx) mx = sc[p];
+          }
+          double sum = 0.0;
+          for (int p = 0; p < seq; ++p) {
+            sc[p] = (float)exp((double)sc[p] - mx);
+            sum += sc[p];
+          }
+          for (int i = 0; i < d; ++i) acc[i] = 0.f;
+          for (int p = 0; p < seq; ++p) {
+            const __m256 pv = _mm256_set1_ps(sc[p]);
+            for (int i = 0; i < d; i += 8) {
+              _mm256_storeu_ps(acc + i, _mm256_fmadd_ps(pv, _mm256_loadu_ps(vb + (size_t)p * d + i),
+                                                        _mm256_loadu_ps(acc + i)));
+            }
+          }
+          for (int i = 0; i < d; ++i) attn[(size_t)t * qd + (size_t)h * d + i] = (float)(acc[i] / sum);
+        }
+      }
+      free(sc);
+    }
+    if (bf) orc_round_bf16_inplace(attn, N * qd);
+
+    gemm_f(proj, H, w->o[l], attn, n, H, qd);
+    if (bf) orc_round_bf16_inplace(proj, N * H);
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < n; ++t) {
+      float* xr = x + (size_t)t * H;
+      float* sr = xsum + (size_t)t * H;
+      for (int i = 0; i < H; ++i) {
+        sr[i] = xr[i] + proj[(size_t)t * H + i];
+        xr[i] = bf ? rb(sr[i]) : sr[i];
+      }
+      rmsnorm_f(normed + (size_t)t * H, xr, sr, w->post_norm[l], H, c->eps, bf);
+    }
+
+    gemm_f(gu, 2 * F, w->gate_up[l], normed, n, 2 * F, H);
+    if (bf) orc_round_bf16_inplace(gu, N * 2 * F);
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < n; ++t) {
+      for (int i = 0; i < F; ++i) {
+        const float a = silu_f(gu[(size_t)t * 2 * F + i]) * gu[(size_t)t * 2 * F + F + i];
+        act[(size_t)t * F + i] = bf ? rb(a) : a;
+      }
+    }
+
+    gemm_f(proj, H, w->down[l], act, n, H, F);
+    if (bf) orc_round_bf16_inplace(proj, N * H);
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < n; ++t) {
+      float* xr = x + (size_t)t * H;
+      float* sr = xsum + (size_t)t * H;
+      for (int i = 0; i < H; ++i) {
+        sr[i] = xr[i] + proj[(size_t)t * H + i];
+        xr[i] = bf ? rb(sr[i]) : sr[i];
+      }
+    }
+  }
+
+  if (last_logits) {
+    const size_t t = N - 1;
+    rmsnorm_f(normed, x + t * H, xsum + t * H, w->final_norm, H, c->eps, bf);
+    gemv_f(last_logits, w->lm_head, normed, c->vocab, H);
+  }
+  free(x); free(xsum); free(normed); free(qkv); free(qr); free(attn);
+  free(proj); free(gu); free(act);
   return 0;
 }
 

@@ -33,6 +33,10 @@
  *   ORC_MODE_BF16_REORDERED  the same with every dot product summed in the
  *                     opposite order: the spread between the two bf16 modes
  *                     is the reproducibility floor of the algorithm itself.
+ *   ORC_MODE_FP32_KV_BF16  fp32 activations with the K/V cache stored as bf16
+ *                     (the reference's cache format, src/kv_cache.cuh:33-57):
+ *                     the closest any implementation on that cache can get to
+ *                     ORC_MODE_FP32.
  *
  * Parity pins: the RoPE table against tests/test_config.cpp:120-182, sampling
  * against tests/test_kernels.cu:468-508, page accounting against
@@ -51,7 +55,7 @@
 extern "C" {
 #endif
 
-enum { ORC_MODE_FP32 = 0, ORC_MODE_BF16 = 1, ORC_MODE_BF16_REORDERED = 2 };
+enum { ORC_MODE_FP32 = 0, ORC_MODE_BF16 = 1, ORC_MODE_BF16_REORDERED = 2, ORC_MODE_FP32_KV_BF16 = 3 };
 
 typedef struct {
   int hidden, ffn, layers, heads, kv_heads, head_dim, vocab;
@@ -96,6 +100,17 @@ void orc_state_reset(orc_state* s);
 int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
                int token, int position, int mode, float* logits, float* taps);
 void orc_set_threads(int n);
+/* n consecutive tokens at positions start..start+n-1 as one chunk (the
+ * reference's chunked prefill, src/model.cu:308-345): the projections as
+ * GEMMs over the chunk, causal attention of each row over the cache up to its
+ * own position; the K/V rows are appended to the state's cache. Writes the
+ * last row's [vocab] logits when last_logits is not NULL. ORC_MODE_FP32 and
+ * ORC_MODE_BF16 only (the same rounding points as orc_decode; the summation
+ * order of the chunk GEMM differs from the decode GEMV). Returns 0 on
+ * success. */
+int orc_prefill(const orc_config* c, const orc_weights* w, orc_state* s,
+                const int32_t* tokens, int n, int start, int mode,
+                float* last_logits);
 
 /* ---- individual kernels' maths, for the per-kernel parity tests ---- */
 void orc_rmsnorm(float* out, const uint16_t* x, const uint16_t* weight,

@@ -33,28 +33,41 @@ def tiny():
     return block, rt.upload_block(block)
 
 
-def test_tiny_prefill_and_greedy_vs_oracle(tiny):
+# With fp32 activations (FLAG_FP32_ACT) the only rounding left is the bf16 KV
+# cache, so the step tracks the oracle's fp32-with-bf16-cache mode closely.
+TINY_F32_ABS = 3e-3
+
+
+@pytest.mark.parametrize("flags", [0, rt.FLAG_FP32_ACT])
+def test_tiny_prefill_and_greedy_vs_oracle(tiny, flags):
+    """Prompt + 16 greedy steps on the tiny model, every step within the
+    north-star gates of the fp32 oracle; the reference rounding (default)
+    also within 1e-2 of the bf16-storage oracle, fp32 activations within 3e-3
+    of the oracle's fp32 evaluation over a bf16 KV cache."""
     block, wdev = tiny
     prompt = ck.prompt_ids(0, 32)
-    m = rt.Model(block, wdev, max_seq=64)
+    m = rt.Model(block, wdev, max_seq=64, flags=flags)
+    own_mode, own_tol = ((oracle.MODE_FP32_KV_BF16, TINY_F32_ABS) if flags
+                         else (oracle.MODE_BF16, 1e-2))
     ref32 = oracle.Model(block, 64)
-    ref16 = oracle.Model(block, 64)
+    own = oracle.Model(block, 64)
     m.prefill(prompt)
     for pos, tok in enumerate(prompt):
         l32 = ref32.decode(int(tok), pos, oracle.MODE_FP32)
-        l16 = ref16.decode(int(tok), pos, oracle.MODE_BF16)
+        lown = own.decode(int(tok), pos, own_mode)
     got = m.logits_to_host()
-    assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS
-    assert np.abs(got - l16).max() <= 1e-2
     pos = len(prompt)
-    for step in range(16):
+    for step in range(17):
+        assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS, step
+        assert np.abs(got - lown).max() <= own_tol, step
+        if step == 16:
+            break
         tok = int(np.argmax(got))
-        assert tok == oracle.argmax(l16), f"step {step}: greedy id differs from the bf16 oracle"
+        assert tok == oracle.argmax(lown), f"step {step}: greedy id differs from the oracle"
         m.decode(tok)
         got = m.logits_to_host()
         l32 = ref32.decode(tok, pos, oracle.MODE_FP32)
-        l16 = ref16.decode(tok, pos, oracle.MODE_BF16)
-        assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS, step
+        lown = own.decode(tok, pos, own_mode)
         pos += 1
 
 
@@ -83,18 +96,27 @@ def test_device_greedy_loop_matches_host_loop(tiny):
                                      dict(flags=rt.FLAG_NO_PERSISTENT | rt.FLAG_NO_GRAPH,
                                           paged=True, page_order_seed=3),
                                      dict(attention_splits=3), dict(gemv_ctas=37,
-                                                                    flags=rt.FLAG_NO_PERSISTENT)])
+                                                                    flags=rt.FLAG_NO_PERSISTENT),
+                                     dict(flags=rt.FLAG_FP32_ACT, paged=True, page_order_seed=5)])
 def test_step_variants_are_bit_identical(tiny, variant):
+    """Layout and scheduling options of the step change no result bit; a
+    different split or CTA count, or the multi-kernel step, changes only the
+    fp32 summation order; fp32 activations stay within the north-star gate of
+    the reference rounding."""
     block, wdev = tiny
     prompt = ck.prompt_ids(3, 40)
+    multi = variant.get("flags", 0) & rt.FLAG_NO_PERSISTENT
     base = rt.Model(block, wdev, max_seq=96)
     other = rt.Model(block, wdev, max_seq=96, **variant)
     base.prefill(prompt)
     other.prefill(prompt)
     a, b = base.logits_to_host(), other.logits_to_host()
-    order_changes = ("attention_splits" in variant or "gemv_ctas" in variant or
-                     variant.get("flags", 0) & rt.FLAG_NO_PERSISTENT)
-    if order_changes:
+    order_changes = ("attention_splits" in variant or "gemv_ctas" in variant or multi)
+    if variant.get("flags", 0) == rt.FLAG_FP32_ACT:
+        # fp32 activations against the reference rounding: the bf16 storage
+        # of the intermediate tensors, not only the order
+        assert np.abs(a - b).max() < 3e-2
+    elif order_changes:
         # a different split / CTA count, or the multi-kernel step's attention
         # partition, changes the fp32 summation order only
         assert np.abs(a - b).max() < 1e-3
@@ -269,3 +291,75 @@ def test_1b_config3_paged_shuffled_matches_contiguous():
     assert np.array_equal(paged.logits_to_host(), flat.logits_to_host())
     paged.close()
     flat.close()
+
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+# Gates against the fp32 host evaluation at 1B (tests/golden/make_golden_1b.py).
+# The fp32-activation step sits on the floor of the bf16 KV cache format: the
+# oracle itself, fp32 everywhere but the cache, is 0.033 from fp32 on the
+# first logits of configuration 2. The reference rounding sits on the floor of
+# its own algorithm (two summation orders differ by 0.07-0.10).
+FIXTURE_GATES = {0: dict(full=0.15, top=0.12), rt.FLAG_FP32_ACT: dict(full=0.04, top=0.03)}
+
+
+def _fixture_run(m, fx, steps, gates, label):
+    """Teacher-forces the fp32 oracle's greedy ids: the first logits against
+    the fixture's full vector, every step's top-32 logits against the
+    fixture's, and the greedy id equal to the fixture's wherever its top-2 gap
+    is more than twice the step's measured distance (a near tie otherwise)."""
+    got = m.logits_to_host()
+    full = float(np.abs(got - fx["logits0"]).max())
+    c = cos(got, fx["logits0"])
+    worst, ties, flips = 0.0, [], []
+    for s in range(steps):
+        ti, tv = fx["top_idx"][s], fx["top_val"][s]
+        dist = float(np.abs(got[ti] - tv).max())
+        worst = max(worst, dist)
+        if int(np.argmax(got)) != int(fx["ids"][s]):
+            (ties if float(fx["gap"][s]) < 2.0 * dist else flips).append((s, float(fx["gap"][s])))
+        if s + 1 < steps:
+            m.decode(int(fx["ids"][s]))
+            got = m.logits_to_host()
+    print(f"{label}: first logits max-abs {full:.4f} cos {c:.6f}; top-32 worst {worst:.4f} "
+          f"over {steps} steps; near-tie flips {ties}")
+    assert not flips, flips
+    assert c >= MIN_COS
+    assert full <= gates["full"] and worst <= gates["top"]
+    return full, worst, ties
+
+
+@pytest.mark.parametrize("flags", [0, rt.FLAG_FP32_ACT])
+def test_1b_config2_vs_fp32_fixture(flags):
+    """Configuration 2 against the committed fp32 oracle run
+    (c2_fp32_1b.npz): 256 teacher-forced steps, then a free-running greedy
+    generation whose first divergence from the oracle's ids (if any) must be
+    at a near tie."""
+    fx = np.load(os.path.join(GOLDEN, "c2_fp32_1b.npz"))
+    block = ck.cached(ck.LLAMA_3_2_1B, 1)
+    wdev = rt.upload_block(block, 0)
+    m = rt.Model(block, wdev, max_seq=512, flags=flags)
+    m.prefill(fx["prompt"])
+    full, worst, _ = _fixture_run(m, fx, 256, FIXTURE_GATES[flags], f"config 2 flags {flags}")
+    free = rt.Model(block, wdev, max_seq=512, flags=flags)
+    free.prefill(fx["prompt"])
+    first = int(np.argmax(free.logits_to_host()))
+    ids = np.concatenate([[first], free.generate_greedy(first, 255)])
+    diverge = np.flatnonzero(ids != fx["ids"])
+    at = int(diverge[0]) if diverge.size else None
+    print(f"config 2 flags {flags}: free-running greedy ids equal to the fp32 oracle's for "
+          f"{256 if at is None else at} of 256 steps" +
+          ("" if at is None else f" (first divergence at a top-2 gap of {float(fx['gap'][at]):.4f})"))
+    if at is not None:
+        assert float(fx["gap"][at]) < 2.0 * worst, "free-running ids left the oracle's at a clear margin"
+
+
+def test_1b_config3_vs_fp32_fixture():
+    """Configuration 3 (8192-id prompt, paged cache in shuffled physical
+    order) against the committed fp32 oracle run (c3_fp32_1b.npz): the logits
+    after the prompt and 16 teacher-forced greedy steps."""
+    fx = np.load(os.path.join(GOLDEN, "c3_fp32_1b.npz"))
+    block = ck.cached(ck.LLAMA_3_2_1B, 1)
+    m = rt.Model(block, max_seq=8192 + 32, paged=True, page_size=16, page_order_seed=2)
+    m.prefill(fx["prompt"])
+    _fixture_run(m, fx, 16, FIXTURE_GATES[0], "config 3")
