@@ -30,6 +30,17 @@ prefill  config 5's 2048-token prefill chunk on tcgen05 (see prefill_bench).
 long_context  config 3: bs1 decode after an 8192-id
          prompt over shuffled 16-position pages (see long_context_bench).
 
+config5  BASELINE configs[4] at this run's GPU count: the 512-request set
+         (lognormal contexts, median 2048, sigma 1.0, clipped to [512, 32768],
+         seed 4) split over the ranks by longest-processing-time, each rank
+         prefilling its prompts in 2048-token chunks and decoding 256 greedy
+         tokens per request; aggregate tok/s over the slowest rank's
+         CUDA-event time.
+reference_gpu  the reference's own build (its src/ compiled unmodified for
+         sm_100 with cuBLAS, baseline/Makefile) on the same GPU and config 2:
+         a baseline, not the target. reference_dropin: the same Model with its
+         kernel launchers forwarding to this library.
+
 --impl reference: the reference has no CPU implementation of the decode step,
 so its arm is the fp32 host evaluation (oracle port) of the same workload on
 the host cores, rank 0 only.
@@ -160,6 +171,32 @@ def reduce_max(world, value):
     return float(t.item())
 
 
+def reduce_sum(world, value):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def reduce_argmax(world, value):
+    """The rank holding the largest `value` (every rank takes part)."""
+    if world == 1:
+        return 0
+    import torch
+    import torch.distributed as dist
+
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.zeros(world, dtype=torch.float64, device=dev)
+    t[dist.get_rank()] = value
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return int(torch.argmax(t).item())
+
+
 def aggregate(world, rank_ms, steps):
     """Whole-job throughput of `world` replicas that each decoded `steps`
     tokens: (slowest rank's ms, all ranks' tokens / that time)."""
@@ -168,24 +205,29 @@ def aggregate(world, rank_ms, steps):
 
 
 def cpu_baseline(block, seconds=12.0, max_tokens=64):
-    """The fp32 host evaluation (oracle port) on this host's cores: decode
-    steps at positions 0.. for about `seconds`."""
+    """The fp32 host evaluation (oracle port) on this host's cores at config
+    2's positions: the prompt's first 127 ids prefilled as one chunk
+    (untimed), then decode steps from position 127 on -- the prompt's last id,
+    then the oracle's own greedy ids -- for about `seconds`."""
     import oracle
 
     from lcr_b200 import checkpoint as ck
 
-    m = oracle.Model(block, max_tokens + 1)
-    ids = ck.prompt_ids(1, max_tokens)
-    m.decode(int(ids[0]), 0, oracle.MODE_FP32)  # warm-up
+    m = oracle.Model(block, PROMPT + max_tokens + 1)
+    prompt = ck.prompt_ids(1, PROMPT)
+    m.prefill(prompt[:-1], 0, oracle.MODE_FP32, logits=False)
+    tok, pos = int(prompt[-1]), PROMPT - 1
     t0 = time.perf_counter()
     n = 0
-    while n + 1 < max_tokens and time.perf_counter() - t0 < seconds:
-        m.decode(int(ids[n + 1]), n + 1, oracle.MODE_FP32)
+    while n < max_tokens and time.perf_counter() - t0 < seconds:
+        tok = oracle.argmax(m.decode(tok, pos, oracle.MODE_FP32))
+        pos += 1
         n += 1
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n} Llama-3.2-1B decode steps of the fp32 host oracle at positions 1..{n} "
-                      f"(OpenMP over output rows, {os.cpu_count()} threads)"}
+            "sample": f"{n} Llama-3.2-1B greedy decode steps of the fp32 host oracle at positions "
+                      f"{PROMPT - 1}..{PROMPT - 2 + n} after the 127-id prompt prefix (config 2's positions; "
+                      f"OpenMP over output rows, {os.cpu_count()} threads)"}
 
 
 def run_reference(args, world, rank):
@@ -195,12 +237,13 @@ def run_reference(args, world, rank):
 
     block = ck.generate(ck.LLAMA_3_2_1B, 1)
     budget = max(1, min(args.steps, 48))
-    base = cpu_baseline(block, seconds=60.0, max_tokens=budget + 1)
+    base = cpu_baseline(block, seconds=60.0, max_tokens=budget)
     line = {"metric": METRIC, "value": base["value"], "unit": "tok/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config2: Llama-3.2-1B geometry seed 1, bs1 decode, contiguous KV",
+            "config": {"workload": "config2: Llama-3.2-1B geometry, bs1 greedy decode, 128-id "
+                                   "prompt, positions 128..383, contiguous KV",
                        "note": "the reference has no CPU decode path; this arm is the fp32 host "
                                "evaluation (oracle port) of the same step"},
             "cpu_baseline": base,
@@ -416,6 +459,83 @@ def prefill_bench(block, weights_dev, local, reps=5):
             "reps": reps, "statistic": "median"}
 
 
+def reference_gpu_bench(block, which="stock", steps=WINDOW - 1):
+    """The reference runtime's own Model on this GPU at config 2
+    (baseline/_ref/ref_bench_<which>, built by baseline/Makefile from the
+    reference's sources): the seed-1 checkpoint written as config.json +
+    model.safetensors and read by the reference's SafetensorsArchive, the
+    128-id prompt, then `steps` greedy steps timed by the reference's own
+    per-step GPU timer. Bytes per token follow the reference's formula at its
+    mean length (src/main.cu:195-220)."""
+    import shutil
+    import tempfile
+
+    from lcr_b200 import checkpoint as ck
+
+    exe = os.path.join(REPO, "baseline", "_ref", f"ref_bench_{which}")
+    if not os.path.exists(exe):
+        return {"unavailable": f"baseline/_ref/ref_bench_{which} is not built (make -C baseline REF=... JSON_INC=...)"}
+    tmp = tempfile.mkdtemp(prefix="lcr_ref_")
+    try:
+        ck.write_safetensors(tmp, block)
+        ids = os.path.join(tmp, "prompt.bin")
+        ck.prompt_ids(1, PROMPT).astype(np.int32).tofile(ids)
+        out = subprocess.run([exe, "--model", tmp, "--prompt", ids, "--steps", str(steps),
+                              "--max-seq", str(PROMPT + WINDOW + 8), "--warmup", "2"],
+                             capture_output=True, text=True, timeout=900)
+        if out.returncode != 0:
+            return {"unavailable": f"ref_bench_{which} exited {out.returncode}: {out.stderr.strip()[-300:]}"}
+        r = json.loads(out.stdout.strip().splitlines()[-1])
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    g = block.geom
+    mean_len = r["prompt_tokens"] + (r["decode_steps"] + 1) / 2.0
+    bytes_tok = g.weight_bytes_per_token() + mean_len * g.kv_bytes_per_position()
+    peak, kind = measured_peaks()
+    ms = r["decode_ms"] / r["decode_steps"]
+    return {"build": "the reference's src/ for sm_100, cuBLAS projections, its own kernels"
+                     if which == "stock" else
+                     "the reference's Model and cuBLAS projections, its kernel launchers forwarding "
+                     "to liblcr_b200 (baseline/kernels_b200.cu)",
+            "value": round(r["decode_tokens_per_s"], 2), "unit": "tok/s", "ms_per_step": round(ms, 5),
+            "steps": r["decode_steps"], "prefill_ms": round(r["prefill_ms"], 3),
+            "hbm_gbs": round(bytes_tok / (ms / 1000) / 1e9, 1),
+            "frac_of_peak": round(bytes_tok / (ms / 1000) / 1e9 / peak, 4), "peak_source": kind,
+            "timer": "the reference's per-step GPU timer (ForwardStats::last_decode_ms), sample + "
+                     "D2H of the id outside it",
+            "loop_tok_per_s": round(r["loop_tokens_per_s"], 2),
+            "greedy_ids": r["ids"][:16]}
+
+
+def config5_bench(block, weights_dev, local, world, rank):
+    """BASELINE configs[4] on this run's ranks (lcr_b200.serve.config5): the
+    512-request set split by longest-processing-time over the ranks, each
+    rank serving its shard on its own GPU with no communication; the
+    aggregate decode tok/s is all ranks' decoded tokens over the slowest
+    rank's CUDA-event time."""
+    import types
+
+    from lcr_b200 import serve
+
+    args = types.SimpleNamespace(sequences=512, sigma=1.0, decode_tokens=256, slots=128,
+                                 shard=f"{rank}/{world}", device=local)
+    r = serve.config5(block, weights_dev, args)
+    total_s = reduce_max(world, r["seconds"])
+    decode_s = reduce_max(world, r["decode_seconds"])
+    decoded = reduce_sum(world, r["decode_tokens"])
+    prompt_tokens = reduce_sum(world, r["prompt_tokens"])
+    slowest = reduce_argmax(world, r["seconds"])
+    return {"workload": "config5: 512 requests, contexts lognormal(median 2048, sigma 1.0) clipped to "
+                        "[512, 32768] (seed 4), LPT-sharded over the ranks, prompts prefilled in 2048-token "
+                        "chunks, 256 greedy tokens each, paged KV 16, 128 slots per GPU",
+            "n_gpus": world, "requests": 512, "prompt_tokens": int(prompt_tokens),
+            "decode_tokens": int(decoded), "seconds": round(total_s, 3),
+            "decode_tok_per_s": round(decoded / total_s, 1),
+            "decode_tok_per_s_in_steps": round(decoded / decode_s, 1),
+            "run_tok_per_s": round((decoded + prompt_tokens) / total_s, 1),
+            "slowest_rank": int(slowest), "timing": "CUDA events on each rank's batch stream, max over ranks"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -427,6 +547,11 @@ def main():
     ap.add_argument("--batched-steps", type=int, default=64)
     ap.add_argument("--no-long-context", action="store_true",
                     help="skip the config-3 long-context measurement")
+    ap.add_argument("--no-config5", action="store_true", help="skip the config-5 request set")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference build's measurement on this GPU")
+    ap.add_argument("--min-timed-s", type=float, default=1.0,
+                    help="repeat the K-step measurement until the timed block lasts this long")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)
@@ -472,17 +597,30 @@ def main():
     enqueue(args.warmup)
     m.sync()
 
+    # The K timed steps, repeated until the timed block lasts --min-timed-s
+    # (so the clock sampler sees it): the median repetition is the value.
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    enqueue(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    reps = int(reduce_max(world, max(1, int(np.ceil(args.min_timed_s * 1000.0 / max(e0.elapsed_time(e1), 1e-3))))))
     barrier(world)
     torch.cuda.synchronize()
+    rep_ms = []
     with Clocks(local) as clk:
-        e0.record(stream)
-        enqueue(args.steps)
-        e1.record(stream)
+        events = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            enqueue(args.steps)
+            b.record(stream)
+            events.append((a, b))
         torch.cuda.synchronize()
+        rep_ms = [a.elapsed_time(b) for a, b in events]
     m.sync()
     barrier(world)
-    max_ms, value = aggregate(world, e0.elapsed_time(e1), args.steps)
+    max_ms, value = aggregate(world, float(np.median(rep_ms)), args.steps)
 
     # end to end: host token in, host token out, every step
     e2e_steps = min(args.steps, 1024)
@@ -527,6 +665,9 @@ def main():
         prefill = prefill_bench(block, m.weights_dev, local)
 
     ms_per_step = max_ms / args.steps
+    config5 = None
+    if not args.no_config5:
+        config5 = config5_bench(block, m.weights_dev, local, world, rank)
     long_ctx = None
     if not args.no_long_context:
         long_ctx = long_context_bench(block, m.weights_dev, local, ms_per_step)
@@ -534,12 +675,17 @@ def main():
     ctx_mean = PROMPT + (WINDOW - 1) / 2
     step_bytes = g.weight_bytes_per_token() + ctx_mean * g.kv_bytes_per_position()
     achieved = step_bytes / (ms_per_step / 1000) / 1e9
+    ref_gpu = ref_dropin = None
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        ref_gpu = reference_gpu_bench(block, "stock")
+        ref_dropin = reference_gpu_bench(block, "dropin")
     if rank == 0:
         base = None if args.no_cpu_baseline or world > 1 else cpu_baseline(block)
         clocks = clk.summary()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "timed_repetitions": reps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, seed 1; uniform prompt ids)",
             "config": {"workload": "config2: Llama-3.2-1B geometry, bs1 greedy decode, 128-id "
@@ -561,12 +707,15 @@ def main():
                          "per_matrix_layer0": per_matrix},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4, "steps": e2e_steps},
-            "gpu_launches": args.steps * m.step_launches(),
+            "gpu_launches": reps * args.steps * m.step_launches(),
             "clocks": clocks,
             "cpu_baseline": base,
             "batched": batched,
             "prefill": prefill,
             "long_context": long_ctx,
+            "config5": config5,
+            "reference_gpu": ref_gpu,
+            "reference_dropin": ref_dropin,
         }
         print(json.dumps(line))
     m.close()

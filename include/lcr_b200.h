@@ -72,43 +72,61 @@ typedef struct lcr_kv_view {
 /* Per-kernel entry points (src/kernels.cuh:17-132)                           */
 /* ------------------------------------------------------------------------- */
 
-/* launch_embedding_lookup, src/kernels.cuh:17-20: out[t,:] = table[ids[t],:] */
+/* launch_embedding_lookup, src/kernels.cuh:16-19: out[t,:] = table[ids[t],:] */
 LCR_API int lcr_embedding_lookup(void* out, const void* table, const int32_t* ids,
                          int tokens, int dim, lcr_stream_t stream);
 
-/* launch_rmsnorm, src/kernels.cuh:22-26 */
+/* launch_rmsnorm, src/kernels.cuh:21-25 */
 LCR_API int lcr_rmsnorm(void* out, const void* x, const void* weight, int tokens,
                 int dim, float eps, lcr_stream_t stream);
 
-/* launch_add_residual, src/kernels.cuh:28-30 */
+/* launch_add_residual, src/kernels.cuh:27-29 */
 LCR_API int lcr_add_residual(void* x, const void* delta, int64_t count,
                      lcr_stream_t stream);
 
-/* launch_add_residual_rmsnorm, src/kernels.cuh:32-43 */
+/* launch_add_residual_rmsnorm, src/kernels.cuh:31-41 */
 LCR_API int lcr_add_residual_rmsnorm(void* out, void* x, const void* delta,
                              const void* weight, int tokens, int dim,
                              float eps, lcr_stream_t stream);
 
-/* launch_swiglu, src/kernels.cuh:45-47 */
+/* launch_swiglu, src/kernels.cuh:43-45 */
 LCR_API int lcr_swiglu(void* out, const void* gate, const void* up, int64_t count,
                lcr_stream_t stream);
 
-/* launch_swiglu_strided, src/kernels.cuh:49-54 */
+/* launch_swiglu_strided, src/kernels.cuh:47-51 */
 LCR_API int lcr_swiglu_strided(void* out, const void* gate, const void* up, int tokens,
                        int width, int src_row_stride, lcr_stream_t stream);
 
-/* launch_rope_q, src/kernels.cuh:56-67: [tokens][heads*d] -> [heads][tokens][d] */
+/* launch_rope_q, src/kernels.cuh:53-64: [tokens][heads*d] -> [heads][tokens][d] */
 LCR_API int lcr_rope_q(void* q_heads, const void* q_proj, const float* inv_freq,
                int tokens, int start_position, int num_heads, int head_dim,
                int src_row_stride, lcr_stream_t stream);
 
-/* launch_rope_write_kv, src/kernels.cuh:69-75 */
+/* launch_rope_write_kv, src/kernels.cuh:66-72 */
 LCR_API int lcr_rope_write_kv(const lcr_kv_view* view, const void* k_proj,
                       const void* v_proj, const float* inv_freq, int tokens,
                       int start_position, int paged, int src_row_stride,
                       lcr_stream_t stream);
 
-/* launch_decode_attention, src/kernels.cuh:96-116: single-token GQA attention
+/* launch_causal_softmax, src/kernels.cuh:74-81: scores [heads][rows][keys]
+ * fp32, row r is query position start_position + r and sees keys up to it;
+ * probs (same layout, bf16) = softmax over those keys, 0 beyond them. */
+LCR_API int lcr_causal_softmax(void* probs, const float* scores, int num_heads,
+                       int rows, int keys, int start_position,
+                       lcr_stream_t stream);
+
+/* launch_merge_heads, src/kernels.cuh:83-86: heads [heads][tokens][d] ->
+ * out [tokens][heads * d]. */
+LCR_API int lcr_merge_heads(void* out, const void* heads, int tokens, int num_heads,
+                    int head_dim, lcr_stream_t stream);
+
+/* launch_gather_kv, src/kernels.cuh:88-94: the cached positions [0, positions)
+ * of a (paged or contiguous) view as contiguous [kv_head][position][d] keys
+ * and values. */
+LCR_API int lcr_gather_kv(void* out_keys, void* out_values, const lcr_kv_view* view,
+                  int positions, lcr_stream_t stream);
+
+/* launch_decode_attention, src/kernels.cuh:106-110: single-token GQA attention
  * over seq_len cached positions, split-K over `splits` blocks per KV head. */
 LCR_API int lcr_decode_attention(void* out, const void* q, const lcr_kv_view* view,
                          int num_heads, int heads_per_kv, int seq_len,
@@ -131,22 +149,22 @@ LCR_API int lcr_decode_attention_noalloc(void* out, const void* q,
                                  int heads_per_kv, int seq_len, float scale,
                                  int paged, int splits, lcr_stream_t stream);
 
-/* decode_attention_scratch_floats, src/kernels.cuh:118-120 */
+/* decode_attention_scratch_floats, src/kernels.cuh:114 */
 LCR_API size_t lcr_decode_attention_scratch_floats(int num_heads, int head_dim,
                                            int splits);
 
-/* choose_attention_splits, src/kernels.cuh:122-124 */
+/* choose_attention_splits, src/kernels.cuh:118 */
 LCR_API int lcr_choose_attention_splits(int num_kv_heads, int seq_len,
                                 int multiprocessors);
 
-/* launch_sample, src/kernels.cuh:130-136: temperature 0 = argmax (ties to the
+/* launch_sample, src/kernels.cuh:128-130: temperature 0 = argmax (ties to the
  * lowest id); otherwise top-k/top-p over the full-vocab softmax with the
  * host's uniform in [0,1). Deterministic: equal inputs give equal ids. */
 LCR_API int lcr_sample(int32_t* out_id, const float* logits, int vocab,
                float temperature, int top_k, float top_p, float uniform,
                float* scratch, lcr_stream_t stream);
 
-/* sample_scratch_floats, src/kernels.cuh:138 */
+/* sample_scratch_floats, src/kernels.cuh:132 */
 LCR_API size_t lcr_sample_scratch_floats(int vocab, int top_k);
 
 /* gemm_nt, src/model.cu:38-45: y[rows][out] = x[rows][in] * w[out][in]^T,

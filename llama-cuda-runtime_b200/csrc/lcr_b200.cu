@@ -189,6 +189,45 @@ extern "C" int lcr_choose_attention_splits(int num_kv_heads, int seq_len, int mu
   return std::max(1, std::min(splits, 64));
 }
 
+extern "C" int lcr_causal_softmax(void* probs, const float* scores, int num_heads, int rows, int keys,
+                                  int start_position, lcr_stream_t stream) {
+  if (rows == 0 || num_heads == 0) return LCR_OK;
+  LCRB_REQUIRE(probs && scores && num_heads > 0 && rows > 0 && keys > 0 && start_position >= 0, LCR_ERR_INVALID,
+               "causal_softmax: null pointer or bad size");
+  LCRB_REQUIRE(rows <= 65535 * 64 && num_heads <= 65535, LCR_ERR_SHAPE, "causal_softmax: %d rows x %d heads",
+               rows, num_heads);
+  causal_softmax_kernel<<<dim3(rows, num_heads), kSmallThreads, 0, cs(stream)>>>(mb(probs), scores, rows, keys,
+                                                                                start_position);
+  return launch_status("causal_softmax");
+}
+
+extern "C" int lcr_merge_heads(void* out, const void* heads, int tokens, int num_heads, int head_dim,
+                               lcr_stream_t stream) {
+  if (tokens == 0) return LCR_OK;
+  LCRB_REQUIRE(out && heads && tokens > 0 && num_heads > 0 && head_dim > 0, LCR_ERR_INVALID,
+               "merge_heads: null pointer or non-positive size");
+  LCRB_REQUIRE(head_dim % 8 != 0 || (aligned16(out) && aligned16(heads)), LCR_ERR_SHAPE,
+               "merge_heads: buffers must be 16-byte aligned");
+  const long long units = static_cast<long long>(tokens) * num_heads * head_dim / (head_dim % 8 == 0 ? 8 : 1);
+  const int blocks = static_cast<int>(std::min<long long>(4096, (units + kSmallThreads - 1) / kSmallThreads));
+  merge_heads_kernel<<<blocks, kSmallThreads, 0, cs(stream)>>>(mb(out), cb(heads), tokens, num_heads, head_dim);
+  return launch_status("merge_heads");
+}
+
+extern "C" int lcr_gather_kv(void* out_keys, void* out_values, const lcr_kv_view* view, int positions,
+                             lcr_stream_t stream) {
+  if (positions == 0) return LCR_OK;
+  LCRB_REQUIRE(out_keys && out_values && view && view->keys && view->values && positions > 0, LCR_ERR_INVALID,
+               "gather_kv: null pointer or non-positive size");
+  LCRB_REQUIRE(positions <= 65535 * 64 && view->num_kv_heads > 0 && view->num_kv_heads <= 65535 &&
+                   view->head_dim > 0 && (view->page_table == nullptr || view->page_size > 0),
+               LCR_ERR_SHAPE, "gather_kv: bad view or %d positions", positions);
+  gather_kv_kernel<<<dim3(positions, view->num_kv_heads), 64, 0, cs(stream)>>>(
+      mb(out_keys), mb(out_values), cb(view->keys), cb(view->values), view->page_table, view->page_size,
+      view->page_stride, view->head_stride, view->head_dim, positions);
+  return launch_status("gather_kv");
+}
+
 extern "C" int lcr_decode_attention(void* out, const void* q, const lcr_kv_view* view, int num_heads,
                                     int heads_per_kv, int seq_len, float scale, int paged, int splits,
                                     float* scratch, lcr_stream_t stream) {

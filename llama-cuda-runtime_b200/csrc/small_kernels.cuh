@@ -170,4 +170,85 @@ static __global__ void gemm_nt_simple_kernel(void* __restrict__ y, int y_fp32, c
   }
 }
 
+// Causal softmax of prefill attention scores (attention.cu:42-100 computes the
+// same distribution): row r of head h is query position start + r and sees
+// keys [0, min(keys, start + r + 1)); probs = bf16(exp(s - max) / sum) there,
+// 0 beyond (the buffer is reused across chunks). One CTA per (row, head),
+// three passes over the row: the maximum, the exponential sum, the write.
+static __global__ void causal_softmax_kernel(bf16* __restrict__ probs, const float* __restrict__ scores,
+                                             int rows, int keys, int start) {
+  __shared__ float red[kSmallThreads / 32];
+  const int row = blockIdx.x;
+  const size_t base = (static_cast<size_t>(blockIdx.y) * rows + row) * keys;
+  const int limit = min(keys, start + row + 1);
+  const float* sr = scores + base;
+  float mx = kNegBig;
+  for (int j = threadIdx.x; j < limit; j += blockDim.x) mx = fmaxf(mx, sr[j]);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kSmallThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < limit; j += blockDim.x) sum += expf(sr[j] - mx);
+  sum = block_sum_256(sum, red);
+  const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+  bf16* pr = probs + base;
+  for (int j = threadIdx.x; j < keys; j += blockDim.x) {
+    pr[j] = __ushort_as_bfloat16(f2bf(j < limit ? expf(sr[j] - mx) * inv : 0.f));
+  }
+}
+
+// heads[h][t][0, d) -> out[t][h * d, h * d + d) (elementwise.cu:124-143): a
+// copy, 16 bytes at a time when d is a multiple of 8.
+static __global__ void merge_heads_kernel(bf16* __restrict__ out, const bf16* __restrict__ heads, int tokens,
+                                          int num_heads, int d) {
+  const int v8 = d % 8 == 0 ? 8 : 1;
+  const long long units = static_cast<long long>(tokens) * num_heads * (d / v8);
+  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < units;
+       u += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(u % (d / v8)) * v8;
+    const long long th = u / (d / v8);
+    const int h = static_cast<int>(th % num_heads);
+    const long long t = th / num_heads;
+    const bf16* src = heads + (static_cast<long long>(h) * tokens + t) * d + i;
+    bf16* dst = out + (t * num_heads + h) * d + i;
+    if (v8 == 8) {
+      *reinterpret_cast<uint4*>(dst) = ldg16(src);
+    } else {
+      *dst = *src;
+    }
+  }
+}
+
+// The cache of positions [0, positions) as contiguous [kv_head][position][d]
+// keys and values (attention.cu:302-316): per (position, head) the row at the
+// view's offset (page_table[p / page_size] * page_stride + head * head_stride
+// + (p % page_size) * d; no table: page 0, slot p). A negative table entry
+// (an unmapped page) gives zero rows.
+static __global__ void gather_kv_kernel(bf16* __restrict__ out_k, bf16* __restrict__ out_v, const bf16* keys,
+                                        const bf16* values, const int32_t* table, int page_size,
+                                        long long page_stride, long long head_stride, int d, int positions) {
+  const int p = blockIdx.x, h = blockIdx.y;
+  long long src;
+  bool mapped = true;
+  if (table != nullptr) {
+    const int page = table[p / page_size];
+    mapped = page >= 0;
+    src = static_cast<long long>(page) * page_stride + h * head_stride + static_cast<long long>(p % page_size) * d;
+  } else {
+    src = h * head_stride + static_cast<long long>(p) * d;
+  }
+  const long long dst = (static_cast<long long>(h) * positions + p) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const bf16 z = __ushort_as_bfloat16(0);
+    out_k[dst + i] = mapped ? keys[src + i] : z;
+    out_v[dst + i] = mapped ? values[src + i] : z;
+  }
+}
+
 }  // namespace lcrb

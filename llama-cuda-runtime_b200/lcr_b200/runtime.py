@@ -99,6 +99,9 @@ _SIGS = {
     "lcr_swiglu_strided": (_I, [_V, _V, _V, _I, _I, _I, _V]),
     "lcr_rope_q": (_I, [_V, _V, _V, _I, _I, _I, _I, _I, _V]),
     "lcr_rope_write_kv": (_I, [ctypes.POINTER(KvView), _V, _V, _V, _I, _I, _I, _I, _V]),
+    "lcr_causal_softmax": (_I, [_V, _V, _I, _I, _I, _I, _V]),
+    "lcr_merge_heads": (_I, [_V, _V, _I, _I, _I, _V]),
+    "lcr_gather_kv": (_I, [_V, _V, ctypes.POINTER(KvView), _I, _V]),
     "lcr_decode_attention": (_I, [_V, _V, ctypes.POINTER(KvView), _I, _I, _I, _F, _I, _I, _V, _V]),
     "lcr_decode_attention_noalloc": (_I, [_V, _V, ctypes.POINTER(KvView), _I, _I, _I, _F, _I, _I, _V]),
     "lcr_decode_attention_scratch_floats": (ctypes.c_size_t, [_I, _I, _I]),

@@ -109,7 +109,10 @@ def config5(block, wdev, args) -> dict:
     sequences in flight, each admitted with its prompt prefilled in 2048-token
     chunks (lcr_batch_prefill), then greedy decode of --decode-tokens tokens
     with continuous batching. Reports decode tokens per second over the whole
-    run (prefill included) and over the decode steps alone."""
+    run (prefill included) and over the decode steps alone, timed with CUDA
+    events on the batch's stream."""
+    import torch
+
     g = block.geom
     shard, shards = (int(x) for x in args.shard.split("/"))
     contexts = config5_requests(args.sequences, args.sigma)
@@ -128,20 +131,31 @@ def config5(block, wdev, args) -> dict:
         prompt = ck.prompt_ids(10_000 + i, int(contexts[i])) % g.vocab_size
         cb.submit(sch.Sequence(sid=i, context=int(contexts[i]), target=args.decode_tokens, seed=i,
                                prompt=prompt.astype(np.int32)))
-    t_start = time.perf_counter()
-    t_decode = 0.0
+    stream = torch.cuda.ExternalStream(bt.stream, device=f"cuda:{args.device}")
+
+    def event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
     prompt_tokens = int(sum(int(contexts[i]) for i in mine))
     decoded = 0
     steps = 0
+    step_events = []
+    bt.sync()
+    e_start = event()
     while cb.waiting or cb.active():
         cb.fill()
-        t0 = time.perf_counter()
+        e0 = event()
         done = cb.step()
-        bt.sync()
-        t_decode += time.perf_counter() - t0
+        step_events.append((e0, event()))
         decoded += done
         steps += 1
-    total = time.perf_counter() - t_start
+    e_end = event()
+    bt.sync()
+    torch.cuda.synchronize()
+    total = e_start.elapsed_time(e_end) / 1000.0
+    t_decode = sum(a.elapsed_time(b) for a, b in step_events) / 1000.0
     bt.close()
     return {"workload": f"config5 shard {shard}/{shards}: {len(mine)} of {args.sequences} requests, contexts "
                         f"lognormal(median 2048, sigma {args.sigma}) in [512, 32768] (seed 4), prompts prefilled "

@@ -272,3 +272,68 @@ def test_argmax_tie_goes_to_lowest_id():
     lg = np.zeros(128256, np.float32)
     lg[[77777, 5000, 128255]] = 2.0
     assert _sample(dev(lg), lg.size, 0.0, 0, 1.0, 0.5) == 5000
+
+
+# --- the prefill launchers of the boundary (src/kernels.cuh:74-94) ----------
+
+@pytest.mark.parametrize("heads,rows,keys,start", [(4, 37, 100, 63), (2, 5, 64, 0), (3, 16, 300, 100)])
+def test_causal_softmax(heads, rows, keys, start):
+    """Nested-loop causal softmax (the structure of tests/test_kernels.cu's
+    prefill softmax case): row r sees keys up to start + r; masked entries,
+    including columns past the chunk when `keys` is wider, are exactly 0."""
+    scores = RNG.normal(0, 3, size=(heads, rows, keys)).astype(np.float32)
+    probs = torch.empty(heads * rows * keys, dtype=torch.int16, device="cuda")
+    run(L.lcr_causal_softmax(probs.data_ptr(), dptr(scores), heads, rows, keys, start, S()))
+    got = fl(host_bf(probs)).reshape(heads, rows, keys)
+    want = np.zeros_like(scores, dtype=np.float64)
+    for h in range(heads):
+        for r in range(rows):
+            lim = min(keys, start + r + 1)
+            e = np.exp(scores[h, r, :lim].astype(np.float64) - scores[h, r, :lim].max())
+            want[h, r, :lim] = e / e.sum()
+            assert not got[h, r, lim:].any()
+    expect_close(got, want, TOL, "causal_softmax")
+    assert np.abs(got - want).max() <= 4e-3  # bf16 rounding of values <= 1
+
+
+@pytest.mark.parametrize("d", [64, 128, 20])
+def test_merge_heads_exact(d):
+    heads, tokens = 6, 9
+    x = bf(RNG.normal(size=(heads, tokens, d)))
+    out = torch.empty(tokens * heads * d, dtype=torch.int16, device="cuda")
+    run(L.lcr_merge_heads(out.data_ptr(), dptr(x), tokens, heads, d, S()))
+    assert np.array_equal(host_bf(out).reshape(tokens, heads * d), x.transpose(1, 0, 2).reshape(tokens, heads * d))
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_gather_kv_exact(paged):
+    """The cached positions as contiguous [kv_head][position][d] rows, through
+    a shuffled page table (a negative entry reads as zero rows)."""
+    kv_heads, d, page, positions = 2, 64, 16, 70
+    max_seq = 96
+    if paged:
+        max_pages = max_seq // page
+        pool = max_pages + 2
+        table = oracle.page_permutation(pool, 5)[:max_pages].astype(np.int32)
+        kp = bf(RNG.normal(size=pool * kv_heads * page * d))
+        vp = bf(RNG.normal(size=pool * kv_heads * page * d))
+        view = rt.KvView(dptr(kp), dptr(vp), dptr(table), page, kv_heads * page * d, page * d, kv_heads, d)
+
+        def row(store, h, p):
+            base = (int(table[p // page]) * kv_heads * page + h * page + p % page) * d
+            return store[base:base + d]
+    else:
+        kp = bf(RNG.normal(size=kv_heads * max_seq * d))
+        vp = bf(RNG.normal(size=kv_heads * max_seq * d))
+        view = rt.KvView(dptr(kp), dptr(vp), None, max_seq, 0, max_seq * d, kv_heads, d)
+
+        def row(store, h, p):
+            base = (h * max_seq + p) * d
+            return store[base:base + d]
+    ok = torch.empty(kv_heads * positions * d, dtype=torch.int16, device="cuda")
+    ov = torch.empty_like(ok)
+    run(L.lcr_gather_kv(ok.data_ptr(), ov.data_ptr(), ctypes.byref(view), positions, S()))
+    gk, gv = host_bf(ok).reshape(kv_heads, positions, d), host_bf(ov).reshape(kv_heads, positions, d)
+    for h in range(kv_heads):
+        for p in range(positions):
+            assert np.array_equal(gk[h, p], row(kp, h, p)) and np.array_equal(gv[h, p], row(vp, h, p)), (h, p)
