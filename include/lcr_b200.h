@@ -141,8 +141,10 @@ LCR_API int lcr_decode_attention(void* out, const void* q, const lcr_kv_view* vi
  * (num_heads x splits x (head_dim + 2), splits after the 16-position clamp)
  * returns LCR_ERR_SHAPE. The first call on each device looks the array up
  * (cudaGetSymbolAddress, with that device current): make it before any stream
- * capture. Every call on a device shares the array, so calls whose kernels
- * may overlap race; order them on one stream. */
+ * capture, and do not use the entry point across a cudaDeviceReset (the
+ * array may move; the looked-up address is kept). Every call on a device
+ * shares the array, so calls whose kernels may overlap race; order them on
+ * one stream. */
 #define LCR_NOALLOC_ATTENTION_SCRATCH_FLOATS (1 << 19)
 LCR_API int lcr_decode_attention_noalloc(void* out, const void* q,
                                  const lcr_kv_view* view, int num_heads,
@@ -230,6 +232,12 @@ typedef struct lcr_ctx lcr_ctx;
 LCR_API int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* weights,
                    const lcr_options* options, lcr_ctx** out);
 LCR_API void lcr_ctx_destroy(lcr_ctx* ctx);
+
+/* compute_rope_inv_freq, src/config.cpp:223-259: the head_dim / 2 inverse
+ * frequencies the context rotates with (theta^(-2i/d) in double, rounded to
+ * float, then the llama3 band rescaling when rope_scaling is set), written to
+ * out[0 .. head_dim / 2). Host only; needs no device. */
+LCR_API int lcr_rope_inv_freq(const lcr_model_desc* desc, float* out, int capacity);
 
 /* Model::reset, src/model.h:91: position back to 0 (the cache is reused). */
 LCR_API int lcr_reset(lcr_ctx* ctx);

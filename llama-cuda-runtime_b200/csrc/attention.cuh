@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       }
       // Never leave the CTA with a copy still writing its shared memory.
       for (int blk = issued > STAGES ? issued - STAGES : 0; blk < issued; ++blk) {
-        mbar_wait(&full[blk % STAGES], (blk / STAGES) & 1, a.status, kStatusTimeoutFull);
+        mbar_wait(&full[blk % STAGES], (blk / STAGES) & 1, nullptr, 0);  // waits even after an abort
       }
     }
   } else {

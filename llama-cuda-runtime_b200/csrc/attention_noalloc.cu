@@ -8,6 +8,11 @@
 // read the cached address and then launch exactly what lcr_decode_attention
 // launches.
 //
+// The cached address belongs to the device's context at the time of the
+// first call: after cudaDeviceReset (or anything else that destroys and
+// re-creates that context) the library's device code is loaded again and the
+// array may move, so do not use this entry point across a reset.
+//
 // Sharing: every call on a device uses the same array. Each split writes its
 // whole (m, l, acc) record before the merge reads it, so nothing has to start
 // at zero, but two calls whose kernels can overlap (different streams, or

@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kAbThreads, D == 64 ? 3 : 1)
     if (lane == 0) {
       // Never leave the CTA with a copy still writing its shared memory.
       for (int q = st > STAGES ? st - STAGES : 0; q < st; ++q) {
-        mbar_wait(&full[q % STAGES], (q / STAGES) & 1, a.status, kStatusTimeoutFull);
+        mbar_wait(&full[q % STAGES], (q / STAGES) & 1, nullptr, 0);  // waits even after an abort
       }
       // The last CTA to finish rearms the counters for the next launch.
       __threadfence();

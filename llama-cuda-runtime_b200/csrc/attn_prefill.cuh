@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kAttnThreads, D == 64 ? 3 : 2) attn_prefill_ke
     pdl_launch_next();
     if (lane == 0) {
       for (int st = issued > STAGES ? issued - STAGES : 0; st < issued; ++st) {
-        mbar_wait(&full[st % STAGES], (st / STAGES) & 1, a.status, kStatusTimeoutFull);
+        mbar_wait(&full[st % STAGES], (st / STAGES) & 1, nullptr, 0);  // waits even after an abort
       }
     }
     return;

@@ -164,16 +164,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // spinning forever.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-// Waits for an mbarrier phase; false (and a status bit) if the bound expired.
+// Waits for an mbarrier phase; false (and a status bit) if the bound expired,
+// or -- without a new bit -- once another CTA raised the abort bit (a
+// stopped step then unwinds at once instead of waiting out every bound).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
                                           uint32_t code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
   for (uint32_t spin = 0;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 255u && globaltimer_ns() - start > kWaitLimitNs) {
-      if (status) atomicOr(status, code);
-      return false;
+    if ((spin & 255u) == 255u) {
+      if (status && (__ldcg(status) & (1u << 8))) return false;  // kStatusAbort
+      if (globaltimer_ns() - start > kWaitLimitNs) {
+        if (status) atomicOr(status, code);
+        return false;
+      }
     }
   }
 }

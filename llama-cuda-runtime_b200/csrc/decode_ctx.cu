@@ -77,7 +77,11 @@ namespace {
 
 // Bit 4: the persistent step with fp32 activations instead of the
 // reference's bf16 storage rounding (closer to the fp32 evaluation, slower).
-enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8, kFlagFp32Act = 16 };
+// Bit 5 (tests only): the persistent step's grid barriers wait at most 50 ms
+// and CTA 0 skips its first arrival, so the first barrier times out -- the
+// timeout path, exercised without faulting or hanging the GPU.
+enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8, kFlagFp32Act = 16,
+             kFlagTestTimeout = 32 };
 constexpr int kPinnedRing = 256;
 constexpr int kTimingSlots = 128;
 
@@ -253,6 +257,8 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.vpool = c->vpool;
   a.trace = c->trace;
   a.prefetch_bytes = c->prefetch_bytes;
+  a.wait_ns = (c->o.flags & kFlagTestTimeout) ? 50000000ull : kWaitLimitNs;
+  a.test_skip_arrival = (c->o.flags & kFlagTestTimeout) ? 1 : 0;
   if (c->o.paged) {
     a.tables = c->tables_dev;
     a.max_pages = c->max_pages;
@@ -376,6 +382,13 @@ int check_status(lcr_ctx* c) {
   LCRB_CUDA(cudaStreamSynchronize(c->stream));
   if (st == 0) return LCR_OK;
   LCRB_CUDA(cudaMemsetAsync(c->status, 0, sizeof st, c->stream));
+  if (st & kStatusAbort) {
+    // A stopped step may leave the many-split merge counters and the argmax
+    // hand-off part way: start the next step from zero.
+    LCRB_CUDA(cudaMemsetAsync(c->attn_ctr, 0, sizeof(unsigned) * c->d.num_layers * c->d.num_kv_heads, c->stream));
+    LCRB_CUDA(cudaMemsetAsync(c->sched, 0, 2 * sizeof(unsigned), c->stream));
+    LCRB_CUDA(cudaMemsetAsync(c->argmax_acc, 0, sizeof(unsigned long long), c->stream));
+  }
   LCRB_CUDA(cudaStreamSynchronize(c->stream));
   if (st & (kStatusTimeoutFull | kStatusTimeoutEmpty | kStatusTimeoutBarrier | kStatusAbort)) {
     return fail(LCR_ERR_TIMEOUT, "a device-side wait gave up (status 0x%x)", st);
@@ -669,6 +682,18 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
 }
 
 extern "C" void lcr_ctx_destroy(lcr_ctx* ctx) { release(ctx); }
+
+extern "C" int lcr_rope_inv_freq(const lcr_model_desc* desc, float* out, int capacity) {
+  LCRB_REQUIRE(desc && out, LCR_ERR_INVALID, "lcr_rope_inv_freq: null argument");
+  LCRB_REQUIRE(desc->head_dim > 0 && desc->head_dim % 2 == 0 && desc->rope_theta > 1.f, LCR_ERR_INVALID,
+               "lcr_rope_inv_freq: head_dim %d / rope_theta %g", desc->head_dim,
+               static_cast<double>(desc->rope_theta));
+  LCRB_REQUIRE(capacity >= desc->head_dim / 2, LCR_ERR_INVALID, "lcr_rope_inv_freq: %d floats needed, %d given",
+               desc->head_dim / 2, capacity);
+  const std::vector<float> f = rope_inv_freq(*desc);
+  std::memcpy(out, f.data(), f.size() * sizeof(float));
+  return LCR_OK;
+}
 
 extern "C" int lcr_reset(lcr_ctx* ctx) {
   LCRB_REQUIRE(ctx, LCR_ERR_INVALID, "null context");

@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       pdl_launch_next();
       tc_commit(acc_full);
       tc_commit(drain);
-      mbar_wait(drain, 0, a.status, kStatusTimeoutFull);
+      mbar_wait(drain, 0, nullptr, 0);  // the MMAs in flight land even after an abort
       if (!ok && a.status) atomicOr(a.status, kStatusAbort);
     }
   } else {
@@ -698,7 +698,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_persist_kernel(const Tc
       }
       pdl_launch_next();
       tc_commit(drain);
-      mbar_wait(drain, 0, a.status, kStatusTimeoutFull);
+      mbar_wait(drain, 0, nullptr, 0);  // the MMAs in flight land even after an abort
       if (!ok && a.status) atomicOr(a.status, kStatusAbort);
     }
   } else {

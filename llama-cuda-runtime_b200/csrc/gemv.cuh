@@ -234,11 +234,12 @@ __device__ __forceinline__ bool gemv_produce(uint8_t* ring, uint64_t* full, uint
 // Waits (bounded) until every copy issued into the ring has landed, so a CTA
 // never exits with a copy still writing its shared memory. `issued` is the
 // producer's stage count; the last STAGES stages are the only ones that can
-// still be in flight.
+// still be in flight. It waits even after an abort (no status word: the
+// abort bit does not cut it short).
 template <int STAGES>
-__device__ __forceinline__ void ring_drain(uint64_t* full, int issued, uint32_t* status) {
+__device__ __forceinline__ void ring_drain(uint64_t* full, int issued, uint32_t*) {
   for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k) {
-    mbar_wait(&full[k % STAGES], (k / STAGES) & 1, status, kStatusTimeoutFull);
+    mbar_wait(&full[k % STAGES], (k / STAGES) & 1, nullptr, 0);
   }
 }
 

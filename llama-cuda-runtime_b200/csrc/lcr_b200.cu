@@ -291,21 +291,18 @@ extern "C" int lcr_sample(int32_t* out_id, const float* logits, int vocab, float
     LCRB_REQUIRE(top_p > 0.0f && top_p <= 1.0f, LCR_ERR_INVALID, "top_p must be in (0, 1], got %g",
                  static_cast<double>(top_p));
   }
-  // The per-row parameter block lives in the caller's scratch (8 floats).
-  float host[4];
-  host[0] = temperature > 0.0f ? 1.0f / temperature : 0.0f;
-  std::memcpy(&host[1], &top_k, sizeof(int));
-  host[2] = top_p;
-  host[3] = uniform;
-  LCRB_CUDA(cudaMemcpyAsync(scratch, host, sizeof host, cudaMemcpyHostToDevice, cs(stream)));
+  // The parameters travel by value in the launch: no host buffer is read at
+  // run time, so the call may be captured in a graph. (The scratch the
+  // reference's signature carries stays unused.)
   SampleArgs a = {};
   a.logits = logits;
   a.row_stride = vocab;
   a.vocab = vocab;
-  a.inv_temperature = scratch;
-  a.top_k = reinterpret_cast<const int*>(scratch + 1);
-  a.top_p = scratch + 2;
-  a.uniform = scratch + 3;
+  a.inline_params = 1;
+  a.inv_temperature_v = temperature > 0.0f ? 1.0f / temperature : 0.0f;
+  a.top_k_v = top_k;
+  a.top_p_v = top_p;
+  a.uniform_v = uniform;
   a.out = out_id;
   return sample_launch(a, 1, cs(stream), false);
 }

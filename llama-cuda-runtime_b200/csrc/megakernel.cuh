@@ -92,6 +92,8 @@ struct MegaArgs {
   int max_pages, pool_pages, page_size;
   long long page_stride, head_stride, layer_stride;  // layer_stride: contiguous
   unsigned long long prefetch_bytes;  // L2 prefetch lead of the producer (0: off)
+  unsigned long long wait_ns;         // bound of each grid-barrier wait
+  int test_skip_arrival;              // test only: CTA 0 does not arrive at the first grid barrier
   // Optional phase trace (globaltimer ns), per CTA kMegaTraceEvents slots:
   // [0] consumers start, [1 + 2k] arrival at barrier k, [2 + 2k] departure,
   // [kMegaTraceProducer + p] producer starting phase p.
@@ -120,13 +122,14 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 // raises the abort bit so every other CTA stops waiting too) if the bounded
 // wait expired or another CTA already aborted.
 __device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, uint32_t* status,
-                                               int* s_abort, unsigned long long* trace = nullptr) {
+                                               int* s_abort, unsigned long long* trace = nullptr,
+                                               uint64_t wait_ns = kWaitLimitNs, bool arrive = true) {
   named_sync(1, kGemvConsumers);
   if (threadIdx.x == 0) {
     if (trace) trace[0] = globaltimer_ns();
     // Release at GPU scope: every write this CTA's consumers made before the
     // named barrier is visible to whoever acquires the count.
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+    if (arrive) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
     uint64_t start = 0;
     for (uint32_t spin = 0;; ++spin) {
       if (ld_acquire_u32(bar) >= target) break;
@@ -138,7 +141,7 @@ __device__ __forceinline__ bool mega_grid_sync(unsigned* bar, unsigned target, u
         const uint64_t now = globaltimer_ns();
         if (start == 0) {
           start = now;
-        } else if (now - start > kWaitLimitNs) {
+        } else if (now - start > wait_ns) {
           atomicOr(status, kStatusTimeoutBarrier | kStatusAbort);
           *s_abort = 1;
           break;
@@ -296,11 +299,15 @@ __device__ __forceinline__ int mega_attn_chunk(int seq_len, int splits, int p) {
 }
 
 // Physical element offset of (kv head, position) in layer `l` of the cache.
+// A page-table entry outside the pool raises kStatusBadPage and reads page 0.
 template <bool PAGED>
 __device__ __forceinline__ long long kv_offset(const MegaArgs& a, int l, int kvh, int pos, int D) {
   if constexpr (PAGED) {
     int page = a.tables[static_cast<size_t>(l) * a.max_pages + pos / a.page_size];
-    if (page < 0 || page >= a.pool_pages) page = 0;  // an unmapped page reads page 0
+    if (page < 0 || page >= a.pool_pages) {
+      atomicOr(a.status, kStatusBadPage);
+      page = 0;
+    }
     return static_cast<long long>(page) * a.page_stride + kvh * a.head_stride +
            static_cast<long long>(pos % a.page_size) * D;
   } else {
@@ -985,7 +992,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       ++nbar;
       if (failed) atomicOr(a.status, kStatusAbort);
       unsigned long long* t = (ctrace && 2 * nbar < kMegaTraceProducer) ? ctrace + 2 * nbar - 1 : nullptr;
-      return mega_grid_sync(a.bar, nbar * static_cast<unsigned>(ctas), a.status, &s_flags[0], t) && !failed;
+      const bool arrive = !(a.test_skip_arrival && nbar == 1 && blockIdx.x == 0);
+      return mega_grid_sync(a.bar, nbar * static_cast<unsigned>(ctas), a.status, &s_flags[0], t, a.wait_ns,
+                            arrive) &&
+             !failed;
     };
     bool run = true;
     for (int l = 0; l < a.layers && run; ++l) {

@@ -102,6 +102,11 @@ struct SampleArgs {
   int32_t* history;
   int history_len;
   int advance;
+  // Single-row calls may pass the parameters by value instead (inline_params
+  // set): nothing is read from memory, so the launch can be captured.
+  int inline_params;
+  float inv_temperature_v, top_p_v, uniform_v;
+  int top_k_v;
 };
 
 __device__ __forceinline__ float block_max_1024(float v, float* red32) {
@@ -174,7 +179,7 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
   pdl_launch_next();
   const float* L = a.logits + static_cast<long long>(row) * a.row_stride;
   const int V = a.vocab;
-  const float inv_t = a.inv_temperature[row];
+  const float inv_t = a.inline_params ? a.inv_temperature_v : a.inv_temperature[row];
   int picked = 0;
 
   if (!(inv_t > 0.0f)) {
@@ -212,7 +217,7 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
     }
     const float total = block_tree_sum_1024(acc, red32);  // synchronises hist too
 
-    int k = a.top_k[row];
+    int k = a.inline_params ? a.top_k_v : a.top_k[row];
     int M = k > 0 ? k : V;
     M = min(M, min(kMaxCandidates, V));
 
@@ -371,14 +376,16 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_rows_kernel(cons
 
     if (tid == 0) {
       float u;
-      if (a.uniform != nullptr) {
+      if (a.inline_params) {
+        u = a.uniform_v;
+      } else if (a.uniform != nullptr) {
         u = a.uniform[row];
       } else {
         // Stream 0: a sequence's draws depend on its seed and position only,
         // not on the batch slot it occupies.
         u = philox_uniform(a.seed[row], static_cast<unsigned long long>(a.counter[row]), 0u);
       }
-      const float top_p = a.top_p[row];
+      const float top_p = a.inline_params ? a.top_p_v : a.top_p[row];
       int keep = 0;
       float kept = 0.0f;
       for (int j = 0; j < M; ++j) {

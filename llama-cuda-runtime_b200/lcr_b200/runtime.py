@@ -33,6 +33,9 @@ FLAG_TRACE = 8
 # reference's bf16 storage rounding: closer to the fp32 host evaluation, about
 # 10 % slower.
 FLAG_FP32_ACT = 16
+# Tests only: the persistent step's grid barriers wait 50 ms and CTA 0 skips
+# its first arrival, so every step stops with LCR_ERR_TIMEOUT.
+FLAG_TEST_TIMEOUT = 32
 
 
 class LcrError(RuntimeError):
@@ -112,6 +115,7 @@ _SIGS = {
     "lcr_ctx_create": (_I, [ctypes.POINTER(ModelDesc), ctypes.POINTER(Weights),
                             ctypes.POINTER(Options), ctypes.POINTER(_V)]),
     "lcr_ctx_destroy": (None, [_V]),
+    "lcr_rope_inv_freq": (_I, [ctypes.POINTER(ModelDesc), _V, _I]),
     "lcr_reset": (_I, [_V]),
     "lcr_position": (_I, [_V]),
     "lcr_decode": (_I, [_V, _I, ctypes.POINTER(_V)]),
@@ -219,6 +223,14 @@ def desc_of(geom: ck.Geometry) -> ModelDesc:
                      geom.rope_theta, int(geom.rope_scaling), geom.rope_factor,
                      geom.rope_low_freq_factor, geom.rope_high_freq_factor,
                      geom.rope_original_max_position_embeddings)
+
+
+def rope_inv_freq(geom: ck.Geometry) -> np.ndarray:
+    """The context's RoPE inverse frequencies for `geom` (lcr_rope_inv_freq)."""
+    out = np.zeros(geom.head_dim // 2, dtype=np.float32)
+    d = desc_of(geom)
+    check(lib().lcr_rope_inv_freq(ctypes.byref(d), out.ctypes.data, out.size))
+    return out
 
 
 class Model:

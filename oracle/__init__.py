@@ -22,10 +22,22 @@ MODE_BF16_REORDERED = 2
 MODE_FP32_KV_BF16 = 3
 
 
-def build(ref: bool = False) -> None:
+def json_include() -> str:
+    """A directory holding nlohmann/json.hpp (the single-header library the
+    reference pins, v3.11): the copy vendored with cudnn_frontend in this
+    Python environment."""
+    import sysconfig
+
+    return os.path.join(sysconfig.get_paths()["purelib"], "include", "cudnn_frontend", "thirdparty")
+
+
+def build(ref_dir: Optional[str] = None) -> None:
+    """Builds liblcr oracle; with `ref_dir` (a reference checkout) also the
+    reference's own host code into _ref/."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref and os.path.isdir("/root/reference"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    if ref_dir and os.path.isdir(os.path.join(ref_dir, "src")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_dir}", f"JSON_INC={json_include()}"],
+                       check=True)
 
 
 class _Config(ctypes.Structure):

@@ -74,3 +74,22 @@ def test_context_without_device_fails_cleanly(L):
     ctx = ctypes.c_void_p()
     st = L.lcr_ctx_create(ctypes.byref(desc), ctypes.byref(w), ctypes.byref(o), ctypes.byref(ctx))
     assert st == 7 and not ctx.value
+
+
+def test_library_rope_table_bit_exact_vs_reference_code(L):
+    """The inverse frequencies the library rotates with are bit-identical to
+    the reference's own compute_rope_inv_freq (src/config.cpp:223-259, its
+    output committed in tests/golden/ref_rope.json), scaled and unscaled."""
+    import json
+
+    import numpy as np
+
+    golden = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "ref_rope.json")))
+    for name, geom in (("llama-3.2-1b", ck.LLAMA_3_2_1B),
+                       ("unscaled", ck.Geometry(hidden_size=2048, intermediate_size=5632, num_layers=22,
+                                                 num_heads=32, num_kv_heads=32, head_dim=64, vocab_size=32000,
+                                                 rope_theta=10000.0, rope_scaling=False))):
+        cfg = golden[name]["config"]
+        assert cfg["rope_theta"] == geom.rope_theta and cfg["head_dim"] == geom.head_dim
+        got = rt.rope_inv_freq(geom).view(np.uint32).tolist()
+        assert got == golden[name]["inv_freq_bits"], name

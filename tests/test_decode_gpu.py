@@ -175,6 +175,37 @@ def test_paged_block_tables_match_oracle_allocator(tiny):
     assert np.array_equal(tables, want)
 
 
+def test_timeout_path_reports_and_recovers(tiny):
+    """A grid barrier that never fills, made on purpose without faulting
+    anything: the test switch has CTA 0 skip its first arrival and bounds
+    every grid-barrier wait at 50 ms. The waiting CTAs give up, raise the
+    abort bit, the producers stop at it and drain the copies they issued, and
+    every step of the prompt ends quickly; the host reads LCR_ERR_TIMEOUT.
+    The context is then destroyed, and fresh contexts on the same device and
+    weights compute the normal result."""
+    import time
+
+    block, wdev = tiny
+    prompt = ck.prompt_ids(0, 8)
+    m = rt.Model(block, wdev, max_seq=32, flags=rt.FLAG_TEST_TIMEOUT)
+    t0 = time.perf_counter()
+    with pytest.raises(rt.LcrError) as e:
+        m.prefill(prompt)
+    assert e.value.status == 4, e.value  # LCR_ERR_TIMEOUT
+    assert time.perf_counter() - t0 < 10.0
+    m.close()
+    a = rt.Model(block, wdev, max_seq=32)
+    a.prefill(prompt)
+    got = a.logits_to_host()
+    ref = oracle.Model(block, 32)
+    for pos, tok in enumerate(prompt):
+        want = ref.decode(int(tok), pos, oracle.MODE_BF16)
+    assert np.abs(got - want).max() <= 1e-2
+    b = rt.Model(block, wdev, max_seq=32)
+    b.prefill(prompt)
+    assert np.array_equal(b.logits_to_host(), got)
+
+
 def test_bad_inputs_are_rejected(tiny):
     block, wdev = tiny
     m = rt.Model(block, wdev, max_seq=8)

@@ -100,22 +100,34 @@ def test_noalloc_matches_scratch_entry(heads, kv, d, pos, splits, paged):
 
 @pytest.mark.gpu
 def test_noalloc_interleaved_shapes():
-    """Calls of different shapes on one stream reuse the array in turn."""
+    """Calls of different shapes, one after another on one stream with no
+    host synchronisation between them, reuse the array in turn: every result
+    equals lcr_decode_attention's on caller scratch (same kernels, so bit for
+    bit), whatever the previous call left in the array."""
     torch = _cuda()
     s = rt.stream_ptr()
-    cases = [CASES[0], CASES[3], CASES[0]]
-    results = []
+    cases = [CASES[0], CASES[3], CASES[2], CASES[0]]
+    keep, pairs = [], []
     for heads, kv, d, pos, splits, paged in cases:
-        view, q, keep = _case(torch, heads, kv, d, pos, splits, paged, seed=7)
+        view, q, k = _case(torch, heads, kv, d, pos, splits, paged, seed=7)
+        keep += [k, view, q]
         scale = float(np.float32(1.0) / np.sqrt(np.float32(d)))
         out = torch.empty(heads * d, dtype=torch.int16, device="cuda")
+        want = torch.empty(heads * d, dtype=torch.int16, device="cuda")
+        nscr = max(2, L.lcr_decode_attention_scratch_floats(heads, d, splits))
+        scratch = torch.empty(nscr, dtype=torch.float32, device="cuda")
+        keep.append(scratch)
         rt.check(L.lcr_decode_attention_noalloc(out.data_ptr(), q.data_ptr(), ctypes.byref(view),
                                                 heads, heads // kv, pos, scale, int(paged),
                                                 splits, s))
-        torch.cuda.synchronize()
-        results.append(out.cpu().numpy().copy())
-        del keep
-    assert np.array_equal(results[0], results[2])
+        rt.check(L.lcr_decode_attention(want.data_ptr(), q.data_ptr(), ctypes.byref(view), heads,
+                                        heads // kv, pos, scale, int(paged), splits,
+                                        scratch.data_ptr(), s))
+        pairs.append((out, want))
+    torch.cuda.synchronize()
+    for k, (out, want) in enumerate(pairs):
+        assert np.array_equal(out.cpu().numpy(), want.cpu().numpy()), f"call {k + 1}"
+    del keep
 
 
 def test_noalloc_rejects_oversized_partials():
