@@ -224,7 +224,10 @@ typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
   int flags;            /* bit 0: no programmatic dependent launch,
                            bit 1: no CUDA graph, bit 2: multi-kernel step
                            instead of the persistent single-kernel step,
-                           bit 3: record per-phase timestamps (trace) */
+                           bit 3: record per-phase timestamps (trace),
+                           bit 4: persistent step with fp32 activations,
+                           bit 5: tests only (grid-barrier timeout path),
+                           bit 6: lcr_prefill one decode step per token */
 } lcr_options;
 
 typedef struct lcr_ctx lcr_ctx;
@@ -249,8 +252,16 @@ LCR_API int lcr_position(const lcr_ctx* ctx);
  * call. Synchronous, like the reference. */
 LCR_API int lcr_decode(lcr_ctx* ctx, int token, const float** logits);
 
-/* Model::prefill, src/model.cu:308-345: the prompt, one decode step per token
- * (the same maths as a decode step); *logits for the last token. */
+/* Model::prefill, src/model.cu:308-345: the prompt at the current position;
+ * *logits for the last token, and the device state as after the reference's
+ * per-token prefill (next token = the argmax of those logits, position
+ * advanced). Prompts of two or more tokens run in chunks of up to 2048 rows on
+ * the tcgen05 path of lcr_batch_prefill (projections as GEMMs over the
+ * chunk, causal attention over the cache), writing this context's own cache;
+ * one decode step per token, as the reference, with options bit 6, with
+ * fp32 activations (bit 4), with a paged cache whose page size is not a
+ * multiple of 16, or for a model the batch kernels are not built for.
+ * Synchronous. */
 LCR_API int lcr_prefill(lcr_ctx* ctx, const int32_t* tokens, int count,
                 const float** logits);
 

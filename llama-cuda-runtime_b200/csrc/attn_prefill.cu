@@ -49,7 +49,12 @@ int by_group(const PrefillAttnArgs& a, const CUtensorMap& k, const CUtensorMap& 
 
 int attn_prefill_launch(const PrefillAttnArgs& a, const CUtensorMap& kmap, const CUtensorMap& vmap, int head_dim,
                         int group, int kv_heads, cudaStream_t s) {
-  LCRB_REQUIRE(a.count >= 1 && a.start >= 0 && a.page_size % kAbUnit == 0, LCR_ERR_SHAPE,
+  // Keys are fetched 16 positions at a time from the page of the first, so
+  // pages hold a multiple of 16 -- except a single page holding every
+  // position (a contiguous cache): its last fetch may run past the page, into
+  // rows of keys after every query (masked) or past the pool (zero fill).
+  const bool one_page = a.pool_pages == 1 && a.start + a.count <= a.page_size;
+  LCRB_REQUIRE(a.count >= 1 && a.start >= 0 && (a.page_size % kAbUnit == 0 || one_page), LCR_ERR_SHAPE,
                "prefill attention: unsupported chunk (%d rows at %d, page size %d)", a.count, a.start, a.page_size);
   if (head_dim == 64) {
     switch (group) {

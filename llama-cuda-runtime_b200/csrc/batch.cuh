@@ -119,6 +119,7 @@ struct KvWriteArgs {
   int page_size, pool_pages;
   long long page_stride, head_stride;
   int start, count;
+  int limit;  // positions the cache holds: padding rows at or past it are skipped
   uint32_t* status;
 };
 
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(128) kv_write_kernel(const KvWriteArgs a) {
   pdl_launch_next();
   const int r = blockIdx.x;
   const int pos = a.start + r;
+  if (pos >= a.limit) return;  // a padding row past the end of the cache
   int page = a.table[pos / a.page_size];
   if (page < 0 || page >= a.pool_pages) {
     if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusBadPage);

@@ -37,6 +37,7 @@
 #include "attn_batch.h"
 #include "attn_prefill.h"
 #include "batch.cuh"
+#include "batch_internal.h"
 #include "common.cuh"
 #include "dispatch.h"
 #include "gemm_tc.h"
@@ -734,22 +735,18 @@ int prefill_reserve(lcr_batch* c, int rows) {
 
 }  // namespace
 
-extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, int count, int start) {
-  LCRB_REQUIRE(c && tokens, LCR_ERR_INVALID, "null argument");
-  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d outside 0..%d", slot,
-               c->o.max_batch - 1);
-  LCRB_REQUIRE(count >= 1 && start >= 0 && start + count <= c->o.max_seq, LCR_ERR_STATE,
-               "prefill of %d positions at %d outside the cache built for %d", count, start, c->o.max_seq);
-  LCRB_REQUIRE((start + count - 1) / c->o.page_size < c->pages_set[static_cast<size_t>(slot)], LCR_ERR_STATE,
-               "slot %d: no page for position %d (its table holds %d pages)", slot, start + count - 1,
-               c->pages_set[static_cast<size_t>(slot)]);
+namespace lcrb {
+
+cudaStream_t batch_stream(lcr_batch* c) { return c->stream; }
+int make_prefill_kv_map(CUtensorMap* out, const bf16* pool, int rows, int head_dim) {
+  return make_kmajor_map(out, pool, rows, head_dim, 1, kAbUnit, head_dim / 64);
+}
+int batch_check_status(lcr_batch* c) { return check_status(c); }
+
+int batch_prefill_into(lcr_batch* c, const PrefillKv& kv, const int32_t* tokens, int count, int start,
+                       float* logits) {
   const lcr_model_desc& d = c->d;
-  for (int i = 0; i < count; ++i) {
-    LCRB_REQUIRE(tokens[i] >= 0 && tokens[i] < d.vocab_size, LCR_ERR_INVALID, "token %d: id %d outside the vocabulary",
-                 i, tokens[i]);
-  }
   LCRB_CUDA(cudaSetDevice(c->device));
-  LCRB_TRY(upload_slot_state(c));
   LCRB_TRY(prefill_reserve(c, count));
   const Acts& v = c->pre;
   const int H = d.hidden_size, F = d.intermediate_size;
@@ -787,12 +784,12 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     LCRB_TRY(make_kmajor_map(&m2.attn, v.attn, c->pre_rows, qd, 1, 256, 1));
     LCRB_TRY(make_kmajor_map(&m2.act, v.act, c->pre_rows, F, 1, 256, 1));
   }
-  const int32_t* table = c->tables + static_cast<size_t>(slot) * c->max_pages;
   const int group = d.num_heads / d.num_kv_heads;
   const int pad_rows = (start + count + 15) / 16 * 16 - start;
   for (int l = 0; l < d.num_layers; ++l) {
     const lcr_layer_weights& w = c->layers[static_cast<size_t>(l)];
     const CUtensorMap* wm = &c->wmaps1[static_cast<size_t>(4 * l)];
+    const int32_t* table = kv.table + static_cast<size_t>(l) * kv.table_layer_stride;
     LCRB_TRY(norm_launch(c, v, count, l == 0, w.input_norm));
     LCRB_TRY(gemm_node(c, v, wm[0], wide_qkv ? m2.xn : m.xn, wide_qkv ? 256 : nb, count, qd + 2 * kvd, H, EPI_ROPE,
                        v.qkv, nullptr, qd + 2 * kvd, 1));
@@ -803,15 +800,16 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     kw.kv_dim = kvd;
     kw.head_dim = d.head_dim;
     kw.kv_heads = d.num_kv_heads;
-    kw.kpool = c->kpool + static_cast<size_t>(l) * c->layer_elems;
-    kw.vpool = c->vpool + static_cast<size_t>(l) * c->layer_elems;
+    kw.kpool = kv.kpool + static_cast<size_t>(l) * kv.layer_elems;
+    kw.vpool = kv.vpool + static_cast<size_t>(l) * kv.layer_elems;
     kw.table = table;
-    kw.page_size = c->o.page_size;
-    kw.pool_pages = c->o.pool_pages;
-    kw.page_stride = static_cast<long long>(d.num_kv_heads) * c->o.page_size * d.head_dim;
-    kw.head_stride = static_cast<long long>(c->o.page_size) * d.head_dim;
+    kw.page_size = kv.page_size;
+    kw.pool_pages = kv.pool_pages;
+    kw.page_stride = static_cast<long long>(d.num_kv_heads) * kv.page_size * d.head_dim;
+    kw.head_stride = static_cast<long long>(kv.page_size) * d.head_dim;
     kw.start = start;
     kw.count = count;
+    kw.limit = kv.limit;
     kw.status = c->status;
     LCRB_TRY(launch_kernel(kv_write_kernel, dim3(static_cast<unsigned>(pad_rows)), dim3(128), 0, c->stream, true, kw));
     PrefillAttnArgs pa = {};
@@ -820,15 +818,15 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     pa.q_dim = qd;
     pa.kv_dim = kvd;
     pa.table = table;
-    pa.page_size = c->o.page_size;
-    pa.pool_pages = c->o.pool_pages;
+    pa.page_size = kv.page_size;
+    pa.pool_pages = kv.pool_pages;
     pa.start = start;
     pa.count = count;
     pa.scale_log2 = (1.0f / std::sqrt(static_cast<float>(d.head_dim))) * kLog2e;
     pa.out = v.attn;
     pa.status = c->status;
-    LCRB_TRY(attn_prefill_launch(pa, c->kvmaps[static_cast<size_t>(2 * l)], c->kvmaps[static_cast<size_t>(2 * l + 1)],
-                                 d.head_dim, group, d.num_kv_heads, c->stream));
+    const CUtensorMap* km = kv.kvmaps + static_cast<size_t>(l) * kv.kvmap_layer_stride;
+    LCRB_TRY(attn_prefill_launch(pa, km[0], km[1], d.head_dim, group, d.num_kv_heads, c->stream));
     LCRB_TRY(gemm_node(c, v, wm[1], wide_o ? m2.attn : m.attn, wide_o ? 256 : nb, count, H, qd, EPI_RESID, nullptr,
                        nullptr, H, 1));
     LCRB_TRY(norm_launch(c, v, count, false, w.post_attention_norm));
@@ -837,17 +835,50 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
     LCRB_TRY(gemm_node(c, v, wm[3], wide_down ? m2.act : m.act, wide_down ? 256 : nb, count, H, F, EPI_RESID, nullptr,
                        nullptr, H, 1));
   }
-  // The last row only: final norm, lm_head into this slot's logits, sample
-  // with this slot's parameters and Philox counter = the last position.
+  // The last row only: final norm, lm_head into fp32 logits.
   Acts last = v;
   last.x += static_cast<size_t>(count - 1) * H;
   last.xsum += static_cast<size_t>(count - 1) * H;
   LCRB_TRY(norm_launch(c, last, 1, false, c->final_norm));
   CUtensorMap xlast;
   LCRB_TRY(make_kmajor_map(&xlast, v.xn, c->pre_rows, H, 1, 16, c->tc_chunks));
+  return gemm_node(c, last, c->wmaps.back(), xlast, 16, 1, d.vocab_size, H, EPI_STORE_F32, nullptr, logits,
+                   d.vocab_size, c->tc_chunks);
+}
+
+}  // namespace lcrb
+
+extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, int count, int start) {
+  LCRB_REQUIRE(c && tokens, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(slot >= 0 && slot < c->o.max_batch, LCR_ERR_INVALID, "slot %d outside 0..%d", slot,
+               c->o.max_batch - 1);
+  LCRB_REQUIRE(count >= 1 && start >= 0 && start + count <= c->o.max_seq, LCR_ERR_STATE,
+               "prefill of %d positions at %d outside the cache built for %d", count, start, c->o.max_seq);
+  LCRB_REQUIRE((start + count - 1) / c->o.page_size < c->pages_set[static_cast<size_t>(slot)], LCR_ERR_STATE,
+               "slot %d: no page for position %d (its table holds %d pages)", slot, start + count - 1,
+               c->pages_set[static_cast<size_t>(slot)]);
+  const lcr_model_desc& d = c->d;
+  for (int i = 0; i < count; ++i) {
+    LCRB_REQUIRE(tokens[i] >= 0 && tokens[i] < d.vocab_size, LCR_ERR_INVALID, "token %d: id %d outside the vocabulary",
+                 i, tokens[i]);
+  }
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(upload_slot_state(c));
+  // The batch's own pools: one per layer, the slot's table shared by all layers.
+  PrefillKv kv = {};
+  kv.kpool = c->kpool;
+  kv.vpool = c->vpool;
+  kv.layer_elems = c->layer_elems;
+  kv.table = c->tables + static_cast<size_t>(slot) * c->max_pages;
+  kv.table_layer_stride = 0;
+  kv.page_size = c->o.page_size;
+  kv.pool_pages = c->o.pool_pages;
+  kv.kvmaps = c->kvmaps.data();
+  kv.kvmap_layer_stride = 2;
+  kv.limit = c->max_pages * c->o.page_size;
   float* logits = c->logits + static_cast<size_t>(slot) * d.vocab_size;
-  LCRB_TRY(gemm_node(c, last, c->wmaps.back(), xlast, 16, 1, d.vocab_size, H, EPI_STORE_F32, nullptr, logits,
-                     d.vocab_size, c->tc_chunks));
+  LCRB_TRY(batch_prefill_into(c, kv, tokens, count, start, logits));
+  // Sample with this slot's parameters and Philox counter = the last position.
   SampleArgs s = {};
   s.logits = logits;
   s.row_stride = d.vocab_size;
@@ -857,7 +888,7 @@ extern "C" int lcr_batch_prefill(lcr_batch* c, int slot, const int32_t* tokens, 
   s.top_p = c->top_p + slot;
   s.uniform = nullptr;
   s.seed = c->seed + slot;
-  s.counter = v.positions + (count - 1);
+  s.counter = c->pre.positions + (count - 1);
   s.out = c->next + slot;
   return sample_launch(s, 1, c->stream, true);
 }

@@ -29,6 +29,7 @@
 #include <new>
 #include <vector>
 
+#include "batch_internal.h"
 #include "common.cuh"
 #include "dispatch.h"
 #include "gemv_dispatch.h"
@@ -77,11 +78,16 @@ namespace {
 
 // Bit 4: the persistent step with fp32 activations instead of the
 // reference's bf16 storage rounding (closer to the fp32 evaluation, slower).
+// Bit 6: lcr_prefill runs the prompt one decode step per token, as the
+// reference does, instead of in tcgen05 chunks.
 // Bit 5 (tests only): the persistent step's grid barriers wait at most 50 ms
 // and CTA 0 skips its first arrival, so the first barrier times out -- the
 // timeout path, exercised without faulting or hanging the GPU.
 enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8, kFlagFp32Act = 16,
-             kFlagTestTimeout = 32 };
+             kFlagTestTimeout = 32, kFlagPerTokenPrefill = 64 };
+// Prompt rows per tcgen05 prefill chunk, and the shortest prompt chunked.
+constexpr int kPrefillChunk = 2048;
+constexpr int kPrefillChunkMin = 2;
 constexpr int kPinnedRing = 256;
 constexpr int kTimingSlots = 128;
 
@@ -160,6 +166,13 @@ struct lcr_ctx {
   int32_t* pinned_prompt = nullptr;
   size_t pinned_prompt_cap = 0;
   float* pinned_params = nullptr;
+
+  // Chunked prefill: a one-slot batch context over the same weights, whose
+  // tcgen05 prefill writes this context's cache (created on first use).
+  lcr_batch* prefill_engine = nullptr;
+  bool prefill_unavailable = false;
+  std::vector<CUtensorMap> prefill_kvmaps;
+  int32_t* prefill_table = nullptr;  // contiguous cache: the one page, {0}
 };
 
 namespace {
@@ -412,11 +425,131 @@ int stage_state(lcr_ctx* c, const int32_t* token_src, int position) {
   return LCR_OK;
 }
 
+// The chunked-prefill engine and the tensor maps of this context's cache
+// rows (created on first use). Returns false where the chunked path does not
+// apply: the fp32-activation step, a paged cache with pages of other than a
+// multiple of 16 positions, or a model the batch kernels are not built for
+// (the prompt then runs one decode step per token).
+bool prefill_engine_ready(lcr_ctx* c) {
+  if (c->prefill_engine) return true;
+  if (c->prefill_unavailable) return false;
+  c->prefill_unavailable = true;
+  const lcr_model_desc& d = c->d;
+  if (c->f32 || (c->o.flags & kFlagPerTokenPrefill)) return false;
+  if (c->o.paged && c->o.page_size % 16 != 0) return false;
+  lcr_weights w = {};
+  w.embedding = c->embed;
+  w.final_norm = c->final_norm;
+  w.lm_head = c->lm_head;
+  w.layers = c->layers.data();
+  lcr_batch_options bo = {};
+  bo.device = c->device;
+  bo.max_batch = 1;
+  bo.max_seq = 16;
+  bo.page_size = 16;
+  bo.pool_pages = 1;
+  bo.flags = 0;
+  lcr_batch* engine = nullptr;
+  if (lcr_batch_create(&d, &w, &bo, &engine) != LCR_OK) return false;
+  std::vector<CUtensorMap> maps;
+  int st = LCR_OK;
+  if (c->o.paged) {
+    const long long rows = static_cast<long long>(c->pool_pages) * d.num_kv_heads * c->o.page_size;
+    maps.resize(2);
+    if (rows > INT32_MAX) st = LCR_ERR_SHAPE;
+    if (st == LCR_OK) st = make_prefill_kv_map(&maps[0], c->kpool, static_cast<int>(rows), d.head_dim);
+    if (st == LCR_OK) st = make_prefill_kv_map(&maps[1], c->vpool, static_cast<int>(rows), d.head_dim);
+  } else {
+    const size_t layer_elems = static_cast<size_t>(d.num_kv_heads) * c->o.max_seq * d.head_dim;
+    const int rows = d.num_kv_heads * c->o.max_seq;
+    maps.resize(static_cast<size_t>(2 * d.num_layers));
+    for (int l = 0; l < d.num_layers && st == LCR_OK; ++l) {
+      st = make_prefill_kv_map(&maps[static_cast<size_t>(2 * l)], c->kpool + l * layer_elems, rows, d.head_dim);
+      if (st == LCR_OK) {
+        st = make_prefill_kv_map(&maps[static_cast<size_t>(2 * l + 1)], c->vpool + l * layer_elems, rows, d.head_dim);
+      }
+    }
+    if (st == LCR_OK && cudaMalloc(&c->prefill_table, sizeof(int32_t)) != cudaSuccess) st = LCR_ERR_CUDA;
+    if (st == LCR_OK && cudaMemset(c->prefill_table, 0, sizeof(int32_t)) != cudaSuccess) st = LCR_ERR_CUDA;
+  }
+  if (st != LCR_OK) {
+    lcr_batch_destroy(engine);
+    cudaFree(c->prefill_table);
+    c->prefill_table = nullptr;
+    return false;
+  }
+  c->prefill_engine = engine;
+  c->prefill_kvmaps = std::move(maps);
+  c->prefill_unavailable = false;
+  return true;
+}
+
+// Prompt positions [c->position, c->position + count) in tcgen05 chunks of up
+// to kPrefillChunk rows: projections as GEMMs over the chunk's rows, causal
+// attention over the cache, K/V written into this context's cache. Leaves the
+// last row's logits in c->logits and the device state as the per-token path
+// does (next token = their argmax, position advanced, history entry set).
+int prefill_chunked(lcr_ctx* c, const int32_t* tokens, int count) {
+  const lcr_model_desc& d = c->d;
+  PrefillKv kv = {};
+  kv.kpool = c->kpool;
+  kv.vpool = c->vpool;
+  kv.kvmaps = c->prefill_kvmaps.data();
+  if (c->o.paged) {
+    kv.layer_elems = 0;
+    kv.table = c->tables_dev;
+    kv.table_layer_stride = static_cast<size_t>(c->max_pages);
+    kv.page_size = c->o.page_size;
+    kv.pool_pages = c->pool_pages;
+    kv.kvmap_layer_stride = 0;
+    kv.limit = c->max_pages * c->o.page_size;
+  } else {
+    kv.layer_elems = static_cast<size_t>(d.num_kv_heads) * c->o.max_seq * d.head_dim;
+    kv.table = c->prefill_table;
+    kv.table_layer_stride = 0;
+    kv.page_size = c->o.max_seq;
+    kv.pool_pages = 1;
+    kv.kvmap_layer_stride = 2;
+    kv.limit = c->o.max_seq;
+  }
+  // The engine's stream follows everything queued on this context's stream.
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  for (int done = 0; done < count;) {
+    const int n = std::min(kPrefillChunk, count - done);
+    LCRB_TRY(batch_prefill_into(c->prefill_engine, kv, tokens + done, n, c->position + done, c->logits));
+    done += n;
+  }
+  LCRB_TRY(batch_check_status(c->prefill_engine));
+  // Device state after the last prompt token: greedy pick of its logits.
+  int32_t* slot = c->pinned + 2 * c->ring_next;
+  c->ring_next = (c->ring_next + 1) % kPinnedRing;
+  slot[0] = tokens[count - 1];
+  slot[1] = c->position + count - 1;
+  LCRB_CUDA(cudaMemcpyAsync(c->state, slot, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+  SampleArgs s = {};
+  s.logits = c->logits;
+  s.row_stride = d.vocab_size;
+  s.vocab = d.vocab_size;
+  s.inline_params = 1;
+  s.inv_temperature_v = 0.f;
+  s.top_p_v = 1.f;
+  s.top_k_v = 0;
+  s.out = c->sampled;
+  s.state_token = c->state;
+  s.state_pos = c->state + 1;
+  s.history = c->history;
+  s.history_len = c->o.max_seq;
+  s.advance = 1;
+  return sample_launch(s, 1, c->stream, false);
+}
+
 void release(lcr_ctx* c) {
   if (c == nullptr) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->exec) cudaGraphExecDestroy(c->exec);
+  lcr_batch_destroy(c->prefill_engine);
+  cudaFree(c->prefill_table);
   cudaFree(c->buf);
   cudaFree(c->kpool);
   cudaFree(c->vpool);
@@ -763,6 +896,13 @@ extern "C" int lcr_prefill(lcr_ctx* c, const int32_t* tokens, int count, const f
   }
   LCRB_CUDA(cudaSetDevice(c->device));
   LCRB_TRY(lcr_reserve_length(c, c->position + count));
+  if (count >= kPrefillChunkMin && prefill_engine_ready(c)) {
+    LCRB_TRY(prefill_chunked(c, tokens, count));
+    LCRB_TRY(check_status(c));
+    c->position += count;
+    if (logits) *logits = c->logits;
+    return LCR_OK;
+  }
   const size_t need = static_cast<size_t>(count) * 2;
   if (c->pinned_prompt_cap < need) {
     LCRB_CUDA(cudaStreamSynchronize(c->stream));

@@ -36,6 +36,9 @@ FLAG_FP32_ACT = 16
 # Tests only: the persistent step's grid barriers wait 50 ms and CTA 0 skips
 # its first arrival, so every step stops with LCR_ERR_TIMEOUT.
 FLAG_TEST_TIMEOUT = 32
+# lcr_prefill one decode step per token, as the reference's Model::prefill,
+# instead of the tcgen05 chunks of up to 2048 prompt rows.
+FLAG_PER_TOKEN_PREFILL = 64
 
 
 class LcrError(RuntimeError):

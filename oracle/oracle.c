@@ -569,7 +569,12 @@ int orc_prefill(const orc_config* c, const orc_weights* w, orc_state* s,
     }
     if (bf) orc_round_bf16_inplace(qr, N * qd);
     /* causal GQA attention of every chunk row over the cache up to its own
-       position, q scaled once, fp32 softmax */
+       position, q scaled once, fp32 softmax. In ORC_MODE_BF16 a chunk of more
+       than one row stores the normalised probabilities as bf16 before they
+       multiply V (causal_softmax_kernel, src/kernels/attention.cu:42-100,
+       feeding the P.V GEMM of src/model.cu:545-551); a chunk of one row takes
+       the decode attention, fp32 throughout (src/model.cu:412-413). */
+    const int round_p = bf && n > 1;
 #pragma omp parallel
     {
       float* sc = (float*)malloc(sizeof(float) * (size_t)(start + n));
@@ -591,6 +596,10 @@ int orc_prefill(const orc_config* c, const orc_weights* w, orc_state* s,
             sc[p] = (float)exp((double)sc[p] - mx);
             sum += sc[p];
           }
+          const float inv_sum = (float)(1.0 / sum);
+          if (round_p) {
+            for (int p = 0; p < seq; ++p) sc[p] = rb(sc[p] * inv_sum);
+          }
           for (int i = 0; i < d; ++i) acc[i] = 0.f;
           for (int p = 0; p < seq; ++p) {
             const __m256 pv = _mm256_set1_ps(sc[p]);
@@ -599,7 +608,9 @@ int orc_prefill(const orc_config* c, const orc_weights* w, orc_state* s,
                                                         _mm256_loadu_ps(acc + i)));
             }
           }
-          for (int i = 0; i < d; ++i) attn[(size_t)t * qd + (size_t)h * d + i] = (float)(acc[i] / sum);
+          for (int i = 0; i < d; ++i) {
+            attn[(size_t)t * qd + (size_t)h * d + i] = round_p ? acc[i] : (float)(acc[i] / sum);
+          }
         }
       }
       free(sc);

@@ -101,13 +101,14 @@ int orc_decode(const orc_config* c, const orc_weights* w, orc_state* s,
                int token, int position, int mode, float* logits, float* taps);
 void orc_set_threads(int n);
 /* n consecutive tokens at positions start..start+n-1 as one chunk (the
- * reference's chunked prefill, src/model.cu:308-345): the projections as
- * GEMMs over the chunk, causal attention of each row over the cache up to its
- * own position; the K/V rows are appended to the state's cache. Writes the
- * last row's [vocab] logits when last_logits is not NULL. ORC_MODE_FP32 and
- * ORC_MODE_BF16 only (the same rounding points as orc_decode; the summation
- * order of the chunk GEMM differs from the decode GEMV). Returns 0 on
- * success. */
+ * reference's chunked prefill, src/model.cu:308-345 and 509-556): the
+ * projections as GEMMs over the chunk, causal attention of each row over the
+ * cache up to its own position; the K/V rows are appended to the state's
+ * cache. Writes the last row's [vocab] logits when last_logits is not NULL.
+ * ORC_MODE_FP32, ORC_MODE_BF16 (the rounding points of orc_decode, plus, for
+ * n > 1, the bf16 probabilities of the reference's prefill softmax) and
+ * ORC_MODE_FP32_KV_BF16. The summation order of the chunk GEMM differs from
+ * the decode GEMV. Returns 0 on success. */
 int orc_prefill(const orc_config* c, const orc_weights* w, orc_state* s,
                 const int32_t* tokens, int n, int start, int mode,
                 float* last_logits);

@@ -38,23 +38,31 @@ def tiny():
 TINY_F32_ABS = 3e-3
 
 
-@pytest.mark.parametrize("flags", [0, rt.FLAG_FP32_ACT])
+@pytest.mark.parametrize("flags", [rt.FLAG_PER_TOKEN_PREFILL, 0, rt.FLAG_FP32_ACT])
 def test_tiny_prefill_and_greedy_vs_oracle(tiny, flags):
     """Prompt + 16 greedy steps on the tiny model, every step within the
-    north-star gates of the fp32 oracle; the reference rounding (default)
-    also within 1e-2 of the bf16-storage oracle, fp32 activations within 3e-3
-    of the oracle's fp32 evaluation over a bf16 KV cache."""
+    north-star gates of the fp32 oracle; the reference rounding also within
+    1e-2 of the bf16-storage oracle (the prompt as decode steps, or as one
+    chunk like the default tcgen05 prefill), fp32 activations within 3e-3 of
+    the oracle's fp32 evaluation over a bf16 KV cache."""
     block, wdev = tiny
     prompt = ck.prompt_ids(0, 32)
     m = rt.Model(block, wdev, max_seq=64, flags=flags)
-    own_mode, own_tol = ((oracle.MODE_FP32_KV_BF16, TINY_F32_ABS) if flags
-                         else (oracle.MODE_BF16, 1e-2))
+    # The chunk's bf16 probabilities are rounded per 16-key tile before
+    # normalisation, the reference's after (tests/test_prefill_chunked_gpu.py).
+    own_mode, own_tol = {rt.FLAG_FP32_ACT: (oracle.MODE_FP32_KV_BF16, TINY_F32_ABS),
+                         rt.FLAG_PER_TOKEN_PREFILL: (oracle.MODE_BF16, 1e-2),
+                         0: (oracle.MODE_BF16, 2e-2)}[flags]
     ref32 = oracle.Model(block, 64)
     own = oracle.Model(block, 64)
     m.prefill(prompt)
     for pos, tok in enumerate(prompt):
         l32 = ref32.decode(int(tok), pos, oracle.MODE_FP32)
-        lown = own.decode(int(tok), pos, own_mode)
+    if flags == 0:
+        lown = own.prefill(prompt, 0, own_mode)
+    else:
+        for pos, tok in enumerate(prompt):
+            lown = own.decode(int(tok), pos, own_mode)
     got = m.logits_to_host()
     pos = len(prompt)
     for step in range(17):
@@ -106,13 +114,15 @@ def test_step_variants_are_bit_identical(tiny, variant):
     block, wdev = tiny
     prompt = ck.prompt_ids(3, 40)
     multi = variant.get("flags", 0) & rt.FLAG_NO_PERSISTENT
-    base = rt.Model(block, wdev, max_seq=96)
+    # The prompt as decode steps, so that it runs through the variant too.
+    variant = dict(variant, flags=variant.get("flags", 0) | rt.FLAG_PER_TOKEN_PREFILL)
+    base = rt.Model(block, wdev, max_seq=96, flags=rt.FLAG_PER_TOKEN_PREFILL)
     other = rt.Model(block, wdev, max_seq=96, **variant)
     base.prefill(prompt)
     other.prefill(prompt)
     a, b = base.logits_to_host(), other.logits_to_host()
     order_changes = ("attention_splits" in variant or "gemv_ctas" in variant or multi)
-    if variant.get("flags", 0) == rt.FLAG_FP32_ACT:
+    if variant["flags"] & rt.FLAG_FP32_ACT:
         # fp32 activations against the reference rounding: the bf16 storage
         # of the intermediate tensors, not only the order
         assert np.abs(a - b).max() < 3e-2
@@ -132,21 +142,23 @@ def test_tiny_long_context_vs_oracle(tiny, paged):
     """700 cached positions: several 128-position KV stages per attention
     split and many splits per KV head, shuffled physical pages when paged --
     the persistent step's long-context path (config 3's shape on the tiny
-    model) against the oracle."""
+    model) against the oracle, after the prompt's chunked prefill (against
+    the oracle's chunk of the same rounding points)."""
     block, wdev = tiny
     prompt = ck.prompt_ids(3, 700)
     m = rt.Model(block, wdev, max_seq=760, paged=paged, page_size=16, page_order_seed=99)
     ref32 = oracle.Model(block, 760)
     ref16 = oracle.Model(block, 760)
     m.prefill(prompt)
-    for pos, tok in enumerate(prompt):
-        l32 = ref32.decode(int(tok), pos, oracle.MODE_FP32)
-        l16 = ref16.decode(int(tok), pos, oracle.MODE_BF16)
+    l32 = ref32.prefill(prompt, 0, oracle.MODE_FP32)
+    l16 = ref16.prefill(prompt, 0, oracle.MODE_BF16)
     got = m.logits_to_host()
     pos = len(prompt)
     for step in range(6):
         assert np.abs(got - l32).max() <= MAX_ABS and cos(got, l32) >= MIN_COS, step
-        assert np.abs(got - l16).max() <= 1e-2, step
+        # 2e-2: the chunk's per-tile bf16 probabilities against the
+        # reference's normalised ones (tests/test_prefill_chunked_gpu.py)
+        assert np.abs(got - l16).max() <= 2e-2, step
         tok = int(np.argmax(got))
         assert tok == oracle.argmax(l16), f"step {step}: greedy id differs from the bf16 oracle"
         m.decode(tok)
@@ -187,21 +199,23 @@ def test_timeout_path_reports_and_recovers(tiny):
 
     block, wdev = tiny
     prompt = ck.prompt_ids(0, 8)
-    m = rt.Model(block, wdev, max_seq=32, flags=rt.FLAG_TEST_TIMEOUT)
+    # The prompt as decode steps: each one a persistent step that times out.
+    per_token = rt.FLAG_PER_TOKEN_PREFILL
+    m = rt.Model(block, wdev, max_seq=32, flags=rt.FLAG_TEST_TIMEOUT | per_token)
     t0 = time.perf_counter()
     with pytest.raises(rt.LcrError) as e:
         m.prefill(prompt)
     assert e.value.status == 4, e.value  # LCR_ERR_TIMEOUT
     assert time.perf_counter() - t0 < 10.0
     m.close()
-    a = rt.Model(block, wdev, max_seq=32)
+    a = rt.Model(block, wdev, max_seq=32, flags=per_token)
     a.prefill(prompt)
     got = a.logits_to_host()
     ref = oracle.Model(block, 32)
     for pos, tok in enumerate(prompt):
         want = ref.decode(int(tok), pos, oracle.MODE_BF16)
     assert np.abs(got - want).max() <= 1e-2
-    b = rt.Model(block, wdev, max_seq=32)
+    b = rt.Model(block, wdev, max_seq=32, flags=per_token)
     b.prefill(prompt)
     assert np.array_equal(b.logits_to_host(), got)
 

@@ -275,7 +275,8 @@ def test_bf16_reproducibility_floor_1b(oracle_lib):
 def test_chunk_prefill_matches_token_steps(oracle_lib):
     """orc_prefill (the chunked prefill, GEMMs over the chunk) computes what
     the token-by-token decode computes: fp32 to summation order, the bf16
-    modes to the rounding of a few intermediate values."""
+    modes to the rounding of a few intermediate values (and, in the
+    reference's bf16 mode, of the prefill's bf16 probabilities)."""
     block = ck.cached(ck.TINY, 0)
     prompt = ck.prompt_ids(0, 40)
     for mode, tol in ((oracle_lib.MODE_FP32, 1e-5), (oracle_lib.MODE_FP32_KV_BF16, 1e-3),

@@ -1,0 +1,155 @@
+"""lcr_prefill's tcgen05 chunk path (the default for prompts of two or more
+tokens) through the C ABI: the prefilled cache's logits and the decode steps
+that follow, against the reference's own per-token prefill (one decode step
+per prompt token, options bit 6) and against the oracle's chunked prefill
+(src/model.cu:308-345) at the same rounding points.
+
+Tolerances: 2e-2 max-abs on the logits against the bf16-storage oracle's
+chunk and against the per-token path. Both the reference's prefill and this
+one multiply bf16 probabilities into V, but the reference rounds the
+normalised probabilities of the whole row (a softmax pass before the P.V
+GEMM) and this one the running-max-relative ones of each 16-key tile (one
+pass, normalised after P.V); with the GEMMs' other summation order that moves
+bf16 roundings of the activations, and the oracle's own chunk and per-token
+evaluations of the same prompt already differ by up to 2e-2 on this model.
+The north-star gates hold against fp32 (max-abs 3e-2, cosine 0.999)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from lcr_b200 import checkpoint as ck
+from lcr_b200 import runtime as rt
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+TOL = 2e-2
+MAX_ABS = 3e-2
+MIN_COS = 0.999
+
+
+def cos(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    block = ck.cached(ck.TINY, 0)
+    return block, rt.upload_block(block)
+
+
+def device_token(m):
+    """The next token the context's device state holds (what a step enqueued
+    without a host token continues from)."""
+    t = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    m.read_token(t.data_ptr())
+    m.sync()
+    return int(t[0])
+
+
+# (max_seq, paged, page_size, page_order_seed, prompt length): a contiguous
+# cache whose length is not a multiple of 16 (the chunk's padding rows stop at
+# the end of the cache), shuffled 16-position pages, 32-position pages.
+CASES = [dict(max_seq=45, paged=False, n=40), dict(max_seq=96, paged=True, page_size=16, seed=11, n=57),
+         dict(max_seq=96, paged=True, page_size=32, seed=0, n=33)]
+
+
+@pytest.mark.parametrize("case", CASES, ids=["contiguous-45", "paged16-shuffled", "paged32"])
+def test_chunked_prefill_vs_per_token_and_oracle(tiny, case):
+    block, wdev = tiny
+    prompt = ck.prompt_ids(6, case["n"])
+    kw = dict(max_seq=case["max_seq"], paged=case["paged"], page_size=case.get("page_size", 16),
+              page_order_seed=case.get("seed", 0))
+    chunk = rt.Model(block, wdev, **kw)
+    token = rt.Model(block, wdev, flags=rt.FLAG_PER_TOKEN_PREFILL, **kw)
+    o16 = oracle.Model(block, case["max_seq"])
+    o32 = oracle.Model(block, case["max_seq"])
+    chunk.prefill(prompt)
+    token.prefill(prompt)
+    want16 = o16.prefill(prompt, 0, oracle.MODE_BF16)
+    want32 = o32.prefill(prompt, 0, oracle.MODE_FP32)
+    a, b = chunk.logits_to_host(), token.logits_to_host()
+    assert np.abs(a - want16).max() <= TOL
+    assert np.abs(a - b).max() <= TOL
+    assert np.abs(a - want32).max() <= MAX_ABS and cos(a, want32) >= MIN_COS
+    # The device state is the per-token path's: next token and position.
+    assert chunk.position == token.position == len(prompt)
+    assert device_token(chunk) == int(np.argmax(a))
+    # Decode steps over the prefilled caches, teacher-forced on the oracle's
+    # greedy ids.
+    pos = len(prompt)
+    steps = min(4, case["max_seq"] - pos)
+    for s in range(steps):
+        tok = oracle.argmax(want16)
+        chunk.decode(tok)
+        token.decode(tok)
+        a, b = chunk.logits_to_host(), token.logits_to_host()
+        want16 = o16.decode(tok, pos, oracle.MODE_BF16)
+        want32 = o32.decode(tok, pos, oracle.MODE_FP32)
+        assert np.abs(a - want16).max() <= TOL, s
+        assert np.abs(a - b).max() <= TOL, s
+        assert np.abs(a - want32).max() <= MAX_ABS and cos(a, want32) >= MIN_COS, s
+        pos += 1
+
+
+def test_chunked_prefill_in_two_calls(tiny):
+    """A prompt in two lcr_prefill calls (the second chunk starting at
+    position 25, inside a 16-row tile) gives the logits of one call, and the
+    greedy continuation is the same."""
+    block, wdev = tiny
+    prompt = ck.prompt_ids(8, 61)
+    one = rt.Model(block, wdev, max_seq=128, paged=True, page_size=16, page_order_seed=4)
+    two = rt.Model(block, wdev, max_seq=128)
+    one.prefill(prompt)
+    two.prefill(prompt[:25])
+    two.prefill(prompt[25:])
+    a, b = one.logits_to_host(), two.logits_to_host()
+    assert np.abs(a - b).max() <= 1e-3
+    ta = one.generate_greedy(int(np.argmax(a)), 12)
+    tb = two.generate_greedy(int(np.argmax(b)), 12)
+    assert ta.tolist() == tb.tolist()
+
+
+def test_chunked_prefill_across_chunks(tiny):
+    """2100 prompt ids: two chunks (2048 + 52 rows), the second attending to
+    the first's cache rows. Paged (shuffled) and contiguous caches give
+    identical bits; both within the gates of the oracle's single chunk."""
+    block, wdev = tiny
+    prompt = ck.prompt_ids(9, 2100)
+    flat = rt.Model(block, wdev, max_seq=2112)
+    paged = rt.Model(block, wdev, max_seq=2112, paged=True, page_size=16, page_order_seed=21)
+    flat.prefill(prompt)
+    paged.prefill(prompt)
+    a, b = flat.logits_to_host(), paged.logits_to_host()
+    assert np.array_equal(a, b)
+    want16 = oracle.Model(block, 2112).prefill(prompt, 0, oracle.MODE_BF16)
+    want32 = oracle.Model(block, 2112).prefill(prompt, 0, oracle.MODE_FP32)
+    assert np.abs(a - want16).max() <= TOL
+    assert np.abs(a - want32).max() <= MAX_ABS and cos(a, want32) >= MIN_COS
+    ta = flat.generate_greedy(int(np.argmax(a)), 8)
+    tb = paged.generate_greedy(int(np.argmax(b)), 8)
+    assert ta.tolist() == tb.tolist()
+
+
+def test_chunked_prefill_rejections(tiny):
+    """The chunk path keeps lcr_prefill's argument checks: an id outside the
+    vocabulary and a prompt past the cache are refused before any launch, and
+    the context stays usable."""
+    block, wdev = tiny
+    m = rt.Model(block, wdev, max_seq=32)
+    with pytest.raises(rt.LcrError) as e:
+        m.prefill([1, 2, block.geom.vocab_size])
+    assert e.value.status == 1
+    with pytest.raises(rt.LcrError) as e:
+        m.prefill(list(range(1, 34)))
+    assert e.value.status == 6
+    m.prefill([5, 6, 7, 8])
+    assert m.position == 4
+    want = oracle.Model(block, 32).prefill([5, 6, 7, 8], 0, oracle.MODE_BF16)
+    assert np.abs(m.logits_to_host() - want).max() <= TOL

@@ -1,7 +1,7 @@
 """Chunked prefill (lcr_batch_prefill: tcgen05 projections over the chunk's
 rows, causal flash attention over the slot's pages) through the C ABI
 against the oracle, which evaluates the same prompt one position at a time
-(Model::prefill's maths): the last row's logits after each chunk, then
+(the decode step's maths): the last row's logits after each chunk, then
 decode steps that read the K/V the prefill wrote. Tolerances are the
 north-star ones used for the batched path: max-abs 3e-2 and cosine 0.999
 against fp32, 2e-2 against the bf16-rounding oracle."""

@@ -77,6 +77,11 @@ def test_dropin_matches_stock_reference(ckpt, paged):
     ref32, ref16 = oracle.Model(block, 64), oracle.Model(block, 64)
     l32 = ref32.prefill(prompt, 0, oracle.MODE_FP32)
     l16 = ref16.prefill(prompt, 0, oracle.MODE_BF16)
+    tok16 = oracle.Model(block, 64)
+    for pos, tok in enumerate(prompt):
+        lt16 = tok16.decode(int(tok), pos, oracle.MODE_BF16)
+    print(f"reference build (paged={paged}) vs oracle: fp32 {np.abs(stock - l32).max():.5f}, "
+          f"bf16 chunk {np.abs(stock - l16).max():.5f}, bf16 per-token {np.abs(stock - lt16).max():.5f}")
     assert np.abs(stock - l32).max() <= MAX_ABS and cos(stock, l32) >= MIN_COS
     assert np.abs(stock - l16).max() <= 1e-2
     # and this library's decode context generates the reference's greedy ids
