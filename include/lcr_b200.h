@@ -227,7 +227,9 @@ typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
                            bit 3: record per-phase timestamps (trace),
                            bit 4: persistent step with fp32 activations,
                            bit 5: tests only (grid-barrier timeout path),
-                           bit 6: lcr_prefill one decode step per token */
+                           bit 6: lcr_prefill one decode step per token,
+                           bit 7: persistent step's attention on CUDA cores
+                           instead of the tensor pipe */
 } lcr_options;
 
 typedef struct lcr_ctx lcr_ctx;

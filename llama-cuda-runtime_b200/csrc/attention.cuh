@@ -347,7 +347,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     for (int g = 0; g < G; ++g) {
       const int h = kvh * G + g;
       if constexpr (FUSED) {
+        // rotated q rounded to bf16, as the reference stores it (rope_q)
         rope8<D>(a.qkv + static_cast<size_t>(b) * a.qkv_stride + h * D, lig, rope_cs, q[g]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[g][e] = rbf(q[g][e]);
       } else {
         unpack8(ldg16(a.q + h * D + lig * 8), q[g]);
       }
@@ -414,6 +417,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         const bf16* row = a.qkv + static_cast<size_t>(b) * a.qkv_stride;
         float kf[8], vf[8];
         rope8<D>(row + a.q_dim + kvh * D, lig, rope_cs, kf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kf[e] = rbf(kf[e]);  // attends to the cache's bf16 key
         unpack8(ldg_cg16(row + a.q_dim + a.kv_dim + kvh * D + lig * 8), vf);
         long long off;
         if constexpr (PAGED) {

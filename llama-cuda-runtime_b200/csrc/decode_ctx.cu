@@ -78,13 +78,14 @@ namespace {
 
 // Bit 4: the persistent step with fp32 activations instead of the
 // reference's bf16 storage rounding (closer to the fp32 evaluation, slower).
-// Bit 6: lcr_prefill runs the prompt one decode step per token, as the
-// reference does, instead of in tcgen05 chunks.
+// Bit 6: lcr_prefill runs the prompt one decode step per token instead of
+// in tcgen05 chunks. Bit 7: the persistent step's attention phase on CUDA
+// cores instead of the tensor pipe.
 // Bit 5 (tests only): the persistent step's grid barriers wait at most 50 ms
 // and CTA 0 skips its first arrival, so the first barrier times out -- the
 // timeout path, exercised without faulting or hanging the GPU.
 enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8, kFlagFp32Act = 16,
-             kFlagTestTimeout = 32, kFlagPerTokenPrefill = 64 };
+             kFlagTestTimeout = 32, kFlagPerTokenPrefill = 64, kFlagCudaCoreAttention = 128 };
 // Prompt rows per tcgen05 prefill chunk, and the shortest prompt chunked.
 constexpr int kPrefillChunk = 2048;
 constexpr int kPrefillChunkMin = 2;
@@ -167,11 +168,17 @@ struct lcr_ctx {
   size_t pinned_prompt_cap = 0;
   float* pinned_params = nullptr;
 
+  // Tensor maps of the cache rows (16-row boxes, 128-byte swizzle): paged,
+  // {K, V} over the whole pool; contiguous, {K, V} per layer. Empty when the
+  // cache does not allow them (head_dim not a multiple of 64, pages of other
+  // than a multiple of 16 positions). Host copy for the chunked prefill,
+  // device copy for the persistent step's tensor-pipe attention.
+  std::vector<CUtensorMap> kvmaps;
+  CUtensorMap* kvmaps_dev = nullptr;
   // Chunked prefill: a one-slot batch context over the same weights, whose
   // tcgen05 prefill writes this context's cache (created on first use).
   lcr_batch* prefill_engine = nullptr;
   bool prefill_unavailable = false;
-  std::vector<CUtensorMap> prefill_kvmaps;
   int32_t* prefill_table = nullptr;  // contiguous cache: the one page, {0}
 };
 
@@ -270,6 +277,10 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.vpool = c->vpool;
   a.trace = c->trace;
   a.prefetch_bytes = c->prefetch_bytes;
+  if (d.head_dim == 64 && !(c->o.flags & kFlagCudaCoreAttention)) {
+    a.kvmaps = c->kvmaps_dev;  // nullptr when the cache has no tensor maps
+    a.kvmap_layer_stride = c->o.paged ? 0 : 2;
+  }
   a.wait_ns = (c->o.flags & kFlagTestTimeout) ? 50000000ull : kWaitLimitNs;
   a.test_skip_arrival = (c->o.flags & kFlagTestTimeout) ? 1 : 0;
   if (c->o.paged) {
@@ -436,7 +447,6 @@ bool prefill_engine_ready(lcr_ctx* c) {
   c->prefill_unavailable = true;
   const lcr_model_desc& d = c->d;
   if (c->f32 || (c->o.flags & kFlagPerTokenPrefill)) return false;
-  if (c->o.paged && c->o.page_size % 16 != 0) return false;
   lcr_weights w = {};
   w.embedding = c->embed;
   w.final_norm = c->final_norm;
@@ -449,27 +459,12 @@ bool prefill_engine_ready(lcr_ctx* c) {
   bo.page_size = 16;
   bo.pool_pages = 1;
   bo.flags = 0;
+  if (c->kvmaps.empty()) return false;
   lcr_batch* engine = nullptr;
   if (lcr_batch_create(&d, &w, &bo, &engine) != LCR_OK) return false;
-  std::vector<CUtensorMap> maps;
   int st = LCR_OK;
-  if (c->o.paged) {
-    const long long rows = static_cast<long long>(c->pool_pages) * d.num_kv_heads * c->o.page_size;
-    maps.resize(2);
-    if (rows > INT32_MAX) st = LCR_ERR_SHAPE;
-    if (st == LCR_OK) st = make_prefill_kv_map(&maps[0], c->kpool, static_cast<int>(rows), d.head_dim);
-    if (st == LCR_OK) st = make_prefill_kv_map(&maps[1], c->vpool, static_cast<int>(rows), d.head_dim);
-  } else {
-    const size_t layer_elems = static_cast<size_t>(d.num_kv_heads) * c->o.max_seq * d.head_dim;
-    const int rows = d.num_kv_heads * c->o.max_seq;
-    maps.resize(static_cast<size_t>(2 * d.num_layers));
-    for (int l = 0; l < d.num_layers && st == LCR_OK; ++l) {
-      st = make_prefill_kv_map(&maps[static_cast<size_t>(2 * l)], c->kpool + l * layer_elems, rows, d.head_dim);
-      if (st == LCR_OK) {
-        st = make_prefill_kv_map(&maps[static_cast<size_t>(2 * l + 1)], c->vpool + l * layer_elems, rows, d.head_dim);
-      }
-    }
-    if (st == LCR_OK && cudaMalloc(&c->prefill_table, sizeof(int32_t)) != cudaSuccess) st = LCR_ERR_CUDA;
+  if (!c->o.paged) {
+    if (cudaMalloc(&c->prefill_table, sizeof(int32_t)) != cudaSuccess) st = LCR_ERR_CUDA;
     if (st == LCR_OK && cudaMemset(c->prefill_table, 0, sizeof(int32_t)) != cudaSuccess) st = LCR_ERR_CUDA;
   }
   if (st != LCR_OK) {
@@ -479,7 +474,6 @@ bool prefill_engine_ready(lcr_ctx* c) {
     return false;
   }
   c->prefill_engine = engine;
-  c->prefill_kvmaps = std::move(maps);
   c->prefill_unavailable = false;
   return true;
 }
@@ -494,7 +488,7 @@ int prefill_chunked(lcr_ctx* c, const int32_t* tokens, int count) {
   PrefillKv kv = {};
   kv.kpool = c->kpool;
   kv.vpool = c->vpool;
-  kv.kvmaps = c->prefill_kvmaps.data();
+  kv.kvmaps = c->kvmaps.data();
   if (c->o.paged) {
     kv.layer_elems = 0;
     kv.table = c->tables_dev;
@@ -550,6 +544,7 @@ void release(lcr_ctx* c) {
   if (c->exec) cudaGraphExecDestroy(c->exec);
   lcr_batch_destroy(c->prefill_engine);
   cudaFree(c->prefill_table);
+  cudaFree(c->kvmaps_dev);
   cudaFree(c->buf);
   cudaFree(c->kpool);
   cudaFree(c->vpool);
@@ -764,6 +759,30 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     if (st == LCR_OK) cuda(cudaMalloc(&c->vpool, elems * sizeof(bf16)), "cudaMalloc(V pool)");
     if (st == LCR_OK) cuda(cudaMemset(c->kpool, 0, elems * sizeof(bf16)), "cudaMemset(K pool)");
     if (st == LCR_OK) cuda(cudaMemset(c->vpool, 0, elems * sizeof(bf16)), "cudaMemset(V pool)");
+  }
+  // Tensor maps of the cache rows.
+  if (st == LCR_OK && d.head_dim % 64 == 0 && (!o.paged || o.page_size % 16 == 0)) {
+    const long long rows = o.paged ? static_cast<long long>(c->pool_pages) * d.num_kv_heads * o.page_size
+                                   : static_cast<long long>(d.num_kv_heads) * o.max_seq;
+    if (rows <= INT32_MAX) {
+      const int maps = o.paged ? 1 : d.num_layers;
+      const size_t layer_elems = o.paged ? 0 : static_cast<size_t>(d.num_kv_heads) * o.max_seq * d.head_dim;
+      c->kvmaps.resize(static_cast<size_t>(2 * maps));
+      for (int l = 0; l < maps && st == LCR_OK; ++l) {
+        st = make_prefill_kv_map(&c->kvmaps[static_cast<size_t>(2 * l)], c->kpool + l * layer_elems,
+                                 static_cast<int>(rows), d.head_dim);
+        if (st == LCR_OK) {
+          st = make_prefill_kv_map(&c->kvmaps[static_cast<size_t>(2 * l + 1)], c->vpool + l * layer_elems,
+                                   static_cast<int>(rows), d.head_dim);
+        }
+      }
+      if (st == LCR_OK) cuda(cudaMalloc(&c->kvmaps_dev, c->kvmaps.size() * sizeof(CUtensorMap)), "cudaMalloc(KV maps)");
+      if (st == LCR_OK) {
+        cuda(cudaMemcpy(c->kvmaps_dev, c->kvmaps.data(), c->kvmaps.size() * sizeof(CUtensorMap),
+                        cudaMemcpyHostToDevice),
+             "upload KV maps");
+      }
+    }
   }
   // Tensor maps of the streamed matrices (one TMA copy per GEMV stage).
   if (st == LCR_OK) {

@@ -7,7 +7,10 @@
 //
 //   QKV   rows of [q;k;v]: RMSNorm prologue (embedding row for layer 0)
 //   ATTN  one (KV head, split) item per CTA: RoPE, KV write, split-K
-//         online softmax over the KV pages, last-CTA merge of the splits
+//         online softmax over the KV pages, last-CTA merge of the splits.
+//         With tensor maps of the cache (head_dim 64): QK^T and PV of each
+//         16-position unit on the tensor pipe (mega_attn_consume_tc);
+//         otherwise CUDA-core dot products, 8 lanes per position.
 //   O     rows of o_proj, residual epilogue
 //   GU    gate/up row pairs: RMSNorm prologue, SwiGLU epilogue
 //   DOWN  rows of down_proj, residual epilogue
@@ -37,6 +40,7 @@
 #pragma once
 
 #include "attention.cuh"
+#include "attn_batch.cuh"  // ab_offset, ldmatrix_x4_trans
 #include "gemv.cuh"
 
 namespace lcrb {
@@ -91,6 +95,13 @@ struct MegaArgs {
   const int32_t* tables;  // paged: [layers][max_pages]
   int max_pages, pool_pages, page_size;
   long long page_stride, head_stride, layer_stride;  // layer_stride: contiguous
+  // Tensor maps of the cache rows ({64, 16, D / 64} boxes, 128-byte swizzle):
+  // [l * kvmap_layer_stride + {0: K, 1: V}], the row of (kv head, position)
+  // being (page * num_kv + kv head) * page_size + position % page_size when
+  // paged, kv head * max_seq + position per layer otherwise. nullptr: the
+  // CUDA-core attention phase.
+  const CUtensorMap* kvmaps;
+  int kvmap_layer_stride;
   unsigned long long prefetch_bytes;  // L2 prefetch lead of the producer (0: off)
   unsigned long long wait_ns;         // bound of each grid-barrier wait
   int test_skip_arrival;              // test only: CTA 0 does not arrive at the first grid barrier
@@ -444,6 +455,128 @@ __device__ __forceinline__ bool mega_attn_produce(uint8_t* ring, uint64_t* full,
   return true;
 }
 
+// Tensor-pipe attention: a stage's 128 positions as 8 units of 16, each one
+// TMA tensor copy of K and one of V ([16 rows][128 bytes], 128-byte swizzle)
+// out of the cache rows. Unit starts are 16-aligned (item starts are
+// multiples of 32), so a unit never straddles a page of a multiple of 16
+// positions; rows past cache_end that the last unit carries are masked by
+// the consumers (contiguous cache: rows past a head's end belong to later
+// positions of the next head, or lie past the tensor and read as zero).
+constexpr int kMegaUnit = 16;
+
+template <int D, int STAGES, bool PAGED>
+__device__ __forceinline__ bool mega_attn_produce_tc(uint8_t* ring, uint64_t* full, uint64_t* empty, int& it,
+                                                     const MegaArgs& a, int l, int pos, uint64_t policy) {
+  using AG = MegaAttnGeom<D>;
+  constexpr int UNITS = AG::STAGE_POS / kMegaUnit;
+  constexpr uint32_t UNIT_BYTES = kMegaUnit * D * 2;
+  const AttnItem item = mega_attn_item<D>(a, pos);
+  const CUtensorMap* km = a.kvmaps + static_cast<size_t>(l) * a.kvmap_layer_stride;
+  for (int blk = 0; blk < item.nblocks; ++blk, ++it) {
+    const int slot = it % STAGES;
+    if (it >= STAGES &&
+        !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, a.status, kStatusTimeoutEmpty)) {
+      return false;
+    }
+    const int p0 = item.begin + blk * AG::STAGE_POS;
+    const int units = min(UNITS, (item.cache_end - p0 + kMegaUnit - 1) / kMegaUnit);
+    uint8_t* dst = ring + slot * kMegaStageBytes;
+    mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(units) * 2 * UNIT_BYTES);
+    for (int u = 0; u < units; ++u) {
+      const int q0 = p0 + u * kMegaUnit;
+      int row;
+      if constexpr (PAGED) {
+        int page = a.tables[static_cast<size_t>(l) * a.max_pages + q0 / a.page_size];
+        if (page < 0 || page >= a.pool_pages) {
+          atomicOr(a.status, kStatusBadPage);
+          page = 0;
+        }
+        row = (page * a.num_kv + item.kvh) * a.page_size + q0 % a.page_size;
+      } else {
+        row = item.kvh * a.max_seq + q0;
+      }
+      tma_load_3d(dst + u * UNIT_BYTES, km, 0, row, 0, &full[slot], policy);
+      tma_load_3d(dst + AG::STAGE_POS * AG::ROWB + u * UNIT_BYTES, km + 1, 0, row, 0, &full[slot], policy);
+    }
+  }
+  return true;
+}
+
+// Publishes the item's per-warp records in `scratch` (per warp and head: m,
+// l, acc[D]) as this split's (acc[D], m, l) record; the O phase merges the
+// splits of every head in its prologue (mega_load_attention_merged), or, with
+// many splits, the last split of the KV head to publish merges them here.
+template <int D, int G, bool F32>
+__device__ __forceinline__ void mega_attn_publish(const MegaArgs& a, int l, const AttnItem& item,
+                                                  const float* scratch, int* s_last) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  float* part_base = a.partials + static_cast<size_t>(item.kvh) * G * a.splits * kMegaPartStride<D>;
+  for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
+    const int g = idx / D, d = idx % D;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < kMegaWarps; ++w) M = fmaxf(M, scratch[(w * G + g) * (D + 2)]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMegaWarps; ++w) {
+      const float* c = scratch + (w * G + g) * (D + 2);
+      const float s = ex2_approx(c[0] - M);
+      L += c[1] * s;
+      A += c[2 + d] * s;
+    }
+    float* rec = part_base + (g * a.splits + item.split) * kMegaPartStride<D>;
+    rec[d] = A;
+    if (d == 0) {
+      rec[D] = M;
+      rec[D + 1] = L;
+    }
+  }
+  if (item.splits <= kMegaPrologueMergeMax) return;
+  // Many splits: the last split of this KV head to publish merges the head
+  // group once (8 threads per 8-dim chunk, splits strided over them) and
+  // writes the bf16 output; the counter resets for the next step.
+  __threadfence();
+  named_sync(1, kGemvConsumers);
+  unsigned* ctr = a.attn_ctr + static_cast<size_t>(l) * a.num_kv + item.kvh;
+  if (tid == 0) *s_last = atomicAdd(ctr, 1u) == static_cast<unsigned>(item.splits - 1);
+  named_sync(1, kGemvConsumers);
+  if (!*s_last) return;
+  __threadfence();
+  const int sg = lane & 7;
+  for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
+    const int g = c * 8 / D, d0 = c * 8 % D;
+    float M = kNegBig, L = 0.f;
+    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    merge_split_records<D>(part_base + static_cast<size_t>(g) * a.splits * kMegaPartStride<D>, sg, item.splits, 8,
+                           d0, M, L, acc8);
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, M, off);
+      const float ol = __shfl_xor_sync(0xffffffffu, L, off);
+      const float Mn = fmaxf(M, om);
+      const float ws = ex2_approx(M - Mn), wo = ex2_approx(om - Mn);
+      L = L * ws + ol * wo;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float oa = __shfl_xor_sync(0xffffffffu, acc8[e], off);
+        acc8[e] = acc8[e] * ws + oa * wo;
+      }
+      M = Mn;
+    }
+    if (sg == 0) {
+      if constexpr (F32) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        float* dst = a.attn_f + static_cast<size_t>(item.kvh * G + g) * D + d0;
+        *reinterpret_cast<float4*>(dst) = make_float4(acc8[0] * inv, acc8[1] * inv, acc8[2] * inv, acc8[3] * inv);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc8[4] * inv, acc8[5] * inv, acc8[6] * inv, acc8[7] * inv);
+      } else {
+        *reinterpret_cast<uint4*>(a.attn + static_cast<size_t>(item.kvh * G + g) * D + d0) = merged_bf16x8(L, acc8);
+      }
+    }
+  }
+  if (tid == 0) *ctr = 0u;
+}
+
 // Consumers: one (KV head, split) item -> partials (or the output when there
 // is a single split); the last CTA of a KV head merges its splits.
 // `cs` is the step's RoPE table, `scratch` >= kMegaWarps * G * (D + 2) floats.
@@ -488,7 +621,10 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
     if constexpr (F32) {
       rope8f<D>(a.qkv_f + (item.kvh * G + g) * D, lig, cs, q[g]);
     } else {
+      // rotated q rounded to bf16, as the reference stores it (rope_q)
       rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, q[g]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q[g][e] = rbf(q[g][e]);
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -564,6 +700,8 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
       vraw.z = pack_bf2(vf[4], vf[5]); vraw.w = pack_bf2(vf[6], vf[7]);
     } else {
       rope8_from<D>(k_self, k_other, lig, cs, kf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kf[e] = rbf(kf[e]);  // attends to the cache's bf16 key
       vraw = v_raw;
       unpack8(vraw, vf);
     }
@@ -624,73 +762,253 @@ __device__ __forceinline__ void mega_attn_consume(const uint8_t* ring, uint64_t*
     }
   }
   named_sync(1, kGemvConsumers);
-  // Publish this split's (acc[D], m, l) record; the O phase merges the splits
-  // of every head in its prologue (mega_load_attention_merged).
-  float* part_base = a.partials + static_cast<size_t>(item.kvh) * G * a.splits * kMegaPartStride<D>;
-  for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
-    const int g = idx / D, d = idx % D;
-    float M = kNegBig;
-#pragma unroll
-    for (int w = 0; w < kMegaWarps; ++w) M = fmaxf(M, scratch[(w * G + g) * (D + 2)]);
-    float L = 0.f, A = 0.f;
-#pragma unroll
-    for (int w = 0; w < kMegaWarps; ++w) {
-      const float* c = scratch + (w * G + g) * (D + 2);
-      const float s = ex2_approx(c[0] - M);
-      L += c[1] * s;
-      A += c[2 + d] * s;
-    }
-    float* rec = part_base + (g * a.splits + item.split) * kMegaPartStride<D>;
-    rec[d] = A;
-    if (d == 0) {
-      rec[D] = M;
-      rec[D + 1] = L;
+  mega_attn_publish<D, G, F32>(a, l, item, scratch, s_last);
+}
+
+// 8 fp32 values as bf16 (hi) and the bf16 of their remainders (lo).
+__device__ __forceinline__ void split_hilo8(const float (&v)[8], uint4& hi, uint4& lo) {
+  hi.x = pack_bf2(v[0], v[1]);
+  hi.y = pack_bf2(v[2], v[3]);
+  hi.z = pack_bf2(v[4], v[5]);
+  hi.w = pack_bf2(v[6], v[7]);
+  lo.x = pack_bf2(v[0] - bf_lo(hi.x), v[1] - bf_hi(hi.x));
+  lo.y = pack_bf2(v[2] - bf_lo(hi.y), v[3] - bf_hi(hi.y));
+  lo.z = pack_bf2(v[4] - bf_lo(hi.z), v[5] - bf_hi(hi.z));
+  lo.w = pack_bf2(v[6] - bf_lo(hi.w), v[7] - bf_hi(hi.w));
+}
+
+// The attention phase on the tensor pipe (head_dim 64, G <= 8 query heads
+// per KV head). Warp w takes unit w (16 positions) of every stage:
+//   S = Q K^T   m16n8k16, the G query heads as MMA rows 0..G-1 (the rest
+//               zero), bf16 q as the reference stores it after RoPE (with
+//               fp32 activations: q as a bf16 pair hi + lo, two MMAs), bf16
+//               K from ldmatrix of the swizzled unit, fp32 sums;
+//   online softmax per head in the log2 domain, fp32, over the quad of lanes
+//               holding a head's 16 scores;
+//   O += P V    P as a bf16 pair hi + lo (two MMAs: the weights keep about
+//               16 significant bits, as the fp32 weights of the reference's
+//               decode attention), V fragments from ldmatrix.trans.
+// The denominator sums the fp32 weights. The new position is folded into
+// warp 0's record by lanes 0-7 after the stages (its K and V go to the
+// cache), then the records are published as in mega_attn_consume. `qs` is
+// shared memory for the rotated q (2 G D bf16).
+template <int D, int G, int STAGES, bool PAGED, bool F32>
+__device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64_t* full, uint64_t* empty, int& it,
+                                                     const MegaArgs& a, int l, int pos, const float* cs,
+                                                     float* scratch, bf16* qs, int* s_last, bool& failed,
+                                                     unsigned long long* wait_cycles = nullptr) {
+  using AG = MegaAttnGeom<D>;
+  static_assert(D == 64 && G >= 1 && G <= 8, "tensor-pipe attention: head_dim 64, at most 8 heads per KV head");
+  constexpr int UNIT_BYTES = kMegaUnit * D * 2;
+  constexpr int KS = D / 16;  // k-steps of Q K^T, and pairs of P V column tiles
+  constexpr int LPP = D / 8;  // lanes per position on the new position
+  const AttnItem item = mega_attn_item<D>(a, pos);
+  if (item.kvh < 0) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int heads = a.num_kv * G;
+  const int qd = heads * D, kvd = a.num_kv * D;
+  bf16* qlo = qs + G * D;
+
+  // The new position's K and V (this step's projection), loaded early.
+  const bool has_new = pos >= item.begin && pos < item.end;
+  const bool new_lane = has_new && warp == 0 && lane < LPP;
+  uint4 k_self = make_uint4(0, 0, 0, 0), k_other = k_self, v_raw = k_self;
+  float k_newf[8], v_newf[8];
+  if (new_lane) {
+    if constexpr (F32) {
+      rope8f<D>(a.qkv_f + qd + item.kvh * D, lane, cs, k_newf);
+      const float* vh = a.qkv_f + qd + kvd + item.kvh * D + lane * 8;
+      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(vh));
+      const float4 v1 = __ldcg(reinterpret_cast<const float4*>(vh + 4));
+      v_newf[0] = v0.x; v_newf[1] = v0.y; v_newf[2] = v0.z; v_newf[3] = v0.w;
+      v_newf[4] = v1.x; v_newf[5] = v1.y; v_newf[6] = v1.z; v_newf[7] = v1.w;
+    } else {
+      const bf16* kh = a.qkv + qd + item.kvh * D;
+      k_self = ldg_cg16(kh + lane * 8);
+      k_other = ldg_cg16(kh + (lane * 8 < D / 2 ? lane * 8 + D / 2 : lane * 8 - D / 2));
+      v_raw = ldg_cg16(a.qkv + qd + kvd + item.kvh * D + lane * 8);
     }
   }
-  if (item.splits <= kMegaPrologueMergeMax) return;
-  // Many splits: the last split of this KV head to publish merges the head
-  // group once (8 threads per 8-dim chunk, splits strided over them) and
-  // writes the bf16 output; the counter resets for the next step.
-  __threadfence();
+  // Rotated q of the group into shared memory: bf16 (and its remainder).
+  if (tid < G * LPP) {
+    const int g = tid / LPP, lig = tid % LPP;
+    float qf[8];
+    if constexpr (F32) {
+      rope8f<D>(a.qkv_f + (item.kvh * G + g) * D, lig, cs, qf);
+    } else {
+      rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, qf);
+    }
+    uint4 hi, lo;
+    split_hilo8(qf, hi, lo);
+    *reinterpret_cast<uint4*>(qs + g * D + lig * 8) = hi;
+    if constexpr (F32) *reinterpret_cast<uint4*>(qlo + g * D + lig * 8) = lo;
+  }
   named_sync(1, kGemvConsumers);
-  unsigned* ctr = a.attn_ctr + static_cast<size_t>(l) * a.num_kv + item.kvh;
-  if (tid == 0) *s_last = atomicAdd(ctr, 1u) == static_cast<unsigned>(item.splits - 1);
-  named_sync(1, kGemvConsumers);
-  if (!*s_last) return;
-  __threadfence();
-  const int sg = lane & 7;
-  for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
-    const int g = c * 8 / D, d0 = c * 8 % D;
-    float M = kNegBig, L = 0.f;
-    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    merge_split_records<D>(part_base + static_cast<size_t>(g) * a.splits * kMegaPartStride<D>, sg, item.splits, 8,
-                           d0, M, L, acc8);
+
+  const int g = lane >> 2, qq = lane & 3;
+  const bool hrow = g < G;
+  uint32_t qa0[KS], qa2[KS], ql0[KS], ql2[KS];
 #pragma unroll
-    for (int off = 1; off < 8; off <<= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, M, off);
-      const float ol = __shfl_xor_sync(0xffffffffu, L, off);
-      const float Mn = fmaxf(M, om);
-      const float ws = ex2_approx(M - Mn), wo = ex2_approx(om - Mn);
-      L = L * ws + ol * wo;
+  for (int ks = 0; ks < KS; ++ks) {
+    const bf16* qrow = qs + g * D + 16 * ks + 2 * qq;
+    qa0[ks] = hrow ? *reinterpret_cast<const uint32_t*>(qrow) : 0u;
+    qa2[ks] = hrow ? *reinterpret_cast<const uint32_t*>(qrow + 8) : 0u;
+    if constexpr (F32) {
+      ql0[ks] = hrow ? *reinterpret_cast<const uint32_t*>(qrow + G * D) : 0u;
+      ql2[ks] = hrow ? *reinterpret_cast<const uint32_t*>(qrow + G * D + 8) : 0u;
+    } else {
+      ql0[ks] = ql2[ks] = 0u;
+    }
+  }
+  const float sl2 = a.scale_log2;
+  float m = kNegBig, lsum = 0.f;
+  float o[2 * KS][4];
+#pragma unroll
+  for (int t = 0; t < 2 * KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+  const int mi = lane >> 3, r8 = lane & 7;
+
+  const bool timed = wait_cycles != nullptr && tid == 0;
+  unsigned long long waited = 0;
+  for (int blk = 0; blk < item.nblocks; ++blk, ++it) {
+    const int slot = it % STAGES;
+    const long long w0 = timed ? clock64() : 0;
+    if (!failed) failed = !mbar_wait(&full[slot], (it / STAGES) & 1, a.status, kStatusTimeoutFull);
+    failed = __any_sync(0xffffffffu, failed);  // the MMAs below are warp-wide
+    if (timed) waited += static_cast<unsigned long long>(clock64() - w0);
+    const int q0 = item.begin + blk * AG::STAGE_POS + warp * kMegaUnit;
+    if (!failed && q0 < item.cache_end) {  // uniform across the warp
+      const uint32_t kbase = smem_addr(ring + slot * kMegaStageBytes) + warp * UNIT_BYTES;
+      const uint32_t vbase = kbase + AG::STAGE_POS * AG::ROWB;
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t kb[4];
+        ldmatrix_x4(kb, kbase + ab_offset(((mi >> 1) << 3) + r8, 2 * ks + (mi & 1)));
+        mma_x_rows(s0, qa0[ks], qa2[ks], kb[0], kb[1]);
+        mma_x_rows(s1, qa0[ks], qa2[ks], kb[2], kb[3]);
+        if constexpr (F32) {
+          mma_x_rows(s0, ql0[ks], ql2[ks], kb[0], kb[1]);
+          mma_x_rows(s1, ql0[ks], ql2[ks], kb[2], kb[3]);
+        }
+      }
+      // This lane's keys: q0 + 2 qq + {0, 1} (tile 0) and + 8 (tile 1).
+      const int k0 = q0 + 2 * qq;
+      const float v[4] = {s0[0] * sl2, s0[1] * sl2, s1[0] * sl2, s1[1] * sl2};
+      const bool in[4] = {k0 < item.cache_end, k0 + 1 < item.cache_end, k0 + 8 < item.cache_end,
+                          k0 + 9 < item.cache_end};
+      float mx = kNegBig;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) mx = in[j] ? fmaxf(mx, v[j]) : mx;
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m, mx);
+      const float alpha = ex2_approx(m - mn);
+      float p[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = in[j] ? ex2_approx(v[j] - mn) : 0.f;
+      lsum = lsum * alpha + ((p[0] + p[1]) + (p[2] + p[3]));
+      m = mn;
+#pragma unroll
+      for (int t = 0; t < 2 * KS; ++t) {
+        o[t][0] *= alpha;
+        o[t][1] *= alpha;
+      }
+      const uint32_t ph0 = pack_bf2(p[0], p[1]), ph2 = pack_bf2(p[2], p[3]);
+      const uint32_t pl0 = pack_bf2(p[0] - bf_lo(ph0), p[1] - bf_hi(ph0));
+      const uint32_t pl2 = pack_bf2(p[2] - bf_lo(ph2), p[3] - bf_hi(ph2));
+#pragma unroll
+      for (int c = 0; c < KS; ++c) {
+        uint32_t vb[4];
+        ldmatrix_x4_trans(vb, vbase + ab_offset(((mi & 1) << 3) + r8, 2 * c + (mi >> 1)));
+        mma_x_rows(o[2 * c], ph0, ph2, vb[0], vb[1]);
+        mma_x_rows(o[2 * c], pl0, pl2, vb[0], vb[1]);
+        mma_x_rows(o[2 * c + 1], ph0, ph2, vb[2], vb[3]);
+        mma_x_rows(o[2 * c + 1], pl0, pl2, vb[2], vb[3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && !failed) mbar_arrive(&empty[slot]);
+  }
+  if (timed) *wait_cycles = waited;
+
+  // This warp's record per head: m, the quad's l, O (dims 8 t + 2 qq + {0, 1}).
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+  if (hrow) {
+    float* c = scratch + (warp * G + g) * (D + 2);
+    if (qq == 0) {
+      c[0] = m;
+      c[1] = lsum;
+    }
+#pragma unroll
+    for (int t = 0; t < 2 * KS; ++t) {
+      c[2 + 8 * t + 2 * qq] = o[t][0];
+      c[3 + 8 * t + 2 * qq] = o[t][1];
+    }
+  }
+  __syncwarp();
+
+  // The new position (this step's token) on warp 0, lanes 0-7: rotate K,
+  // store K and V, fold them into warp 0's records. Attention reads the
+  // cache's bf16 K and V (with fp32 activations: the unrounded ones).
+  if (new_lane) {
+    float kf[8], vf[8];
+    uint4 kw, vw;
+    if constexpr (F32) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float oa = __shfl_xor_sync(0xffffffffu, acc8[e], off);
-        acc8[e] = acc8[e] * ws + oa * wo;
+        kf[e] = k_newf[e];
+        vf[e] = v_newf[e];
       }
-      M = Mn;
+      kw.x = pack_bf2(kf[0], kf[1]); kw.y = pack_bf2(kf[2], kf[3]);
+      kw.z = pack_bf2(kf[4], kf[5]); kw.w = pack_bf2(kf[6], kf[7]);
+      vw.x = pack_bf2(vf[0], vf[1]); vw.y = pack_bf2(vf[2], vf[3]);
+      vw.z = pack_bf2(vf[4], vf[5]); vw.w = pack_bf2(vf[6], vf[7]);
+    } else {
+      float kr[8];
+      rope8_from<D>(k_self, k_other, lane, cs, kr);
+      kw.x = pack_bf2(kr[0], kr[1]); kw.y = pack_bf2(kr[2], kr[3]);
+      kw.z = pack_bf2(kr[4], kr[5]); kw.w = pack_bf2(kr[6], kr[7]);
+      unpack8(kw, kf);
+      vw = v_raw;
+      unpack8(vw, vf);
     }
-    if (sg == 0) {
+    const long long off = kv_offset<PAGED>(a, l, item.kvh, pos, D);
+    *reinterpret_cast<uint4*>(a.kpool + off + lane * 8) = kw;
+    *reinterpret_cast<uint4*>(a.vpool + off + lane * 8) = vw;
+    constexpr unsigned kLanes = 0xffffffffu >> (32 - LPP);
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float qf[8];
+      unpack8(*reinterpret_cast<const uint4*>(qs + h * D + lane * 8), qf);
       if constexpr (F32) {
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        float* dst = a.attn_f + static_cast<size_t>(item.kvh * G + g) * D + d0;
-        *reinterpret_cast<float4*>(dst) = make_float4(acc8[0] * inv, acc8[1] * inv, acc8[2] * inv, acc8[3] * inv);
-        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc8[4] * inv, acc8[5] * inv, acc8[6] * inv, acc8[7] * inv);
-      } else {
-        *reinterpret_cast<uint4*>(a.attn + static_cast<size_t>(item.kvh * G + g) * D + d0) = merged_bf16x8(L, acc8);
+        float ql[8];
+        unpack8(*reinterpret_cast<const uint4*>(qlo + h * D + lane * 8), ql);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qf[e] += ql[e];
       }
+      float sc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sc = fmaf(qf[e], kf[e], sc);
+#pragma unroll
+      for (int off2 = LPP / 2; off2 >= 1; off2 >>= 1) sc += __shfl_xor_sync(kLanes, sc, off2, LPP);
+      sc *= sl2;
+      float* c = scratch + h * (D + 2);  // warp 0's record of head h
+      const float c0 = c[0], c1 = c[1];
+      const float mn = fmaxf(c0, sc);
+      const float al = ex2_approx(c0 - mn), pw = ex2_approx(sc - mn);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) c[2 + lane * 8 + e] = c[2 + lane * 8 + e] * al + pw * vf[e];
+      __syncwarp(kLanes);
+      if (lane == 0) {
+        c[0] = mn;
+        c[1] = c1 * al + pw;
+      }
+      __syncwarp(kLanes);
     }
   }
-  if (tid == 0) *ctr = 0u;
+  named_sync(1, kGemvConsumers);
+  mega_attn_publish<D, G, F32>(a, l, item, scratch, s_last);
 }
 
 // O-phase prologue: the attention output staged in shared memory, each thread
@@ -944,7 +1262,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
                                                      gemv_share(nqkv, blockIdx.x, ctas),
                                                      gemv_share(nqkv, blockIdx.x + 1, ctas), policy, a.status,
                                                      pf, &issued, pwait());
-        ok = ok && mark() && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
+        if constexpr (D == 64 && G <= 8) {
+          ok = ok && mark() &&
+               (a.kvmaps ? mega_attn_produce_tc<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos, policy)
+                         : mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos));
+        } else {
+          ok = ok && mark() && mega_attn_produce<D, STAGES, PAGED>(ring, full, empty, it, a, l, pos);
+        }
         ok = ok && mark() && gemv_produce<QD, STAGES, false>(ring, full, empty, it, a.wmaps + 4 * l + 1, w.o, H,
                                                       gemv_share(H, blockIdx.x, ctas),
                                                       gemv_share(H, blockIdx.x + 1, ctas), policy, a.status,
@@ -1032,8 +1356,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       }
       if (!(run = sync())) break;
       pro_done();  // attention: no separate prologue
-      mega_attn_consume<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
-                                                  cwait());
+      if constexpr (D == 64 && G <= 8) {
+        if (a.kvmaps) {
+          mega_attn_consume_tc<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, xs, &s_flags[1],
+                                                         failed, cwait());
+        } else {
+          mega_attn_consume<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
+                                                      cwait());
+        }
+      } else {
+        mega_attn_consume<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
+                                                    cwait());
+      }
       if (!(run = sync())) break;
       {  // O
         GemvArgs g = {};

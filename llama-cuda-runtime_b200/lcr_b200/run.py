@@ -86,6 +86,10 @@ def main(argv=None) -> int:
                          "bf16 storage rounding)")
     ap.add_argument("--no-persistent", action="store_true",
                     help="the multi-kernel step instead of the persistent kernel")
+    ap.add_argument("--cuda-core-attention", action="store_true",
+                    help="persistent step's attention phase on CUDA cores instead of the tensor pipe")
+    ap.add_argument("--per-token-prefill", action="store_true",
+                    help="the prompt as decode steps instead of tcgen05 chunks")
     ap.add_argument("--trace", action="store_true",
                     help="per-phase timeline of the last decode step (persistent kernel)")
     ap.add_argument("--trace-out", default=None,
@@ -106,7 +110,9 @@ def main(argv=None) -> int:
                  page_order_seed=args.page_order_seed,
                  flags=(rt.FLAG_TRACE if args.trace else 0)
                  | (rt.FLAG_FP32_ACT if args.fp32_act else 0)
-                 | (rt.FLAG_NO_PERSISTENT if args.no_persistent else 0))
+                 | (rt.FLAG_NO_PERSISTENT if args.no_persistent else 0)
+                 | (rt.FLAG_CUDA_CORE_ATTENTION if args.cuda_core_attention else 0)
+                 | (rt.FLAG_PER_TOKEN_PREFILL if args.per_token_prefill else 0))
     load_ms = (time.perf_counter() - t0) * 1000
 
     t0 = time.perf_counter()

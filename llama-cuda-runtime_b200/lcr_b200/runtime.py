@@ -39,6 +39,9 @@ FLAG_TEST_TIMEOUT = 32
 # lcr_prefill one decode step per token, as the reference's Model::prefill,
 # instead of the tcgen05 chunks of up to 2048 prompt rows.
 FLAG_PER_TOKEN_PREFILL = 64
+# The persistent step's attention phase on CUDA cores (8 lanes per cached
+# position) instead of the tensor pipe (mma.sync over 16-position units).
+FLAG_CUDA_CORE_ATTENTION = 128
 
 
 class LcrError(RuntimeError):

@@ -105,18 +105,29 @@ def test_device_greedy_loop_matches_host_loop(tiny):
                                           paged=True, page_order_seed=3),
                                      dict(attention_splits=3), dict(gemv_ctas=37,
                                                                     flags=rt.FLAG_NO_PERSISTENT),
-                                     dict(flags=rt.FLAG_FP32_ACT, paged=True, page_order_seed=5)])
+                                     dict(flags=rt.FLAG_FP32_ACT, paged=True, page_order_seed=5),
+                                     dict(tensor_pipe=True), dict(tensor_pipe=True, paged=True, page_order_seed=9),
+                                     dict(tensor_pipe=True, flags=rt.FLAG_FP32_ACT, paged=True, page_order_seed=5)])
 def test_step_variants_are_bit_identical(tiny, variant):
     """Layout and scheduling options of the step change no result bit; a
     different split or CTA count, or the multi-kernel step, changes only the
     fp32 summation order; fp32 activations stay within the north-star gate of
-    the reference rounding."""
+    the reference rounding. These compare the persistent step with its
+    CUDA-core attention phase, which shares its device functions with the
+    multi-kernel step. The tensor-pipe attention phase (the default) sums in
+    another order and carries the softmax weights as a bf16 pair, so its
+    attention outputs may round to the neighbouring bf16 value; on this model
+    one such flip moves the logits by about 6e-3, so it is held to 1e-2, the
+    tolerance against the bf16-storage oracle, and to the same greedy ids."""
     block, wdev = tiny
     prompt = ck.prompt_ids(3, 40)
+    variant = dict(variant)
+    tensor_pipe = variant.pop("tensor_pipe", False)
     multi = variant.get("flags", 0) & rt.FLAG_NO_PERSISTENT
     # The prompt as decode steps, so that it runs through the variant too.
-    variant = dict(variant, flags=variant.get("flags", 0) | rt.FLAG_PER_TOKEN_PREFILL)
-    base = rt.Model(block, wdev, max_seq=96, flags=rt.FLAG_PER_TOKEN_PREFILL)
+    cc = rt.FLAG_CUDA_CORE_ATTENTION
+    variant["flags"] = variant.get("flags", 0) | rt.FLAG_PER_TOKEN_PREFILL | (0 if tensor_pipe else cc)
+    base = rt.Model(block, wdev, max_seq=96, flags=rt.FLAG_PER_TOKEN_PREFILL | cc)
     other = rt.Model(block, wdev, max_seq=96, **variant)
     base.prefill(prompt)
     other.prefill(prompt)
@@ -126,6 +137,8 @@ def test_step_variants_are_bit_identical(tiny, variant):
         # fp32 activations against the reference rounding: the bf16 storage
         # of the intermediate tensors, not only the order
         assert np.abs(a - b).max() < 3e-2
+    elif tensor_pipe:
+        assert np.abs(a - b).max() < 1e-2
     elif order_changes:
         # a different split / CTA count, or the multi-kernel step's attention
         # partition, changes the fp32 summation order only
