@@ -376,6 +376,7 @@ def long_context_bench(block, weights_dev, local, short_ms_per_step, warmup=16):
     prefill_ms = float(np.median(prefill_times))
     pinned = torch.empty(2, dtype=torch.int32, pin_memory=True)
     pinned[0] = int(prompt[-1])
+    m.reserve_length(LONG_PROMPT + LONG_DECODE)  # every page the timed steps write, mapped up front
     m.set_token(pinned.data_ptr(), LONG_PROMPT - 1)
     m.enqueue_steps(warmup)
     m.sync()

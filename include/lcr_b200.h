@@ -284,7 +284,8 @@ LCR_API int lcr_generate_greedy(lcr_ctx* ctx, int first_token, int steps,
 
 /* Asynchronous pieces of the same loop, for timing and for host pipelines:
  * lcr_set_token stages (token, position) into device state on the context's
- * stream from host memory; lcr_enqueue_steps launches `steps` step graphs;
+ * stream from host memory; lcr_enqueue_steps launches `steps` step graphs
+ * (mapping first, when paged, the pages of the positions they write);
  * lcr_read_token copies the latest device token to host memory (pinned for
  * true async) and lcr_sync waits for the stream. */
 LCR_API int lcr_set_token(lcr_ctx* ctx, const int32_t* host_token, int position);

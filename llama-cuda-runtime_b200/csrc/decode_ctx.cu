@@ -1028,6 +1028,9 @@ extern "C" int lcr_set_token(lcr_ctx* c, const int32_t* host_token, int position
 
 extern "C" int lcr_enqueue_steps(lcr_ctx* c, int steps) {
   LCRB_REQUIRE(c && steps >= 0, LCR_ERR_INVALID, "bad arguments");
+  // Pages for the positions the steps write (a synchronisation only when
+  // new pages are mapped).
+  LCRB_TRY(lcr_reserve_length(c, c->position + steps));
   LCRB_TRY(launch_steps(c, steps));
   c->position += steps;
   return LCR_OK;
