@@ -229,7 +229,9 @@ typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
                            bit 5: tests only (grid-barrier timeout path),
                            bit 6: lcr_prefill one decode step per token,
                            bit 7: persistent step's attention on CUDA cores
-                           instead of the tensor pipe */
+                           instead of the tensor pipe,
+                           bit 8: persistent step's phases meet at grid
+                           barriers instead of exchanging tagged words */
 } lcr_options;
 
 typedef struct lcr_ctx lcr_ctx;

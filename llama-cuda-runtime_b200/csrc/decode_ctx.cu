@@ -80,12 +80,15 @@ namespace {
 // reference's bf16 storage rounding (closer to the fp32 evaluation, slower).
 // Bit 6: lcr_prefill runs the prompt one decode step per token instead of
 // in tcgen05 chunks. Bit 7: the persistent step's attention phase on CUDA
-// cores instead of the tensor pipe.
-// Bit 5 (tests only): the persistent step's grid barriers wait at most 50 ms
-// and CTA 0 skips its first arrival, so the first barrier times out -- the
-// timeout path, exercised without faulting or hanging the GPU.
+// cores instead of the tensor pipe. Bit 8: the persistent step's phases meet
+// at grid barriers instead of exchanging tagged words (ll.cuh).
+// Bit 5 (tests only): the persistent step's waits give up after 50 ms and CTA
+// 0 skips its first arrival at a grid barrier (with the exchange: its first
+// q/k/v words), so the first wait times out -- the timeout path, exercised
+// without faulting or hanging the GPU.
 enum : int { kFlagNoPdl = 1, kFlagNoGraph = 2, kFlagNoPersistent = 4, kFlagTrace = 8, kFlagFp32Act = 16,
-             kFlagTestTimeout = 32, kFlagPerTokenPrefill = 64, kFlagCudaCoreAttention = 128 };
+             kFlagTestTimeout = 32, kFlagPerTokenPrefill = 64, kFlagCudaCoreAttention = 128,
+             kFlagGridBarriers = 256 };
 // Prompt rows per tcgen05 prefill chunk, and the shortest prompt chunked.
 constexpr int kPrefillChunk = 2048;
 constexpr int kPrefillChunkMin = 2;
@@ -139,6 +142,15 @@ struct lcr_ctx {
   float* inv_freq = nullptr;
   float* sample_params = nullptr;
   int32_t* sampled = nullptr;
+  // Low-latency exchange words of the persistent step (ll.cuh), and the
+  // per-step epoch base of their tags.
+  bool ll = false;
+  uint32_t* epoch = nullptr;
+  uint32_t* qkv_ll = nullptr;
+  unsigned long long* part_ll = nullptr;
+  uint32_t* attn_ll = nullptr;
+  unsigned long long* x_ll = nullptr;
+  uint32_t* act_ll = nullptr;
 
   bf16* kpool = nullptr;
   bf16* vpool = nullptr;
@@ -281,6 +293,15 @@ int enqueue_persistent_step(lcr_ctx* c) {
     a.kvmaps = c->kvmaps_dev;  // nullptr when the cache has no tensor maps
     a.kvmap_layer_stride = c->o.paged ? 0 : 2;
   }
+  if (c->ll) {
+    a.ll = 1;
+    a.epoch = c->epoch;
+    a.qkv_ll = c->qkv_ll;
+    a.part_ll = c->part_ll;
+    a.attn_ll = c->attn_ll;
+    a.x_ll = c->x_ll;
+    a.act_ll = c->act_ll;
+  }
   a.wait_ns = (c->o.flags & kFlagTestTimeout) ? 50000000ull : kWaitLimitNs;
   a.test_skip_arrival = (c->o.flags & kFlagTestTimeout) ? 1 : 0;
   if (c->o.paged) {
@@ -408,10 +429,17 @@ int check_status(lcr_ctx* c) {
   LCRB_CUDA(cudaMemsetAsync(c->status, 0, sizeof st, c->stream));
   if (st & kStatusAbort) {
     // A stopped step may leave the many-split merge counters and the argmax
-    // hand-off part way: start the next step from zero.
+    // hand-off part way: start the next step from zero. Its exchange words
+    // may carry tags the next step would expect (it did not advance the
+    // epoch): move the epoch well past them.
     LCRB_CUDA(cudaMemsetAsync(c->attn_ctr, 0, sizeof(unsigned) * c->d.num_layers * c->d.num_kv_heads, c->stream));
     LCRB_CUDA(cudaMemsetAsync(c->sched, 0, 2 * sizeof(unsigned), c->stream));
     LCRB_CUDA(cudaMemsetAsync(c->argmax_acc, 0, sizeof(unsigned long long), c->stream));
+    uint32_t ep = 0;
+    LCRB_CUDA(cudaMemcpyAsync(&ep, c->epoch, sizeof ep, cudaMemcpyDeviceToHost, c->stream));
+    LCRB_CUDA(cudaStreamSynchronize(c->stream));
+    ep += 4096u;
+    LCRB_CUDA(cudaMemcpyAsync(c->epoch, &ep, sizeof ep, cudaMemcpyHostToDevice, c->stream));
   }
   LCRB_CUDA(cudaStreamSynchronize(c->stream));
   if (st & (kStatusTimeoutFull | kStatusTimeoutEmpty | kStatusTimeoutBarrier | kStatusAbort)) {
@@ -701,6 +729,12 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   const size_t o_freq = carve(sizeof(float) * d.head_dim / 2);
   const size_t o_sparams = carve(sizeof(float) * 8);
   const size_t o_sampled = carve(sizeof(int32_t) * 4);
+  const size_t o_epoch = carve(sizeof(uint32_t));
+  const size_t o_qkvll = carve(sizeof(uint32_t) * (qd + 2 * kvd));
+  const size_t o_partll = carve(sizeof(unsigned long long) * d.num_heads * c->splits * (4 + d.head_dim));
+  const size_t o_attnll = carve(sizeof(uint32_t) * qd);
+  const size_t o_xll = carve(sizeof(unsigned long long) * d.hidden_size);
+  const size_t o_actll = carve(sizeof(uint32_t) * d.intermediate_size);
   if (st == LCR_OK) cuda(cudaMalloc(&c->buf, off), "cudaMalloc(activations)");
   if (st == LCR_OK) cuda(cudaMemset(c->buf, 0, off), "cudaMemset(activations)");
   if (st == LCR_OK) {
@@ -724,6 +758,14 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     c->inv_freq = reinterpret_cast<float*>(b + o_freq);
     c->sample_params = reinterpret_cast<float*>(b + o_sparams);
     c->sampled = reinterpret_cast<int32_t*>(b + o_sampled);
+    c->epoch = reinterpret_cast<uint32_t*>(b + o_epoch);
+    c->qkv_ll = reinterpret_cast<uint32_t*>(b + o_qkvll);
+    c->part_ll = reinterpret_cast<unsigned long long*>(b + o_partll);
+    c->attn_ll = reinterpret_cast<uint32_t*>(b + o_attnll);
+    c->x_ll = reinterpret_cast<unsigned long long*>(b + o_xll);
+    c->act_ll = reinterpret_cast<uint32_t*>(b + o_actll);
+    const uint32_t epoch0 = 16;  // no tag of the first step is the zero of an unwritten word
+    cuda(cudaMemcpy(c->epoch, &epoch0, sizeof epoch0, cudaMemcpyHostToDevice), "upload epoch");
     const std::vector<float> freq = rope_inv_freq(d);
     cuda(cudaMemcpy(c->inv_freq, freq.data(), freq.size() * sizeof(float), cudaMemcpyHostToDevice),
          "upload inv_freq");
@@ -823,6 +865,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
       if (st == LCR_OK) cuda(cudaMemset(c->trace, 0, n * sizeof(unsigned long long)), "cudaMemset(trace)");
     }
   }
+  // The exchange needs the tensor-pipe attention phase and bf16 activations.
+  c->ll = c->persistent && !c->f32 && c->kvmaps_dev != nullptr && d.head_dim == 64 && group <= 8 &&
+          !(o.flags & (kFlagGridBarriers | kFlagCudaCoreAttention));
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * kPinnedRing), "cudaMallocHost");
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned_params, sizeof(float) * 8), "cudaMallocHost");
   if (st != LCR_OK) {

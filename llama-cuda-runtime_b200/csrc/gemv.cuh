@@ -37,6 +37,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "ll.cuh"
 
 namespace lcrb {
 
@@ -96,6 +97,18 @@ struct GemvArgs {
   int32_t* state_gen;         // LOGITS_ARGMAX: step generation, advanced by one (nullable)
   unsigned long long* wait_cycles;  // trace: SM cycles thread 0 waited on full stages (nullable)
   unsigned long long* stage_ns;     // trace: [s] stage s ready, [64 + s] released (nullable)
+  // Low-latency exchange (the persistent step, ll.cuh); nullptr: plain memory.
+  const unsigned long long* ll_x;  // NORM input: [K] LL64 residual sums (x = their bf16)
+  const uint32_t* ll_v;            // PLAIN input: [K] LL32 values
+  uint32_t ll_in_tag;
+  uint32_t* ll_y32;                // STORE / SWIGLU output: LL32 words
+  unsigned long long* ll_y64;      // RESID output: LL64 residual sums
+  const unsigned long long* ll_resid;  // RESID: the residual sums of this CTA's rows (its own words)
+  const bf16* resid_embed;         // RESID at the first layer: the embedding row is the residual
+  uint32_t ll_out_tag;
+  uint64_t ll_wait_ns;
+  uint32_t* epoch;          // LOGITS_ARGMAX: the last CTA writes epoch_next there (nullable)
+  uint32_t epoch_next;
 };
 
 // Stage geometry for a K-column matrix. A stage holds RPS rows of KC columns
@@ -250,15 +263,31 @@ __device__ __forceinline__ void ring_drain(uint64_t* full, int issued, uint32_t*
 // applied to the bf16 residual, rounded to bf16 as the reference stores
 // `normed`). Uses named barrier 1; `xs` is complete on return.
 template <int K, int PRO>
-__device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, bf16* xs, float* red8) {
+__device__ __forceinline__ bool gemv_stage_x(const GemvArgs& a, bf16* xs, float* red8) {
   constexpr int KC = K / 8;
   constexpr int PER = (KC + kGemvConsumers - 1) / kGemvConsumers;  // chunks per thread
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  bool ok = true;
   if constexpr (PRO == PRO_PLAIN) {
+    if (a.ll_v != nullptr) {
+      // every chunk of this thread in one poll (KC is a multiple of the
+      // thread count for the persistent step's shapes; others repeat chunks)
+      LLWait wt{a.status, a.ll_wait_ns};
+      uint4 v[2 * PER];
+      ok = ll_poll_groups<2 * PER, false>(
+          [&](int i) -> const void* { return a.ll_v + min(tid + (i >> 1) * kGemvConsumers, KC - 1) * 8 + (i & 1) * 4; },
+          v, a.ll_in_tag, wt);
 #pragma unroll
-    for (int p = 0; p < PER; ++p) {
-      const int c = tid + p * kGemvConsumers;
-      if (c < KC) reinterpret_cast<uint4*>(xs)[c] = ldg_cg16(a.x_in + c * 8);
+      for (int p = 0; p < PER; ++p) {
+        const int c = tid + p * kGemvConsumers;
+        if (c < KC) reinterpret_cast<uint4*>(xs)[c] = ll32_values8(v[2 * p], v[2 * p + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int p = 0; p < PER; ++p) {
+        const int c = tid + p * kGemvConsumers;
+        if (c < KC) reinterpret_cast<uint4*>(xs)[c] = ldg_cg16(a.x_in + c * 8);
+      }
     }
   } else {
     const bf16* src = a.x_in;
@@ -272,19 +301,39 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, bf16* xs, float*
     }
     uint4 raw[PER], gain[PER];
     float ss = 0.f;
+    // With the exchange: the residual sums of every chunk of this thread in
+    // one poll; the residual is their bf16 (the RESID epilogue's store).
+    uint4 lv[PER == 0 ? 1 : 4 * PER];
+    if (PRO == PRO_NORM && a.ll_x != nullptr) {
+      LLWait wt{a.status, a.ll_wait_ns};
+      ok = ll_poll_groups<4 * PER, true>(
+          [&](int i) -> const void* { return a.ll_x + min(tid + (i >> 2) * kGemvConsumers, KC - 1) * 8 + (i & 3) * 2; },
+          lv, a.ll_in_tag, wt);
+    }
 #pragma unroll
     for (int p = 0; p < PER; ++p) {
       const int c = tid + p * kGemvConsumers;
       if (c < KC) {
         gain[p] = ldg16(a.norm_w + c * 8);
-        raw[p] = ldg_cg16(src + c * 8);
         float v[8];
-        if (PRO == PRO_NORM && a.xsum != nullptr) {
+        if (PRO == PRO_NORM && a.ll_x != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            v[2 * q] = __uint_as_float(lv[4 * p + q].y);
+            v[2 * q + 1] = __uint_as_float(lv[4 * p + q].w);
+          }
+          raw[p].x = pack_bf2(v[0], v[1]);
+          raw[p].y = pack_bf2(v[2], v[3]);
+          raw[p].z = pack_bf2(v[4], v[5]);
+          raw[p].w = pack_bf2(v[6], v[7]);
+        } else if (PRO == PRO_NORM && a.xsum != nullptr) {
+          raw[p] = ldg_cg16(src + c * 8);
           const float4 s0 = __ldcg(reinterpret_cast<const float4*>(a.xsum + c * 8));
           const float4 s1 = __ldcg(reinterpret_cast<const float4*>(a.xsum + c * 8 + 4));
           v[0] = s0.x; v[1] = s0.y; v[2] = s0.z; v[3] = s0.w;
           v[4] = s1.x; v[5] = s1.y; v[6] = s1.z; v[7] = s1.w;
         } else {
+          raw[p] = ldg_cg16(src + c * 8);
           unpack8(raw[p], v);
         }
 #pragma unroll
@@ -322,7 +371,8 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, bf16* xs, float*
       }
     }
   }
-  named_sync(1, kGemvConsumers);  // xs complete (and red8 free again)
+  // xs complete (and red8 free again); false: a poll gave up (the step aborts)
+  return !named_sync_or(1, kGemvConsumers, !ok);
 }
 
 // ldmatrix.x4: lane l supplies the shared address of row l % 8 of 8x8 tile
@@ -469,15 +519,29 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
       for (int w = 0; w < WPG; ++w) y += rr[w];
       const int out = first + v;
       if constexpr (EPI == EPI_STORE) {
-        a.y[out] = __ushort_as_bfloat16(f2bf(y));
+        if (a.ll_y32 != nullptr) {
+          st_relaxed_u32(a.ll_y32 + out, ll32_word(y, a.ll_out_tag));
+        } else {
+          a.y[out] = __ushort_as_bfloat16(f2bf(y));
+        }
       } else if constexpr (EPI == EPI_STORE_F32) {
         a.yf[out] = a.round_out ? rbf(y) : y;
       } else if constexpr (EPI == EPI_RESID) {
-        const float s = a.exact_resid
-                            ? __fadd_rn(__ldcg(a.resid_sum + out), y)
-                            : __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)), rbf(y));
-        a.resid[out] = __ushort_as_bfloat16(f2bf(s));
-        a.resid_sum[out] = s;
+        if (a.ll_y64 != nullptr) {
+          // the residual: the embedding row at the first layer, else the bf16
+          // of this CTA's own previous sum
+          const float r = a.resid_embed != nullptr
+                              ? bf2f(__ldg(reinterpret_cast<const unsigned short*>(a.resid_embed) + out))
+                              : rbf(ll64_value(__ldcg(a.ll_resid + out)));
+          st_relaxed_u64(a.ll_y64 + out, ll64_word(__fadd_rn(r, rbf(y)), a.ll_out_tag));
+        } else {
+          const float s = a.exact_resid
+                              ? __fadd_rn(__ldcg(a.resid_sum + out), y)
+                              : __fadd_rn(bf2f(__ldcg(reinterpret_cast<const unsigned short*>(a.resid) + out)),
+                                          rbf(y));
+          a.resid[out] = __ushort_as_bfloat16(f2bf(s));
+          a.resid_sum[out] = s;
+        }
       } else if constexpr (EPI == EPI_SWIGLU) {
         const float* ru = red + (un * RPS + r + PAIRS) * WPG;
         float up = 0.f;
@@ -485,7 +549,11 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
         for (int w = 0; w < WPG; ++w) up += ru[w];
         const float g = rbf(y);
         const float silu = g / (1.0f + __expf(-g));
-        a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
+        if (a.ll_y32 != nullptr) {
+          st_relaxed_u32(a.ll_y32 + out, ll32_word(silu * rbf(up), a.ll_out_tag));
+        } else {
+          a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
+        }
       } else if constexpr (EPI == EPI_SWIGLU_F32) {
         const float* ru = red + (un * RPS + r + PAIRS) * WPG;
         float up = 0.f;
@@ -529,6 +597,7 @@ __device__ __forceinline__ void argmax_finish(const GemvArgs& a, unsigned long l
     if (a.history != nullptr && pos >= 0 && pos < a.history_len) a.history[pos] = next;
     if (a.advance) *a.state_pos = pos + 1;
     if (a.state_gen) *a.state_gen += 1;
+    if (a.epoch) *a.epoch = a.epoch_next;
   }
 }
 

@@ -4,9 +4,9 @@
 namespace lcrb {
 namespace {
 
-template <int H, int QD, int F, int D, int G, bool PAGED, bool F32>
+template <int H, int QD, int F, int D, int G, bool PAGED, bool F32, bool LL = false>
 int launch_t(const MegaArgs& a, int ctas, cudaStream_t stream) {
-  auto kernel = decode_step_kernel<H, QD, F, D, G, PAGED, F32>;
+  auto kernel = decode_step_kernel<H, QD, F, D, G, PAGED, F32, LL>;
   constexpr size_t smem = MegaShape<H, QD, F, D, G, PAGED, F32>::SMEM;
   LCRB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)));
@@ -30,12 +30,16 @@ int launch_t(const MegaArgs& a, int ctas, cudaStream_t stream) {
 
 template <int H, int QD, int F, int D, int G>
 int launch_g(const MegaArgs& a, bool paged, bool f32, int ctas, cudaStream_t stream) {
+  // Three instances per layout: fp32 activations; bf16 activations with grid
+  // barriers; bf16 activations with the tagged-word exchange (a.ll).
   if (paged) {
-    return f32 ? launch_t<H, QD, F, D, G, true, true>(a, ctas, stream)
-               : launch_t<H, QD, F, D, G, true, false>(a, ctas, stream);
+    if (f32) return launch_t<H, QD, F, D, G, true, true>(a, ctas, stream);
+    return a.ll ? launch_t<H, QD, F, D, G, true, false, true>(a, ctas, stream)
+                : launch_t<H, QD, F, D, G, true, false>(a, ctas, stream);
   }
-  return f32 ? launch_t<H, QD, F, D, G, false, true>(a, ctas, stream)
-             : launch_t<H, QD, F, D, G, false, false>(a, ctas, stream);
+  if (f32) return launch_t<H, QD, F, D, G, false, true>(a, ctas, stream);
+  return a.ll ? launch_t<H, QD, F, D, G, false, false, true>(a, ctas, stream)
+              : launch_t<H, QD, F, D, G, false, false>(a, ctas, stream);
 }
 
 }  // namespace

@@ -102,9 +102,21 @@ struct MegaArgs {
   // CUDA-core attention phase.
   const CUtensorMap* kvmaps;
   int kvmap_layer_stride;
+  // Low-latency exchange between phases (ll.cuh) instead of grid barriers
+  // (the kernel instance with LL; bf16 activations with the tensor-pipe
+  // attention only). Tags: epoch base + 5 layer + phase + 1; the step's last
+  // CTA advances the base.
+  int ll;
+  uint32_t* epoch;
+  uint32_t* qkv_ll;              // [QD + 2 KVD] LL32, phase 0
+  unsigned long long* part_ll;   // [heads][splits][D + 4] LL64 split records, phase 1
+  uint32_t* attn_ll;             // [QD] LL32 merged output (many splits), phase 1
+  unsigned long long* x_ll;      // [H] LL64 residual sums, phases 2 (O) and 4 (DOWN)
+  uint32_t* act_ll;              // [F] LL32, phase 3
   unsigned long long prefetch_bytes;  // L2 prefetch lead of the producer (0: off)
   unsigned long long wait_ns;         // bound of each grid-barrier wait
   int test_skip_arrival;              // test only: CTA 0 does not arrive at the first grid barrier
+                                      // (exchange: does not publish its first q/k/v rows)
   // Optional phase trace (globaltimer ns), per CTA kMegaTraceEvents slots:
   // [0] consumers start, [1 + 2k] arrival at barrier k, [2 + 2k] departure,
   // [kMegaTraceProducer + p] producer starting phase p.
@@ -384,6 +396,57 @@ __device__ __forceinline__ void merge_split_records(const float* rec0, int s_beg
   }
 }
 
+// merge_split_records over LL64 records (the same arithmetic, so the result
+// is the same bits): false if a poll gave up.
+template <int D>
+__device__ __forceinline__ bool merge_split_records_ll(const unsigned long long* rec0, int s_begin, int s_end,
+                                                       int step, int d0, uint32_t tag, float& M, float& L,
+                                                       float (&acc)[8], LLWait& w) {
+  constexpr int B = 4;
+  for (int s0 = s_begin; s0 < s_end; s0 += B * step) {
+    float ms[B], ls[B];
+    float4 lo[B], hi[B];
+    // the B records' words in one poll (a missing record reads split s_begin's)
+    uint4 g[5 * B];
+    const bool polled = ll_poll_groups<5 * B, true>(
+        [&](int i) -> const void* {
+          const int s = s0 + (i / 5) * step;
+          const unsigned long long* rec = rec0 + static_cast<size_t>(s < s_end ? s : s_begin) * kMegaPartStride<D>;
+          return i % 5 == 4 ? rec + D : rec + d0 + 2 * (i % 5);
+        },
+        g, tag, w);
+    if (!polled) return false;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const bool in = s0 + b * step < s_end;
+      ms[b] = in ? __uint_as_float(g[5 * b + 4].y) : kNegBig;
+      ls[b] = in ? __uint_as_float(g[5 * b + 4].w) : 0.f;
+      lo[b] = in ? make_float4(__uint_as_float(g[5 * b].y), __uint_as_float(g[5 * b].w),
+                               __uint_as_float(g[5 * b + 1].y), __uint_as_float(g[5 * b + 1].w))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      hi[b] = in ? make_float4(__uint_as_float(g[5 * b + 2].y), __uint_as_float(g[5 * b + 2].w),
+                               __uint_as_float(g[5 * b + 3].y), __uint_as_float(g[5 * b + 3].w))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float Mn = M;
+#pragma unroll
+    for (int b = 0; b < B; ++b) Mn = fmaxf(Mn, ms[b]);
+    const float keep = ex2_approx(M - Mn);
+    L *= keep;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= keep;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const float wgt = s0 + b * step < s_end ? ex2_approx(ms[b] - Mn) : 0.f;
+      L += ls[b] * wgt;
+      acc[0] += lo[b].x * wgt; acc[1] += lo[b].y * wgt; acc[2] += lo[b].z * wgt; acc[3] += lo[b].w * wgt;
+      acc[4] += hi[b].x * wgt; acc[5] += hi[b].y * wgt; acc[6] += hi[b].z * wgt; acc[7] += hi[b].w * wgt;
+    }
+    M = Mn;
+  }
+  return true;
+}
+
 // 8 dims of the merged output, rounded to bf16 as the reference stores attn_out.
 __device__ __forceinline__ uint4 merged_bf16x8(float L, const float (&acc)[8]) {
   const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -506,10 +569,71 @@ __device__ __forceinline__ bool mega_attn_produce_tc(uint8_t* ring, uint64_t* fu
 // l, acc[D]) as this split's (acc[D], m, l) record; the O phase merges the
 // splits of every head in its prologue (mega_load_attention_merged), or, with
 // many splits, the last split of the KV head to publish merges them here.
+// With `ll_tag` (the low-latency exchange) the records go out as LL64 words,
+// and with many splits the KV head's split 0 polls the others' records and
+// merges them (no counter, no fence); false if a poll gave up.
 template <int D, int G, bool F32>
-__device__ __forceinline__ void mega_attn_publish(const MegaArgs& a, int l, const AttnItem& item,
-                                                  const float* scratch, int* s_last) {
+__device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, const AttnItem& item,
+                                                  const float* scratch, int* s_last, uint32_t ll_tag = 0) {
   const int tid = threadIdx.x, lane = tid & 31;
+  if (ll_tag != 0) {
+    unsigned long long* lbase = a.part_ll + static_cast<size_t>(item.kvh) * G * a.splits * kMegaPartStride<D>;
+    for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
+      const int g = idx / D, d = idx % D;
+      float M = kNegBig;
+#pragma unroll
+      for (int w = 0; w < kMegaWarps; ++w) M = fmaxf(M, scratch[(w * G + g) * (D + 2)]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kMegaWarps; ++w) {
+        const float* c = scratch + (w * G + g) * (D + 2);
+        const float sc = ex2_approx(c[0] - M);
+        L += c[1] * sc;
+        A += c[2 + d] * sc;
+      }
+      unsigned long long* rec = lbase + (g * a.splits + item.split) * kMegaPartStride<D>;
+      st_relaxed_u64(rec + d, ll64_word(A, ll_tag));
+      if (d == 0) {
+        st_relaxed_u64(rec + D, ll64_word(M, ll_tag));
+        st_relaxed_u64(rec + D + 1, ll64_word(L, ll_tag));
+      }
+    }
+    if (item.splits <= kMegaPrologueMergeMax || item.split != 0) return true;
+    named_sync(1, kGemvConsumers);  // this CTA's own record is written
+    LLWait wt{a.status, a.wait_ns};
+    bool ok = true;
+    const int sg = lane & 7;
+    for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
+      const int g = c * 8 / D, d0 = c * 8 % D;
+      float M = kNegBig, L = 0.f;
+      float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+        ok = merge_split_records_ll<D>(lbase + static_cast<size_t>(g) * a.splits * kMegaPartStride<D>, sg,
+                                       item.splits, 8, d0, ll_tag, M, L, acc8, wt);
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, M, off);
+        const float ol = __shfl_xor_sync(0xffffffffu, L, off);
+        const float Mn = fmaxf(M, om);
+        const float ws = ex2_approx(M - Mn), wo = ex2_approx(om - Mn);
+        L = L * ws + ol * wo;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float oa = __shfl_xor_sync(0xffffffffu, acc8[e], off);
+          acc8[e] = acc8[e] * ws + oa * wo;
+        }
+        M = Mn;
+      }
+      if (sg == 0) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        uint32_t* dst = a.attn_ll + static_cast<size_t>(item.kvh * G + g) * D + d0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) st_relaxed_u32(dst + e, ll32_word(acc8[e] * inv, ll_tag));
+      }
+    }
+    return ok;
+  }
   float* part_base = a.partials + static_cast<size_t>(item.kvh) * G * a.splits * kMegaPartStride<D>;
   for (int idx = tid; idx < G * D; idx += kGemvConsumers) {
     const int g = idx / D, d = idx % D;
@@ -531,7 +655,7 @@ __device__ __forceinline__ void mega_attn_publish(const MegaArgs& a, int l, cons
       rec[D + 1] = L;
     }
   }
-  if (item.splits <= kMegaPrologueMergeMax) return;
+  if (item.splits <= kMegaPrologueMergeMax) return true;
   // Many splits: the last split of this KV head to publish merges the head
   // group once (8 threads per 8-dim chunk, splits strided over them) and
   // writes the bf16 output; the counter resets for the next step.
@@ -540,7 +664,7 @@ __device__ __forceinline__ void mega_attn_publish(const MegaArgs& a, int l, cons
   unsigned* ctr = a.attn_ctr + static_cast<size_t>(l) * a.num_kv + item.kvh;
   if (tid == 0) *s_last = atomicAdd(ctr, 1u) == static_cast<unsigned>(item.splits - 1);
   named_sync(1, kGemvConsumers);
-  if (!*s_last) return;
+  if (!*s_last) return true;
   __threadfence();
   const int sg = lane & 7;
   for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
@@ -575,6 +699,7 @@ __device__ __forceinline__ void mega_attn_publish(const MegaArgs& a, int l, cons
     }
   }
   if (tid == 0) *ctr = 0u;
+  return true;
 }
 
 // Consumers: one (KV head, split) item -> partials (or the output when there
@@ -796,7 +921,8 @@ template <int D, int G, int STAGES, bool PAGED, bool F32>
 __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64_t* full, uint64_t* empty, int& it,
                                                      const MegaArgs& a, int l, int pos, const float* cs,
                                                      float* scratch, bf16* qs, int* s_last, bool& failed,
-                                                     unsigned long long* wait_cycles = nullptr) {
+                                                     unsigned long long* wait_cycles = nullptr,
+                                                     uint32_t ll_in_tag = 0, uint32_t ll_out_tag = 0) {
   using AG = MegaAttnGeom<D>;
   static_assert(D == 64 && G >= 1 && G <= 8, "tensor-pipe attention: head_dim 64, at most 8 heads per KV head");
   constexpr int UNIT_BYTES = kMegaUnit * D * 2;
@@ -814,7 +940,20 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
   const bool new_lane = has_new && warp == 0 && lane < LPP;
   uint4 k_self = make_uint4(0, 0, 0, 0), k_other = k_self, v_raw = k_self;
   float k_newf[8], v_newf[8];
-  if (new_lane) {
+  LLWait wt{a.status, a.wait_ns};
+  bool ll_ok = true;
+  if (new_lane && ll_in_tag != 0) {
+    const uint32_t* kh = a.qkv_ll + qd + item.kvh * D;
+    const uint32_t* ko = kh + (lane * 8 < D / 2 ? lane * 8 + D / 2 : lane * 8 - D / 2);
+    const uint32_t* vh = a.qkv_ll + qd + kvd + item.kvh * D + lane * 8;
+    const uint32_t* const grp[3] = {kh + lane * 8, ko, vh};
+    uint4 g6[6];
+    ll_ok = ll_poll_groups<6, false>([&](int i) -> const void* { return grp[i >> 1] + (i & 1) * 4; }, g6,
+                                     ll_in_tag, wt);
+    k_self = ll32_values8(g6[0], g6[1]);
+    k_other = ll32_values8(g6[2], g6[3]);
+    v_raw = ll32_values8(g6[4], g6[5]);
+  } else if (new_lane) {
     if constexpr (F32) {
       rope8f<D>(a.qkv_f + qd + item.kvh * D, lane, cs, k_newf);
       const float* vh = a.qkv_f + qd + kvd + item.kvh * D + lane * 8;
@@ -836,13 +975,24 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
     if constexpr (F32) {
       rope8f<D>(a.qkv_f + (item.kvh * G + g) * D, lig, cs, qf);
     } else {
-      rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, qf);
+      if (ll_in_tag != 0) {
+        const uint32_t* qh = a.qkv_ll + (item.kvh * G + g) * D;
+        const uint32_t* qo = qh + (lig * 8 < D / 2 ? lig * 8 + D / 2 : lig * 8 - D / 2);
+        const uint32_t* const grp[2] = {qh + lig * 8, qo};
+        uint4 g4[4];
+        ll_ok = ll_ok && ll_poll_groups<4, false>([&](int i) -> const void* { return grp[i >> 1] + (i & 1) * 4; },
+                                                  g4, ll_in_tag, wt);
+        rope8_from<D>(ll32_values8(g4[0], g4[1]), ll32_values8(g4[2], g4[3]), lig, cs, qf);
+      } else {
+        rope8<D>(a.qkv + (item.kvh * G + g) * D, lig, cs, qf);
+      }
     }
     uint4 hi, lo;
     split_hilo8(qf, hi, lo);
     *reinterpret_cast<uint4*>(qs + g * D + lig * 8) = hi;
     if constexpr (F32) *reinterpret_cast<uint4*>(qlo + g * D + lig * 8) = lo;
   }
+  if (!ll_ok) failed = true;
   named_sync(1, kGemvConsumers);
 
   const int g = lane >> 2, qq = lane & 3;
@@ -1008,7 +1158,7 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
     }
   }
   named_sync(1, kGemvConsumers);
-  mega_attn_publish<D, G, F32>(a, l, item, scratch, s_last);
+  if (!mega_attn_publish<D, G, F32>(a, l, item, scratch, s_last, ll_out_tag)) failed = true;
 }
 
 // O-phase prologue: the attention output staged in shared memory, each thread
@@ -1020,8 +1170,31 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
 // With fp32 activations the output is staged unrounded, as the bf16 pair
 // xs + xs_lo.
 template <int QD, int D, bool F32>
-__device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos, bf16* xs, bf16* xs_lo) {
+__device__ __forceinline__ bool mega_stage_attention(const MegaArgs& a, int pos, bf16* xs, bf16* xs_lo,
+                                                     uint32_t ll_tag = 0) {
   const int splits = mega_attn_splits(pos + 1, a.splits, MegaAttnGeom<D>::P);
+  if (ll_tag != 0) {  // the same values, from the attention phase's LL words
+    LLWait wt{a.status, a.wait_ns};
+    bool ok = true;
+    for (int c = threadIdx.x; c < QD / 8 && ok; c += kGemvConsumers) {
+      const int col = c * 8;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (splits > kMegaPrologueMergeMax) {
+        uint4 g2[2];
+        ok = ll_poll_groups<2, false>([&](int i) -> const void* { return a.attn_ll + col + 4 * i; }, g2, ll_tag, wt);
+        v = ll32_values8(g2[0], g2[1]);
+      } else {
+        const int h = col / D, d0 = col % D;
+        float M = kNegBig, L = 0.f;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        ok = merge_split_records_ll<D>(a.part_ll + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>, 0,
+                                       splits, 1, d0, ll_tag, M, L, acc, wt);
+        v = merged_bf16x8(L, acc);
+      }
+      reinterpret_cast<uint4*>(xs)[c] = v;
+    }
+    return !named_sync_or(1, kGemvConsumers, !ok);
+  }
   for (int c = threadIdx.x; c < QD / 8; c += kGemvConsumers) {
     const int col = c * 8;
     if (splits > kMegaPrologueMergeMax) {  // merged by the attention phase
@@ -1051,6 +1224,7 @@ __device__ __forceinline__ void mega_stage_attention(const MegaArgs& a, int pos,
     }
   }
   named_sync(1, kGemvConsumers);
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -1194,7 +1368,7 @@ struct MegaShape {
                                  static_cast<size_t>(XS) * 2 * (F32 ? 2 : 1) + 64;
 };
 
-template <int H, int QD, int F, int D, int G, bool PAGED, bool F32>
+template <int H, int QD, int F, int D, int G, bool PAGED, bool F32, bool LL = false>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const MegaArgs a) {
   using Shape = MegaShape<H, QD, F, D, G, PAGED, F32>;
   constexpr int STAGES = Shape::STAGES;
@@ -1205,9 +1379,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
   uint64_t* empty = full + STAGES;
   unsigned long long* cta_best = reinterpret_cast<unsigned long long*>(empty + STAGES);
   int* s_flags = reinterpret_cast<int*>(cta_best + 1);  // [0] abort, [1] last-CTA
-  // s_flags[2..3]: the producer's issued-bytes word read by the prefetcher
+  // s_flags[2..3]: the producer's issued-bytes word read by the prefetcher;
+  // [4]: the exchange's epoch base, [5]: the step's token (clamped) -- kept
+  // in shared memory, not in registers across the step
   volatile unsigned long long* s_issued = reinterpret_cast<volatile unsigned long long*>(s_flags + 2);
-  float* red8 = reinterpret_cast<float*>(s_flags + 4);
+  float* red8 = reinterpret_cast<float*>(s_flags + 8);
   float* red = red8 + 8;
   float* cs = red + Shape::RED_FLOATS;  // RoPE cos/sin [D]
   bf16* xs = align_smem<bf16>(cs + D, 128);  // staged input vector [max(H, QD, F)], 16-byte access
@@ -1223,6 +1399,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     *cta_best = 0ull;
     s_flags[0] = 0;
     s_flags[1] = 0;
+    if constexpr (LL) {
+      s_flags[4] = static_cast<int>(__ldcg(a.epoch));
+      int tok = __ldcg(a.state);
+      s_flags[5] = (tok < 0 || tok >= a.vocab) ? 0 : tok;
+    }
     *s_issued = 0;
     mbar_fence_init();
     if (blockIdx.x == 0 && (pos < 0 || pos >= a.max_seq)) atomicOr(a.status, kStatusBadPosition);
@@ -1312,15 +1493,33 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       if (ctrace && tid == 0 && 163 + phase_no < kMegaTraceProducer - 1) ctrace[163 + phase_no] = globaltimer_ns();
       ++phase_no;
     };
+    // Low-latency exchange: the phase outputs carry tags, so a phase ends
+    // with a CTA-local barrier only; the next phase's prologue polls its
+    // inputs. Tag of (layer l, phase p): ep0 + 5 l + p + 1.
+    constexpr bool ll = LL;  // a compile-time choice: each instance carries one exchange
+    auto tag = [&](int layer, int ph) -> uint32_t {
+      return static_cast<uint32_t>(s_flags[4]) + 5u * static_cast<uint32_t>(layer) + ph + 1u;
+    };
     auto sync = [&]() -> bool {
       ++nbar;
-      if (failed) atomicOr(a.status, kStatusAbort);
       unsigned long long* t = (ctrace && 2 * nbar < kMegaTraceProducer) ? ctrace + 2 * nbar - 1 : nullptr;
+      if (ll) {
+        if (t && tid == 0) t[0] = t[1] = globaltimer_ns();
+        const bool any = named_sync_or(1, kGemvConsumers, failed);
+        if (any && tid == 0) atomicOr(a.status, kStatusAbort);
+        return !any;
+      }
+      if (failed) atomicOr(a.status, kStatusAbort);
       const bool arrive = !(a.test_skip_arrival && nbar == 1 && blockIdx.x == 0);
       return mega_grid_sync(a.bar, nbar * static_cast<unsigned>(ctas), a.status, &s_flags[0], t, a.wait_ns,
                             arrive) &&
              !failed;
     };
+    // With the exchange, a CTA without rows in a phase reads none of its
+    // inputs: every reader of an exchange buffer then also produces output
+    // that the buffer's next writer must see first.
+    auto hrow0 = [&]() { return gemv_share(H, blockIdx.x, ctas); };
+    auto hrow1 = [&]() { return gemv_share(H, blockIdx.x + 1, ctas); };
     bool run = true;
     for (int l = 0; l < a.layers && run; ++l) {
       const MegaLayer& w = a.L[l];
@@ -1332,9 +1531,21 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.norm_w = w.input_norm;
         g.y = a.qkv;
         g.yf = a.qkv_f;
+        const int r0 = gemv_share(nqkv, blockIdx.x, ctas), r1 = gemv_share(nqkv, blockIdx.x + 1, ctas);
+        if (ll) {
+          g.ll_wait_ns = a.wait_ns;
+          // test switch: CTA 0 keeps its first q/k/v rows out of the exchange
+          // (plain stores), so the attention phase's polls time out
+          g.ll_y32 = (a.test_skip_arrival && l == 0 && blockIdx.x == 0) ? nullptr : a.qkv_ll;
+          g.ll_out_tag = tag(l, 0);
+          g.ll_x = l > 0 ? a.x_ll : nullptr;
+          g.ll_in_tag = l > 0 ? tag(l - 1, 4) : 0u;
+        }
         if constexpr (F32) {
           mega_stage_norm_f32<H>(a.xsum, l == 0 ? a.embed : nullptr, a.state, a.vocab, a.status, a.x, a.xsum,
                                  w.input_norm, a.eps, xs, xs_lo, red8);
+        } else if (ll && r0 >= r1) {
+          // no rows: nothing to stage
         } else if (l == 0) {
           g.embed = a.embed;
           g.token = a.state;
@@ -1345,13 +1556,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         } else {
           g.x_in = a.x;
           g.xsum = a.xsum;
-          gemv_stage_x<H, PRO_NORM>(g, xs, red8);
+          if (!gemv_stage_x<H, PRO_NORM>(g, xs, red8)) failed = true;
         }
         pro_done();
         g.wait_cycles = cwait();
-        gemv_consume<H, STAGES, F32 ? EPI_STORE_F32 : EPI_STORE, F32>(ring, full, empty, it, g,
-                                                                      gemv_share(nqkv, blockIdx.x, ctas),
-                                                                      gemv_share(nqkv, blockIdx.x + 1, ctas), xs, red,
+        gemv_consume<H, STAGES, F32 ? EPI_STORE_F32 : EPI_STORE, F32>(ring, full, empty, it, g, r0, r1, xs, red,
                                                                       best, failed, xs_lo);
       }
       if (!(run = sync())) break;
@@ -1359,7 +1568,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       if constexpr (D == 64 && G <= 8) {
         if (a.kvmaps) {
           mega_attn_consume_tc<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, xs, &s_flags[1],
-                                                         failed, cwait());
+                                                         failed, cwait(), ll ? tag(l, 0) : 0u,
+                                                         ll ? tag(l, 1) : 0u);
         } else {
           mega_attn_consume<D, G, STAGES, PAGED, F32>(ring, full, empty, it, a, l, pos, cs, red, &s_flags[1], failed,
                                                       cwait());
@@ -1375,11 +1585,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.resid = a.x;
         g.resid_sum = a.xsum;
         g.exact_resid = F32 ? 1 : 0;
-        mega_stage_attention<QD, D, F32>(a, pos, xs, xs_lo);
+        if (ll) {
+          g.ll_y64 = a.x_ll;
+          g.ll_resid = a.x_ll;
+          g.resid_embed = l == 0 ? a.embed + static_cast<size_t>(s_flags[5]) * H : nullptr;
+          g.ll_out_tag = tag(l, 2);
+          if (hrow0() < hrow1() && !mega_stage_attention<QD, D, F32>(a, pos, xs, xs_lo, tag(l, 1))) failed = true;
+        } else {
+          mega_stage_attention<QD, D, F32>(a, pos, xs, xs_lo);
+        }
         pro_done();
         g.wait_cycles = cwait();
-        gemv_consume<QD, STAGES, EPI_RESID, F32>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
-                                                 gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed, xs_lo);
+        gemv_consume<QD, STAGES, EPI_RESID, F32>(ring, full, empty, it, g, hrow0(), hrow1(), xs, red, best, failed,
+                                                 xs_lo);
       }
       if (!(run = sync())) break;
       {  // GU
@@ -1391,18 +1609,24 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.norm_w = w.post_norm;
         g.y = a.act;
         g.yf = a.act_f;
+        const int f0 = gemv_share(F, blockIdx.x, ctas), f1 = gemv_share(F, blockIdx.x + 1, ctas);
+        if (ll) {
+          g.ll_wait_ns = a.wait_ns;
+          g.ll_x = a.x_ll;
+          g.ll_in_tag = tag(l, 2);
+          g.ll_y32 = a.act_ll;
+          g.ll_out_tag = tag(l, 3);
+        }
         if constexpr (F32) {
           mega_stage_norm_f32<H>(a.xsum, nullptr, nullptr, 0, a.status, nullptr, nullptr, w.post_norm, a.eps, xs,
                                  xs_lo, red8);
-        } else {
-          gemv_stage_x<H, PRO_NORM>(g, xs, red8);
+        } else if (!ll || f0 < f1) {
+          if (!gemv_stage_x<H, PRO_NORM>(g, xs, red8)) failed = true;
         }
         pro_done();
         g.wait_cycles = cwait();
         g.stage_ns = (ctrace && l == kMegaTraceStageLayer) ? ctrace + kMegaTraceStages + 64 : nullptr;
-        gemv_consume<H, STAGES, F32 ? EPI_SWIGLU_F32 : EPI_SWIGLU, F32>(ring, full, empty, it, g,
-                                                                        gemv_share(F, blockIdx.x, ctas),
-                                                                        gemv_share(F, blockIdx.x + 1, ctas), xs, red,
+        gemv_consume<H, STAGES, F32 ? EPI_SWIGLU_F32 : EPI_SWIGLU, F32>(ring, full, empty, it, g, f0, f1, xs, red,
                                                                         best, failed, xs_lo);
       }
       if (!(run = sync())) break;
@@ -1413,15 +1637,23 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.resid = a.x;
         g.resid_sum = a.xsum;
         g.exact_resid = F32 ? 1 : 0;
+        if (ll) {
+          g.ll_wait_ns = a.wait_ns;
+          g.ll_v = a.act_ll;
+          g.ll_in_tag = tag(l, 3);
+          g.ll_y64 = a.x_ll;
+          g.ll_resid = a.x_ll;
+          g.ll_out_tag = tag(l, 4);
+        }
         if constexpr (F32) {
           mega_stage_vec_f32(a.act_f, F, xs, xs_lo);
-        } else {
-          gemv_stage_x<F, PRO_PLAIN>(g, xs, red8);
+        } else if (!ll || hrow0() < hrow1()) {
+          if (!gemv_stage_x<F, PRO_PLAIN>(g, xs, red8)) failed = true;
         }
         pro_done();
         g.wait_cycles = cwait();
-        gemv_consume<F, STAGES, EPI_RESID, F32>(ring, full, empty, it, g, gemv_share(H, blockIdx.x, ctas),
-                                                gemv_share(H, blockIdx.x + 1, ctas), xs, red, best, failed, xs_lo);
+        gemv_consume<F, STAGES, EPI_RESID, F32>(ring, full, empty, it, g, hrow0(), hrow1(), xs, red, best, failed,
+                                                xs_lo);
       }
       if (!(run = sync())) break;
     }
@@ -1433,18 +1665,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       g.xsum = a.xsum;
       g.norm_w = a.final_norm;
       g.yf = a.logits;
+      const int v0 = gemv_share(a.vocab, blockIdx.x, ctas), v1 = gemv_share(a.vocab, blockIdx.x + 1, ctas);
+      if (ll) {
+        g.ll_wait_ns = a.wait_ns;
+        g.ll_x = a.x_ll;
+        g.ll_in_tag = tag(a.layers - 1, 4);
+      }
       if constexpr (F32) {
         mega_stage_norm_f32<H>(a.xsum, nullptr, nullptr, 0, a.status, nullptr, nullptr, a.final_norm, a.eps, xs,
                                xs_lo, red8);
-      } else {
-        gemv_stage_x<H, PRO_NORM>(g, xs, red8);
+      } else if (!ll || v0 < v1) {
+        if (!gemv_stage_x<H, PRO_NORM>(g, xs, red8)) failed = true;
       }
       pro_done();
       g.wait_cycles = cwait();
-      gemv_consume<H, STAGES, EPI_LOGITS_ARGMAX, F32>(ring, full, empty, it, g,
-                                                      gemv_share(a.vocab, blockIdx.x, ctas),
-                                                      gemv_share(a.vocab, blockIdx.x + 1, ctas), xs, red,
-                                                      best, failed, xs_lo);
+      gemv_consume<H, STAGES, EPI_LOGITS_ARGMAX, F32>(ring, full, empty, it, g, v0, v1, xs, red, best, failed,
+                                                      xs_lo);
       if (best != 0ull) atomicMax(cta_best, best);
       if (ctrace && tid == 0) ctrace[kMegaTraceProducer - 1] = globaltimer_ns();
     }
@@ -1460,6 +1696,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     g.history = a.history;
     g.history_len = a.history_len;
     g.advance = 1;
+    if constexpr (LL) {  // the next step's epoch base, past every tag of this one
+      g.epoch = a.epoch;
+      g.epoch_next = __ldcg(a.epoch) + 5u * static_cast<uint32_t>(a.layers) + 8u;
+    }
     argmax_finish(g, *cta_best);
   }
 }

@@ -1,9 +1,10 @@
 """llama-run for the B200 build (the reference's src/main.cu CLI surface, on the
-seeded random-init checkpoints: there is no tokenizer on this path, so the
-prompt is token ids).
+seeded random-init checkpoints or a safetensors checkpoint directory: there is
+no tokenizer on this path, so the prompt is token ids).
 
   python -m lcr_b200.run --model 1b --prompt-len 128 --max-tokens 256 --bench
   python -m lcr_b200.run --model tiny --prompt 1,2,3 --max-tokens 16 --json
+  python -m lcr_b200.run --model /path/to/checkpoint --prompt 1,2,3 --max-tokens 16
 
 --bench / --json report the numbers of main.cu:195-334: decode tokens/s,
 ms/token, bytes per token (weights + mean-length KV read) and the achieved
@@ -64,7 +65,9 @@ def print_trace(t: np.ndarray, layers: int, sm_mhz: float = 1965.0) -> None:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="lcr_b200.run")
-    ap.add_argument("--model", default="1b", choices=sorted(MODELS))
+    ap.add_argument("--model", default="1b",
+                    help="1b or tiny (seeded random-init checkpoints) or a checkpoint directory "
+                         "(config.json + safetensors)")
     ap.add_argument("--seed", type=int, default=None, help="checkpoint seed (1b: 1, tiny: 0)")
     ap.add_argument("--prompt", default=None, help="comma-separated token ids")
     ap.add_argument("--prompt-len", type=int, default=128, help="uniform random prompt length")
@@ -88,6 +91,8 @@ def main(argv=None) -> int:
                     help="the multi-kernel step instead of the persistent kernel")
     ap.add_argument("--cuda-core-attention", action="store_true",
                     help="persistent step's attention phase on CUDA cores instead of the tensor pipe")
+    ap.add_argument("--grid-barriers", action="store_true",
+                    help="persistent step's phases meet at grid barriers instead of exchanging tagged words")
     ap.add_argument("--per-token-prefill", action="store_true",
                     help="the prompt as decode steps instead of tcgen05 chunks")
     ap.add_argument("--trace", action="store_true",
@@ -96,9 +101,13 @@ def main(argv=None) -> int:
                     help="with --trace: also save the raw per-CTA timestamps (.npy)")
     args = ap.parse_args(argv)
 
-    geom = MODELS[args.model]
     seed = args.seed if args.seed is not None else (1 if args.model == "1b" else 0)
-    block = ck.generate(geom, seed)
+    if args.model in MODELS:
+        geom = MODELS[args.model]
+        block = ck.generate(geom, seed)
+    else:
+        block = ck.load_checkpoint(args.model)
+        geom = block.geom
     if args.prompt:
         prompt = np.array([int(t) for t in args.prompt.split(",")], np.int32)
     else:
@@ -112,6 +121,7 @@ def main(argv=None) -> int:
                  | (rt.FLAG_FP32_ACT if args.fp32_act else 0)
                  | (rt.FLAG_NO_PERSISTENT if args.no_persistent else 0)
                  | (rt.FLAG_CUDA_CORE_ATTENTION if args.cuda_core_attention else 0)
+                 | (rt.FLAG_GRID_BARRIERS if args.grid_barriers else 0)
                  | (rt.FLAG_PER_TOKEN_PREFILL if args.per_token_prefill else 0))
     load_ms = (time.perf_counter() - t0) * 1000
 

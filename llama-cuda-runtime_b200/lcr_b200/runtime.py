@@ -33,8 +33,9 @@ FLAG_TRACE = 8
 # reference's bf16 storage rounding: closer to the fp32 host evaluation, about
 # 10 % slower.
 FLAG_FP32_ACT = 16
-# Tests only: the persistent step's grid barriers wait 50 ms and CTA 0 skips
-# its first arrival, so every step stops with LCR_ERR_TIMEOUT.
+# Tests only: the persistent step's waits give up after 50 ms and CTA 0 skips
+# its first arrival (a grid barrier, or its first exchange words), so every
+# step stops with LCR_ERR_TIMEOUT.
 FLAG_TEST_TIMEOUT = 32
 # lcr_prefill one decode step per token, as the reference's Model::prefill,
 # instead of the tcgen05 chunks of up to 2048 prompt rows.
@@ -42,6 +43,10 @@ FLAG_PER_TOKEN_PREFILL = 64
 # The persistent step's attention phase on CUDA cores (8 lanes per cached
 # position) instead of the tensor pipe (mma.sync over 16-position units).
 FLAG_CUDA_CORE_ATTENTION = 128
+# The persistent step's phases meet at grid barriers instead of exchanging
+# tagged words (the default with bf16 activations and the tensor-pipe
+# attention; the results are the same bits).
+FLAG_GRID_BARRIERS = 256
 
 
 class LcrError(RuntimeError):
@@ -258,7 +263,7 @@ class Model:
         addr = lambda name: base + block.offsets[name][0] * 2
         self._layers = (LayerWeights * g.num_layers)(*[
             LayerWeights(*[addr(n) for n in block.layer_groups(l)]) for l in range(g.num_layers)])
-        self._weights = Weights(addr("embed"), addr("final_norm"), addr("embed"), self._layers)
+        self._weights = Weights(addr("embed"), addr("final_norm"), addr(block.lm_head_group), self._layers)
         self._desc = desc_of(g)
         self.options = Options(device, max_seq, int(paged), page_size, attention_splits,
                                page_order_seed, gemv_ctas, flags)
@@ -398,7 +403,7 @@ class Batch:
         addr = lambda name: base + block.offsets[name][0] * 2
         self._layers = (LayerWeights * g.num_layers)(*[
             LayerWeights(*[addr(n) for n in block.layer_groups(l)]) for l in range(g.num_layers)])
-        self._weights = Weights(addr("embed"), addr("final_norm"), addr("embed"), self._layers)
+        self._weights = Weights(addr("embed"), addr("final_norm"), addr(block.lm_head_group), self._layers)
         self._desc = desc_of(g)
         self.options = BatchOptions(device, max_batch, max_seq, page_size, pool_pages, flags)
         h = ctypes.c_void_p()

@@ -154,7 +154,7 @@ class Model:
         n = g.num_layers
         arr = lambda suffix: (_u16p * n)(*[p(f"layers.{l}.{suffix}") for l in range(n)])
         self._keep = [arr(s) for s in ("input_norm", "qkv", "o", "post_norm", "gate_up", "down")]
-        self.w = _Weights(p("embed"), p("final_norm"), p("embed"), *self._keep)
+        self.w = _Weights(p("embed"), p("final_norm"), p(block.lm_head_group), *self._keep)
         self.state = L.orc_state_new(ctypes.byref(self.cfg), max_seq)
         self.max_seq = max_seq
 

@@ -151,6 +151,27 @@ def test_step_variants_are_bit_identical(tiny, variant):
 
 
 @pytest.mark.parametrize("paged", [False, True])
+@pytest.mark.parametrize("length", [40, 700])
+def test_exchange_matches_grid_barriers(tiny, paged, length):
+    """The persistent step's tagged-word exchange between phases (default)
+    and its grid barriers compute the same bits: the prompt as decode steps,
+    then greedy steps -- one split per KV head at 40 positions, six (merged by
+    a designated split through the exchange) at 700."""
+    block, wdev = tiny
+    prompt = ck.prompt_ids(5, length)
+    kw = dict(max_seq=length + 24, paged=paged, page_size=16, page_order_seed=13)
+    a = rt.Model(block, wdev, flags=rt.FLAG_PER_TOKEN_PREFILL, **kw)
+    b = rt.Model(block, wdev, flags=rt.FLAG_PER_TOKEN_PREFILL | rt.FLAG_GRID_BARRIERS, **kw)
+    a.prefill(prompt)
+    b.prefill(prompt)
+    la, lb = a.logits_to_host(), b.logits_to_host()
+    assert np.array_equal(la, lb)
+    first = int(np.argmax(la))
+    assert a.generate_greedy(first, 12).tolist() == b.generate_greedy(first, 12).tolist()
+    assert np.array_equal(a.logits_to_host(), b.logits_to_host())
+
+
+@pytest.mark.parametrize("paged", [False, True])
 def test_tiny_long_context_vs_oracle(tiny, paged):
     """700 cached positions: several 128-position KV stages per attention
     split and many splits per KV head, shuffled physical pages when paged --
@@ -200,10 +221,12 @@ def test_paged_block_tables_match_oracle_allocator(tiny):
     assert np.array_equal(tables, want)
 
 
-def test_timeout_path_reports_and_recovers(tiny):
-    """A grid barrier that never fills, made on purpose without faulting
-    anything: the test switch has CTA 0 skip its first arrival and bounds
-    every grid-barrier wait at 50 ms. The waiting CTAs give up, raise the
+@pytest.mark.parametrize("sync", [0, rt.FLAG_GRID_BARRIERS], ids=["exchange", "grid-barriers"])
+def test_timeout_path_reports_and_recovers(tiny, sync):
+    """A wait that never ends, made on purpose without faulting anything: the
+    test switch bounds every wait at 50 ms and has CTA 0 skip its first
+    arrival at a grid barrier, or, with the tagged-word exchange, keep its
+    first q/k/v rows out of the exchange. The waiting CTAs give up, raise the
     abort bit, the producers stop at it and drain the copies they issued, and
     every step of the prompt ends quickly; the host reads LCR_ERR_TIMEOUT.
     The context is then destroyed, and fresh contexts on the same device and
@@ -213,7 +236,7 @@ def test_timeout_path_reports_and_recovers(tiny):
     block, wdev = tiny
     prompt = ck.prompt_ids(0, 8)
     # The prompt as decode steps: each one a persistent step that times out.
-    per_token = rt.FLAG_PER_TOKEN_PREFILL
+    per_token = rt.FLAG_PER_TOKEN_PREFILL | sync
     m = rt.Model(block, wdev, max_seq=32, flags=rt.FLAG_TEST_TIMEOUT | per_token)
     t0 = time.perf_counter()
     with pytest.raises(rt.LcrError) as e:
