@@ -714,8 +714,9 @@ def main():
                     "achieved_gbs": round(step_bytes / (ms_per_step / 1000) / 1e9, 1),
                     "frac_of_peak": round(step_bytes / (ms_per_step / 1000) / 1e9 / peak, 4),
                     "peak_gbs": peak},
-            "roofline": {"kernel": "decode_step_kernel<2048, 2048, 8192, 64, 4, 0> "
-                                   "(persistent step, one launch per token)",
+            "roofline": {"kernel": "decode_step_kernel<2048, 2048, 8192, 64, 4, 0, 0, 1> "
+                                   "(persistent step, tagged-word exchange between phases, "
+                                   "one launch per token)",
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profile_traffic(), "peak_source": peak_kind,

@@ -257,15 +257,16 @@ LCR_API int lcr_position(const lcr_ctx* ctx);
 LCR_API int lcr_decode(lcr_ctx* ctx, int token, const float** logits);
 
 /* Model::prefill, src/model.cu:308-345: the prompt at the current position;
- * *logits for the last token, and the device state as after the reference's
- * per-token prefill (next token = the argmax of those logits, position
- * advanced). Prompts of two or more tokens run in chunks of up to 2048 rows on
- * the tcgen05 path of lcr_batch_prefill (projections as GEMMs over the
- * chunk, causal attention over the cache), writing this context's own cache;
- * one decode step per token, as the reference, with options bit 6, with
- * fp32 activations (bit 4), with a paged cache whose page size is not a
- * multiple of 16, or for a model the batch kernels are not built for.
- * Synchronous. */
+ * *logits for the last token, and the device state ready for the next step
+ * (next token = the argmax of those logits, position advanced). Like the
+ * reference, which runs the prompt in chunks of prefill_chunk positions
+ * (cuBLAS projections, a bf16 softmax and the P.V GEMM), prompts of two or
+ * more tokens run in chunks -- of up to 2048 rows, on the tcgen05 path of
+ * lcr_batch_prefill (projections as GEMMs over the chunk, causal flash
+ * attention over the cache), writing this context's own cache. One decode
+ * step per token instead with options bit 6, with fp32 activations (bit 4),
+ * with a paged cache whose page size is not a multiple of 16, or for a model
+ * the batch kernels are not built for. Synchronous. */
 LCR_API int lcr_prefill(lcr_ctx* ctx, const int32_t* tokens, int count,
                 const float** logits);
 

@@ -37,8 +37,8 @@ FLAG_FP32_ACT = 16
 # its first arrival (a grid barrier, or its first exchange words), so every
 # step stops with LCR_ERR_TIMEOUT.
 FLAG_TEST_TIMEOUT = 32
-# lcr_prefill one decode step per token, as the reference's Model::prefill,
-# instead of the tcgen05 chunks of up to 2048 prompt rows.
+# lcr_prefill one decode step per token (the decode step's maths) instead of
+# the tcgen05 chunks of up to 2048 prompt rows.
 FLAG_PER_TOKEN_PREFILL = 64
 # The persistent step's attention phase on CUDA cores (8 lanes per cached
 # position) instead of the tensor pipe (mma.sync over 16-position units).

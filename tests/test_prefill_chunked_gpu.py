@@ -1,8 +1,8 @@
 """lcr_prefill's tcgen05 chunk path (the default for prompts of two or more
 tokens) through the C ABI: the prefilled cache's logits and the decode steps
-that follow, against the reference's own per-token prefill (one decode step
-per prompt token, options bit 6) and against the oracle's chunked prefill
-(src/model.cu:308-345) at the same rounding points.
+that follow, against the per-token path (one decode step per prompt token,
+options bit 6) and against the oracle's chunked prefill (the reference's
+src/model.cu:308-345 and 509-556) at the same rounding points.
 
 Tolerances: 2e-2 max-abs on the logits against the bf16-storage oracle's
 chunk and against the per-token path. Both the reference's prefill and this
