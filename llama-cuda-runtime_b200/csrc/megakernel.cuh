@@ -1517,7 +1517,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     };
     // With the exchange, a CTA without rows in a phase reads none of its
     // inputs: every reader of an exchange buffer then also produces output
-    // that the buffer's next writer must see first.
+    // that the buffer's next writer must see first, so no word is rewritten
+    // while a reader still needs its previous value:
+    //   qkv_ll  read by ATTN(l); rewritten by QKV(l+1), whose writers polled
+    //           every DOWN(l) residual word, written after each DOWN-row owner
+    //           finished O(l), which needed every attention record of layer l;
+    //   part_ll / attn_ll  read by O(l); rewritten by ATTN(l+1), whose CTAs
+    //           polled q/k/v rows written after their owners' QKV(l+1)
+    //           prologue, which needed every DOWN(l) word -- written after
+    //           each O-row owner (the same rows as DOWN) finished O(l);
+    //   x_ll    read by GU(l) (O's sums) and QKV(l+1) (DOWN's); rewritten by
+    //           DOWN(l) after polling every act word of GU(l), and by
+    //           O(l+1) after polling records that needed every q/k/v row of
+    //           QKV(l+1);
+    //   act_ll  read by DOWN(l); rewritten by GU(l+1) after polling every
+    //           O(l+1) residual word, written by the DOWN-row owners after
+    //           DOWN(l).
     auto hrow0 = [&]() { return gemv_share(H, blockIdx.x, ctas); };
     auto hrow1 = [&]() { return gemv_share(H, blockIdx.x + 1, ctas); };
     bool run = true;
