@@ -169,6 +169,8 @@ struct lcr_ctx {
   unsigned* mega_bar = nullptr;
   unsigned long long* trace = nullptr;  // kFlagTrace: per-CTA phase timestamps
   unsigned long long prefetch_bytes = 0;  // persistent step: L2 prefetch lead per CTA
+  int split_positions = 0;                // persistent step: cached positions per attention split
+  size_t ll_copy_bytes = 0;               // stride of the exchange buffers' replicas
 
   cudaGraphExec_t exec = nullptr;
   int launches = 0;
@@ -289,6 +291,7 @@ int enqueue_persistent_step(lcr_ctx* c) {
   a.vpool = c->vpool;
   a.trace = c->trace;
   a.prefetch_bytes = c->prefetch_bytes;
+  a.split_positions = c->split_positions;
   if (d.head_dim == 64 && !(c->o.flags & kFlagCudaCoreAttention)) {
     a.kvmaps = c->kvmaps_dev;  // nullptr when the cache has no tensor maps
     a.kvmap_layer_stride = c->o.paged ? 0 : 2;
@@ -301,6 +304,7 @@ int enqueue_persistent_step(lcr_ctx* c) {
     a.attn_ll = c->attn_ll;
     a.x_ll = c->x_ll;
     a.act_ll = c->act_ll;
+    a.ll_copy_bytes = c->ll_copy_bytes;
   }
   a.wait_ns = (c->o.flags & kFlagTestTimeout) ? 50000000ull : kWaitLimitNs;
   a.test_skip_arrival = (c->o.flags & kFlagTestTimeout) ? 1 : 0;
@@ -677,6 +681,13 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   } else {
     c->prefetch_bytes = 384ull << 10;
   }
+  // LCR_SPLIT_POSITIONS: the cached positions per attention split the
+  // persistent step aims at, a tuning knob like the prefetch lead. Each merge
+  // hop costs about as much as a few 128-position stages, so a split takes
+  // about three stages: one split up to 384 positions (config 2), 18 at 8192
+  // (config 3, the one-CTA-per-SM cap).
+  c->split_positions = 384;
+  if (const char* env = std::getenv("LCR_SPLIT_POSITIONS")) c->split_positions = std::max(32, std::atoi(env));
   c->persistent = (o.flags & kFlagNoPersistent) == 0 &&
                   mega_supported(d.hidden_size, qd, d.intermediate_size, d.head_dim, group);
   c->f32 = (o.flags & kFlagFp32Act) != 0;
@@ -730,11 +741,21 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   const size_t o_sparams = carve(sizeof(float) * 8);
   const size_t o_sampled = carve(sizeof(int32_t) * 4);
   const size_t o_epoch = carve(sizeof(uint32_t));
-  const size_t o_qkvll = carve(sizeof(uint32_t) * (qd + 2 * kvd));
+  // The exchange buffers: qkv, attn, x and act are held in kLLCopies
+  // replicas ll_copy_bytes apart (4 KB past a 64 KB multiple, so the
+  // replicas start at different offsets within 64 KB).
+  {
+    const size_t biggest = std::max({sizeof(uint32_t) * (qd + 2 * kvd), sizeof(uint32_t) * qd,
+                                     sizeof(unsigned long long) * d.hidden_size,
+                                     sizeof(uint32_t) * d.intermediate_size});
+    c->ll_copy_bytes = (biggest + 65535) / 65536 * 65536 + 4096;
+  }
+  const size_t rep = c->ll_copy_bytes * static_cast<size_t>(kLLCopies);
+  const size_t o_qkvll = carve(rep);
   const size_t o_partll = carve(sizeof(unsigned long long) * d.num_heads * c->splits * (4 + d.head_dim));
-  const size_t o_attnll = carve(sizeof(uint32_t) * qd);
-  const size_t o_xll = carve(sizeof(unsigned long long) * d.hidden_size);
-  const size_t o_actll = carve(sizeof(uint32_t) * d.intermediate_size);
+  const size_t o_attnll = carve(rep);
+  const size_t o_xll = carve(rep);
+  const size_t o_actll = carve(rep);
   if (st == LCR_OK) cuda(cudaMalloc(&c->buf, off), "cudaMalloc(activations)");
   if (st == LCR_OK) cuda(cudaMemset(c->buf, 0, off), "cudaMemset(activations)");
   if (st == LCR_OK) {

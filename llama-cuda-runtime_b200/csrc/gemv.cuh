@@ -109,7 +109,22 @@ struct GemvArgs {
   uint64_t ll_wait_ns;
   uint32_t* epoch;          // LOGITS_ARGMAX: the last CTA writes epoch_next there (nullable)
   uint32_t epoch_next;
+  unsigned long long ll_copy_bytes;  // ll_y32 / ll_y64: kLLCopies replicas this far apart
 };
+
+// Stores an exchange word into each of the buffer's kLLCopies replicas.
+template <class T>
+__device__ __forceinline__ void ll_store_all(T* p, T w, unsigned long long copy_bytes) {
+#pragma unroll
+  for (int r = 0; r < kLLCopies; ++r) {
+    T* q = reinterpret_cast<T*>(reinterpret_cast<char*>(p) + r * copy_bytes);
+    if constexpr (sizeof(T) == 8) {
+      st_relaxed_u64(reinterpret_cast<unsigned long long*>(q), w);
+    } else {
+      st_relaxed_u32(reinterpret_cast<uint32_t*>(q), w);
+    }
+  }
+}
 
 // Stage geometry for a K-column matrix. A stage holds RPS rows of KC columns
 // (the whole row for K <= 2048, a 2048-column segment beyond), 32 KB of
@@ -520,7 +535,7 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
       const int out = first + v;
       if constexpr (EPI == EPI_STORE) {
         if (a.ll_y32 != nullptr) {
-          st_relaxed_u32(a.ll_y32 + out, ll32_word(y, a.ll_out_tag));
+          ll_store_all(a.ll_y32 + out, ll32_word(y, a.ll_out_tag), a.ll_copy_bytes);
         } else {
           a.y[out] = __ushort_as_bfloat16(f2bf(y));
         }
@@ -533,7 +548,7 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
           const float r = a.resid_embed != nullptr
                               ? bf2f(__ldg(reinterpret_cast<const unsigned short*>(a.resid_embed) + out))
                               : rbf(ll64_value(__ldcg(a.ll_resid + out)));
-          st_relaxed_u64(a.ll_y64 + out, ll64_word(__fadd_rn(r, rbf(y)), a.ll_out_tag));
+          ll_store_all(a.ll_y64 + out, ll64_word(__fadd_rn(r, rbf(y)), a.ll_out_tag), a.ll_copy_bytes);
         } else {
           const float s = a.exact_resid
                               ? __fadd_rn(__ldcg(a.resid_sum + out), y)
@@ -550,7 +565,7 @@ __device__ __forceinline__ void gemv_consume(const uint8_t* ring, uint64_t* full
         const float g = rbf(y);
         const float silu = g / (1.0f + __expf(-g));
         if (a.ll_y32 != nullptr) {
-          st_relaxed_u32(a.ll_y32 + out, ll32_word(silu * rbf(up), a.ll_out_tag));
+          ll_store_all(a.ll_y32 + out, ll32_word(silu * rbf(up), a.ll_out_tag), a.ll_copy_bytes);
         } else {
           a.y[out] = __ushort_as_bfloat16(f2bf(silu * rbf(up)));
         }

@@ -50,6 +50,11 @@ __device__ __forceinline__ float ll64_value(unsigned long long w) {
   return __uint_as_float(static_cast<uint32_t>(w >> 32));
 }
 
+// Replicas of each exchange buffer: writers store every replica and CTA c
+// polls replica c % kLLCopies, so each line is polled by a quarter of the
+// CTAs (with one replica the bs1 step measured 4-5 % slower).
+constexpr int kLLCopies = 4;
+
 // Bounded wait bookkeeping shared by the polls: true to keep waiting.
 struct LLWait {
   uint32_t* status;

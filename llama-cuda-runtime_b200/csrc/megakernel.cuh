@@ -113,7 +113,12 @@ struct MegaArgs {
   uint32_t* attn_ll;             // [QD] LL32 merged output (many splits), phase 1
   unsigned long long* x_ll;      // [H] LL64 residual sums, phases 2 (O) and 4 (DOWN)
   uint32_t* act_ll;              // [F] LL32, phase 3
+  // qkv_ll, attn_ll, x_ll and act_ll are held in kLLCopies replicas
+  // ll_copy_bytes apart: writers store every replica, CTA c reads replica
+  // c % kLLCopies (fewer CTAs polling each line).
+  unsigned long long ll_copy_bytes;
   unsigned long long prefetch_bytes;  // L2 prefetch lead of the producer (0: off)
+  int split_positions;                // attention: cached positions per split this step aims at
   unsigned long long wait_ns;         // bound of each grid-barrier wait
   int test_skip_arrival;              // test only: CTA 0 does not arrive at the first grid barrier
                                       // (exchange: does not publish its first q/k/v rows)
@@ -343,8 +348,15 @@ struct AttnItem {
   int kvh, split, splits, begin, end, cache_end, nblocks;
 };
 
-__device__ __forceinline__ int mega_attn_splits(int seq_len, int max_splits, int p) {
-  return max(1, min(max_splits, (seq_len + 2 * p - 1) / (2 * p)));
+// This CTA's replica of an exchange buffer (kLLCopies of them).
+template <class T>
+__device__ __forceinline__ T* mega_ll_mine(const MegaArgs& a, T* p) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) +
+                              static_cast<unsigned long long>(blockIdx.x % kLLCopies) * a.ll_copy_bytes);
+}
+
+__device__ __forceinline__ int mega_attn_splits(int seq_len, int max_splits, int per_split) {
+  return max(1, min(max_splits, (seq_len + per_split - 1) / per_split));
 }
 
 // Split partial record: acc[D], m, l, two floats of padding (16-byte rows).
@@ -352,9 +364,13 @@ template <int D>
 constexpr int kMegaPartStride = D + 4;
 // Largest split count the persistent step uses.
 constexpr int kMegaMaxMergeSplits = 32;
-// Up to this many splits the O projection's prologue merges them (one round
-// of L2 loads); beyond it the last split of each KV head to finish merges its
-// heads once and the prologue loads the bf16 result.
+// Grid-barrier form: up to this many splits the O projection's prologue
+// merges them (one round of L2 loads); beyond it the last split of each KV
+// head to finish merges its heads once and the prologue loads the bf16
+// result. The exchange form always merges in the attention phase (split 0
+// of each KV head, with the prologue's arithmetic up to this count, so the
+// two forms give the same bits), because every O-phase CTA polling every
+// split record (80 KB per CTA per attempt) cost ~4.7 us per layer.
 constexpr int kMegaPrologueMergeMax = 4;
 
 // Online logsumexp merge of the split records rec0[s * stride_s] for s in
@@ -469,9 +485,9 @@ __device__ __forceinline__ AttnItem mega_attn_item(const MegaArgs& a, int pos) {
     return it;
   }
   const int seq_len = pos + 1;
-  // Splits this step: enough for about two stages of positions each, at most
-  // the configured count -- a short context merges a handful, not all.
-  const int splits = mega_attn_splits(seq_len, a.splits, AG::P);
+  // Splits this step: about split_positions cached positions each, at most
+  // the configured count -- a short context is one split, and needs no merge.
+  const int splits = mega_attn_splits(seq_len, a.splits, a.split_positions);
   if (static_cast<int>(blockIdx.x) >= a.num_kv * splits) {
     it.nblocks = 0;
     it.kvh = -1;
@@ -591,6 +607,14 @@ __device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, cons
         L += c[1] * sc;
         A += c[2 + d] * sc;
       }
+      if (item.splits == 1) {
+        // One split: the record is the whole softmax, so the output is what
+        // the merge of one record gives (bf16(A / L), merged_bf16x8).
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        ll_store_all(a.attn_ll + static_cast<size_t>(item.kvh * G + g) * D + d, ll32_word(A * inv, ll_tag),
+                     a.ll_copy_bytes);
+        continue;
+      }
       unsigned long long* rec = lbase + (g * a.splits + item.split) * kMegaPartStride<D>;
       st_relaxed_u64(rec + d, ll64_word(A, ll_tag));
       if (d == 0) {
@@ -598,10 +622,33 @@ __device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, cons
         st_relaxed_u64(rec + D + 1, ll64_word(L, ll_tag));
       }
     }
-    if (item.splits <= kMegaPrologueMergeMax || item.split != 0) return true;
+    if (item.splits == 1 || item.split != 0) return true;
     named_sync(1, kGemvConsumers);  // this CTA's own record is written
     LLWait wt{a.status, a.wait_ns};
     bool ok = true;
+    if (item.splits <= kMegaPrologueMergeMax) {
+      // Few splits: the merge the O prologue of the barrier form does
+      // (merge_split_records from split 0, one thread per 8-dim chunk), so
+      // both forms compute the same bits.
+      for (int c = tid; c < G * D / 8; c += kGemvConsumers) {
+        const int g = c * 8 / D, d0 = c * 8 % D;
+        float M = kNegBig, L = 0.f;
+        float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+          ok = merge_split_records_ll<D>(lbase + static_cast<size_t>(g) * a.splits * kMegaPartStride<D>, 0,
+                                         item.splits, 1, d0, ll_tag, M, L, acc8, wt);
+        }
+        const uint4 o = merged_bf16x8(L, acc8);
+        uint32_t* dst = a.attn_ll + static_cast<size_t>(item.kvh * G + g) * D + d0;
+        const uint32_t t16 = ll_tag & 0xffffu;
+        const uint32_t words[8] = {(o.x << 16) | t16, (o.x & 0xffff0000u) | t16, (o.y << 16) | t16,
+                                   (o.y & 0xffff0000u) | t16, (o.z << 16) | t16, (o.z & 0xffff0000u) | t16,
+                                   (o.w << 16) | t16, (o.w & 0xffff0000u) | t16};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ll_store_all(dst + e, words[e], a.ll_copy_bytes);
+      }
+      return ok;
+    }
     const int sg = lane & 7;
     for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
       const int g = c * 8 / D, d0 = c * 8 % D;
@@ -629,7 +676,7 @@ __device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, cons
         const float inv = L > 0.f ? 1.f / L : 0.f;
         uint32_t* dst = a.attn_ll + static_cast<size_t>(item.kvh * G + g) * D + d0;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) st_relaxed_u32(dst + e, ll32_word(acc8[e] * inv, ll_tag));
+        for (int e = 0; e < 8; ++e) ll_store_all(dst + e, ll32_word(acc8[e] * inv, ll_tag), a.ll_copy_bytes);
       }
     }
     return ok;
@@ -942,10 +989,11 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
   float k_newf[8], v_newf[8];
   LLWait wt{a.status, a.wait_ns};
   bool ll_ok = true;
+  const uint32_t* qkvll = a.qkv_ll != nullptr ? mega_ll_mine(a, a.qkv_ll) : nullptr;
   if (new_lane && ll_in_tag != 0) {
-    const uint32_t* kh = a.qkv_ll + qd + item.kvh * D;
+    const uint32_t* kh = qkvll + qd + item.kvh * D;
     const uint32_t* ko = kh + (lane * 8 < D / 2 ? lane * 8 + D / 2 : lane * 8 - D / 2);
-    const uint32_t* vh = a.qkv_ll + qd + kvd + item.kvh * D + lane * 8;
+    const uint32_t* vh = qkvll + qd + kvd + item.kvh * D + lane * 8;
     const uint32_t* const grp[3] = {kh + lane * 8, ko, vh};
     uint4 g6[6];
     ll_ok = ll_poll_groups<6, false>([&](int i) -> const void* { return grp[i >> 1] + (i & 1) * 4; }, g6,
@@ -976,7 +1024,7 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
       rope8f<D>(a.qkv_f + (item.kvh * G + g) * D, lig, cs, qf);
     } else {
       if (ll_in_tag != 0) {
-        const uint32_t* qh = a.qkv_ll + (item.kvh * G + g) * D;
+        const uint32_t* qh = qkvll + (item.kvh * G + g) * D;
         const uint32_t* qo = qh + (lig * 8 < D / 2 ? lig * 8 + D / 2 : lig * 8 - D / 2);
         const uint32_t* const grp[2] = {qh + lig * 8, qo};
         uint4 g4[4];
@@ -1162,7 +1210,9 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
 }
 
 // O-phase prologue: the attention output staged in shared memory, each thread
-// one 8-element chunk. Up to kMegaPrologueMergeMax splits it is merged here
+// one 8-element chunk. With the exchange it is polled as the attention
+// phase's merged LL32 words. Otherwise, up to kMegaPrologueMergeMax splits it
+// is merged here
 // from the split partials with the logsumexp rule (merge_split_records) and
 // rounded to bf16 as the reference stores attn_out; beyond that the attention
 // phase has already merged it into `attn`. Uses named barrier 1; `xs` is
@@ -1172,26 +1222,18 @@ __device__ __forceinline__ void mega_attn_consume_tc(const uint8_t* ring, uint64
 template <int QD, int D, bool F32>
 __device__ __forceinline__ bool mega_stage_attention(const MegaArgs& a, int pos, bf16* xs, bf16* xs_lo,
                                                      uint32_t ll_tag = 0) {
-  const int splits = mega_attn_splits(pos + 1, a.splits, MegaAttnGeom<D>::P);
-  if (ll_tag != 0) {  // the same values, from the attention phase's LL words
+  const int splits = mega_attn_splits(pos + 1, a.splits, a.split_positions);
+  if (ll_tag != 0) {
+    // The same values, merged by the attention phase (every split count)
+    // and exchanged as LL32 words: 2 KB of polls per 512 outputs instead of
+    // every split record.
     LLWait wt{a.status, a.wait_ns};
     bool ok = true;
+    const uint32_t* attn_in = mega_ll_mine(a, a.attn_ll);
     for (int c = threadIdx.x; c < QD / 8 && ok; c += kGemvConsumers) {
-      const int col = c * 8;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (splits > kMegaPrologueMergeMax) {
-        uint4 g2[2];
-        ok = ll_poll_groups<2, false>([&](int i) -> const void* { return a.attn_ll + col + 4 * i; }, g2, ll_tag, wt);
-        v = ll32_values8(g2[0], g2[1]);
-      } else {
-        const int h = col / D, d0 = col % D;
-        float M = kNegBig, L = 0.f;
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        ok = merge_split_records_ll<D>(a.part_ll + static_cast<size_t>(h) * a.splits * kMegaPartStride<D>, 0,
-                                       splits, 1, d0, ll_tag, M, L, acc, wt);
-        v = merged_bf16x8(L, acc);
-      }
-      reinterpret_cast<uint4*>(xs)[c] = v;
+      uint4 g2[2];
+      ok = ll_poll_groups<2, false>([&](int i) -> const void* { return attn_in + c * 8 + 4 * i; }, g2, ll_tag, wt);
+      reinterpret_cast<uint4*>(xs)[c] = ll32_values8(g2[0], g2[1]);
     }
     return !named_sync_or(1, kGemvConsumers, !ok);
   }
@@ -1518,18 +1560,21 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
     // With the exchange, a CTA without rows in a phase reads none of its
     // inputs: every reader of an exchange buffer then also produces output
     // that the buffer's next writer must see first, so no word is rewritten
-    // while a reader still needs its previous value:
+    // while a reader still needs its previous value (the argument holds for
+    // each replica of a buffer, since every replica has the same writers):
     //   qkv_ll  read by ATTN(l); rewritten by QKV(l+1), whose writers polled
     //           every DOWN(l) residual word, written after each DOWN-row owner
-    //           finished O(l), which needed every attention record of layer l;
-    //   part_ll / attn_ll  read by O(l); rewritten by ATTN(l+1), whose CTAs
+    //           finished O(l), which needed the whole attention output of
+    //           layer l, written after the attention reads;
+    //   part_ll read by ATTN(l)'s split-0 mergers before they write attn_ll;
+    //   attn_ll read by O(l); both rewritten by ATTN(l+1), whose CTAs
     //           polled q/k/v rows written after their owners' QKV(l+1)
     //           prologue, which needed every DOWN(l) word -- written after
     //           each O-row owner (the same rows as DOWN) finished O(l);
     //   x_ll    read by GU(l) (O's sums) and QKV(l+1) (DOWN's); rewritten by
     //           DOWN(l) after polling every act word of GU(l), and by
-    //           O(l+1) after polling records that needed every q/k/v row of
-    //           QKV(l+1);
+    //           O(l+1) after polling the attention output, which needed
+    //           every q/k/v row of QKV(l+1);
     //   act_ll  read by DOWN(l); rewritten by GU(l+1) after polling every
     //           O(l+1) residual word, written by the DOWN-row owners after
     //           DOWN(l).
@@ -1552,8 +1597,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
           // test switch: CTA 0 keeps its first q/k/v rows out of the exchange
           // (plain stores), so the attention phase's polls time out
           g.ll_y32 = (a.test_skip_arrival && l == 0 && blockIdx.x == 0) ? nullptr : a.qkv_ll;
+          g.ll_copy_bytes = a.ll_copy_bytes;
           g.ll_out_tag = tag(l, 0);
-          g.ll_x = l > 0 ? a.x_ll : nullptr;
+          g.ll_x = l > 0 ? mega_ll_mine(a, a.x_ll) : nullptr;
           g.ll_in_tag = l > 0 ? tag(l - 1, 4) : 0u;
         }
         if constexpr (F32) {
@@ -1602,6 +1648,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.exact_resid = F32 ? 1 : 0;
         if (ll) {
           g.ll_y64 = a.x_ll;
+          g.ll_copy_bytes = a.ll_copy_bytes;
           g.ll_resid = a.x_ll;
           g.resid_embed = l == 0 ? a.embed + static_cast<size_t>(s_flags[5]) * H : nullptr;
           g.ll_out_tag = tag(l, 2);
@@ -1627,9 +1674,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         const int f0 = gemv_share(F, blockIdx.x, ctas), f1 = gemv_share(F, blockIdx.x + 1, ctas);
         if (ll) {
           g.ll_wait_ns = a.wait_ns;
-          g.ll_x = a.x_ll;
+          g.ll_x = mega_ll_mine(a, a.x_ll);
           g.ll_in_tag = tag(l, 2);
           g.ll_y32 = a.act_ll;
+          g.ll_copy_bytes = a.ll_copy_bytes;
           g.ll_out_tag = tag(l, 3);
         }
         if constexpr (F32) {
@@ -1654,9 +1702,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
         g.exact_resid = F32 ? 1 : 0;
         if (ll) {
           g.ll_wait_ns = a.wait_ns;
-          g.ll_v = a.act_ll;
+          g.ll_v = mega_ll_mine(a, a.act_ll);
           g.ll_in_tag = tag(l, 3);
           g.ll_y64 = a.x_ll;
+          g.ll_copy_bytes = a.ll_copy_bytes;
           g.ll_resid = a.x_ll;
           g.ll_out_tag = tag(l, 4);
         }
@@ -1683,7 +1732,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_step_kernel(const Mega
       const int v0 = gemv_share(a.vocab, blockIdx.x, ctas), v1 = gemv_share(a.vocab, blockIdx.x + 1, ctas);
       if (ll) {
         g.ll_wait_ns = a.wait_ns;
-        g.ll_x = a.x_ll;
+        g.ll_x = mega_ll_mine(a, a.x_ll);
         g.ll_in_tag = tag(a.layers - 1, 4);
       }
       if constexpr (F32) {
