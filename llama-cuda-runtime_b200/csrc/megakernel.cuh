@@ -372,6 +372,9 @@ constexpr int kMegaMaxMergeSplits = 32;
 // two forms give the same bits), because every O-phase CTA polling every
 // split record (80 KB per CTA per attempt) cost ~4.7 us per layer.
 constexpr int kMegaPrologueMergeMax = 4;
+// Exchange form, more than kMegaPrologueMergeMax splits: this many split CTAs
+// per KV head share the merge.
+constexpr int kMegaMergers = 4;
 
 // Online logsumexp merge of the split records rec0[s * stride_s] for s in
 // [s_begin, s_end) stepping by `step`, dims d0..d0+7, into (M, L, acc) --
@@ -622,7 +625,10 @@ __device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, cons
         st_relaxed_u64(rec + D + 1, ll64_word(L, ll_tag));
       }
     }
-    if (item.splits == 1 || item.split != 0) return true;
+    // Mergers: split 0 for a few splits; splits 0 .. kMegaMergers - 1 for
+    // many, each merging a quarter of the head group's 8-dim chunks (a
+    // quarter of the records' bytes polled per attempt).
+    if (item.splits == 1 || item.split >= (item.splits <= kMegaPrologueMergeMax ? 1 : kMegaMergers)) return true;
     named_sync(1, kGemvConsumers);  // this CTA's own record is written
     LLWait wt{a.status, a.wait_ns};
     bool ok = true;
@@ -650,11 +656,15 @@ __device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, cons
       return ok;
     }
     const int sg = lane & 7;
-    for (int c = tid >> 3; c < G * D / 8; c += kGemvConsumers / 8) {
+    constexpr int kChunks = G * D / 8;
+    const int c0 = item.split * ((kChunks + kMegaMergers - 1) / kMegaMergers);
+    const int c1 = min(kChunks, c0 + (kChunks + kMegaMergers - 1) / kMegaMergers);
+    for (int c = tid >> 3; c < kChunks; c += kGemvConsumers / 8) {
       const int g = c * 8 / D, d0 = c * 8 % D;
+      const bool mine = c >= c0 && c < c1;  // the same for the 8 lanes of a chunk
       float M = kNegBig, L = 0.f;
       float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (ok) {
+      if (ok && mine) {
         ok = merge_split_records_ll<D>(lbase + static_cast<size_t>(g) * a.splits * kMegaPartStride<D>, sg,
                                        item.splits, 8, d0, ll_tag, M, L, acc8, wt);
       }
@@ -672,7 +682,7 @@ __device__ __forceinline__ bool mega_attn_publish(const MegaArgs& a, int l, cons
         }
         M = Mn;
       }
-      if (sg == 0) {
+      if (sg == 0 && mine) {
         const float inv = L > 0.f ? 1.f / L : 0.f;
         uint32_t* dst = a.attn_ll + static_cast<size_t>(item.kvh * G + g) * D + d0;
 #pragma unroll
