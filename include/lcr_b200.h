@@ -286,8 +286,9 @@ LCR_API int lcr_generate_greedy(lcr_ctx* ctx, int first_token, int steps,
                         int32_t* tokens_out);
 
 /* Asynchronous pieces of the same loop, for timing and for host pipelines:
- * lcr_set_token stages (token, position) into device state on the context's
- * stream from host memory; lcr_enqueue_steps launches `steps` step graphs
+ * lcr_set_token reads the token from host memory during the call and stages
+ * (token, position) into device state on the context's stream, as one
+ * 8-byte copy; lcr_enqueue_steps launches `steps` step graphs
  * (mapping first, when paged, the pages of the positions they write);
  * lcr_read_token copies the latest device token to host memory (pinned for
  * true async) and lcr_sync waits for the stream. */

@@ -426,9 +426,13 @@ int launch_steps(lcr_ctx* c, int steps) {
 }
 
 int check_status(lcr_ctx* c) {
-  uint32_t st = 0;
-  LCRB_CUDA(cudaMemcpyAsync(&st, c->status, sizeof st, cudaMemcpyDeviceToHost, c->stream));
+  // The status word comes back through a pinned word (an asynchronous copy;
+  // a pageable destination would be a staged, slower one).
+  uint32_t* pst = reinterpret_cast<uint32_t*>(c->pinned + 2 * kPinnedRing);
+  *pst = 0;
+  LCRB_CUDA(cudaMemcpyAsync(pst, c->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
   LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  const uint32_t st = *pst;
   if (st == 0) return LCR_OK;
   LCRB_CUDA(cudaMemsetAsync(c->status, 0, sizeof st, c->stream));
   if (st & kStatusAbort) {
@@ -462,9 +466,12 @@ int stage_state(lcr_ctx* c, const int32_t* token_src, int position) {
     LCRB_CUDA(cudaMemcpyAsync(c->state + 1, slot + 1, sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
     return LCR_OK;
   }
+  // The token is read here, on the host, and travels with the position in
+  // one 8-byte copy (one copy fewer per step than copying each from where
+  // it lies).
+  slot[0] = *token_src;
   slot[1] = position;
-  LCRB_CUDA(cudaMemcpyAsync(c->state, token_src, sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
-  LCRB_CUDA(cudaMemcpyAsync(c->state + 1, slot + 1, sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+  LCRB_CUDA(cudaMemcpyAsync(c->state, slot, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
   return LCR_OK;
 }
 
@@ -889,7 +896,8 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   // The exchange needs the tensor-pipe attention phase and bf16 activations.
   c->ll = c->persistent && !c->f32 && c->kvmaps_dev != nullptr && d.head_dim == 64 && group <= 8 &&
           !(o.flags & (kFlagGridBarriers | kFlagCudaCoreAttention));
-  if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * 2 * kPinnedRing), "cudaMallocHost");
+  // The (token, position) ring, then one word for the status read-back.
+  if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * (2 * kPinnedRing + 2)), "cudaMallocHost");
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned_params, sizeof(float) * 8), "cudaMallocHost");
   if (st != LCR_OK) {
     release(c);
