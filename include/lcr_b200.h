@@ -217,7 +217,9 @@ typedef struct lcr_options { /* Model::Options, src/model.h:62-77 */
   int max_seq;          /* KV positions per sequence */
   int paged;            /* 0 = contiguous, 1 = paged */
   int page_size;        /* positions per page (paged); 16 in the reference */
-  int attention_splits; /* split-K blocks per KV head; 0 = choose */
+  int attention_splits; /* split-K blocks per KV head (at most; fewer only when
+                           the context has fewer than 32 positions per split);
+                           0 = choose: one split per ~384 cached positions */
   uint64_t page_order_seed; /* 0 = pages handed out in counter order;
                                otherwise a seeded permutation of the pool */
   int gemv_ctas;        /* CTAs per streaming GEMV; 0 = one per SM */

@@ -693,7 +693,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   // hop costs about as much as a few 128-position stages, so a split takes
   // about three stages: one split up to 384 positions (config 2), 18 at 8192
   // (config 3, the one-CTA-per-SM cap).
-  c->split_positions = 384;
+  // An explicit Options::attention_splits asks for that many splits: the
+  // step then splits down to 32-position chunks.
+  c->split_positions = o.attention_splits > 0 ? 32 : 384;
   if (const char* env = std::getenv("LCR_SPLIT_POSITIONS")) c->split_positions = std::max(32, std::atoi(env));
   c->persistent = (o.flags & kFlagNoPersistent) == 0 &&
                   mega_supported(d.hidden_size, qd, d.intermediate_size, d.head_dim, group);

@@ -151,15 +151,16 @@ def test_step_variants_are_bit_identical(tiny, variant):
 
 
 @pytest.mark.parametrize("paged", [False, True])
-@pytest.mark.parametrize("length", [40, 700])
-def test_exchange_matches_grid_barriers(tiny, paged, length):
+@pytest.mark.parametrize("length,splits", [(40, 0), (700, 0), (700, 6), (700, 11)])
+def test_exchange_matches_grid_barriers(tiny, paged, length, splits):
     """The persistent step's tagged-word exchange between phases (default)
     and its grid barriers compute the same bits: the prompt as decode steps,
-    then greedy steps -- one split per KV head at 40 positions, six (merged by
-    a designated split through the exchange) at 700."""
+    then greedy steps -- one split per KV head at 40 positions, the default
+    two at 700 (merged by split 0 with the O prologue's arithmetic), and six
+    and eleven at 700 (merged by four split CTAs per KV head)."""
     block, wdev = tiny
     prompt = ck.prompt_ids(5, length)
-    kw = dict(max_seq=length + 24, paged=paged, page_size=16, page_order_seed=13)
+    kw = dict(max_seq=length + 24, paged=paged, page_size=16, page_order_seed=13, attention_splits=splits)
     a = rt.Model(block, wdev, flags=rt.FLAG_PER_TOKEN_PREFILL, **kw)
     b = rt.Model(block, wdev, flags=rt.FLAG_PER_TOKEN_PREFILL | rt.FLAG_GRID_BARRIERS, **kw)
     a.prefill(prompt)
@@ -172,7 +173,8 @@ def test_exchange_matches_grid_barriers(tiny, paged, length):
 
 
 @pytest.mark.parametrize("paged", [False, True])
-def test_tiny_long_context_vs_oracle(tiny, paged):
+@pytest.mark.parametrize("splits", [0, 11])
+def test_tiny_long_context_vs_oracle(tiny, paged, splits):
     """700 cached positions: several 128-position KV stages per attention
     split and many splits per KV head, shuffled physical pages when paged --
     the persistent step's long-context path (config 3's shape on the tiny
@@ -180,7 +182,8 @@ def test_tiny_long_context_vs_oracle(tiny, paged):
     the oracle's chunk of the same rounding points)."""
     block, wdev = tiny
     prompt = ck.prompt_ids(3, 700)
-    m = rt.Model(block, wdev, max_seq=760, paged=paged, page_size=16, page_order_seed=99)
+    m = rt.Model(block, wdev, max_seq=760, paged=paged, page_size=16, page_order_seed=99,
+                 attention_splits=splits)
     ref32 = oracle.Model(block, 760)
     ref16 = oracle.Model(block, 760)
     m.prefill(prompt)
