@@ -34,6 +34,31 @@ namespace lcrb {
 
 constexpr int kApTcThreads = 192;
 constexpr int kApTcStages = 4;
+// Of the 8 groups of 8 exponentials per row and block, this many are
+// computed by exp2_fma on the FMA and integer pipes instead of ex2.approx:
+// the transcendental unit was the busiest pipe (61 % of its peak, the FMA
+// pipe 9 %).
+constexpr int kApTcFmaGroups = 2;
+
+// 2^x for x <= 8 without the transcendental unit: Cody-Waite reduction
+// x = n + f with n = round(x) (the 1.5 * 2^23 shift leaves n in the low
+// mantissa bits of t), 2^f for |f| <= 1/2 by a degree-4 polynomial, and n
+// added to the exponent field (modulo 2^9, which the 32-bit add carries out
+// of). The coefficients were fitted here to 2^f on [-1/2, 1/2] by
+// iteratively reweighted least squares on the relative error: at most
+// 2.7e-6 relative in fp32, far inside the bf16 rounding of P. Below 2^-125
+// it returns 0 (ex2.approx returns a value that is 0 after the MMA's scale).
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
+  float p = 0.009569993242621422f;
+  p = fmaf(p, f, 0.055917542427778244f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931218504905701f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  const int bits = __float_as_int(p) + static_cast<int>(static_cast<unsigned>(__float_as_int(t)) << 23);
+  return x < -125.0f ? 0.0f : __int_as_float(bits);
+}
 
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
@@ -286,7 +311,10 @@ __global__ void __launch_bounds__(kApTcThreads, 2) attn_prefill_tc_kernel(const 
       for (int g = 0; g < 8; ++g) {
         float p[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) p[e] = ex2_approx(fmaf(s[8 * g + e], a.scale_log2, -na));
+        for (int e = 0; e < 8; ++e) {
+          const float x = fmaf(s[8 * g + e], a.scale_log2, -na);
+          p[e] = g >= 8 - kApTcFmaGroups ? exp2_fma(x) : ex2_approx(x);
+        }
         sums[g] = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
 #pragma unroll
         for (int e = 0; e < 4; ++e) pk[4 * g + e] = pack_bf2(p[2 * e], p[2 * e + 1]);
