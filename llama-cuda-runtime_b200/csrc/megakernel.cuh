@@ -1,16 +1,20 @@
 // The whole decode step as ONE persistent cooperative kernel.
 //
-// One CTA per SM (cooperative launch guarantees they are co-resident), 8
-// consumer warps + 1 producer warp, a 12-stage x 16 KB shared-memory ring.
-// Per layer the step has five phases, each needing every output of the one
-// before (a batch-1 step is a chain of full reductions):
+// One CTA per SM (cooperative launch guarantees they are co-resident): 8
+// consumer warps, the ring producer (warp 8) and an L2 prefetcher (warp 9);
+// a 6-stage x 33 KB shared-memory ring of weight (or K/V) stages. Per layer
+// the step has five phases, each needing every output of the one before (a
+// batch-1 step is a chain of full reductions):
 //
 //   QKV   rows of [q;k;v]: RMSNorm prologue (embedding row for layer 0)
 //   ATTN  one (KV head, split) item per CTA: RoPE, KV write, split-K
-//         online softmax over the KV pages, last-CTA merge of the splits.
-//         With tensor maps of the cache (head_dim 64): QK^T and PV of each
-//         16-position unit on the tensor pipe (mega_attn_consume_tc);
-//         otherwise CUDA-core dot products, 8 lanes per position.
+//         online softmax over the KV pages; the splits are merged in this
+//         phase (split 0 of each KV head up to 4 splits, splits 0-3 each a
+//         quarter of the head group beyond; the grid-barrier form merges up
+//         to 4 in the O prologue). With tensor maps of the cache (head_dim
+//         64): QK^T and PV of each 16-position unit on the tensor pipe
+//         (mega_attn_consume_tc); otherwise CUDA-core dot products, 8 lanes
+//         per position.
 //   O     rows of o_proj, residual epilogue
 //   GU    gate/up row pairs: RMSNorm prologue, SwiGLU epilogue
 //   DOWN  rows of down_proj, residual epilogue
@@ -29,14 +33,15 @@
 //                bf16 normed inputs, qkv, roped q/k, attention output,
 //                projections, residual stream and SwiGLU output, with the
 //                unrounded residual sum feeding the norm.
-// Between
-// phases the consumers meet at a grid barrier (an arrival counter with a
-// bounded acquire spin). The producer never waits at barriers: it walks the
-// same schedule -- this CTA's rows of every matrix, and the KV blocks of its
-// attention item -- and keeps the ring full, so HBM keeps streaming the next
-// matrices while the consumers synchronise. The arithmetic per output is that
-// of the multi-kernel step (the same device functions), so the two paths
-// agree bit for bit.
+// Between phases (template LL): by default the phases exchange their outputs
+// as tagged words (ll.cuh) and each phase polls only its own inputs; the
+// other instance meets at a grid barrier (an arrival counter with a bounded
+// acquire spin). Both compute the same bits. The producer never waits at
+// phase boundaries: it walks the same schedule -- this CTA's rows of every
+// matrix, and the KV blocks of its attention item -- and keeps the ring full,
+// so HBM keeps streaming the next matrices while the consumers wait. The
+// arithmetic per output is that of the multi-kernel step (the same device
+// functions).
 #pragma once
 
 #include "attention.cuh"
