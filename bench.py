@@ -9,9 +9,10 @@ L2, so no L2 flush is needed between steps.
 
   value  device throughput: tokens/s from CUDA events on the context's stream
          around graph launches of the step, token feedback on the device.
-  e2e    the same through the C ABI with host buffers: every step copies its
-         token and position from pinned host memory, runs, and reads the next
-         token back, synchronising each step (the reference's decode loop).
+  e2e    the same through the C ABI with host buffers, one lcr_step_host call
+         per step: the token and position go down from host memory, the step
+         runs, the next token comes back with the status, synchronising each
+         step (the reference's decode loop).
   roofline  decode_step_kernel, the dominant kernel (one persistent launch per
          token): algorithmic bytes per launch (weights + the KV read at the
          window's mean context) / the CUDA-event time per launch measured
@@ -649,13 +650,13 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     pos = PROMPT - 1
+    tok = int(first)
     for i in range(e2e_steps):
         if pos >= PROMPT - 1 + WINDOW:
             pos = PROMPT - 1
-        m.set_token(tok_ptr, pos)        # H2D: token + position
-        m.enqueue_steps(1)
-        m.read_token(tok_ptr)            # D2H: next token
-        m.sync()
+        # one call per step (lcr_step_host): H2D token + position (8 B), the
+        # step, D2H next token + status (16 B), synchronised
+        tok = m.step_host(tok, pos)
         pos += 1
     e1.record(stream)
     torch.cuda.synchronize()
@@ -724,7 +725,7 @@ def main():
                          "launch_us": round(ms_per_step * 1000, 2),
                          "per_matrix_layer0": per_matrix},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4, "steps": e2e_steps},
+                    "d2h_bytes_per_step": 16, "steps": e2e_steps},
             "gpu_launches": reps * args.steps * m.step_launches(),
             "clocks": clocks,
             "cpu_baseline": base,

@@ -295,6 +295,12 @@ LCR_API int lcr_generate_greedy(lcr_ctx* ctx, int first_token, int steps,
  * lcr_read_token copies the latest device token to host memory (pinned for
  * true async) and lcr_sync waits for the stream. */
 LCR_API int lcr_set_token(lcr_ctx* ctx, const int32_t* host_token, int position);
+/* One step of the reference's host decode loop in one call: Model::decode
+ * (src/model.cu:347-368) of `token` at `position`, then the greedy pick of
+ * the logits that llama-run's loop reads back (src/main.cu:455-463,
+ * temperature 0). The next token arrives in *next_token with the step's
+ * status in the same read-back; synchronous. */
+LCR_API int lcr_step_host(lcr_ctx* ctx, int32_t token, int position, int32_t* next_token);
 LCR_API int lcr_enqueue_steps(lcr_ctx* ctx, int steps);
 LCR_API int lcr_read_token(lcr_ctx* ctx, int32_t* host_token);
 LCR_API int lcr_sync(lcr_ctx* ctx);

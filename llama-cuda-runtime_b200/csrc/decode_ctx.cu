@@ -745,7 +745,6 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   const size_t o_amax = carve(sizeof(unsigned long long));
   const size_t o_state = carve(sizeof(int32_t) * 4);
   const size_t o_hist = carve(sizeof(int32_t) * o.max_seq);
-  const size_t o_status = carve(sizeof(uint32_t));
   const size_t o_freq = carve(sizeof(float) * d.head_dim / 2);
   const size_t o_sparams = carve(sizeof(float) * 8);
   const size_t o_sampled = carve(sizeof(int32_t) * 4);
@@ -784,7 +783,9 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
     c->argmax_acc = reinterpret_cast<unsigned long long*>(b + o_amax);
     c->state = reinterpret_cast<int32_t*>(b + o_state);
     c->history = reinterpret_cast<int32_t*>(b + o_hist);
-    c->status = reinterpret_cast<uint32_t*>(b + o_status);
+    // The status word shares the state's 16 bytes (token, position, -,
+    // status), so one read-back carries the next token and the status.
+    c->status = reinterpret_cast<uint32_t*>(c->state + 3);
     c->inv_freq = reinterpret_cast<float*>(b + o_freq);
     c->sample_params = reinterpret_cast<float*>(b + o_sparams);
     c->sampled = reinterpret_cast<int32_t*>(b + o_sampled);
@@ -898,8 +899,8 @@ extern "C" int lcr_ctx_create(const lcr_model_desc* desc, const lcr_weights* wei
   // The exchange needs the tensor-pipe attention phase and bf16 activations.
   c->ll = c->persistent && !c->f32 && c->kvmaps_dev != nullptr && d.head_dim == 64 && group <= 8 &&
           !(o.flags & (kFlagGridBarriers | kFlagCudaCoreAttention));
-  // The (token, position) ring, then one word for the status read-back.
-  if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * (2 * kPinnedRing + 2)), "cudaMallocHost");
+  // The (token, position) ring, then four words for the state read-back.
+  if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned, sizeof(int32_t) * (2 * kPinnedRing + 4)), "cudaMallocHost");
   if (st == LCR_OK) cuda(cudaMallocHost(&c->pinned_params, sizeof(float) * 8), "cudaMallocHost");
   if (st != LCR_OK) {
     release(c);
@@ -1115,6 +1116,26 @@ extern "C" int lcr_enqueue_steps(lcr_ctx* c, int steps) {
 extern "C" int lcr_read_token(lcr_ctx* c, int32_t* host_token) {
   LCRB_REQUIRE(c && host_token, LCR_ERR_INVALID, "null argument");
   LCRB_CUDA(cudaMemcpyAsync(host_token, c->state, sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream));
+  return LCR_OK;
+}
+
+extern "C" int lcr_step_host(lcr_ctx* c, int32_t token, int position, int32_t* next_token) {
+  LCRB_REQUIRE(c && next_token, LCR_ERR_INVALID, "null argument");
+  LCRB_REQUIRE(position >= 0 && position < c->o.max_seq, LCR_ERR_STATE,
+               "position %d outside the cache built for %d", position, c->o.max_seq);
+  LCRB_REQUIRE(token >= 0 && token < c->d.vocab_size, LCR_ERR_INVALID, "token %d outside the vocabulary", token);
+  LCRB_CUDA(cudaSetDevice(c->device));
+  LCRB_TRY(stage_state(c, &token, position));
+  c->position = position;
+  LCRB_TRY(lcr_reserve_length(c, c->position + 1));
+  LCRB_TRY(launch_steps(c, 1));
+  c->position += 1;
+  // One read-back: the next token and, in the same 16 bytes, the status.
+  int32_t* back = c->pinned + 2 * kPinnedRing;
+  LCRB_CUDA(cudaMemcpyAsync(back, c->state, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream));
+  LCRB_CUDA(cudaStreamSynchronize(c->stream));
+  if (back[3] != 0) return check_status(c);
+  *next_token = back[0];
   return LCR_OK;
 }
 

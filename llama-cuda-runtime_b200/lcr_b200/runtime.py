@@ -135,6 +135,7 @@ _SIGS = {
     "lcr_sample_logits": (_I, [_V, _V, _F, _I, _F, _F, ctypes.POINTER(_I)]),
     "lcr_generate_greedy": (_I, [_V, _I, _I, _V]),
     "lcr_set_token": (_I, [_V, _V, _I]),
+    "lcr_step_host": (_I, [_V, ctypes.c_int32, _I, _V]),
     "lcr_enqueue_steps": (_I, [_V, _I]),
     "lcr_read_token": (_I, [_V, _V]),
     "lcr_sync": (_I, [_V]),
@@ -354,6 +355,13 @@ class Model:
     # --- async loop pieces ------------------------------------------------
     def set_token(self, host_token_ptr: int, position: int) -> None:
         check(lib().lcr_set_token(self.ctx, host_token_ptr, int(position)))
+
+    def step_host(self, token: int, position: int) -> int:
+        """One decode step of `token` at `position` and its greedy next token,
+        synchronously, in one call (lcr_step_host)."""
+        out = ctypes.c_int32()
+        check(lib().lcr_step_host(self.ctx, int(token), int(position), ctypes.byref(out)))
+        return int(out.value)
 
     def enqueue_steps(self, steps: int) -> None:
         check(lib().lcr_enqueue_steps(self.ctx, int(steps)))
